@@ -1,0 +1,434 @@
+#!/usr/bin/env python
+"""QORA-TTS decode-path benchmark (one JSON line on rank 0).
+
+Workload (BASELINE.json metric "talker+predictor frames/s per B200 (batch 1 &
+32) and Q4 GEMV HBM GB/s vs roofline"): the per-frame loop of
+generate_new.rs:606-665 on the 1.7B dims (28-layer talker, 5-layer code
+predictor with head_dim 128 as in the reference config), random-init
+N(0, 0.02) Q4 weights, 64-token N(0,1) prefill per stream, sampling with
+top-k 50 / temperature 0.9 / repetition penalty 1.05, EOS ignored.
+One step = one frame for every stream on the GPU: talker step + 15-code
+predictor + sampling, replayed as one CUDA graph.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Multi-GPU: one process per GPU (torchrun); each GPU runs its own B streams
+(replicas, no data-path collective); value = all frames / max-over-ranks time.
+--impl reference times the reference's CPU algorithm (the oracle port of the
+Rust path: AVX-512 Q4 GEMV + worker pool) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "qora-tts-12hz-1.7b_b200"))
+sys.path.insert(0, os.path.join(ROOT, "oracle"))
+
+import numpy as np  # noqa: E402
+
+METRIC = "talker+predictor frames/s per B200 (batch 1 & 32) and Q4 GEMV HBM GB/s vs roofline"
+PREFILL = 64
+REF_FRAMES_PER_S = 1.0 / 0.35   # README.md:272-280: 0.35 s/frame talker+predictor, laptop CPU
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=400)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-batch32", action="store_true")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------- CPU arm
+def oracle_model_from(tw, pw):
+    """Wrap the engine's host weight arrays (reference layout) for the oracle."""
+    import pyoracle as po
+    c = tw.cfg
+
+    def q(w):
+        return po.Q4Weight(w.packed, w.scales, w.k, w.n)
+
+    def lay(lw):
+        return po.LayerWeights(q(lw.q_proj), q(lw.k_proj), q(lw.v_proj), q(lw.o_proj),
+                               q(lw.gate_proj), q(lw.up_proj), q(lw.down_proj), lw.q_norm,
+                               lw.k_norm, lw.input_norm, lw.post_attn_norm)
+
+    ocfg = po.ModelConfig(**{k: getattr(c, k) for k in po.ModelConfig.__dataclass_fields__})
+    half = c.t_head_dim // 2
+    return po.Model(cfg=ocfg, t_layers=[lay(x) for x in tw.layers],
+                    codec_embedding=q(tw.codec_embedding), codec_head=q(tw.codec_head),
+                    t_final_norm=tw.final_norm,
+                    t_rope=po.rope_tables(c.t_head_dim, c.t_max_pos, c.rope_theta,
+                                          [24, 20, 20] if half == 64 else [half]),
+                    p_layers=[lay(x) for x in pw.layers],
+                    input_proj=q(pw.input_proj) if pw.input_proj is not None else None,
+                    input_proj_bias=pw.input_proj_bias,
+                    codec_embeddings=[q(e) for e in pw.codec_embeddings],
+                    lm_heads=[q(h) for h in pw.lm_heads], p_final_norm=pw.final_norm,
+                    p_rope=po.rope_tables(c.p_head_dim, c.p_max_pos, c.rope_theta))
+
+
+def cpu_frames(model, frames: int, warmup: int, budget_s: float | None = None):
+    """Times the oracle frame loop (batch 1) on the host; returns frames/s."""
+    import pyoracle as po
+    om = po.OracleModel(model)
+    c = model.cfg
+    tkv = om.talker_kv(PREFILL + warmup + frames + 8)
+    pkv = om.predictor_kv()
+    x = po.synth_normal(1000, 1.0, PREFILL * c.t_hidden).reshape(PREFILL, c.t_hidden)
+    hidden = om.talker_prefill(x, tkv, 0)
+    st = {"logits": om.codec_head(hidden), "hidden": hidden.copy(),
+          "prev": np.zeros(16, np.uint32), "rng": 1000}
+    text = po.synth_normal(77, 1.0, c.t_hidden)
+    params = po.SampleParams(0.9, 50, 1.0, 1.05)
+    pos = PREFILL
+    for _ in range(warmup):
+        om.frame(tkv, pkv, params, text, pos, st)
+        pos += 1
+    t0 = time.perf_counter()
+    done = 0
+    while done < frames:
+        om.frame(tkv, pkv, params, text, pos, st)
+        pos += 1
+        done += 1
+        if budget_s is not None and time.perf_counter() - t0 > budget_s and done >= 3:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt, done, dt, po.lib().oq_pool_workers()
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import pyoracle as po
+    po.build()
+    cfg = po.ModelConfig()
+    model = po.Model.synth(cfg)
+    fps, done, dt, cores = cpu_frames(model, args.steps, args.warmup)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": fps, "unit": "frames/s",
+        "n_gpus": args.gpus, "steps": done, "warmup": args.warmup, "ms_per_step": 1000.0 * dt / done,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": fps / REF_FRAMES_PER_S,
+        "dtype": "f32 (Q4 weights)", "data": "synthetic: random-init N(0,0.02) Q4 weights",
+        "config": {"workload": "frame loop batch 1 (talker step + 15-code predictor + top-k 50 "
+                               "sampling), 1.7B dims, predictor head_dim 128, 64-token prefill",
+                   "batch_per_gpu": 1},
+        "cpu_baseline": {"value": fps, "unit": "frames/s", "cores": cores, "kind": "port",
+                         "sample": f"{done} frames after {args.warmup} warm-up and a 64-token prefill"},
+        "e2e": {"value": fps, "unit": "frames/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+# ----------------------------------------------------------------- GPU arm
+def gemv_stream_roofline(E, ctx, tw, torch, reps=3):
+    """k_gemv over the whole talker weight set at batch 1, back to back
+    (197 launches, 796 MB > L2): average launch duration and algorithmic GB/s."""
+    mats = []
+    for lw in tw.layers:
+        for nm in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
+            mats.append(E.DeviceQ4(ctx, getattr(lw, nm)))
+    mats.append(E.DeviceQ4(ctx, tw.codec_head))
+    xs = {k: torch.randn(1, k, device="cuda") for k in {m.k for m in mats}}
+    ys = {n: torch.empty(1, n, device="cuda") for n in {m.n for m in mats}}
+    byts = sum(0.5625 * m.k * m.n + 4 * (m.k + m.n) for m in mats)
+    st = torch.cuda.current_stream()
+    for m in mats:
+        m.gemv(xs[m.k], ys[m.n])
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        for m in mats:
+            m.gemv(xs[m.k], ys[m.n])
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    del mats
+    return byts, ms
+
+
+def gemv_sweep(E, ctx, torch, qb):
+    """Config 1: per-shape GB/s at batch 1/4/16, rotating weight copies >= 512 MB."""
+    shapes = [(2048, 4096), (2048, 1024), (2048, 2048), (2048, 6144), (6144, 2048), (2048, 3072)]
+    out = {}
+    for k, n in shapes:
+        w = qb.synth_q4(4242 + k + n, 0.02, k, n)
+        wbytes = 0.5625 * k * n
+        copies = max(4, int(np.ceil(4 * L2_BYTES / wbytes)))
+        devs = [E.DeviceQ4(ctx, w) for _ in range(copies)]
+        res = {}
+        for B in (1, 4, 16):
+            x = torch.randn(B, k, device="cuda")
+            y = torch.empty(B, n, device="cuda")
+            for d in devs[:4]:
+                d.gemv(x, y)
+            torch.cuda.synchronize()
+            iters = max(100, copies)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for i in range(iters):
+                devs[i % copies].gemv(x, y)
+            e1.record()
+            torch.cuda.synchronize()
+            us = 1000.0 * e0.elapsed_time(e1) / iters
+            gbs = (wbytes + 4 * B * (k + n)) / (us * 1e-6) / 1e9
+            res[f"b{B}"] = {"us": round(us, 2), "GB/s": round(gbs, 1)}
+        out[f"{k}x{n}"] = res
+        del devs
+        torch.cuda.empty_cache()
+    return out
+
+
+def engine_rate(E, talker, pred, torch, qb, B, K, W, seed0, with_e2e=False):
+    cfg = talker.cfg
+    max_pos = PREFILL + W + (2 * K if with_e2e else K) + 8
+    eng = E.Engine(talker, pred, B, max_pos)
+    x = np.stack([qb.synth_normal(seed0 + b, 1.0, PREFILL * cfg.t_hidden).reshape(PREFILL, cfg.t_hidden)
+                  for b in range(B)])
+    eng.prefill(x, [seed0 + b for b in range(B)])
+    eng.use_graph(True)
+    text = torch.from_numpy(qb.synth_normal(77, 1.0, B * cfg.t_hidden).reshape(B, cfg.t_hidden)).cuda()
+    codes = torch.zeros(B, 16, dtype=torch.int32, device="cuda")
+    for _ in range(W):
+        eng.frame(text, codes)
+    torch.cuda.synchronize()
+    return eng, text, codes
+
+
+def run_ours(args):
+    import torch
+    import qora_b200 as qb
+    from qora_b200 import engine as E
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+
+    K, W, B = args.steps, max(3, args.warmup), args.batch
+    cfg = qb.ModelConfig()
+    tw, pw = qb.synth_talker(cfg), qb.synth_predictor(cfg)
+    ctx = E.Context(local)
+    maxb = max(B, 1 if args.no_batch32 else 32)
+    talker = E.Talker(ctx, tw, max_batch=maxb)
+    pred = E.CodePredictor(ctx, pw, max_batch=maxb)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- device-resident frame loop (value)
+    eng, text, codes = engine_rate(E, talker, pred, torch, qb, B, K, W, 1000 + rank * B, True)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    with ClockSampler(local) as clk:
+        e0.record(st)
+        for _ in range(K):
+            eng.frame(text, codes)
+        e1.record(st)
+        torch.cuda.synchronize()
+    ms = max_over_ranks(e0.elapsed_time(e1))
+    kernels = eng.kernels_per_frame()
+    ctx.check_device_error()
+    frames = B * K * world
+    value = frames / (ms / 1000.0)
+
+    # ---- end to end through the public host API (pinned host buffers)
+    text_pin = text.cpu().pin_memory()
+    codes_pin = torch.zeros(B, 16, dtype=torch.int32).pin_memory()
+    text_h, codes_h = text_pin.numpy(), codes_pin.numpy()
+    barrier()
+    e0.record(st)
+    for _ in range(K):
+        eng.frame_host(text_h, codes_h)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ms_e2e = max_over_ranks(e0.elapsed_time(e1))
+    e2e = {"value": frames / (ms_e2e / 1000.0), "unit": "frames/s",
+           "h2d_bytes_per_step": int(B * cfg.t_hidden * 4), "d2h_bytes_per_step": int(B * 16 * 4)}
+    del eng
+    torch.cuda.synchronize()
+
+    # ---- batch 32
+    b32 = None
+    if not args.no_batch32:
+        K32 = max(10, min(K, 60))
+        eng32, text32, codes32 = engine_rate(E, talker, pred, torch, qb, 32, K32, W,
+                                             50000 + rank * 32)
+        barrier()
+        e0.record(st)
+        for _ in range(K32):
+            eng32.frame(text32, codes32)
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms32 = max_over_ranks(e0.elapsed_time(e1))
+        b32 = {"value": 32 * K32 * world / (ms32 / 1000.0), "unit": "frames/s", "steps": K32,
+               "ms_per_step": ms32 / K32}
+        del eng32
+        torch.cuda.synchronize()
+
+    if rank != 0:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    # ---- roofline of the dominant kernel (k_gemv over the talker weights, batch 1)
+    peak, peak_src = peaks()
+    byts, gms = gemv_stream_roofline(E, ctx, tw, torch)
+    n_launch = 7 * len(tw.layers) + 1
+    achieved = byts / (gms / 1000.0) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
+            traffic = json.load(f).get("k_gemv_talker_b1_bytes_per_launch")
+    except Exception:
+        pass
+    roof = {"bound": "hbm", "kernel": "k_gemv (talker Q4 GEMVs, batch 1, back-to-back)",
+            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+            "frac": round(achieved / peak, 4), "peak_source": peak_src,
+            "traffic": traffic, "launches": n_launch,
+            "us_per_launch": round(1000.0 * gms / n_launch, 2),
+            "algorithmic_bytes_per_launch": round(byts / n_launch)}
+
+    sweep = None if args.no_sweep else gemv_sweep(E, ctx, torch, qb)
+
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        model = oracle_model_from(tw, pw)
+        fps, done, dt, cores = cpu_frames(model, 60, 1, budget_s=20.0)
+        cpu = {"value": round(fps, 3), "unit": "frames/s", "cores": cores, "kind": "port",
+               "sample": f"{done} frames (batch 1) after 1 warm-up frame and a 64-token prefill, "
+                         f"oracle port of the reference AVX-512 GEMV + worker pool"}
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "frames/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": round(ms / K, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": round(value / REF_FRAMES_PER_S, 2), "dtype": "f32 (Q4 weights)",
+        "data": "synthetic: random-init N(0,0.02) Q4 weights, N(0,1) prefill and text rows",
+        "config": {"workload": "frame loop: talker step + 15-code predictor + top-k 50 sampling "
+                               "(one CUDA graph per frame)",
+                   "batch_per_gpu": B, "prefill_tokens": PREFILL, "talker_layers": cfg.t_layers,
+                   "predictor_head_dim": cfg.p_head_dim, "parallelism": f"replicas x{world}",
+                   "l2": "per-frame weight stream 0.95 GB > 126 MB L2, no flush",
+                   "vs_baseline_ref": "README.md:280 0.35 s/frame (laptop CPU)"},
+        "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
+        "gpu_launches": int(kernels * K),
+        "kernels_per_step": kernels,
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+        "batch32": b32,
+        "gemv_sweep": sweep,
+    }
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,227 @@
+/*
+ * qora_cuda.h — C ABI of the B200 decode engine for QORA-TTS-12Hz-1.7B.
+ *
+ * Drop-in boundary for the reference's Rust operator surface (paths are
+ * within swordreforge/QORA-TTS-12Hz-1.7B).  Each entry point names the
+ * reference function it replaces.  Conventions:
+ *   - every function returns a status (QORA_OK = 0); no exceptions cross the
+ *     ABI; qora_last_error() gives a message for the calling thread;
+ *   - tensor pointers are DEVICE pointers unless the name ends in _host;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default);
+ *   - handles are owned by the library and freed by their *_destroy; a
+ *     context, and everything created from it, is used from one host thread
+ *     or stream at a time (calls on one stream are ordered by that stream);
+ *   - weights arrive in the reference layout (gemv.rs:26-31, input-major
+ *     [k][n], 4-bit nibbles in 32-wide output groups, f16 scale per group)
+ *     and are repacked on upload.
+ * The reference has no Result on its hot path; its panics (slice bounds,
+ * argmax unwrap, debug asserts) become QORA_ERR_* statuses here.
+ */
+#ifndef QORA_CUDA_H
+#define QORA_CUDA_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define QORA_OK 0
+#define QORA_ERR_INVALID 1   /* null pointer, bad argument */
+#define QORA_ERR_SHAPE 2     /* shape mismatch (e.g. x length != k) */
+#define QORA_ERR_CUDA 3      /* a CUDA runtime call failed */
+#define QORA_ERR_OOM 4       /* device allocation failed */
+#define QORA_ERR_RANGE 5     /* position past RoPE table or KV capacity */
+#define QORA_ERR_UNSUPPORTED 6
+#define QORA_ERR_TIMEOUT 7   /* bounded device wait expired */
+
+typedef struct qora_ctx qora_ctx;             /* per-device context */
+typedef struct qora_w4 qora_w4;               /* device Q4 weight */
+typedef struct qora_kv qora_kv;               /* device KV cache, `streams` slabs */
+typedef struct qora_talker qora_talker;       /* device TalkerWeights */
+typedef struct qora_predictor qora_predictor; /* device CodePredictorWeights */
+typedef struct qora_engine qora_engine;       /* per-GPU frame-loop state */
+
+/* Host view of one Q4 weight in the reference layout (gemv.rs:26-31). */
+typedef struct qora_q4_host {
+    const uint8_t *packed;   /* k * (n/32) * 16 bytes */
+    const uint16_t *scales;  /* k * (n/32) f16 bit patterns */
+    int64_t k;               /* input dim (rows)  */
+    int64_t n;               /* output dim (cols) */
+} qora_q4_host;
+
+/* TalkerLayerWeights / PredictorLayerWeights (talker.rs:19-31,
+ * code_predictor.rs:14-26). Norm vectors are f16 bit patterns. */
+typedef struct qora_layer_host {
+    qora_q4_host q_proj, k_proj, v_proj, o_proj, gate_proj, up_proj, down_proj;
+    const uint16_t *q_norm, *k_norm, *input_norm, *post_attn_norm;
+} qora_layer_host;
+
+/* TalkerWeights hot-path fields (talker.rs:33-56). */
+typedef struct qora_talker_host {
+    int32_t num_layers, hidden, num_heads, num_kv_heads, head_dim, ffn, vocab;
+    int32_t rope_max_pos;            /* max_position_embeddings (config.rs:142) */
+    double rope_theta;               /* 1e6 (config.rs:135) */
+    const qora_layer_host *layers;
+    qora_q4_host codec_embedding;    /* [vocab][hidden] */
+    qora_q4_host codec_head;         /* [hidden][vocab] */
+    const uint16_t *final_norm;
+} qora_talker_host;
+
+/* CodePredictorWeights (code_predictor.rs:28-46). */
+typedef struct qora_predictor_host {
+    int32_t num_layers, hidden, num_heads, num_kv_heads, head_dim, ffn, vocab;
+    int32_t num_groups;              /* 15 acoustic code groups */
+    int32_t rope_max_pos;
+    double rope_theta;
+    const qora_layer_host *layers;
+    qora_q4_host input_proj;         /* [talker_hidden][hidden]; packed == NULL => identity */
+    const float *input_proj_bias;    /* [hidden] or NULL */
+    const qora_q4_host *codec_embeddings; /* num_groups x [vocab][talker_hidden] */
+    const qora_q4_host *lm_heads;         /* num_groups x [hidden][vocab] */
+    const uint16_t *final_norm;
+} qora_predictor_host;
+
+/* TTSParams sampling fields (generate_new.rs:38-79). */
+typedef struct qora_sample_params {
+    float temperature;         /* 0.9 */
+    int32_t top_k;             /* 50 */
+    float top_p;               /* 1.0 (off) */
+    float repetition_penalty;  /* 1.05 */
+} qora_sample_params;
+
+/* ---------------------------------------------------------------- context */
+int qora_ctx_create(int32_t device, qora_ctx **out);
+void qora_ctx_destroy(qora_ctx *ctx);
+const char *qora_status_string(int32_t status);
+const char *qora_last_error(void);
+/* Device-side error flag raised by kernels (range errors, bounded waits);
+ * reading it synchronises `stream`; the flag is cleared. */
+int qora_ctx_check_device_error(qora_ctx *ctx, void *stream);
+
+/* ------------------------------------------------------------ gemv.rs */
+/* quantize_f32_to_q4 (gemv.rs:92-130), on the host. */
+int qora_q4_quantize_host(const float *data_host, int64_t k, int64_t n, uint8_t *packed_host,
+                          uint16_t *scales_host);
+/* Deterministic synthetic weights (random-init N(0, sigma), then quantised by
+ * quantize_f32_to_q4): counter-based splitmix64 + Box-Muller on the host. */
+int qora_synth_normal_host(uint64_t seed, float sigma, int64_t count, float *out_host);
+int qora_synth_q4_host(uint64_t seed, float sigma, int64_t k, int64_t n, uint8_t *packed_host,
+                       uint16_t *scales_host);
+/* Q4Weight -> device (repacked to the engine's column-group-major layout). */
+int qora_q4_weight_upload(qora_ctx *ctx, const qora_q4_host *w, qora_w4 **out);
+void qora_q4_weight_destroy(qora_w4 *w);
+/* gemv (gemv.rs:149, 290-346) for `batch` input rows:
+ * y[b][0..n) = x[b][0..k) @ W, rows strided by k and n.  batch 1..512. */
+int qora_q4_gemv(qora_ctx *ctx, const qora_w4 *w, const float *x, float *y, int32_t batch,
+                 void *stream);
+/* gemm (gemv.rs:157, 349-412): seq_len token rows. */
+int qora_q4_gemm(qora_ctx *ctx, const qora_w4 *w, const float *x, int64_t seq_len, float *y,
+                 void *stream);
+/* embed_lookup (gemv.rs:165, 415-437): out[i][0..n) = dequantised row tokens[i]. */
+int qora_q4_embed_rows(qora_ctx *ctx, const qora_w4 *w, const uint32_t *tokens, int32_t count,
+                       float *out, void *stream);
+/* rms_norm_f16 (gemv.rs:445-454) over `rows` rows of length n. */
+int qora_rms_norm_f16(qora_ctx *ctx, const float *x, const uint16_t *gamma, int64_t n,
+                      int32_t rows, float *out, void *stream);
+
+/* ------------------------------------------------------------ rope.rs */
+/* build_mrope_tables (rope.rs:11-41; predictor: loader.rs:859-874), host. */
+int qora_rope_tables_host(int32_t head_dim, int32_t max_pos, double theta,
+                          const int32_t *sections, int32_t n_sections, float *cos_host,
+                          float *sin_host);
+
+/* ------------------------------------------------------------ KV cache */
+/* RawKvCache / empty_kv_cache (gemv.rs:75-86) for `streams` independent
+ * streams, preallocated to max_pos positions.  Device layout per layer:
+ * [stream][kv_head][max_pos][head_dim] f32, plus a length per stream. */
+int qora_kv_create(qora_ctx *ctx, int32_t num_layers, int32_t kv_heads, int32_t head_dim,
+                   int32_t max_pos, int32_t streams, qora_kv **out);
+void qora_kv_destroy(qora_kv *kv);
+/* Clear streams (code_predictor.rs:227-231).  ids_host NULL => all streams. */
+int qora_kv_reset(qora_kv *kv, const int32_t *ids_host, int32_t count, void *stream);
+int qora_kv_lengths_host(qora_kv *kv, int32_t *len_host, void *stream);
+/* Copy one stream's cache (prefix snapshot / restore, generate_new.rs:317-355). */
+int qora_kv_copy_stream(qora_kv *dst, int32_t dst_stream, const qora_kv *src,
+                        int32_t src_stream, void *stream);
+/* Device pointers of one layer's K and V slabs and the length array. */
+int qora_kv_layer_ptrs(qora_kv *kv, int32_t layer, float **k, float **v, int32_t **len);
+/* Copy one layer's K and V slabs (all streams, [stream][kv_head][max_pos][head_dim])
+ * into caller device buffers (KV snapshot of the reference's RawKvCache). */
+int qora_kv_export_layer(qora_kv *kv, int32_t layer, float *k_out, float *v_out, void *stream);
+
+/* ------------------------------------------------------------ talker.rs */
+int qora_talker_create(qora_ctx *ctx, const qora_talker_host *host, int32_t max_batch,
+                       qora_talker **out);
+void qora_talker_destroy(qora_talker *t);
+/* forward_with_embedding (talker.rs:263-360) for B streams of `kv`:
+ * emb [B][hidden] (not modified); positions [B] RoPE positions (int32);
+ * hidden [B][hidden] final-normed; logits [B][vocab] (may be NULL).
+ * Appends one position to each stream's cache. */
+int qora_talker_step(qora_talker *t, qora_kv *kv, const float *emb, const int32_t *positions,
+                     int32_t B, float *hidden, float *logits, void *stream);
+/* prefill_talker_raw_from (talker.rs:379-482) for one stream:
+ * x [T][hidden], start_pos must equal the stream's cache length. */
+int qora_talker_prefill(qora_talker *t, qora_kv *kv, int32_t kv_stream, const float *x,
+                        int32_t T, int32_t start_pos, float *hidden, void *stream);
+/* apply_codec_head (talker.rs:647-649). */
+int qora_talker_codec_head(qora_talker *t, const float *hidden, int32_t B, float *logits,
+                           void *stream);
+/* embed_codec_token (talker.rs:152-154) for B tokens. */
+int qora_talker_embed_codec(qora_talker *t, const uint32_t *tokens, int32_t B, float *out,
+                            void *stream);
+
+/* ------------------------------------------------------------ code_predictor.rs */
+int qora_predictor_create(qora_ctx *ctx, const qora_predictor_host *host, int32_t max_batch,
+                          qora_predictor **out);
+void qora_predictor_destroy(qora_predictor *p);
+/* generate_acoustic_codes (code_predictor.rs:218-273) for B streams:
+ * hidden [B][talker_hidden], semantic [B][talker_hidden] -> codes [B][num_groups].
+ * logits [B][num_groups][vocab] optional (NULL).  forced [B][num_groups]
+ * optional: teacher forcing, the forced code (not the argmax) feeds the next
+ * step.  kv must have num_groups+1 positions per stream; it is reset. */
+int qora_predictor_frame(qora_predictor *p, qora_kv *kv, const float *hidden,
+                         const float *semantic, int32_t B, uint32_t *codes, float *logits,
+                         const uint32_t *forced, void *stream);
+/* get_acoustic_embeddings_sum (code_predictor.rs:287-300): codes [B][num_groups]. */
+int qora_predictor_embed_sum(qora_predictor *p, const uint32_t *codes, int32_t B, float *out,
+                             void *stream);
+
+/* ------------------------------------------------------------ generate_new.rs */
+/* sample_token (generate_new.rs:771-862) for B rows of V logits.
+ * prev [B][n_prev] (repetition penalty), rng [B] xorshift64 states (in/out),
+ * out [B].  top_p in (0,1) needs 0 < top_k <= 1024. */
+int qora_sample(qora_ctx *ctx, const float *logits, int32_t B, int32_t V, const uint32_t *prev,
+                int32_t n_prev, uint64_t *rng, const qora_sample_params *params, uint32_t *out,
+                void *stream);
+
+/* The frame loop (generate_new.rs:606-665) for B streams on one GPU: sample
+ * code0 -> semantic embedding -> predictor (15 codes) -> embedding sum +
+ * text row -> talker step.  EOS is not acted on (streams run every frame). */
+int qora_engine_create(qora_talker *t, qora_predictor *p, int32_t B, int32_t max_pos,
+                       const qora_sample_params *params, qora_engine **out);
+void qora_engine_destroy(qora_engine *e);
+/* Prefill every stream with x_host [B][T][hidden] (one talker prefill per
+ * stream), set RNG seeds (seeds_host [B]) and clear the previous-code window. */
+int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const uint64_t *seeds_host,
+                        void *stream);
+/* Run one frame (device buffers): text [B][hidden] -> codes [B][16]. */
+int qora_engine_frame(qora_engine *e, const float *text, uint32_t *codes, void *stream);
+/* Run one frame from HOST buffers: text_host [B][hidden] in, codes_host [B][16]
+ * out; both copies are issued on `stream` and the call returns after the
+ * codes have landed. */
+int qora_engine_frame_host(qora_engine *e, const float *text_host, uint32_t *codes_host,
+                           void *stream);
+/* Capture one frame into a CUDA graph (enable=1) and replay it per frame. */
+int qora_engine_use_graph(qora_engine *e, int32_t enable);
+/* Number of kernels one frame launches (for launch accounting). */
+int qora_engine_kernels_per_frame(qora_engine *e, int32_t *count);
+/* Device pointers of the engine state: logits [B][vocab], hidden [B][hidden],
+ * prev [B][16], rng [B], positions [B]. */
+int qora_engine_state(qora_engine *e, float **logits, float **hidden, uint32_t **prev,
+                      uint64_t **rng, int32_t **positions);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* QORA_CUDA_H */

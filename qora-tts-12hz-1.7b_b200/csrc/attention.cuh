@@ -1,0 +1,50 @@
+// Decode / prefill attention over the device KV cache.
+#pragma once
+
+#include "common.cuh"
+
+namespace qora {
+
+// Layer view of the KV cache: [stream][kv_head][max_pos][head_dim] f32.
+struct KVLayer {
+    float *k = nullptr;
+    float *v = nullptr;
+    int kv_heads = 0, head_dim = 0, max_pos = 0;
+};
+
+struct AttnArgs {
+    // raw projections, row r = stream * T + t: [q (heads*hd) | k (kvh*hd) | v (kvh*hd)]
+    float *qkv = nullptr;
+    int64_t ldqkv = 0;
+    int heads = 0, kv_heads = 0;
+    int T = 1;                      // query tokens per stream in this call
+    int streams = 0;
+    const __half *q_gamma = nullptr, *k_gamma = nullptr;  // qk-norm (talker.rs:89-99)
+    const float *rope_cos = nullptr, *rope_sin = nullptr; // [rope_max_pos][hd/2]
+    int rope_max_pos = 0;
+    const int *pos = nullptr;       // RoPE position of token 0 per stream; NULL => cache length
+    const int *len = nullptr;       // cache length per stream before this call
+    KVLayer kv;
+    bool preappended = false;       // q/k already normed+roped and K/V appended
+    float *out = nullptr;           // [rows][heads*hd]
+    int64_t ldout = 0;
+    // split merge scratch
+    float *part_o = nullptr;        // [rows][kvh][kAttnMaxSplit][G][hd]
+    float *part_ml = nullptr;       // [rows][kvh][kAttnMaxSplit][G][2]
+    unsigned *tickets = nullptr;    // [rows][kvh]
+    int *err = nullptr;
+};
+
+// qk-norm + RoPE + append for T tokens per stream (used when T > 1).
+int launch_qkv_post(const AttnArgs &a, cudaStream_t stream);
+// Attention for every row; fused qk-norm/RoPE/append when !a.preappended (T == 1).
+int launch_attention(const AttnArgs &a, cudaStream_t stream);
+
+inline size_t attn_part_o_floats(int rows, int kvh, int heads, int hd) {
+    return (size_t)rows * kvh * kAttnMaxSplit * (heads / kvh) * hd;
+}
+inline size_t attn_part_ml_floats(int rows, int kvh, int heads) {
+    return (size_t)rows * kvh * kAttnMaxSplit * (heads / kvh) * 2;
+}
+
+}  // namespace qora

@@ -1,0 +1,193 @@
+// Internal shared definitions of the QORA B200 engine (sm_100a).
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+#include <vector>
+
+#include "qora_cuda.h"
+
+namespace qora {
+
+constexpr int kGroup = 32;          // Q4 group width (gemv.rs:18)
+constexpr int kMaxRows = 512;       // rows (streams x tokens) per GEMV launch
+constexpr int kAttnMaxSplit = 16;   // position splits per (row, kv head)
+constexpr int kEngineKernelsUnknown = -1;
+
+// ------------------------------------------------------------------ errors
+int set_error(int code, const char *fmt, ...);
+
+#define QORA_TRY(expr)                   \
+    do {                                 \
+        int rc__ = (expr);               \
+        if (rc__ != QORA_OK) return rc__; \
+    } while (0)
+
+#define QORA_CUDA(call)                                                                      \
+    do {                                                                                     \
+        cudaError_t e__ = (call);                                                            \
+        if (e__ != cudaSuccess)                                                              \
+            return ::qora::set_error(e__ == cudaErrorMemoryAllocation ? QORA_ERR_OOM         \
+                                                                      : QORA_ERR_CUDA,       \
+                                     "%s:%d %s: %s", __FILE__, __LINE__, #call,              \
+                                     cudaGetErrorString(e__));                               \
+    } while (0)
+
+#define QORA_LAUNCH_CHECK() QORA_CUDA(cudaGetLastError())
+
+inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Device error flag codes (written by kernels, read by the host).
+enum DeviceError : int {
+    kDevOk = 0,
+    kDevRange = 1,   // position past the RoPE table or KV capacity
+    kDevNaN = 2,     // NaN logits reached an argmax / sampler
+    kDevTimeout = 3, // bounded wait expired
+};
+
+// ------------------------------------------------------------ device memory
+// Owning device buffer (freed on destruction).
+struct DevBuf {
+    void *p = nullptr;
+    size_t bytes = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    DevBuf(DevBuf &&o) noexcept : p(o.p), bytes(o.bytes) {
+        o.p = nullptr;
+        o.bytes = 0;
+    }
+    DevBuf &operator=(DevBuf &&o) noexcept {
+        if (this != &o) {
+            release();
+            p = o.p;
+            bytes = o.bytes;
+            o.p = nullptr;
+            o.bytes = 0;
+        }
+        return *this;
+    }
+    ~DevBuf() { release(); }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    int alloc(size_t n) {
+        release();
+        if (n == 0) return QORA_OK;
+        cudaError_t e = cudaMalloc(&p, n);
+        if (e != cudaSuccess) {
+            p = nullptr;
+            return set_error(QORA_ERR_OOM, "cudaMalloc(%zu): %s", n, cudaGetErrorString(e));
+        }
+        bytes = n;
+        return QORA_OK;
+    }
+    int zero(cudaStream_t s = nullptr) {
+        if (!p) return QORA_OK;
+        QORA_CUDA(cudaMemsetAsync(p, 0, bytes, s));
+        return QORA_OK;
+    }
+    template <class T>
+    T *as() const { return reinterpret_cast<T *>(p); }
+};
+
+// ------------------------------------------------------------ device helpers
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float &lo, float &hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+// Packed 2-wide fp32 FMA / add (sm_100a): d = a * b + c lane-wise, one rounding.
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 128-bit streaming load through the non-coherent path, no L1 allocation.
+__device__ __forceinline__ uint4 ldg_stream(const uint4 *p) {
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float silu_ref(float x) {
+    // gemv.rs:486-488: x / (1 + exp(-x))
+    return __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
+}
+
+__device__ __forceinline__ void raise_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// ------------------------------------------------------------ weights
+// Device Q4 weight: column-group-major copy of the reference layout.
+//   nib[c][k] : 16 bytes = the 32 nibbles of group c in row k (byte j holds
+//               columns 32c+2j (low) and 32c+2j+1 (high), as in gemv.rs)
+//   scl[c][k] : f16 scale of group c in row k
+// A warp reading rows k0..k0+31 of one group reads 512 contiguous bytes.
+struct Q4Dev {
+    const uint4 *nib = nullptr;
+    const __half *scl = nullptr;
+    int64_t k = 0, n = 0;  // n may exceed 32*C: the tail stays zero (gemv.rs:846-861)
+    int64_t C = 0;         // full groups
+};
+
+// Row-major device copy of an embedding table in the reference layout
+// (row = token): packed[tok][n/2], scales[tok][n/32].
+struct EmbDev {
+    const uint8_t *packed = nullptr;
+    const __half *scl = nullptr;
+    int64_t rows = 0, n = 0;
+};
+
+}  // namespace qora
+
+struct qora_ctx {
+    int device = 0;
+    int num_sms = 148;
+    qora::DevBuf scratch;   // split-K partials for the generic GEMV entry points
+    qora::DevBuf tickets;   // split-K arrival counters (self-resetting)
+    qora::DevBuf err;       // device error flag
+    int ensure_scratch(size_t part_bytes, size_t ticket_count);
+};
+
+struct qora_w4 {
+    qora_ctx *ctx = nullptr;
+    qora::DevBuf nib, scl, rowmajor_packed, rowmajor_scl;
+    qora::Q4Dev dev;
+    qora::EmbDev emb;  // valid after qora_q4_embed_rows first use (lazy)
+    std::vector<uint8_t> host_packed;   // kept only until the row-major copy exists
+    std::vector<uint16_t> host_scales;
+};

@@ -1,0 +1,545 @@
+// Q4 GEMV kernels for sm_100a (CUDA cores, packed f32x2 FMA).
+//
+// Replaces the reference's gemv/gemm (gemv.rs:149-162, 290-412) and its
+// AVX-512 inner kernel (simd.rs:203-269).  Math per output column j:
+//     y[j] = sum_k  (f32(scale[k][g]) * x[k]) * (q[k][j] - 8)
+// The per-row product s = scale * x is formed exactly as gemv.rs:265 does;
+// the per-weight multiply-add is one fused f32 FMA (the reference rounds the
+// product and the sum separately; the difference is within the 1e-3
+// chunk-assembly tolerance the reference itself accepts, gemv.rs:806-809).
+//
+// Work decomposition: the weight is stored column-group-major (see Q4Dev), a
+// warp owns one 32-column group and 128 rows (4 per lane, lanes = consecutive
+// rows, so every load instruction reads 512 contiguous bytes).  Lane partials
+// are combined by a butterfly reduce-scatter (lane l ends with column l),
+// then across the CTA's warps in fixed order, then across split-K CTAs by
+// the last-arriving CTA in fixed split order.  The result is deterministic.
+#include "gemv.cuh"
+
+namespace qora {
+
+namespace {
+
+constexpr int kRowsPerLane = 4;
+constexpr uint32_t kMagic = 0x4B000000u;  // 2^23 as f32 bits
+
+template <int XM>
+__device__ __forceinline__ float load_x(const GemvArgs &a, int r, int64_t kr, float inv) {
+    if constexpr (XM == X_PLAIN) {
+        return __ldg(a.x + (int64_t)r * a.ldx + kr);
+    } else if constexpr (XM == X_RMSNORM) {
+        // rms_norm_f16 (gemv.rs:451): x * inv_rms * gamma
+        float xv = __ldg(a.x + (int64_t)r * a.ldx + kr);
+        return __fmul_rn(__fmul_rn(xv, inv), __half2float(a.gamma[kr]));
+    } else {
+        // embed_lookup_q4 (gemv.rs:425-433): scale * (q - 8)
+        const uint32_t t = a.tok[(int64_t)r * a.ldtok];
+        const uint8_t byte = a.emb.packed[(int64_t)t * (a.emb.n >> 1) + (kr >> 1)];
+        const int q = (kr & 1) ? (byte >> 4) : (byte & 15);
+        const float sc = __half2float(a.emb.scl[(int64_t)t * (a.emb.n >> 5) + (kr >> 5)]);
+        return __fmul_rn(sc, (float)(q - 8));
+    }
+}
+
+// Sum of a per-thread value over the CTA's split-K partial rows, or the
+// epilogue for one (row, column) result.
+template <int EM>
+__device__ __forceinline__ float epilogue_value(const GemvArgs &a, int r, int64_t col, float v) {
+    if constexpr (EM == E_BIAS) return __fadd_rn(v, a.bias[col]);
+    if constexpr (EM == E_RESID) return __fadd_rn(a.y[(int64_t)r * a.ldy + col], v);
+    return v;
+}
+
+// Writes the final values for one warp-group (32 columns of one row).
+// For E_SWIGLU, v is the gate sum and u the up sum (silu(gate) * up, talker.rs:344).
+template <int EM>
+__device__ __forceinline__ void finalize_group(const GemvArgs &a, int r, int64_t out_group,
+                                               int lane, float v, float u, int64_t n_out) {
+    const int64_t col = out_group * 32 + lane;
+    float y;
+    if constexpr (EM == E_SWIGLU) {
+        y = __fmul_rn(silu_ref(v), u);
+    } else {
+        y = epilogue_value<EM>(a, r, col, v);
+    }
+    if (col < n_out) a.y[(int64_t)r * a.ldy + col] = y;
+    if (a.ss_out) {
+        const float sq = warp_sum(__fmul_rn(y, y));
+        if (lane == 0) a.ss_out[(int64_t)r * a.ldss_out + out_group] = sq;
+    }
+    if (a.tbest_v) {
+        // per-tile argmax, last index on ties (code_predictor.rs:336-339)
+        float bv = y;
+        int bi = (int)col;
+        if (y != y) raise_error(a.err, kDevNaN);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi > bi)) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if (lane == 0) {
+            a.tbest_v[(int64_t)r * gridDim.x + blockIdx.x] = bv;
+            a.tbest_i[(int64_t)r * gridDim.x + blockIdx.x] = bi;
+        }
+    }
+}
+
+template <int B, int XM, int EM>
+__global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
+    constexpr int CPC = (EM == E_SWIGLU) ? 2 : 1;
+    constexpr int R = kRowsPerLane;
+    __shared__ float inv_s[kMaxRows];
+    __shared__ float red[8][B][32];
+    __shared__ int last_flag;
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int WR = a.WR;
+    const int cc = warp / WR, wr = warp % WR;
+    const int64_t c = (int64_t)blockIdx.x * CPC + cc;
+    const int s = blockIdx.y, z = blockIdx.z;
+    const int64_t k = a.w.k;
+    const int64_t k_begin = (int64_t)s * a.rows_per_cta_k;
+    const int64_t k_end = min(k, k_begin + (int64_t)a.rows_per_cta_k);
+    const int64_t wrow0 = k_begin + (int64_t)wr * 32 * R;
+    const int r_begin = z * a.rows_per_z;
+    const int r_end = min(a.rows, r_begin + a.rows_per_z);
+    const int64_t C = a.w.C;
+    const int64_t n32 = C * 32;
+    const int64_t n_out = (EM == E_SWIGLU) ? (C / 2) * 32 : a.w.n;
+
+    if constexpr (XM == X_RMSNORM) {
+        for (int r = r_begin + threadIdx.x; r < r_end; r += blockDim.x) {
+            const float *ssr = a.ss + (int64_t)r * a.ldss;
+            float t = 0.0f;
+            for (int i = 0; i < a.ss_tiles; i++) t = __fadd_rn(t, ssr[i]);
+            // gemv.rs:448: 1 / sqrt(sum/size + 1e-6)
+            inv_s[r - r_begin] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
+        }
+        __syncthreads();
+    }
+
+    const uint4 *nibc = a.w.nib + c * k;
+    const __half *sclc = a.w.scl + c * k;
+    const bool write_side = (XM == X_RMSNORM) && a.side && blockIdx.x == 0 && cc == 0;
+    const uint64_t neg01 = pk2(-8388616.0f, -8388736.0f);    // -(2^23 + 8),    -(2^23 + 8*16)
+    const uint64_t neg23 = pk2(-8390656.0f, -8421376.0f);    // -(2^23 + 8*256), -(2^23 + 8*4096)
+    const int items = CPC * B * 32;
+
+    for (int r0 = r_begin; r0 < r_end; r0 += B) {
+        uint64_t acc[B][16];
+#pragma unroll
+        for (int b = 0; b < B; b++)
+#pragma unroll
+            for (int j = 0; j < 16; j++) acc[b][j] = 0ull;
+
+        uint4 wv[R];
+        float sc[R];
+        float xs[R][B];
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            const int64_t kr = wrow0 + lane + 32 * i;
+            const bool ok = kr < k_end;
+            wv[i] = ok ? ldg_stream(nibc + kr) : make_uint4(0u, 0u, 0u, 0u);
+            sc[i] = ok ? __half2float(sclc[kr]) : 0.0f;
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const int r = r0 + b;
+                const float inv = (XM == X_RMSNORM && r < r_end) ? inv_s[r - r_begin] : 0.0f;
+                xs[i][b] = (ok && r < r_end) ? load_x<XM>(a, r, kr, inv) : 0.0f;
+            }
+        }
+        if (write_side) {
+#pragma unroll
+            for (int i = 0; i < R; i++) {
+                const int64_t kr = wrow0 + lane + 32 * i;
+#pragma unroll
+                for (int b = 0; b < B; b++)
+                    if (kr < k_end && r0 + b < r_end) a.side[(int64_t)(r0 + b) * a.ldside + kr] = xs[i][b];
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            uint64_t s01[B], s23[B];
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const float sv = __fmul_rn(sc[i], xs[i][b]);  // gemv.rs:265
+                s01[b] = pk2(sv, sv * 0.0625f);
+                s23[b] = pk2(sv * 0.00390625f, sv * 0.000244140625f);
+            }
+            const uint32_t words[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+#pragma unroll
+                for (int h = 0; h < 2; h++) {
+                    const uint32_t v = h ? (words[q] >> 16) : words[q];
+                    // nibble p of v -> 16^p * (q_p - 8) exactly: OR into the
+                    // mantissa of 2^23, subtract 2^23 + 8 * 16^p.
+                    const uint64_t f01 = fadd2(pk2(__uint_as_float((v & 0xFu) | kMagic),
+                                                   __uint_as_float((v & 0xF0u) | kMagic)),
+                                               neg01);
+                    const uint64_t f23 = fadd2(pk2(__uint_as_float((v & 0xF00u) | kMagic),
+                                                   __uint_as_float((v & 0xF000u) | kMagic)),
+                                               neg23);
+                    const int j = 4 * q + 2 * h;
+#pragma unroll
+                    for (int b = 0; b < B; b++) {
+                        acc[b][j] = ffma2(s01[b], f01, acc[b][j]);
+                        acc[b][j + 1] = ffma2(s23[b], f23, acc[b][j + 1]);
+                    }
+                }
+            }
+        }
+        // butterfly reduce-scatter: lane l ends with the warp total of column l
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 16; j++) upk2(acc[b][j], v[2 * j], v[2 * j + 1]);
+#pragma unroll
+            for (int sft = 16; sft >= 1; sft >>= 1) {
+                const bool up = (lane & sft) != 0;
+#pragma unroll
+                for (int j = 0; j < sft; j++) {
+                    const float send = up ? v[j] : v[j + sft];
+                    const float keep = up ? v[j + sft] : v[j];
+                    v[j] = keep + __shfl_xor_sync(0xffffffffu, send, sft);
+                }
+            }
+            red[warp][b][lane] = v[0];
+        }
+        __syncthreads();
+        if (a.S == 1) {
+            // whole K in this CTA: finish here
+            const int nitems = (EM == E_SWIGLU) ? B * 32 : items;
+            for (int it = threadIdx.x; it < nitems; it += blockDim.x) {
+                const int l = it & 31;
+                const int b = (it >> 5) % B;
+                const int cc2 = (it >> 5) / B;
+                const int r = r0 + b;
+                float v = 0.0f, u = 0.0f;
+                for (int w = 0; w < WR; w++) v += red[cc2 * WR + w][b][l];
+                if constexpr (EM == E_SWIGLU)
+                    for (int w = 0; w < WR; w++) u += red[WR + w][b][l];
+                if (r < r_end) {
+                    const int64_t grp = (EM == E_SWIGLU) ? (int64_t)blockIdx.x
+                                                         : (int64_t)blockIdx.x * CPC + cc2;
+                    finalize_group<EM>(a, r, grp, l, v, u, n_out);
+                }
+            }
+        } else {
+            for (int it = threadIdx.x; it < items; it += blockDim.x) {
+                const int l = it & 31;
+                const int b = (it >> 5) % B;
+                const int cc2 = (it >> 5) / B;
+                const int r = r0 + b;
+                float v = 0.0f;
+                for (int w = 0; w < WR; w++) v += red[cc2 * WR + w][b][l];
+                if (r < r_end) {
+                    const int64_t col = ((int64_t)blockIdx.x * CPC + cc2) * 32 + l;
+                    __stcg(a.part + ((int64_t)s * a.rows + r) * n32 + col, v);
+                }
+            }
+        }
+        __syncthreads();
+    }
+
+    // tail columns beyond the last full group stay zero (gemv.rs:846-861)
+    if (EM == E_STORE && a.w.n > n32 && blockIdx.x == 0 && s == 0) {
+        for (int r = r_begin; r < r_end; r++)
+            for (int64_t col = n32 + threadIdx.x; col < a.w.n; col += blockDim.x)
+                a.y[(int64_t)r * a.ldy + col] = 0.0f;
+    }
+
+    if (a.S > 1) {
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned t = atomicAdd(&a.tickets[(int64_t)z * gridDim.x + blockIdx.x], 1u);
+            last_flag = (t == (unsigned)(a.S - 1));
+        }
+        __syncthreads();
+        if (!last_flag) return;
+        __threadfence();
+        // last arriver: sum the S partials in split order, then the epilogue
+        const int nitems = (EM == E_SWIGLU) ? B * 32 : items;
+        for (int r0 = r_begin; r0 < r_end; r0 += B) {
+            for (int it = threadIdx.x; it < nitems; it += blockDim.x) {
+                const int l = it & 31;
+                const int b = (it >> 5) % B;
+                const int cc2 = (it >> 5) / B;
+                const int r = r0 + b;
+                if (r >= r_end) continue;  // whole warp shares r: uniform
+                const int64_t col = ((int64_t)blockIdx.x * CPC + cc2) * 32 + l;
+                float v = 0.0f, u = 0.0f;
+                for (int sp = 0; sp < a.S; sp++) {
+                    v += __ldcg(a.part + ((int64_t)sp * a.rows + r) * n32 + col);
+                    if constexpr (EM == E_SWIGLU)
+                        u += __ldcg(a.part + ((int64_t)sp * a.rows + r) * n32 + col + 32);
+                }
+                const int64_t grp = (EM == E_SWIGLU) ? (int64_t)blockIdx.x
+                                                     : (int64_t)blockIdx.x * CPC + cc2;
+                finalize_group<EM>(a, r, grp, l, v, u, n_out);
+            }
+        }
+        if (threadIdx.x == 0) a.tickets[(int64_t)z * gridDim.x + blockIdx.x] = 0u;
+    }
+
+    if (a.gticket) {
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            const unsigned t = atomicAdd(a.gticket, 1u);
+            last_flag = (t == (unsigned)(gridDim.x * gridDim.z - 1));
+        }
+        __syncthreads();
+        if (!last_flag) return;
+        __threadfence();
+        if (a.amax) {
+            for (int r = threadIdx.x; r < a.rows; r += blockDim.x) {
+                float bv = __ldcg(a.tbest_v + (int64_t)r * gridDim.x);
+                int bi = __ldcg(a.tbest_i + (int64_t)r * gridDim.x);
+                for (unsigned t = 1; t < gridDim.x; t++) {
+                    const float v = __ldcg(a.tbest_v + (int64_t)r * gridDim.x + t);
+                    const int i = __ldcg(a.tbest_i + (int64_t)r * gridDim.x + t);
+                    if (v >= bv) {  // later tile holds later indices: last max wins
+                        bv = v;
+                        bi = i;
+                    }
+                }
+                a.amax[(int64_t)r * a.ldamax] = (uint32_t)bi;
+            }
+        }
+        if (a.adv_len) {
+            for (int st = threadIdx.x; st < a.adv_streams; st += blockDim.x) {
+                a.adv_len[st] += a.adv_T;
+                if (a.adv_pos) a.adv_pos[st] += a.adv_T;
+            }
+        }
+        if (threadIdx.x == 0) *a.gticket = 0u;
+    }
+}
+
+template <int XM, int EM>
+int launch_b(const GemvArgs &a, const GemvPlan &p, cudaStream_t st) {
+    switch (p.B) {
+        case 1: k_gemv<1, XM, EM><<<p.grid, p.block, 0, st>>>(a); break;
+        case 2: k_gemv<2, XM, EM><<<p.grid, p.block, 0, st>>>(a); break;
+        default: k_gemv<4, XM, EM><<<p.grid, p.block, 0, st>>>(a); break;
+    }
+    QORA_LAUNCH_CHECK();
+    return QORA_OK;
+}
+
+template <int XM>
+int launch_e(const GemvArgs &a, int emode, const GemvPlan &p, cudaStream_t st) {
+    switch (emode) {
+        case E_STORE: return launch_b<XM, E_STORE>(a, p, st);
+        case E_BIAS: return launch_b<XM, E_BIAS>(a, p, st);
+        case E_RESID: return launch_b<XM, E_RESID>(a, p, st);
+        case E_SWIGLU: return launch_b<XM, E_SWIGLU>(a, p, st);
+    }
+    return set_error(QORA_ERR_INVALID, "bad epilogue mode %d", emode);
+}
+
+// ---------------------------------------------------------------- repack
+__global__ void k_repack(const uint8_t *__restrict__ src, const __half *__restrict__ src_scl,
+                         int64_t k, int64_t C, uint4 *__restrict__ dst, __half *__restrict__ dst_scl,
+                         int64_t dst_k_stride, int64_t dst_off, int64_t dst_stride) {
+    const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (idx >= k * C) return;
+    const int64_t c = idx / k, kr = idx % k;  // consecutive threads: consecutive rows
+    const uint4 *s16 = reinterpret_cast<const uint4 *>(src + (kr * C + c) * 16);
+    const int64_t cd = dst_off + c * dst_stride;
+    dst[cd * dst_k_stride + kr] = *s16;
+    dst_scl[cd * dst_k_stride + kr] = src_scl[kr * C + c];
+}
+
+__global__ void k_embed_rows(EmbDev e, const uint32_t *__restrict__ tok, int64_t ldtok,
+                             float *__restrict__ out, int64_t ldout) {
+    const int i = blockIdx.x;
+    const uint32_t t = tok[(int64_t)i * ldtok];
+    const uint8_t *p = e.packed + (int64_t)t * (e.n >> 1);
+    const __half *s = e.scl + (int64_t)t * (e.n >> 5);
+    for (int64_t j = threadIdx.x; j < e.n; j += blockDim.x) {
+        const uint8_t byte = p[j >> 1];
+        const int q = (j & 1) ? (byte >> 4) : (byte & 15);
+        out[(int64_t)i * ldout + j] = __fmul_rn(__half2float(s[j >> 5]), (float)(q - 8));
+    }
+}
+
+__global__ void k_copy_rowstats(const float *__restrict__ src, int64_t ldsrc, float *__restrict__ dst,
+                                int64_t lddst, int n, float *__restrict__ ss, int64_t ldss) {
+    const int r = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    for (int g = warp; g * 32 < n; g += nw) {
+        const int j = g * 32 + lane;
+        const float v = j < n ? src[(int64_t)r * ldsrc + j] : 0.0f;
+        if (j < n && dst) dst[(int64_t)r * lddst + j] = v;
+        const float sq = warp_sum(__fmul_rn(v, v));
+        if (lane == 0) ss[(int64_t)r * ldss + g] = sq;
+    }
+}
+
+__global__ void k_rmsnorm_rows(const float *__restrict__ x, const __half *__restrict__ gamma,
+                               int64_t n, float *__restrict__ out) {
+    __shared__ float red[32];
+    __shared__ float inv;
+    const int r = blockIdx.x;
+    const float *xr = x + (int64_t)r * n;
+    float t = 0.0f;
+    for (int64_t j = threadIdx.x; j < n; j += blockDim.x) t += __fmul_rn(xr[j], xr[j]);
+    t = warp_sum(t);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s = 0.0f;
+        for (int w = 0; w < (int)(blockDim.x >> 5); w++) s += red[w];
+        inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(s, (float)n), 1e-6f)));
+    }
+    __syncthreads();
+    for (int64_t j = threadIdx.x; j < n; j += blockDim.x)
+        out[(int64_t)r * n + j] = __fmul_rn(__fmul_rn(xr[j], inv), __half2float(gamma[j]));
+}
+
+}  // namespace
+
+GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms) {
+    GemvPlan p{};
+    p.cpc = (emode == E_SWIGLU) ? 2 : 1;
+    p.B = rows >= 4 ? 4 : (rows >= 2 ? 2 : 1);
+    if (rows == 3) p.B = 4;
+    p.rows_per_z = rows <= 16 ? rows : 16;
+    p.Z = (rows + p.rows_per_z - 1) / p.rows_per_z;
+    const int64_t tiles = C / p.cpc;
+    int WR = 8 / p.cpc;
+    const int64_t max_wr_rows = (k + 127) / 128;
+    while (WR > 1 && WR / 2 >= max_wr_rows) WR /= 2;  // do not exceed K
+    int64_t S = (k + WR * 128 - 1) / (WR * 128);
+    while (WR > 1 && tiles * S * p.Z < 2LL * num_sms) {
+        WR /= 2;
+        S = (k + WR * 128 - 1) / (WR * 128);
+    }
+    p.WR = WR;
+    p.S = (int)S;
+    p.rows_per_cta_k = WR * 128;
+    p.grid = dim3((unsigned)tiles, (unsigned)p.S, (unsigned)p.Z);
+    p.block = dim3(32 * p.cpc * WR);
+    p.part_floats = p.S > 1 ? (size_t)p.S * rows * C * 32 : 0;
+    p.tickets = (size_t)tiles * p.Z;
+    return p;
+}
+
+int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &p, float *part,
+                unsigned *tickets, unsigned *gticket, cudaStream_t st) {
+    if (a.rows <= 0 || a.rows > kMaxRows)
+        return set_error(QORA_ERR_SHAPE, "gemv rows %d outside 1..%d", a.rows, kMaxRows);
+    if (p.S > 1 && (!part || !tickets))
+        return set_error(QORA_ERR_INVALID, "split-K GEMV needs scratch");
+    if (a.gticket == nullptr && (a.amax || a.adv_len)) a.gticket = gticket;
+    if ((a.amax || a.adv_len) && !a.gticket)
+        return set_error(QORA_ERR_INVALID, "global stage needs a ticket");
+    a.B = p.B;
+    a.WR = p.WR;
+    a.S = p.S;
+    a.Z = p.Z;
+    a.rows_per_cta_k = p.rows_per_cta_k;
+    a.rows_per_z = p.rows_per_z;
+    a.part = part;
+    a.tickets = tickets;
+    switch (xmode) {
+        case X_PLAIN: return launch_e<X_PLAIN>(a, emode, p, st);
+        case X_RMSNORM: return launch_e<X_RMSNORM>(a, emode, p, st);
+        case X_EMBED: return launch_e<X_EMBED>(a, emode, p, st);
+    }
+    return set_error(QORA_ERR_INVALID, "bad prologue mode %d", xmode);
+}
+
+int repack_q4(const uint8_t *src_packed, const __half *src_scl, int64_t k, int64_t n,
+              uint4 *dst_nib, __half *dst_scl, int64_t dst_k_stride, int64_t dst_off,
+              int64_t dst_stride, cudaStream_t stream) {
+    const int64_t C = n / kGroup;
+    const int64_t total = k * C;
+    if (total == 0) return QORA_OK;
+    const int threads = 256;
+    const int64_t blocks = (total + threads - 1) / threads;
+    k_repack<<<(unsigned)blocks, threads, 0, stream>>>(src_packed, src_scl, k, C, dst_nib, dst_scl,
+                                                       dst_k_stride, dst_off, dst_stride);
+    QORA_LAUNCH_CHECK();
+    return QORA_OK;
+}
+
+int launch_embed_rows(const EmbDev &e, const uint32_t *tok, int64_t ldtok, int count, float *out,
+                      int64_t ldout, cudaStream_t stream) {
+    if (count <= 0) return QORA_OK;
+    k_embed_rows<<<count, 256, 0, stream>>>(e, tok, ldtok, out, ldout);
+    QORA_LAUNCH_CHECK();
+    return QORA_OK;
+}
+
+int launch_copy_rowstats(const float *src, int64_t ldsrc, float *dst, int64_t lddst, int rows,
+                         int n, float *ss, int64_t ldss, cudaStream_t stream) {
+    if (rows <= 0) return QORA_OK;
+    k_copy_rowstats<<<rows, 256, 0, stream>>>(src, ldsrc, dst, lddst, n, ss, ldss);
+    QORA_LAUNCH_CHECK();
+    return QORA_OK;
+}
+
+int launch_rmsnorm_rows(const float *x, const __half *gamma, int64_t n, int rows, float *out,
+                        cudaStream_t stream) {
+    if (rows <= 0) return QORA_OK;
+    k_rmsnorm_rows<<<rows, 256, 0, stream>>>(x, gamma, n, out);
+    QORA_LAUNCH_CHECK();
+    return QORA_OK;
+}
+
+// Upload reference-layout parts of one fused weight (all with the same k) into
+// a column-group-major buffer of C_total groups: part i's group c lands at
+// group offs[i] + c * strides[i].
+int upload_q4_parts(const qora_q4_host *parts, const int64_t *offs, const int64_t *strides,
+                    int nparts, int64_t k, int64_t C_total, DevBuf &nib, DevBuf &scl, Q4Dev &out,
+                    cudaStream_t stream) {
+    QORA_TRY(nib.alloc((size_t)(C_total * k) * 16));
+    QORA_TRY(scl.alloc((size_t)(C_total * k) * 2));
+    for (int i = 0; i < nparts; i++) {
+        const qora_q4_host &h = parts[i];
+        if (!h.packed || !h.scales) return set_error(QORA_ERR_INVALID, "null weight part");
+        if (h.k != k || h.n % kGroup != 0)
+            return set_error(QORA_ERR_SHAPE, "weight part %d: k=%lld n=%lld (need k=%lld, n%%32==0)",
+                             i, (long long)h.k, (long long)h.n, (long long)k);
+        const int64_t C = h.n / kGroup;
+        DevBuf tp, ts;
+        QORA_TRY(tp.alloc((size_t)(k * C) * 16));
+        QORA_TRY(ts.alloc((size_t)(k * C) * 2));
+        QORA_CUDA(cudaMemcpyAsync(tp.p, h.packed, tp.bytes, cudaMemcpyHostToDevice, stream));
+        QORA_CUDA(cudaMemcpyAsync(ts.p, h.scales, ts.bytes, cudaMemcpyHostToDevice, stream));
+        QORA_TRY(repack_q4(tp.as<uint8_t>(), ts.as<__half>(), k, h.n, nib.as<uint4>(),
+                           scl.as<__half>(), k, offs[i], strides[i], stream));
+        QORA_CUDA(cudaStreamSynchronize(stream));
+    }
+    out.nib = nib.as<uint4>();
+    out.scl = scl.as<__half>();
+    out.k = k;
+    out.C = C_total;
+    out.n = C_total * kGroup;
+    return QORA_OK;
+}
+
+int upload_emb(const qora_q4_host &h, DevBuf &packed, DevBuf &scl, EmbDev &out) {
+    if (!h.packed || !h.scales) return set_error(QORA_ERR_INVALID, "null embedding");
+    if (h.n % kGroup != 0) return set_error(QORA_ERR_SHAPE, "embedding n %% 32 != 0");
+    QORA_TRY(packed.alloc((size_t)(h.k * h.n / 2)));
+    QORA_TRY(scl.alloc((size_t)(h.k * (h.n / kGroup)) * 2));
+    QORA_CUDA(cudaMemcpy(packed.p, h.packed, packed.bytes, cudaMemcpyHostToDevice));
+    QORA_CUDA(cudaMemcpy(scl.p, h.scales, scl.bytes, cudaMemcpyHostToDevice));
+    out.packed = packed.as<uint8_t>();
+    out.scl = scl.as<__half>();
+    out.rows = h.k;
+    out.n = h.n;
+    return QORA_OK;
+}
+
+}  // namespace qora

@@ -1,0 +1,87 @@
+// Q4 GEMV engine: kernel arguments, launch planning and launchers.
+#pragma once
+
+#include "common.cuh"
+
+namespace qora {
+
+enum XMode : int { X_PLAIN = 0, X_RMSNORM = 1, X_EMBED = 2 };
+enum EMode : int { E_STORE = 0, E_BIAS = 1, E_RESID = 2, E_SWIGLU = 3 };
+
+// One fused GEMV launch:  y[r] = epilogue( prologue(x[r]) @ W )  for rows r.
+struct GemvArgs {
+    Q4Dev w;
+    int rows = 0;
+    // ---- input prologue
+    const float *x = nullptr;
+    int64_t ldx = 0;
+    const __half *gamma = nullptr;  // X_RMSNORM: f16 gamma[k]
+    const float *ss = nullptr;      // X_RMSNORM: per-row sum-of-squares partials
+    int64_t ldss = 0;
+    int ss_tiles = 0;
+    EmbDev emb;                     // X_EMBED: x[r] = dequantised emb row tok[r*ldtok]
+    const uint32_t *tok = nullptr;
+    int64_t ldtok = 1;
+    float *side = nullptr;          // X_RMSNORM: also write the normalised rows here
+    int64_t ldside = 0;
+    // ---- output epilogue
+    float *y = nullptr;
+    int64_t ldy = 0;
+    const float *bias = nullptr;    // E_BIAS
+    float *ss_out = nullptr;        // per-row, per-32-column sum of squares of y
+    int64_t ldss_out = 0;
+    // ---- global final stage (one CTA after all column tiles are done)
+    float *tbest_v = nullptr;       // [rows][tiles] per-tile max (argmax)
+    int *tbest_i = nullptr;
+    uint32_t *amax = nullptr;       // argmax output per row (last index on ties)
+    int64_t ldamax = 1;
+    int *adv_len = nullptr;         // len[s] += adv_T for s < adv_streams
+    int *adv_pos = nullptr;         // pos[s] += adv_T
+    int adv_T = 0, adv_streams = 0;
+    int *err = nullptr;
+    // ---- filled by plan_gemv
+    int B = 1, WR = 1, S = 1, Z = 1;
+    int rows_per_cta_k = 128, rows_per_z = 0;
+    float *part = nullptr;          // [S][rows][32*C] split-K partials
+    unsigned *tickets = nullptr;    // [tiles * Z]
+    unsigned *gticket = nullptr;    // [1]
+};
+
+struct GemvPlan {
+    int B, WR, S, Z, rows_per_cta_k, rows_per_z, cpc;
+    dim3 grid, block;
+    size_t part_floats;   // split-K scratch floats
+    size_t tickets;       // split-K counters
+};
+
+// Chooses tiling so that at least ~2 CTAs per SM are launched.
+GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms);
+
+// Launches the fused GEMV; `a` holds everything but the plan fields and the
+// scratch (part / tickets / gticket), which are taken from plan and buffers.
+int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &plan, float *part,
+                unsigned *tickets, unsigned *gticket, cudaStream_t stream);
+
+// Repack reference-layout Q4 rows (device copy) into column-group-major
+// chunks at destination chunk index dst_off + c * dst_stride.
+int repack_q4(const uint8_t *src_packed, const __half *src_scl, int64_t k, int64_t n,
+              uint4 *dst_nib, __half *dst_scl, int64_t dst_k_stride, int64_t dst_off,
+              int64_t dst_stride, cudaStream_t stream);
+
+int launch_embed_rows(const EmbDev &e, const uint32_t *tok, int64_t ldtok, int count, float *out,
+                      int64_t ldout, cudaStream_t stream);
+
+// Copy rows and write their per-32-column sum-of-squares partials.
+int launch_copy_rowstats(const float *src, int64_t ldsrc, float *dst, int64_t lddst, int rows,
+                         int n, float *ss, int64_t ldss, cudaStream_t stream);
+
+int launch_rmsnorm_rows(const float *x, const __half *gamma, int64_t n, int rows, float *out,
+                        cudaStream_t stream);
+
+// Host-side helpers shared by the model code.
+int upload_q4_parts(const qora_q4_host *parts, const int64_t *offs, const int64_t *strides,
+                    int nparts, int64_t k, int64_t C_total, DevBuf &nib, DevBuf &scl,
+                    Q4Dev &out, cudaStream_t stream);
+int upload_emb(const qora_q4_host &h, DevBuf &packed, DevBuf &scl, EmbDev &out);
+
+}  // namespace qora

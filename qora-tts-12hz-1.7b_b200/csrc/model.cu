@@ -1,0 +1,1048 @@
+// Talker, code predictor, KV cache and the per-frame engine (host orchestration).
+//
+// Kernel sequence of one talker step for B streams (talker.rs:263-360):
+//   per layer (5 launches):
+//     [qkv GEMV, RMSNorm prologue] -> [attention: qk-norm, RoPE, KV append,
+//     split-position GQA] -> [o GEMV + residual] -> [gate|up GEMV, RMSNorm
+//     prologue, SwiGLU epilogue] -> [down GEMV + residual]
+//   then [codec head GEMV, final-norm prologue, hidden side output, length advance].
+// Residual-producing epilogues also write per-32-column sum-of-squares
+// partials, which the next RMSNorm prologue sums in fixed order.
+//
+// The predictor frame (code_predictor.rs:218-273) runs the same layer
+// sequence: one 2-token pass (projected talker hidden + projected semantic
+// embedding) and 14 one-token passes; each pass ends in a head GEMV whose
+// final CTA takes the argmax (last index on ties) and advances the cache.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "attention.cuh"
+#include "gemv.cuh"
+#include "sampler.cuh"
+
+namespace qora {
+
+int host_rope_tables(int32_t head_dim, int32_t max_pos, double theta, const int32_t *sections,
+                     int32_t n_sections, float *cos_t, float *sin_t);
+
+namespace {
+
+__global__ void k_advance(int *len, int *pos, int count, int by) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) {
+        len[i] += by;
+        if (pos) pos[i] += by;
+    }
+}
+
+__global__ void k_fill_i32(int *p, int count, int v) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < count) p[i] = v;
+}
+
+int upload_f16(const uint16_t *h, int64_t n, DevBuf &buf) {
+    if (!h) return set_error(QORA_ERR_INVALID, "null norm vector");
+    QORA_TRY(buf.alloc((size_t)n * 2));
+    QORA_CUDA(cudaMemcpy(buf.p, h, (size_t)n * 2, cudaMemcpyHostToDevice));
+    return QORA_OK;
+}
+
+}  // namespace
+
+// --------------------------------------------------------------------- layers
+struct LayerDev {
+    DevBuf qkv_nib, qkv_scl, o_nib, o_scl, gu_nib, gu_scl, dn_nib, dn_scl;
+    Q4Dev qkv, o, gu, dn;
+    DevBuf q_norm, k_norm, in_norm, post_norm;
+
+    int upload(const qora_layer_host &h, int64_t hidden, int heads, int kvh, int hd, int64_t ffn) {
+        const int64_t qd = (int64_t)heads * hd, kd = (int64_t)kvh * hd;
+        if (h.q_proj.k != hidden || h.q_proj.n != qd || h.k_proj.n != kd || h.v_proj.n != kd ||
+            h.o_proj.k != qd || h.o_proj.n != hidden || h.gate_proj.n != ffn ||
+            h.up_proj.n != ffn || h.down_proj.k != ffn || h.down_proj.n != hidden)
+            return set_error(QORA_ERR_SHAPE, "layer weight shapes do not match the config");
+        {   // fused [q | k | v]
+            const qora_q4_host parts[3] = {h.q_proj, h.k_proj, h.v_proj};
+            const int64_t offs[3] = {0, qd / kGroup, (qd + kd) / kGroup};
+            const int64_t strides[3] = {1, 1, 1};
+            QORA_TRY(upload_q4_parts(parts, offs, strides, 3, hidden, (qd + 2 * kd) / kGroup,
+                                     qkv_nib, qkv_scl, qkv, nullptr));
+        }
+        {
+            const int64_t off = 0, st = 1;
+            QORA_TRY(upload_q4_parts(&h.o_proj, &off, &st, 1, qd, hidden / kGroup, o_nib, o_scl, o,
+                                     nullptr));
+            QORA_TRY(upload_q4_parts(&h.down_proj, &off, &st, 1, ffn, hidden / kGroup, dn_nib,
+                                     dn_scl, dn, nullptr));
+        }
+        {   // gate/up interleaved by 32-column group: g0 u0 g1 u1 ...
+            const qora_q4_host parts[2] = {h.gate_proj, h.up_proj};
+            const int64_t offs[2] = {0, 1};
+            const int64_t strides[2] = {2, 2};
+            QORA_TRY(upload_q4_parts(parts, offs, strides, 2, hidden, 2 * ffn / kGroup, gu_nib,
+                                     gu_scl, gu, nullptr));
+        }
+        QORA_TRY(upload_f16(h.q_norm, hd, q_norm));
+        QORA_TRY(upload_f16(h.k_norm, hd, k_norm));
+        QORA_TRY(upload_f16(h.input_norm, hidden, in_norm));
+        QORA_TRY(upload_f16(h.post_attn_norm, hidden, post_norm));
+        return QORA_OK;
+    }
+};
+
+// Activation and scratch buffers sized for `rows` rows.
+struct Work {
+    DevBuf x, ss, qkv, attn, h, logits, part, tickets, gticket, tbest_v, tbest_i, apo, apml, atk;
+    int rows = 0;
+    size_t part_floats = 0, ntickets = 0;
+
+    int alloc(int rows_, int64_t hidden, int64_t qkvn, int64_t qd, int64_t ffn, int64_t vocab,
+              int kvh, int heads, int hd, size_t part_f, size_t tick) {
+        rows = rows_;
+        QORA_TRY(x.alloc((size_t)rows * hidden * 4));
+        QORA_TRY(ss.alloc((size_t)rows * (hidden / kGroup) * 4));
+        QORA_TRY(qkv.alloc((size_t)rows * qkvn * 4));
+        QORA_TRY(attn.alloc((size_t)rows * qd * 4));
+        QORA_TRY(h.alloc((size_t)rows * ffn * 4));
+        QORA_TRY(logits.alloc((size_t)rows * vocab * 4));
+        part_floats = part_f;
+        ntickets = tick;
+        QORA_TRY(part.alloc(std::max<size_t>(part_f, 1) * 4));
+        QORA_TRY(tickets.alloc(std::max<size_t>(tick, 1) * 4));
+        QORA_TRY(tickets.zero());
+        QORA_TRY(gticket.alloc(64));
+        QORA_TRY(gticket.zero());
+        QORA_TRY(tbest_v.alloc((size_t)rows * (vocab / kGroup + 1) * 4));
+        QORA_TRY(tbest_i.alloc((size_t)rows * (vocab / kGroup + 1) * 4));
+        QORA_TRY(apo.alloc(attn_part_o_floats(rows, kvh, heads, hd) * 4));
+        QORA_TRY(apml.alloc(attn_part_ml_floats(rows, kvh, heads) * 4));
+        QORA_TRY(atk.alloc((size_t)rows * kvh * 4));
+        QORA_TRY(atk.zero());
+        QORA_CUDA(cudaDeviceSynchronize());
+        return QORA_OK;
+    }
+};
+
+// Largest split-K scratch any GEMV of a layer stack needs for `rows` rows.
+static void scratch_need(int64_t k, int64_t C, int rows, int emode, int sms, size_t &pf,
+                         size_t &tk) {
+    const GemvPlan p = plan_gemv(k, C, rows, emode, sms);
+    pf = std::max(pf, p.part_floats);
+    tk = std::max(tk, p.tickets);
+}
+
+}  // namespace qora
+
+using namespace qora;
+
+// ------------------------------------------------------------------------- KV
+struct qora_kv {
+    qora_ctx *ctx = nullptr;
+    int layers = 0, kvh = 0, hd = 0, max_pos = 0, streams = 0;
+    DevBuf k, v, len;
+    size_t layer_elems() const { return (size_t)streams * kvh * max_pos * hd; }
+    KVLayer layer(int l, int stream0 = 0) const {
+        KVLayer L;
+        const size_t off = (size_t)l * layer_elems() + (size_t)stream0 * kvh * max_pos * hd;
+        L.k = k.as<float>() + off;
+        L.v = v.as<float>() + off;
+        L.kv_heads = kvh;
+        L.head_dim = hd;
+        L.max_pos = max_pos;
+        return L;
+    }
+    int *lens() const { return len.as<int>(); }
+};
+
+// --------------------------------------------------------------------- talker
+struct qora_talker {
+    qora_ctx *ctx = nullptr;
+    int L = 0, H = 0, heads = 0, kvh = 0, hd = 0, ffn = 0, vocab = 0, rope_max = 0;
+    std::vector<LayerDev> layers;
+    DevBuf ce_packed, ce_scl, head_nib, head_scl, final_norm, rope_cos, rope_sin;
+    EmbDev codec_emb;
+    Q4Dev head;
+    int max_batch = 0;
+    Work w;
+
+    int64_t qd() const { return (int64_t)heads * hd; }
+    int64_t kd() const { return (int64_t)kvh * hd; }
+    int64_t qkvn() const { return qd() + 2 * kd(); }
+};
+
+namespace qora {
+
+struct Launcher {
+    qora_ctx *ctx;
+    Work *w;
+    cudaStream_t st;
+    int count = 0;  // kernels launched
+
+    int gemv(GemvArgs a, int xm, int em) {
+        const GemvPlan p = plan_gemv(a.w.k, a.w.C, a.rows, em, ctx->num_sms);
+        if (p.part_floats > w->part_floats || p.tickets > w->ntickets)
+            return set_error(QORA_ERR_INVALID, "internal: GEMV scratch too small");
+        if (!a.err) a.err = ctx->err.as<int>();
+        count++;
+        return launch_gemv(a, xm, em, p, w->part.as<float>(), w->tickets.as<unsigned>(),
+                           w->gticket.as<unsigned>(), st);
+    }
+};
+
+// One decoder layer over `rows` rows (T tokens per stream).
+static int run_layer(Launcher &ln, const LayerDev &ld, int H, int heads, int kvh, int hd,
+                     int64_t ffn, int rows, int T, const KVLayer &kv, const int *len,
+                     const int *pos, const float *rope_cos, const float *rope_sin, int rope_max) {
+    Work &w = *ln.w;
+    const int64_t qd = (int64_t)heads * hd, qkvn = qd + 2 * (int64_t)kvh * hd;
+    {
+        GemvArgs a;
+        a.w = ld.qkv;
+        a.rows = rows;
+        a.x = w.x.as<float>();
+        a.ldx = H;
+        a.gamma = ld.in_norm.as<__half>();
+        a.ss = w.ss.as<float>();
+        a.ldss = H / kGroup;
+        a.ss_tiles = H / kGroup;
+        a.y = w.qkv.as<float>();
+        a.ldy = qkvn;
+        QORA_TRY(ln.gemv(a, X_RMSNORM, E_STORE));
+    }
+    AttnArgs at;
+    at.qkv = w.qkv.as<float>();
+    at.ldqkv = qkvn;
+    at.heads = heads;
+    at.kv_heads = kvh;
+    at.T = T;
+    at.streams = rows / T;
+    at.q_gamma = ld.q_norm.as<__half>();
+    at.k_gamma = ld.k_norm.as<__half>();
+    at.rope_cos = rope_cos;
+    at.rope_sin = rope_sin;
+    at.rope_max_pos = rope_max;
+    at.pos = pos;
+    at.len = len;
+    at.kv = kv;
+    at.out = w.attn.as<float>();
+    at.ldout = qd;
+    at.part_o = w.apo.as<float>();
+    at.part_ml = w.apml.as<float>();
+    at.tickets = w.atk.as<unsigned>();
+    at.err = ln.ctx->err.as<int>();
+    if (T > 1) {
+        QORA_TRY(launch_qkv_post(at, ln.st));
+        ln.count++;
+        at.preappended = true;
+    }
+    QORA_TRY(launch_attention(at, ln.st));
+    ln.count++;
+    {
+        GemvArgs a;
+        a.w = ld.o;
+        a.rows = rows;
+        a.x = w.attn.as<float>();
+        a.ldx = qd;
+        a.y = w.x.as<float>();
+        a.ldy = H;
+        a.ss_out = w.ss.as<float>();
+        a.ldss_out = H / kGroup;
+        QORA_TRY(ln.gemv(a, X_PLAIN, E_RESID));
+    }
+    {
+        GemvArgs a;
+        a.w = ld.gu;
+        a.rows = rows;
+        a.x = w.x.as<float>();
+        a.ldx = H;
+        a.gamma = ld.post_norm.as<__half>();
+        a.ss = w.ss.as<float>();
+        a.ldss = H / kGroup;
+        a.ss_tiles = H / kGroup;
+        a.y = w.h.as<float>();
+        a.ldy = ffn;
+        QORA_TRY(ln.gemv(a, X_RMSNORM, E_SWIGLU));
+    }
+    {
+        GemvArgs a;
+        a.w = ld.dn;
+        a.rows = rows;
+        a.x = w.h.as<float>();
+        a.ldx = ffn;
+        a.y = w.x.as<float>();
+        a.ldy = H;
+        a.ss_out = w.ss.as<float>();
+        a.ldss_out = H / kGroup;
+        QORA_TRY(ln.gemv(a, X_PLAIN, E_RESID));
+    }
+    return QORA_OK;
+}
+
+// Talker forward for B streams (T = 1) starting from w.x / w.ss.
+// hidden: final-normed rows (ldh); logits may be null (then a plain norm).
+static int talker_forward_step(qora_talker *t, qora_kv *kv, Launcher &ln, int B, const int *pos,
+                               float *hidden, int64_t ldh, float *logits, int64_t ldl,
+                               int *adv_pos) {
+    for (int l = 0; l < t->L; l++)
+        QORA_TRY(run_layer(ln, t->layers[l], t->H, t->heads, t->kvh, t->hd, t->ffn, B, 1,
+                           kv->layer(l), kv->lens(), pos, t->rope_cos.as<float>(),
+                           t->rope_sin.as<float>(), t->rope_max));
+    GemvArgs a;
+    a.w = t->head;
+    a.rows = B;
+    a.x = ln.w->x.as<float>();
+    a.ldx = t->H;
+    a.gamma = t->final_norm.as<__half>();
+    a.ss = ln.w->ss.as<float>();
+    a.ldss = t->H / kGroup;
+    a.ss_tiles = t->H / kGroup;
+    a.side = hidden;
+    a.ldside = ldh;
+    a.y = logits ? logits : ln.w->logits.as<float>();
+    a.ldy = logits ? ldl : t->vocab;
+    a.adv_len = kv->lens();
+    a.adv_pos = adv_pos;
+    a.adv_T = 1;
+    a.adv_streams = B;
+    return ln.gemv(a, X_RMSNORM, E_STORE);
+}
+
+}  // namespace qora
+
+// ------------------------------------------------------------------ predictor
+struct qora_predictor {
+    qora_ctx *ctx = nullptr;
+    int L = 0, H = 0, heads = 0, kvh = 0, hd = 0, ffn = 0, vocab = 0, groups = 0, rope_max = 0;
+    int64_t Ht = 0;  // talker hidden (input / embedding width)
+    std::vector<LayerDev> layers;
+    bool has_proj = false;
+    DevBuf proj_nib, proj_scl, proj_bias, final_norm, rope_cos, rope_sin;
+    Q4Dev proj;
+    std::vector<DevBuf> emb_packed, emb_scl, head_nib, head_scl;
+    std::vector<EmbDev> embs;
+    std::vector<Q4Dev> heads_w;
+    int max_batch = 0;
+    Work w;
+    DevBuf x2;     // [rows][2][Ht]: talker hidden | semantic embedding
+    DevBuf codes;  // [rows][groups] internal code buffer
+    DevBuf xe;     // identity-projection staging [rows][Ht]
+};
+
+namespace qora {
+
+// Projects rows of width Ht into w.x (+ ss).  Source: plain rows, or the
+// embedding row of a code (X_EMBED).
+static int predictor_project(qora_predictor *p, Launcher &ln, int rows, const float *x,
+                             int64_t ldx, const EmbDev *emb, const uint32_t *tok, int64_t ldtok) {
+    Work &w = *ln.w;
+    if (!p->has_proj) {
+        const float *src = x;
+        int64_t lds = ldx;
+        if (emb) {
+            QORA_TRY(launch_embed_rows(*emb, tok, ldtok, rows, p->xe.as<float>(), p->Ht, ln.st));
+            ln.count++;
+            src = p->xe.as<float>();
+            lds = p->Ht;
+        }
+        QORA_TRY(launch_copy_rowstats(src, lds, w.x.as<float>(), p->H, rows, p->H,
+                                      w.ss.as<float>(), p->H / kGroup, ln.st));
+        ln.count++;
+        return QORA_OK;
+    }
+    GemvArgs a;
+    a.w = p->proj;
+    a.rows = rows;
+    a.x = x;
+    a.ldx = ldx;
+    if (emb) {
+        a.emb = *emb;
+        a.tok = tok;
+        a.ldtok = ldtok;
+    }
+    a.bias = p->proj_bias.as<float>();
+    a.y = w.x.as<float>();
+    a.ldy = p->H;
+    a.ss_out = w.ss.as<float>();
+    a.ldss_out = p->H / kGroup;
+    return ln.gemv(a, emb ? X_EMBED : X_PLAIN, E_BIAS);
+}
+
+static int predictor_head(qora_predictor *p, Launcher &ln, int B, int g, int T, qora_kv *kv,
+                          uint32_t *codes, int64_t ldcodes, float *logits, int64_t ldl) {
+    Work &w = *ln.w;
+    GemvArgs a;
+    a.w = p->heads_w[g];
+    a.rows = B;
+    // last token of each stream: row b*T + T-1
+    a.x = w.x.as<float>() + (int64_t)(T - 1) * p->H;
+    a.ldx = (int64_t)T * p->H;
+    a.gamma = p->final_norm.as<__half>();
+    a.ss = w.ss.as<float>() + (int64_t)(T - 1) * (p->H / kGroup);
+    a.ldss = (int64_t)T * (p->H / kGroup);
+    a.ss_tiles = p->H / kGroup;
+    a.y = logits ? logits + (int64_t)g * p->vocab : w.logits.as<float>();
+    a.ldy = logits ? ldl : p->vocab;
+    a.tbest_v = w.tbest_v.as<float>();
+    a.tbest_i = w.tbest_i.as<int>();
+    a.amax = codes + g;
+    a.ldamax = ldcodes;
+    a.adv_len = kv->lens();
+    a.adv_T = T;
+    a.adv_streams = B;
+    return ln.gemv(a, X_RMSNORM, E_STORE);
+}
+
+// generate_acoustic_codes for B streams; hidden rows are x2[b][0], semantic x2[b][1]
+// (x2 row stride 2*Ht).  codes [B][groups] (ldcodes), optional logits, forced.
+static int predictor_frame_impl(qora_predictor *p, qora_kv *kv, Launcher &ln, int B,
+                                const float *x2, uint32_t *codes, int64_t ldcodes, float *logits,
+                                int64_t ldl, const uint32_t *forced, int64_t ldforced) {
+    // reset the per-frame cache (code_predictor.rs:227-231)
+    k_fill_i32<<<(B + 255) / 256, 256, 0, ln.st>>>(kv->lens(), B, 0);
+    QORA_LAUNCH_CHECK();
+    ln.count++;
+    // 2-token prefill: [proj(hidden), proj(semantic)]
+    QORA_TRY(predictor_project(p, ln, 2 * B, x2, p->Ht, nullptr, nullptr, 0));
+    for (int l = 0; l < p->L; l++)
+        QORA_TRY(run_layer(ln, p->layers[l], p->H, p->heads, p->kvh, p->hd, p->ffn, 2 * B, 2,
+                           kv->layer(l), kv->lens(), nullptr, p->rope_cos.as<float>(),
+                           p->rope_sin.as<float>(), p->rope_max));
+    QORA_TRY(predictor_head(p, ln, B, 0, 2, kv, codes, ldcodes, logits, ldl));
+    for (int g = 1; g < p->groups; g++) {
+        const uint32_t *tok = forced ? forced + (g - 1) : codes + (g - 1);
+        const int64_t ldtok = forced ? ldforced : ldcodes;
+        QORA_TRY(predictor_project(p, ln, B, nullptr, 0, &p->embs[g - 1], tok, ldtok));
+        for (int l = 0; l < p->L; l++)
+            QORA_TRY(run_layer(ln, p->layers[l], p->H, p->heads, p->kvh, p->hd, p->ffn, B, 1,
+                               kv->layer(l), kv->lens(), nullptr, p->rope_cos.as<float>(),
+                               p->rope_sin.as<float>(), p->rope_max));
+        QORA_TRY(predictor_head(p, ln, B, g, 1, kv, codes, ldcodes, logits, ldl));
+    }
+    return QORA_OK;
+}
+
+}  // namespace qora
+
+// --------------------------------------------------------------------- engine
+struct qora_engine {
+    qora_talker *t = nullptr;
+    qora_predictor *p = nullptr;
+    int B = 0, max_pos = 0;
+    qora_sample_params params{};
+    qora_kv *tkv = nullptr, *pkv = nullptr;
+    DevBuf logits, codes, prev, rng, pos, text;
+    bool use_graph = false;
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t exec = nullptr;
+    const float *graph_text = nullptr;
+    uint32_t *graph_codes = nullptr;
+    int kernels = kEngineKernelsUnknown;
+    cudaStream_t cap_stream = nullptr;
+};
+
+// =========================================================================
+// extern "C" entry points
+// =========================================================================
+extern "C" {
+
+int qora_kv_create(qora_ctx *ctx, int32_t num_layers, int32_t kv_heads, int32_t head_dim,
+                   int32_t max_pos, int32_t streams, qora_kv **out) {
+    if (!ctx || !out || num_layers <= 0 || kv_heads <= 0 || max_pos <= 0 || streams <= 0)
+        return set_error(QORA_ERR_INVALID, "qora_kv_create: bad arguments");
+    if (head_dim != 64 && head_dim != 128 && head_dim != 32)
+        return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d (supported: 32, 64, 128)", head_dim);
+    QORA_CUDA(cudaSetDevice(ctx->device));
+    qora_kv *kv = new qora_kv();
+    kv->ctx = ctx;
+    kv->layers = num_layers;
+    kv->kvh = kv_heads;
+    kv->hd = head_dim;
+    kv->max_pos = max_pos;
+    kv->streams = streams;
+    const size_t bytes = kv->layer_elems() * num_layers * 4;
+    int rc = kv->k.alloc(bytes);
+    if (rc == QORA_OK) rc = kv->v.alloc(bytes);
+    if (rc == QORA_OK) rc = kv->len.alloc((size_t)streams * 4);
+    if (rc == QORA_OK) rc = kv->len.zero();
+    if (rc == QORA_OK && cudaDeviceSynchronize() != cudaSuccess)
+        rc = set_error(QORA_ERR_CUDA, "qora_kv_create: sync failed");
+    if (rc != QORA_OK) {
+        delete kv;
+        return rc;
+    }
+    *out = kv;
+    return QORA_OK;
+}
+
+void qora_kv_destroy(qora_kv *kv) { delete kv; }
+
+int qora_kv_reset(qora_kv *kv, const int32_t *ids_host, int32_t count, void *stream) {
+    if (!kv) return set_error(QORA_ERR_INVALID, "null kv");
+    cudaStream_t st = as_stream(stream);
+    if (!ids_host) {
+        QORA_CUDA(cudaMemsetAsync(kv->len.p, 0, kv->len.bytes, st));
+        return QORA_OK;
+    }
+    for (int i = 0; i < count; i++) {
+        if (ids_host[i] < 0 || ids_host[i] >= kv->streams)
+            return set_error(QORA_ERR_INVALID, "stream id %d out of range", ids_host[i]);
+        QORA_CUDA(cudaMemsetAsync(kv->lens() + ids_host[i], 0, 4, st));
+    }
+    return QORA_OK;
+}
+
+int qora_kv_lengths_host(qora_kv *kv, int32_t *len_host, void *stream) {
+    if (!kv || !len_host) return set_error(QORA_ERR_INVALID, "null argument");
+    QORA_CUDA(cudaMemcpyAsync(len_host, kv->len.p, kv->len.bytes, cudaMemcpyDeviceToHost,
+                              as_stream(stream)));
+    QORA_CUDA(cudaStreamSynchronize(as_stream(stream)));
+    return QORA_OK;
+}
+
+int qora_kv_copy_stream(qora_kv *dst, int32_t ds, const qora_kv *src, int32_t ss, void *stream) {
+    if (!dst || !src || dst->layers != src->layers || dst->kvh != src->kvh || dst->hd != src->hd ||
+        dst->max_pos < src->max_pos || ds < 0 || ds >= dst->streams || ss < 0 || ss >= src->streams)
+        return set_error(QORA_ERR_INVALID, "qora_kv_copy_stream: incompatible caches");
+    cudaStream_t st = as_stream(stream);
+    const size_t row = (size_t)src->hd * 4;
+    for (int l = 0; l < src->layers; l++) {
+        KVLayer a = dst->layer(l, ds), b = src->layer(l, ss);
+        for (int h = 0; h < src->kvh; h++) {
+            QORA_CUDA(cudaMemcpyAsync(a.k + (size_t)h * dst->max_pos * dst->hd,
+                                      b.k + (size_t)h * src->max_pos * src->hd,
+                                      row * src->max_pos, cudaMemcpyDeviceToDevice, st));
+            QORA_CUDA(cudaMemcpyAsync(a.v + (size_t)h * dst->max_pos * dst->hd,
+                                      b.v + (size_t)h * src->max_pos * src->hd,
+                                      row * src->max_pos, cudaMemcpyDeviceToDevice, st));
+        }
+    }
+    QORA_CUDA(cudaMemcpyAsync(dst->lens() + ds, src->lens() + ss, 4, cudaMemcpyDeviceToDevice, st));
+    return QORA_OK;
+}
+
+int qora_kv_layer_ptrs(qora_kv *kv, int32_t layer, float **k, float **v, int32_t **len) {
+    if (!kv || layer < 0 || layer >= kv->layers) return set_error(QORA_ERR_INVALID, "bad layer");
+    KVLayer L = kv->layer(layer);
+    if (k) *k = L.k;
+    if (v) *v = L.v;
+    if (len) *len = kv->lens();
+    return QORA_OK;
+}
+
+int qora_kv_export_layer(qora_kv *kv, int32_t layer, float *k_out, float *v_out, void *stream) {
+    if (!kv || layer < 0 || layer >= kv->layers || !k_out || !v_out)
+        return set_error(QORA_ERR_INVALID, "qora_kv_export_layer: bad arguments");
+    KVLayer L = kv->layer(layer);
+    const size_t bytes = kv->layer_elems() * 4;
+    QORA_CUDA(cudaMemcpyAsync(k_out, L.k, bytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
+    QORA_CUDA(cudaMemcpyAsync(v_out, L.v, bytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
+    return QORA_OK;
+}
+
+// ------------------------------------------------------------------ talker
+int qora_talker_create(qora_ctx *ctx, const qora_talker_host *h, int32_t max_batch,
+                       qora_talker **out) {
+    if (!ctx || !h || !out || !h->layers || max_batch <= 0 || max_batch > kMaxRows)
+        return set_error(QORA_ERR_INVALID, "qora_talker_create: bad arguments");
+    if (h->hidden % kGroup || h->ffn % kGroup || h->vocab % kGroup || h->num_heads % h->num_kv_heads)
+        return set_error(QORA_ERR_SHAPE, "talker dims must be multiples of 32");
+    QORA_CUDA(cudaSetDevice(ctx->device));
+    auto *t = new qora_talker();
+    t->ctx = ctx;
+    t->L = h->num_layers;
+    t->H = h->hidden;
+    t->heads = h->num_heads;
+    t->kvh = h->num_kv_heads;
+    t->hd = h->head_dim;
+    t->ffn = h->ffn;
+    t->vocab = h->vocab;
+    t->rope_max = h->rope_max_pos;
+    t->max_batch = max_batch;
+    t->layers.resize(t->L);
+    int rc = QORA_OK;
+    for (int l = 0; l < t->L && rc == QORA_OK; l++)
+        rc = t->layers[l].upload(h->layers[l], t->H, t->heads, t->kvh, t->hd, t->ffn);
+    if (rc == QORA_OK) rc = upload_emb(h->codec_embedding, t->ce_packed, t->ce_scl, t->codec_emb);
+    if (rc == QORA_OK && (h->codec_head.k != t->H || h->codec_head.n != t->vocab))
+        rc = set_error(QORA_ERR_SHAPE, "codec_head shape");
+    if (rc == QORA_OK) {
+        const int64_t off = 0, st = 1;
+        rc = upload_q4_parts(&h->codec_head, &off, &st, 1, t->H, t->vocab / kGroup, t->head_nib,
+                             t->head_scl, t->head, nullptr);
+    }
+    if (rc == QORA_OK) rc = upload_f16(h->final_norm, t->H, t->final_norm);
+    if (rc == QORA_OK) {
+        const int half = t->hd / 2;
+        std::vector<float> c((size_t)t->rope_max * half), s((size_t)t->rope_max * half);
+        int32_t secs[3] = {24, 20, 20};
+        const bool mrope = (half == 64);
+        rc = host_rope_tables(t->hd, t->rope_max, h->rope_theta, mrope ? secs : &half,
+                              mrope ? 3 : 1, c.data(), s.data());
+        if (rc == QORA_OK) rc = t->rope_cos.alloc(c.size() * 4);
+        if (rc == QORA_OK) rc = t->rope_sin.alloc(s.size() * 4);
+        if (rc == QORA_OK && (cudaMemcpy(t->rope_cos.p, c.data(), c.size() * 4, cudaMemcpyHostToDevice) ||
+                              cudaMemcpy(t->rope_sin.p, s.data(), s.size() * 4, cudaMemcpyHostToDevice)))
+            rc = set_error(QORA_ERR_CUDA, "rope upload");
+    }
+    if (rc == QORA_OK) {
+        const int rows = kMaxRows;  // prefill chunks use up to kMaxRows rows
+        size_t pf = 0, tk = 0;
+        for (int r : {max_batch, rows}) {
+            scratch_need(t->H, t->qkvn() / kGroup, r, E_STORE, ctx->num_sms, pf, tk);
+            scratch_need(t->qd(), t->H / kGroup, r, E_RESID, ctx->num_sms, pf, tk);
+            scratch_need(t->H, 2 * t->ffn / kGroup, r, E_SWIGLU, ctx->num_sms, pf, tk);
+            scratch_need(t->ffn, t->H / kGroup, r, E_RESID, ctx->num_sms, pf, tk);
+            scratch_need(t->H, t->vocab / kGroup, r, E_STORE, ctx->num_sms, pf, tk);
+        }
+        rc = t->w.alloc(rows, t->H, t->qkvn(), t->qd(), t->ffn, t->vocab, t->kvh, t->heads, t->hd,
+                        pf, tk);
+    }
+    if (rc != QORA_OK) {
+        delete t;
+        return rc;
+    }
+    *out = t;
+    return QORA_OK;
+}
+
+void qora_talker_destroy(qora_talker *t) { delete t; }
+
+int qora_talker_step(qora_talker *t, qora_kv *kv, const float *emb, const int32_t *positions,
+                     int32_t B, float *hidden, float *logits, void *stream) {
+    if (!t || !kv || !emb || !positions || !hidden || B <= 0 || B > t->max_batch || B > kv->streams)
+        return set_error(QORA_ERR_INVALID, "qora_talker_step: bad arguments");
+    if (kv->layers != t->L || kv->kvh != t->kvh || kv->hd != t->hd)
+        return set_error(QORA_ERR_SHAPE, "KV cache does not match the talker");
+    Launcher ln{t->ctx, &t->w, as_stream(stream)};
+    QORA_TRY(launch_copy_rowstats(emb, t->H, t->w.x.as<float>(), t->H, B, t->H,
+                                  t->w.ss.as<float>(), t->H / kGroup, ln.st));
+    return talker_forward_step(t, kv, ln, B, positions, hidden, t->H, logits, t->vocab, nullptr);
+}
+
+namespace {
+// Prefill `T` tokens for streams [s0, s0+ns) (ns*T <= kMaxRows); x rows are
+// stream-major [ns][T][H] with row stride H.  Appends T positions per stream.
+int talker_prefill_rows(qora_talker *t, qora_kv *kv, int s0, int ns, int T, const float *x,
+                        cudaStream_t st) {
+    Launcher ln{t->ctx, &t->w, st};
+    const int rows = ns * T;
+    QORA_TRY(launch_copy_rowstats(x, t->H, t->w.x.as<float>(), t->H, rows, t->H,
+                                  t->w.ss.as<float>(), t->H / kGroup, st));
+    for (int l = 0; l < t->L; l++)
+        QORA_TRY(run_layer(ln, t->layers[l], t->H, t->heads, t->kvh, t->hd, t->ffn, rows, T,
+                           kv->layer(l, s0), kv->lens() + s0, nullptr, t->rope_cos.as<float>(),
+                           t->rope_sin.as<float>(), t->rope_max));
+    k_advance<<<(ns + 255) / 256, 256, 0, st>>>(kv->lens() + s0, nullptr, ns, T);
+    QORA_LAUNCH_CHECK();
+    return QORA_OK;
+}
+}  // namespace
+
+int qora_talker_prefill(qora_talker *t, qora_kv *kv, int32_t kv_stream, const float *x, int32_t T,
+                        int32_t start_pos, float *hidden, void *stream) {
+    if (!t || !kv || !x || !hidden || T <= 0 || kv_stream < 0 || kv_stream >= kv->streams)
+        return set_error(QORA_ERR_INVALID, "qora_talker_prefill: bad arguments");
+    cudaStream_t st = as_stream(stream);
+    int32_t cur = 0;
+    QORA_CUDA(cudaMemcpyAsync(&cur, kv->lens() + kv_stream, 4, cudaMemcpyDeviceToHost, st));
+    QORA_CUDA(cudaStreamSynchronize(st));
+    if (cur != start_pos)  // talker.rs:422-423
+        return set_error(QORA_ERR_INVALID, "prefix cache length %d != start_pos %d", cur, start_pos);
+    if (start_pos + T > kv->max_pos || start_pos + T > t->rope_max)
+        return set_error(QORA_ERR_RANGE, "prefill past capacity");
+    for (int t0 = 0; t0 < T; t0 += kMaxRows) {
+        const int tc = std::min(kMaxRows, T - t0);
+        QORA_TRY(talker_prefill_rows(t, kv, kv_stream, 1, tc, x + (int64_t)t0 * t->H, st));
+    }
+    // final norm of the last token (talker.rs:480-481)
+    const int last = (T - 1) % kMaxRows;
+    QORA_TRY(launch_rmsnorm_rows(t->w.x.as<float>() + (int64_t)last * t->H,
+                                 t->final_norm.as<__half>(), t->H, 1, hidden, st));
+    return QORA_OK;
+}
+
+int qora_talker_codec_head(qora_talker *t, const float *hidden, int32_t B, float *logits,
+                           void *stream) {
+    if (!t || !hidden || !logits || B <= 0 || B > kMaxRows)
+        return set_error(QORA_ERR_INVALID, "qora_talker_codec_head: bad arguments");
+    Launcher ln{t->ctx, &t->w, as_stream(stream)};
+    GemvArgs a;
+    a.w = t->head;
+    a.rows = B;
+    a.x = hidden;
+    a.ldx = t->H;
+    a.y = logits;
+    a.ldy = t->vocab;
+    return ln.gemv(a, X_PLAIN, E_STORE);
+}
+
+int qora_talker_embed_codec(qora_talker *t, const uint32_t *tokens, int32_t B, float *out,
+                            void *stream) {
+    if (!t || !tokens || !out || B <= 0) return set_error(QORA_ERR_INVALID, "bad arguments");
+    return launch_embed_rows(t->codec_emb, tokens, 1, B, out, t->H, as_stream(stream));
+}
+
+// --------------------------------------------------------------- predictor
+int qora_predictor_create(qora_ctx *ctx, const qora_predictor_host *h, int32_t max_batch,
+                          qora_predictor **out) {
+    if (!ctx || !h || !out || !h->layers || !h->codec_embeddings || !h->lm_heads ||
+        max_batch <= 0 || 2 * max_batch > kMaxRows || h->num_groups > kMaxEmbedGroups)
+        return set_error(QORA_ERR_INVALID, "qora_predictor_create: bad arguments");
+    QORA_CUDA(cudaSetDevice(ctx->device));
+    auto *p = new qora_predictor();
+    p->ctx = ctx;
+    p->L = h->num_layers;
+    p->H = h->hidden;
+    p->heads = h->num_heads;
+    p->kvh = h->num_kv_heads;
+    p->hd = h->head_dim;
+    p->ffn = h->ffn;
+    p->vocab = h->vocab;
+    p->groups = h->num_groups;
+    p->rope_max = h->rope_max_pos;
+    p->Ht = h->codec_embeddings[0].n;
+    p->max_batch = max_batch;
+    p->layers.resize(p->L);
+    int rc = QORA_OK;
+    for (int l = 0; l < p->L && rc == QORA_OK; l++)
+        rc = p->layers[l].upload(h->layers[l], p->H, p->heads, p->kvh, p->hd, p->ffn);
+    p->has_proj = h->input_proj.packed != nullptr;
+    if (rc == QORA_OK && p->has_proj) {
+        if (h->input_proj.k != p->Ht || h->input_proj.n != p->H)
+            rc = set_error(QORA_ERR_SHAPE, "input_proj shape");
+        const int64_t off = 0, st = 1;
+        if (rc == QORA_OK)
+            rc = upload_q4_parts(&h->input_proj, &off, &st, 1, p->Ht, p->H / kGroup, p->proj_nib,
+                                 p->proj_scl, p->proj, nullptr);
+        if (rc == QORA_OK) {
+            rc = p->proj_bias.alloc((size_t)p->H * 4);
+            std::vector<float> zero(p->H, 0.0f);
+            const float *b = h->input_proj_bias ? h->input_proj_bias : zero.data();
+            if (rc == QORA_OK && cudaMemcpy(p->proj_bias.p, b, (size_t)p->H * 4, cudaMemcpyHostToDevice))
+                rc = set_error(QORA_ERR_CUDA, "bias upload");
+        }
+    } else if (rc == QORA_OK && p->Ht != p->H) {
+        rc = set_error(QORA_ERR_SHAPE, "identity projection needs talker hidden == predictor hidden");
+    }
+    p->emb_packed.resize(p->groups);
+    p->emb_scl.resize(p->groups);
+    p->head_nib.resize(p->groups);
+    p->head_scl.resize(p->groups);
+    p->embs.resize(p->groups);
+    p->heads_w.resize(p->groups);
+    for (int g = 0; g < p->groups && rc == QORA_OK; g++) {
+        rc = upload_emb(h->codec_embeddings[g], p->emb_packed[g], p->emb_scl[g], p->embs[g]);
+        if (rc == QORA_OK && (h->lm_heads[g].k != p->H || h->lm_heads[g].n != p->vocab))
+            rc = set_error(QORA_ERR_SHAPE, "lm_head shape");
+        const int64_t off = 0, st = 1;
+        if (rc == QORA_OK)
+            rc = upload_q4_parts(&h->lm_heads[g], &off, &st, 1, p->H, p->vocab / kGroup,
+                                 p->head_nib[g], p->head_scl[g], p->heads_w[g], nullptr);
+    }
+    if (rc == QORA_OK) rc = upload_f16(h->final_norm, p->H, p->final_norm);
+    if (rc == QORA_OK) {
+        const int half = p->hd / 2;
+        std::vector<float> c((size_t)p->rope_max * half), s((size_t)p->rope_max * half);
+        rc = host_rope_tables(p->hd, p->rope_max, h->rope_theta, &half, 1, c.data(), s.data());
+        if (rc == QORA_OK) rc = p->rope_cos.alloc(c.size() * 4);
+        if (rc == QORA_OK) rc = p->rope_sin.alloc(s.size() * 4);
+        if (rc == QORA_OK && (cudaMemcpy(p->rope_cos.p, c.data(), c.size() * 4, cudaMemcpyHostToDevice) ||
+                              cudaMemcpy(p->rope_sin.p, s.data(), s.size() * 4, cudaMemcpyHostToDevice)))
+            rc = set_error(QORA_ERR_CUDA, "rope upload");
+    }
+    if (rc == QORA_OK) {
+        const int rows = 2 * max_batch;
+        size_t pf = 0, tk = 0;
+        const int64_t qkvn = (int64_t)(p->heads + 2 * p->kvh) * p->hd;
+        for (int r : {max_batch, rows}) {
+            if (p->has_proj) scratch_need(p->Ht, p->H / kGroup, r, E_BIAS, ctx->num_sms, pf, tk);
+            scratch_need(p->H, qkvn / kGroup, r, E_STORE, ctx->num_sms, pf, tk);
+            scratch_need((int64_t)p->heads * p->hd, p->H / kGroup, r, E_RESID, ctx->num_sms, pf, tk);
+            scratch_need(p->H, 2 * p->ffn / kGroup, r, E_SWIGLU, ctx->num_sms, pf, tk);
+            scratch_need(p->ffn, p->H / kGroup, r, E_RESID, ctx->num_sms, pf, tk);
+            scratch_need(p->H, p->vocab / kGroup, r, E_STORE, ctx->num_sms, pf, tk);
+        }
+        rc = p->w.alloc(rows, p->H, qkvn, (int64_t)p->heads * p->hd, p->ffn, p->vocab, p->kvh,
+                        p->heads, p->hd, pf, tk);
+        if (rc == QORA_OK) rc = p->x2.alloc((size_t)rows * p->Ht * 4);
+        if (rc == QORA_OK) rc = p->codes.alloc((size_t)max_batch * p->groups * 4);
+        if (rc == QORA_OK) rc = p->xe.alloc((size_t)rows * p->Ht * 4);
+    }
+    if (rc != QORA_OK) {
+        delete p;
+        return rc;
+    }
+    *out = p;
+    return QORA_OK;
+}
+
+void qora_predictor_destroy(qora_predictor *p) { delete p; }
+
+int qora_predictor_frame(qora_predictor *p, qora_kv *kv, const float *hidden, const float *semantic,
+                         int32_t B, uint32_t *codes, float *logits, const uint32_t *forced,
+                         void *stream) {
+    if (!p || !kv || !hidden || !semantic || !codes || B <= 0 || B > p->max_batch || B > kv->streams)
+        return set_error(QORA_ERR_INVALID, "qora_predictor_frame: bad arguments");
+    if (kv->layers != p->L || kv->kvh != p->kvh || kv->hd != p->hd || kv->max_pos < p->groups + 1)
+        return set_error(QORA_ERR_SHAPE, "KV cache does not match the predictor");
+    cudaStream_t st = as_stream(stream);
+    // interleave [hidden | semantic] rows into x2
+    const size_t row = (size_t)p->Ht * 4;
+    QORA_CUDA(cudaMemcpy2DAsync(p->x2.p, 2 * row, hidden, row, row, B, cudaMemcpyDeviceToDevice, st));
+    QORA_CUDA(cudaMemcpy2DAsync(p->x2.as<char>() + row, 2 * row, semantic, row, row, B,
+                                cudaMemcpyDeviceToDevice, st));
+    Launcher ln{p->ctx, &p->w, st};
+    return predictor_frame_impl(p, kv, ln, B, p->x2.as<float>(), codes, p->groups, logits,
+                                (int64_t)p->groups * p->vocab, forced, p->groups);
+}
+
+int qora_predictor_embed_sum(qora_predictor *p, const uint32_t *codes, int32_t B, float *out,
+                             void *stream) {
+    if (!p || !codes || !out || B <= 0) return set_error(QORA_ERR_INVALID, "bad arguments");
+    FrameEmbedArgs a;
+    a.n = p->Ht;
+    for (int g = 0; g < p->groups; g++) a.tables[g] = p->embs[g];
+    a.ngroups = p->groups;
+    a.codes = codes;
+    a.ldcodes = p->groups;
+    a.out = out;
+    a.ldout = p->Ht;
+    return launch_frame_embed(a, B, as_stream(stream));
+}
+
+// ------------------------------------------------------------------ engine
+int qora_engine_create(qora_talker *t, qora_predictor *p, int32_t B, int32_t max_pos,
+                       const qora_sample_params *params, qora_engine **out) {
+    if (!t || !p || !params || !out || B <= 0 || B > t->max_batch || B > p->max_batch ||
+        max_pos <= 0 || max_pos > t->rope_max || p->Ht != t->H || p->groups + 1 > 16)
+        return set_error(QORA_ERR_INVALID, "qora_engine_create: bad arguments");
+    auto *e = new qora_engine();
+    e->t = t;
+    e->p = p;
+    e->B = B;
+    e->max_pos = max_pos;
+    e->params = *params;
+    int rc = qora_kv_create(t->ctx, t->L, t->kvh, t->hd, max_pos, B, &e->tkv);
+    if (rc == QORA_OK) rc = qora_kv_create(t->ctx, p->L, p->kvh, p->hd, p->groups + 1, B, &e->pkv);
+    if (rc == QORA_OK) rc = e->logits.alloc((size_t)B * t->vocab * 4);
+    if (rc == QORA_OK) rc = e->codes.alloc((size_t)B * 16 * 4);
+    if (rc == QORA_OK) rc = e->prev.alloc((size_t)B * 16 * 4);
+    if (rc == QORA_OK) rc = e->rng.alloc((size_t)B * 8);
+    if (rc == QORA_OK) rc = e->pos.alloc((size_t)B * 4);
+    if (rc == QORA_OK) rc = e->text.alloc((size_t)B * t->H * 4);
+    if (rc == QORA_OK) rc = e->prev.zero();
+    if (rc == QORA_OK) rc = e->pos.zero();
+    if (rc == QORA_OK) rc = e->codes.zero();
+    if (rc != QORA_OK) {
+        qora_engine_destroy(e);
+        return rc;
+    }
+    *out = e;
+    return QORA_OK;
+}
+
+void qora_engine_destroy(qora_engine *e) {
+    if (!e) return;
+    if (e->exec) cudaGraphExecDestroy(e->exec);
+    if (e->graph) cudaGraphDestroy(e->graph);
+    qora_kv_destroy(e->tkv);
+    qora_kv_destroy(e->pkv);
+    delete e;
+}
+
+int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const uint64_t *seeds_host,
+                        void *stream) {
+    if (!e || !x_host || !seeds_host || T <= 0 || T >= e->max_pos)
+        return set_error(QORA_ERR_INVALID, "qora_engine_prefill: bad arguments");
+    qora_talker *t = e->t;
+    qora_predictor *p = e->p;
+    cudaStream_t st = as_stream(stream);
+    QORA_TRY(qora_kv_reset(e->tkv, nullptr, 0, stream));
+    DevBuf xd;
+    QORA_TRY(xd.alloc((size_t)e->B * T * t->H * 4));
+    QORA_CUDA(cudaMemcpyAsync(xd.p, x_host, xd.bytes, cudaMemcpyHostToDevice, st));
+    const int per = std::max(1, kMaxRows / T);
+    for (int s0 = 0; s0 < e->B; s0 += per) {
+        const int ns = std::min(per, e->B - s0);
+        if (T <= kMaxRows) {
+            QORA_TRY(talker_prefill_rows(t, e->tkv, s0, ns, T, xd.as<float>() + (int64_t)s0 * T * t->H, st));
+            // last-token hidden of each stream -> predictor input row 0
+            for (int i = 0; i < ns; i++)
+                QORA_TRY(launch_rmsnorm_rows(t->w.x.as<float>() + ((int64_t)i * T + T - 1) * t->H,
+                                             t->final_norm.as<__half>(), t->H, 1,
+                                             p->x2.as<float>() + (int64_t)(s0 + i) * 2 * p->Ht, st));
+        } else {
+            for (int i = 0; i < ns; i++)
+                QORA_TRY(qora_talker_prefill(t, e->tkv, s0 + i, xd.as<float>() + (int64_t)(s0 + i) * T * t->H,
+                                             T, 0, p->x2.as<float>() + (int64_t)(s0 + i) * 2 * p->Ht, stream));
+        }
+    }
+    // first logits (generate_new.rs:473)
+    {
+        Launcher ln{t->ctx, &t->w, st};
+        GemvArgs a;
+        a.w = t->head;
+        a.rows = e->B;
+        a.x = p->x2.as<float>();
+        a.ldx = 2 * p->Ht;
+        a.y = e->logits.as<float>();
+        a.ldy = t->vocab;
+        QORA_TRY(ln.gemv(a, X_PLAIN, E_STORE));
+    }
+    k_fill_i32<<<(e->B + 255) / 256, 256, 0, st>>>(e->pos.as<int>(), e->B, T);
+    QORA_LAUNCH_CHECK();
+    QORA_CUDA(cudaMemcpyAsync(e->rng.p, seeds_host, (size_t)e->B * 8, cudaMemcpyHostToDevice, st));
+    QORA_CUDA(cudaMemsetAsync(e->prev.p, 0, e->prev.bytes, st));
+    QORA_CUDA(cudaStreamSynchronize(st));
+    return QORA_OK;
+}
+
+namespace {
+int engine_frame_kernels(qora_engine *e, const float *text, uint32_t *codes_out, cudaStream_t st,
+                         int *count) {
+    qora_talker *t = e->t;
+    qora_predictor *p = e->p;
+    const int B = e->B;
+    int n = 0;
+    // 1. code0 = sample_token(logits); prev[0] = code0; semantic row -> x2[b][1]
+    SampleArgs sa;
+    sa.logits = e->logits.as<float>();
+    sa.ldlogits = t->vocab;
+    sa.V = t->vocab;
+    sa.prev = e->prev.as<uint32_t>();
+    sa.ldprev = 16;
+    sa.n_prev = 16;
+    sa.rng = e->rng.as<uint64_t>();
+    sa.params = e->params;
+    sa.out = e->codes.as<uint32_t>();
+    sa.ldout = 16;
+    sa.prev_update = e->prev.as<uint32_t>();
+    sa.ldprev_update = 16;
+    sa.emb = t->codec_emb;
+    sa.emb_out = p->x2.as<float>() + p->Ht;
+    sa.ldemb_out = 2 * p->Ht;
+    sa.err = t->ctx->err.as<int>();
+    QORA_TRY(launch_sample(sa, B, st));
+    n++;
+    // 2. acoustic codes 1..15
+    {
+        Launcher ln{p->ctx, &p->w, st};
+        QORA_TRY(predictor_frame_impl(p, e->pkv, ln, B, p->x2.as<float>(),
+                                      e->codes.as<uint32_t>() + 1, 16, nullptr, 0, nullptr, 0));
+        n += ln.count;
+    }
+    // 3. talker input: (semantic + acoustic sum) + text; prev[1..15] = codes
+    {
+        FrameEmbedArgs fa;
+        fa.n = t->H;
+        for (int g = 0; g < p->groups; g++) fa.tables[g] = p->embs[g];
+        fa.ngroups = p->groups;
+        fa.codes = e->codes.as<uint32_t>();
+        fa.ldcodes = 16;
+        fa.code_off = 1;
+        fa.sem = p->x2.as<float>() + p->Ht;
+        fa.ldsem = 2 * p->Ht;
+        fa.text = text;
+        fa.ldtext = t->H;
+        fa.out = t->w.x.as<float>();
+        fa.ldout = t->H;
+        fa.ss = t->w.ss.as<float>();
+        fa.ldss = t->H / kGroup;
+        fa.prev = e->prev.as<uint32_t>();
+        fa.ldprev = 16;
+        QORA_TRY(launch_frame_embed(fa, B, st));
+        n++;
+    }
+    // 4. talker step: hidden -> x2[b][0], logits -> engine logits, advance len and pos
+    {
+        Launcher ln{t->ctx, &t->w, st};
+        QORA_TRY(talker_forward_step(t, e->tkv, ln, B, e->pos.as<int>(), p->x2.as<float>(),
+                                     2 * p->Ht, e->logits.as<float>(), t->vocab, e->pos.as<int>()));
+        n += ln.count;
+    }
+    if (codes_out && codes_out != e->codes.as<uint32_t>())
+        QORA_CUDA(cudaMemcpyAsync(codes_out, e->codes.p, (size_t)B * 16 * 4, cudaMemcpyDeviceToDevice, st));
+    if (count) *count = n;
+    return QORA_OK;
+}
+}  // namespace
+
+int qora_engine_frame(qora_engine *e, const float *text, uint32_t *codes, void *stream) {
+    if (!e || !text) return set_error(QORA_ERR_INVALID, "qora_engine_frame: bad arguments");
+    cudaStream_t st = as_stream(stream);
+    if (!e->use_graph) {
+        int n = 0;
+        QORA_TRY(engine_frame_kernels(e, text, codes, st, &n));
+        e->kernels = n;
+        return QORA_OK;
+    }
+    if (!e->exec || e->graph_text != text || e->graph_codes != codes || e->cap_stream != st) {
+        if (e->exec) cudaGraphExecDestroy(e->exec);
+        if (e->graph) cudaGraphDestroy(e->graph);
+        e->exec = nullptr;
+        e->graph = nullptr;
+        cudaStream_t cs = st;
+        bool own = false;
+        if (cs == nullptr) {  // the legacy stream cannot be captured
+            QORA_CUDA(cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking));
+            own = true;
+        }
+        QORA_CUDA(cudaStreamBeginCapture(cs, cudaStreamCaptureModeThreadLocal));
+        int n = 0;
+        const int rc = engine_frame_kernels(e, text, codes, cs, &n);
+        cudaGraph_t g = nullptr;
+        const cudaError_t ce = cudaStreamEndCapture(cs, &g);
+        if (own) cudaStreamDestroy(cs);
+        if (rc != QORA_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (ce != cudaSuccess) return set_error(QORA_ERR_CUDA, "graph capture: %s", cudaGetErrorString(ce));
+        e->graph = g;
+        QORA_CUDA(cudaGraphInstantiate(&e->exec, g, 0));
+        e->graph_text = text;
+        e->graph_codes = codes;
+        e->cap_stream = st;
+        e->kernels = n;
+    }
+    QORA_CUDA(cudaGraphLaunch(e->exec, st));
+    return QORA_OK;
+}
+
+int qora_engine_frame_host(qora_engine *e, const float *text_host, uint32_t *codes_host, void *stream) {
+    if (!e || !text_host || !codes_host) return set_error(QORA_ERR_INVALID, "bad arguments");
+    cudaStream_t st = as_stream(stream);
+    QORA_CUDA(cudaMemcpyAsync(e->text.p, text_host, (size_t)e->B * e->t->H * 4,
+                              cudaMemcpyHostToDevice, st));
+    QORA_TRY(qora_engine_frame(e, e->text.as<float>(), e->codes.as<uint32_t>(), stream));
+    QORA_CUDA(cudaMemcpyAsync(codes_host, e->codes.p, (size_t)e->B * 16 * 4, cudaMemcpyDeviceToHost, st));
+    QORA_CUDA(cudaStreamSynchronize(st));
+    return QORA_OK;
+}
+
+int qora_engine_use_graph(qora_engine *e, int32_t enable) {
+    if (!e) return set_error(QORA_ERR_INVALID, "null engine");
+    e->use_graph = enable != 0;
+    return QORA_OK;
+}
+
+int qora_engine_kernels_per_frame(qora_engine *e, int32_t *count) {
+    if (!e || !count) return set_error(QORA_ERR_INVALID, "bad arguments");
+    *count = e->kernels;
+    return QORA_OK;
+}
+
+int qora_engine_state(qora_engine *e, float **logits, float **hidden, uint32_t **prev,
+                      uint64_t **rng, int32_t **positions) {
+    if (!e) return set_error(QORA_ERR_INVALID, "null engine");
+    if (logits) *logits = e->logits.as<float>();
+    if (hidden) *hidden = e->p->x2.as<float>();
+    if (prev) *prev = e->prev.as<uint32_t>();
+    if (rng) *rng = e->rng.as<uint64_t>();
+    if (positions) *positions = e->pos.as<int>();
+    return QORA_OK;
+}
+
+}  // extern "C"
