@@ -2,7 +2,8 @@
 
 Host-side mirror of the reference operator surface (gemv.rs, rope.rs,
 talker.rs, code_predictor.rs, generate_new.rs) over the C ABI in
-include/qora_cuda.h, implemented by libqora_b200.so.
+include/qora_cuda.h, implemented by libqora_b200.so.  The device API lives in
+qora_b200.engine (imports torch).
 """
 from . import _lib
 from .weights import (ModelConfig, Q4Weight, LayerWeights, TalkerWeights, PredictorWeights,
@@ -10,9 +11,3 @@ from .weights import (ModelConfig, Q4Weight, LayerWeights, TalkerWeights, Predic
 
 __all__ = ["_lib", "ModelConfig", "Q4Weight", "LayerWeights", "TalkerWeights", "PredictorWeights",
            "quantize_f32_to_q4", "synth_q4", "synth_normal", "synth_talker", "synth_predictor"]
-
-
-def engine():
-    """The device API (imports torch)."""
-    from . import engine as _e
-    return _e

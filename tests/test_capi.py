@@ -108,3 +108,13 @@ def test_rope_tables_match_oracle(lib, orc):
             sin.ctypes.data)
     c2, s2 = orc.rope_tables(128, 300, 1e6, [24, 20, 20])
     assert np.array_equal(cos, c2) and np.array_equal(sin, s2)
+
+
+def test_engine_module_imports_and_fails_loudly_without_gpu(lib):
+    import torch
+    from qora_b200 import engine as E
+    assert hasattr(E, "Context") and hasattr(E, "Engine") and hasattr(E, "Talker")
+    if not torch.cuda.is_available():
+        import qora_b200
+        with pytest.raises(qora_b200._lib.QoraError):
+            E.Context(0)
