@@ -145,3 +145,16 @@ def test_rms_norm(E, ctx, orc):
     for r in range(3):
         ref = orc.rms_norm_f16(x[r], gamma)
         assert np.max(np.abs(got[r] - ref)) <= 1e-5 * np.max(np.abs(ref))
+
+
+@pytest.mark.parametrize("k,rows", [(128, 1), (128, 2), (128, 3), (128, 4), (128, 6), (256, 2),
+                                    (256, 5), (96, 2), (32, 4)])
+def test_small_k_single_split(E, ctx, orc, k, rows):
+    """k <= 256 runs without split-K (one CTA holds all rows of a column group)."""
+    import torch
+    n = 512
+    w = orc.synth_q4(123 + k, 0.02, k, n)
+    x = orc.synth_normal(124 + rows, 1.0, rows * k).reshape(rows, k)
+    got = _dev(E, ctx, w.packed, w.scales, k, n).gemv(torch.from_numpy(x).cuda()).cpu().numpy()
+    for r in range(rows):
+        _close(got[r], orc.gemv_single(x[r], w))
