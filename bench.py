@@ -50,6 +50,7 @@ def parse():
     ap.add_argument("--no-batch32", action="store_true")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-roofline", action="store_true")
     return ap.parse_args()
 
 
@@ -370,7 +371,10 @@ def run_ours(args):
 
     # ---- roofline of the dominant kernel (k_gemv over the talker weights, batch 1)
     peak, peak_src = peaks()
-    byts, gms = gemv_stream_roofline(E, ctx, tw, torch)
+    if args.no_roofline:
+        byts, gms = float("nan"), float("nan")
+    else:
+        byts, gms = gemv_stream_roofline(E, ctx, tw, torch)
     n_launch = 7 * len(tw.layers) + 1
     achieved = byts / (gms / 1000.0) / 1e9
     traffic = None

@@ -315,7 +315,7 @@ class ModelConfig:
     def tiny(**kw) -> "ModelConfig":
         base = dict(t_layers=2, t_hidden=256, t_heads=4, t_kv_heads=2, t_head_dim=64, t_ffn=512,
                     t_vocab=320, t_max_pos=128, p_layers=2, p_hidden=128, p_heads=4, p_kv_heads=2,
-                    p_head_dim=32, p_ffn=256, p_vocab=192, p_groups=15, p_max_pos=32)
+                    p_head_dim=64, p_ffn=256, p_vocab=192, p_groups=15, p_max_pos=32)
         base.update(kw)
         return ModelConfig(**base)
 

@@ -118,3 +118,11 @@ def test_engine_module_imports_and_fails_loudly_without_gpu(lib):
         import qora_b200
         with pytest.raises(qora_b200._lib.QoraError):
             E.Context(0)
+
+
+def test_tiny_and_full_configs_agree_with_oracle(orc):
+    import dataclasses
+    import qora_b200
+    for a, b in [(qora_b200.ModelConfig.tiny(), orc.ModelConfig.tiny()),
+                 (qora_b200.ModelConfig(), orc.ModelConfig())]:
+        assert dataclasses.asdict(a) == dataclasses.asdict(b)
