@@ -371,24 +371,23 @@ def run_ours(args):
 
     # ---- roofline of the dominant kernel (k_gemv over the talker weights, batch 1)
     peak, peak_src = peaks()
-    if args.no_roofline:
-        byts, gms = float("nan"), float("nan")
-    else:
+    roof = None
+    if not args.no_roofline:
         byts, gms = gemv_stream_roofline(E, ctx, tw, torch)
-    n_launch = 7 * len(tw.layers) + 1
-    achieved = byts / (gms / 1000.0) / 1e9
-    traffic = None
-    try:
-        with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
-            traffic = json.load(f).get("k_gemv_talker_b1_bytes_per_launch")
-    except Exception:
-        pass
-    roof = {"bound": "hbm", "kernel": "k_gemv (talker Q4 GEMVs, batch 1, back-to-back)",
-            "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-            "frac": round(achieved / peak, 4), "peak_source": peak_src,
-            "traffic": traffic, "launches": n_launch,
-            "us_per_launch": round(1000.0 * gms / n_launch, 2),
-            "algorithmic_bytes_per_launch": round(byts / n_launch)}
+        n_launch = 7 * len(tw.layers) + 1
+        achieved = byts / (gms / 1000.0) / 1e9
+        traffic = None
+        try:
+            with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
+                traffic = json.load(f).get("k_gemv_talker_b1_bytes_per_launch")
+        except Exception:
+            pass
+        roof = {"bound": "hbm", "kernel": "k_gemv (talker Q4 GEMVs, batch 1, back-to-back)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                "traffic": traffic, "launches": n_launch,
+                "us_per_launch": round(1000.0 * gms / n_launch, 2),
+                "algorithmic_bytes_per_launch": round(byts / n_launch)}
 
     sweep = None if args.no_sweep else gemv_sweep(E, ctx, torch, qb)
 
