@@ -201,9 +201,32 @@ def run_reference(args):
 
 
 # ----------------------------------------------------------------- GPU arm
-def gemv_stream_roofline(E, ctx, tw, torch, reps=3):
-    """k_gemv over the whole talker weight set at batch 1, back to back
-    (197 launches, 796 MB > L2): average launch duration and algorithmic GB/s."""
+def _graph_time_ms(torch, fn, reps):
+    """Capture fn() (a sequence of engine launches) in a CUDA graph and return
+    the average replay time in ms (CUDA events on the replay stream)."""
+    fn()                                  # warm-up: sizes scratch outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            fn()
+    torch.cuda.synchronize()
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st = torch.cuda.current_stream()
+    e0.record(st)
+    for _ in range(reps):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def gemv_stream_roofline(E, ctx, tw, torch, reps=5):
+    """k_gemv over the whole talker weight set at batch 1, back to back in one
+    CUDA graph (197 launches, 796 MB > L2): algorithmic bytes and time."""
     mats = []
     for lw in tw.layers:
         for nm in ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj"):
@@ -212,24 +235,19 @@ def gemv_stream_roofline(E, ctx, tw, torch, reps=3):
     xs = {k: torch.randn(1, k, device="cuda") for k in {m.k for m in mats}}
     ys = {n: torch.empty(1, n, device="cuda") for n in {m.n for m in mats}}
     byts = sum(0.5625 * m.k * m.n + 4 * (m.k + m.n) for m in mats)
-    st = torch.cuda.current_stream()
-    for m in mats:
-        m.gemv(xs[m.k], ys[m.n])
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(st)
-    for _ in range(reps):
+
+    def run():
         for m in mats:
             m.gemv(xs[m.k], ys[m.n])
-    e1.record(st)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / reps
+
+    ms = _graph_time_ms(torch, run, reps)
     del mats
     return byts, ms
 
 
 def gemv_sweep(E, ctx, torch, qb):
-    """Config 1: per-shape GB/s at batch 1/4/16, rotating weight copies >= 512 MB."""
+    """Config 1: per-shape GB/s at batch 1/4/16; each replay walks weight copies
+    totalling >= 4x L2 so every launch streams from HBM."""
     shapes = [(2048, 4096), (2048, 1024), (2048, 2048), (2048, 6144), (6144, 2048), (2048, 3072)]
     out = {}
     for k, n in shapes:
@@ -241,17 +259,13 @@ def gemv_sweep(E, ctx, torch, qb):
         for B in (1, 4, 16):
             x = torch.randn(B, k, device="cuda")
             y = torch.empty(B, n, device="cuda")
-            for d in devs[:4]:
-                d.gemv(x, y)
-            torch.cuda.synchronize()
-            iters = max(100, copies)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record()
-            for i in range(iters):
-                devs[i % copies].gemv(x, y)
-            e1.record()
-            torch.cuda.synchronize()
-            us = 1000.0 * e0.elapsed_time(e1) / iters
+
+            def run():
+                for d in devs:
+                    d.gemv(x, y)
+
+            ms = _graph_time_ms(torch, run, 3)
+            us = 1000.0 * ms / copies
             gbs = (wbytes + 4 * B * (k + n)) / (us * 1e-6) / 1e9
             res[f"b{B}"] = {"us": round(us, 2), "GB/s": round(gbs, 1)}
         out[f"{k}x{n}"] = res
