@@ -48,7 +48,7 @@ __device__ __forceinline__ void norm_rope_head(float (&v)[HD / 32], const __half
 template <int HD>
 __device__ __forceinline__ bool rope_rows(const AttnArgs &a, int b, int t, int L0,
                                           const float *&cr, const float *&sr) {
-    const int rp = (a.pos ? a.pos[b] : L0) + t;
+    const int rp = (a.pos ? __ldcg(a.pos + b) : L0) + t;
     if (rp < 0 || rp >= a.rope_max_pos) return false;
     cr = a.rope_cos + (int64_t)rp * (HD / 2);
     sr = a.rope_sin + (int64_t)rp * (HD / 2);
@@ -58,10 +58,12 @@ __device__ __forceinline__ bool rope_rows(const AttnArgs &a, int b, int t, int L
 template <int HD>
 __global__ void __launch_bounds__(kThreads) k_qkv_post(const AttnArgs a) {
     constexpr int J = HD / 32;
+    griddep_launch_dependents();
+    griddep_wait();
     const int r = blockIdx.x;
     const int b = r / a.T, t = r % a.T;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int L0 = a.len[b];
+    const int L0 = __ldcg(a.len + b);
     if (L0 + a.T > a.kv.max_pos) {
         if (threadIdx.x == 0) raise_error(a.err, kDevRange);
         return;
@@ -110,10 +112,12 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnArgs a) {
     __shared__ float m_s[G], l_s[G], corr_s[G];
     __shared__ int last_flag;
 
+    griddep_launch_dependents();
+    griddep_wait();
     const int kvh = blockIdx.x, split = blockIdx.y, r = blockIdx.z;
     const int b = r / a.T, t = r % a.T;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int L0 = a.len[b];
+    const int L0 = __ldcg(a.len + b);
     if (L0 + a.T > a.kv.max_pos) {
         if (threadIdx.x == 0 && split == 0 && kvh == 0) raise_error(a.err, kDevRange);
         return;
@@ -281,13 +285,11 @@ int launch_attn_hd(const AttnArgs &a, cudaStream_t st) {
     const int rows = a.streams * a.T;
     dim3 grid(a.kv_heads, kAttnMaxSplit, rows);
     switch (G) {
-        case 1: k_attention<HD, 1><<<grid, kThreads, 0, st>>>(a); break;
-        case 2: k_attention<HD, 2><<<grid, kThreads, 0, st>>>(a); break;
-        case 4: k_attention<HD, 4><<<grid, kThreads, 0, st>>>(a); break;
-        default: return set_error(QORA_ERR_UNSUPPORTED, "heads/kv_heads = %d", G);
+        case 1: return launch_ex(k_attention<HD, 1>, grid, dim3(kThreads), 0, st, 1u, a);
+        case 2: return launch_ex(k_attention<HD, 2>, grid, dim3(kThreads), 0, st, 1u, a);
+        case 4: return launch_ex(k_attention<HD, 4>, grid, dim3(kThreads), 0, st, 1u, a);
     }
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
+    return set_error(QORA_ERR_UNSUPPORTED, "heads/kv_heads = %d", G);
 }
 
 }  // namespace
@@ -296,13 +298,10 @@ int launch_qkv_post(const AttnArgs &a, cudaStream_t st) {
     const int rows = a.streams * a.T;
     if (rows <= 0) return QORA_OK;
     switch (a.kv.head_dim) {
-        case 64: k_qkv_post<64><<<rows, kThreads, 0, st>>>(a); break;
-        case 128: k_qkv_post<128><<<rows, kThreads, 0, st>>>(a); break;
-        case 32: k_qkv_post<32><<<rows, kThreads, 0, st>>>(a); break;
-        default: return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d", a.kv.head_dim);
+        case 64: return launch_ex(k_qkv_post<64>, dim3(rows), dim3(kThreads), 0, st, 1u, a);
+        case 128: return launch_ex(k_qkv_post<128>, dim3(rows), dim3(kThreads), 0, st, 1u, a);
     }
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
+    return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d", a.kv.head_dim);
 }
 
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
@@ -312,7 +311,6 @@ int launch_attention(const AttnArgs &a, cudaStream_t st) {
     switch (a.kv.head_dim) {
         case 64: return launch_attn_hd<64>(a, st);
         case 128: return launch_attn_hd<128>(a, st);
-        case 32: return launch_attn_hd<32>(a, st);
     }
     return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d", a.kv.head_dim);
 }

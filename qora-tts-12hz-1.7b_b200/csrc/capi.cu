@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <thread>
 #include <vector>
@@ -142,14 +143,12 @@ int host_rope_tables(int32_t head_dim, int32_t max_pos, double theta, const int3
 
 using namespace qora;
 
-int qora_ctx::ensure_scratch(size_t part_floats, size_t ticket_count) {
-    if (scratch.bytes < part_floats * 4) QORA_TRY(scratch.alloc(part_floats * 4));
-    if (tickets.bytes < std::max<size_t>(ticket_count, 64) * 4) {
-        QORA_TRY(tickets.alloc(std::max<size_t>(ticket_count, 64) * 4));
-        QORA_TRY(tickets.zero());
-        QORA_CUDA(cudaDeviceSynchronize());
-    }
-    return QORA_OK;
+bool qora::pdl_enabled() {
+    static const bool on = [] {
+        const char *e = getenv("QORA_PDL");
+        return !(e && e[0] == '0');
+    }();
+    return on;
 }
 
 extern "C" {
@@ -186,7 +185,9 @@ int qora_ctx_create(int32_t device, qora_ctx **out) {
     c->num_sms = prop.multiProcessorCount;
     int rc = c->err.alloc(64);
     if (rc == QORA_OK) rc = c->err.zero();
-    if (rc == QORA_OK) rc = c->ensure_scratch(0, 64);
+    if (rc == QORA_OK) rc = gemv_init();
+    if (rc == QORA_OK && cudaDeviceSynchronize() != cudaSuccess)
+        rc = set_error(QORA_ERR_CUDA, "qora_ctx_create: sync failed");
     if (rc != QORA_OK) {
         delete c;
         return rc;
@@ -261,7 +262,6 @@ void qora_q4_weight_destroy(qora_w4 *w) { delete w; }
 static int generic_gemv(qora_ctx *ctx, const qora_w4 *w, const float *x, float *y, int rows,
                         cudaStream_t st) {
     const GemvPlan p = plan_gemv(w->dev.k, w->dev.C, rows, E_STORE, ctx->num_sms);
-    QORA_TRY(ctx->ensure_scratch(p.part_floats, p.tickets));
     GemvArgs a;
     a.w = w->dev;
     a.rows = rows;
@@ -270,8 +270,7 @@ static int generic_gemv(qora_ctx *ctx, const qora_w4 *w, const float *x, float *
     a.y = y;
     a.ldy = w->dev.n;
     a.err = ctx->err.as<int>();
-    return launch_gemv(a, X_PLAIN, E_STORE, p, ctx->scratch.as<float>(), ctx->tickets.as<unsigned>(),
-                       nullptr, st);
+    return launch_gemv(a, X_PLAIN, E_STORE, p, nullptr, st);
 }
 
 int qora_q4_gemv(qora_ctx *ctx, const qora_w4 *w, const float *x, float *y, int32_t batch, void *stream) {

@@ -7,6 +7,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <utility>
 #include <vector>
 
 #include "qora_cuda.h"
@@ -151,6 +152,47 @@ __device__ __forceinline__ void raise_error(int *err, int code) {
     if (err) atomicCAS(err, 0, code);
 }
 
+// Programmatic dependent launch: a kernel may start while its predecessor in
+// the stream is still running.  Everything it reads or writes that another
+// kernel produces or consumes must come after griddep_wait(); only immutable
+// data (weights, norms, tables) may be touched before it.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Whether launches carry the programmatic-serialization attribute
+// (QORA_PDL=0 in the environment turns it off).
+bool pdl_enabled();
+
+// Launch with cudaLaunchKernelEx: PDL attribute and an optional (1, cy, 1)
+// thread-block cluster.
+template <typename... KArgs, typename... Args>
+int launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+              unsigned cluster_y, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attrs[2];
+    unsigned n = 0;
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+    n++;
+    if (cluster_y > 1) {
+        attrs[n].id = cudaLaunchAttributeClusterDimension;
+        attrs[n].val.clusterDim.x = 1;
+        attrs[n].val.clusterDim.y = cluster_y;
+        attrs[n].val.clusterDim.z = 1;
+        n++;
+    }
+    cfg.attrs = attrs;
+    cfg.numAttrs = n;
+    QORA_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+    return QORA_OK;
+}
+
 // ------------------------------------------------------------ weights
 // Device Q4 weight: column-group-major copy of the reference layout.
 //   nib[c][k] : 16 bytes = the 32 nibbles of group c in row k (byte j holds
@@ -177,10 +219,7 @@ struct EmbDev {
 struct qora_ctx {
     int device = 0;
     int num_sms = 148;
-    qora::DevBuf scratch;   // split-K partials for the generic GEMV entry points
-    qora::DevBuf tickets;   // split-K arrival counters (self-resetting)
     qora::DevBuf err;       // device error flag
-    int ensure_scratch(size_t part_bytes, size_t ticket_count);
 };
 
 struct qora_w4 {

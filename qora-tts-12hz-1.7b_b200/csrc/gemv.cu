@@ -12,9 +12,20 @@
 // warp owns one 32-column group and 128 rows (4 per lane, lanes = consecutive
 // rows, so every load instruction reads 512 contiguous bytes).  Lane partials
 // are combined by a butterfly reduce-scatter (lane l ends with column l),
-// then across the CTA's warps in fixed order, then across split-K CTAs by
-// the last-arriving CTA in fixed split order.  The result is deterministic.
+// then across the CTA's warps in fixed order, then across the K-split CTAs
+// of one thread-block cluster by rank 0 over distributed shared memory, in
+// rank order.  The result is deterministic.
+//
+// Launch: programmatic dependent launch.  Each CTA fetches its first weight
+// tile (immutable) before griddepcontrol.wait, so weight traffic and launch
+// latency overlap the previous kernel.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
 #include "gemv.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace qora {
 
@@ -23,17 +34,14 @@ namespace {
 constexpr int kRowsPerLane = 4;
 constexpr uint32_t kMagic = 0x4B000000u;  // 2^23 as f32 bits
 
+// Input element x[r][kr] before the RMSNorm scaling (applied by the caller).
 template <int XM>
-__device__ __forceinline__ float load_x(const GemvArgs &a, int r, int64_t kr, float inv) {
-    if constexpr (XM == X_PLAIN) {
-        return __ldg(a.x + (int64_t)r * a.ldx + kr);
-    } else if constexpr (XM == X_RMSNORM) {
-        // rms_norm_f16 (gemv.rs:451): x * inv_rms * gamma
-        float xv = __ldg(a.x + (int64_t)r * a.ldx + kr);
-        return __fmul_rn(__fmul_rn(xv, inv), __half2float(a.gamma[kr]));
+__device__ __forceinline__ float load_x(const GemvArgs &a, int r, int64_t kr) {
+    if constexpr (XM == X_PLAIN || XM == X_RMSNORM) {
+        return __ldcg(a.x + (int64_t)r * a.ldx + kr);
     } else {
         // embed_lookup_q4 (gemv.rs:425-433): scale * (q - 8)
-        const uint32_t t = a.tok[(int64_t)r * a.ldtok];
+        const uint32_t t = __ldcg(a.tok + (int64_t)r * a.ldtok);
         const uint8_t byte = a.emb.packed[(int64_t)t * (a.emb.n >> 1) + (kr >> 1)];
         const int q = (kr & 1) ? (byte >> 4) : (byte & 15);
         const float sc = __half2float(a.emb.scl[(int64_t)t * (a.emb.n >> 5) + (kr >> 5)]);
@@ -41,12 +49,11 @@ __device__ __forceinline__ float load_x(const GemvArgs &a, int r, int64_t kr, fl
     }
 }
 
-// Sum of a per-thread value over the CTA's split-K partial rows, or the
-// epilogue for one (row, column) result.
+// Epilogue value for one (row, column) result.
 template <int EM>
 __device__ __forceinline__ float epilogue_value(const GemvArgs &a, int r, int64_t col, float v) {
     if constexpr (EM == E_BIAS) return __fadd_rn(v, a.bias[col]);
-    if constexpr (EM == E_RESID) return __fadd_rn(a.y[(int64_t)r * a.ldy + col], v);
+    if constexpr (EM == E_RESID) return __fadd_rn(__ldcg(a.y + (int64_t)r * a.ldy + col), v);
     return v;
 }
 
@@ -92,8 +99,8 @@ template <int B, int XM, int EM>
 __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
     constexpr int CPC = (EM == E_SWIGLU) ? 2 : 1;
     constexpr int R = kRowsPerLane;
-    __shared__ float inv_s[kMaxRows];
     __shared__ float red[8][B][32];
+    __shared__ float cta_red[kRowsPerZ][CPC][32];
     __shared__ int last_flag;
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -111,45 +118,67 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
     const int64_t n32 = C * 32;
     const int64_t n_out = (EM == E_SWIGLU) ? (C / 2) * 32 : a.w.n;
 
-    if constexpr (XM == X_RMSNORM) {
-        for (int r = r_begin + threadIdx.x; r < r_end; r += blockDim.x) {
-            const float *ssr = a.ss + (int64_t)r * a.ldss;
-            float t = 0.0f;
-            for (int i = 0; i < a.ss_tiles; i++) t = __fadd_rn(t, ssr[i]);
-            // gemv.rs:448: 1 / sqrt(sum/size + 1e-6)
-            inv_s[r - r_begin] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
-        }
-        __syncthreads();
-    }
-
     const uint4 *nibc = a.w.nib + c * k;
     const __half *sclc = a.w.scl + c * k;
     const bool write_side = (XM == X_RMSNORM) && a.side && blockIdx.x == 0 && cc == 0;
     const uint64_t neg01 = pk2(-8388616.0f, -8388736.0f);    // -(2^23 + 8),    -(2^23 + 8*16)
     const uint64_t neg23 = pk2(-8390656.0f, -8421376.0f);    // -(2^23 + 8*256), -(2^23 + 8*4096)
-    const int items = CPC * B * 32;
+
+    // Weights are immutable: fetch the first tile before waiting on the
+    // kernel that produces x, so the fetch overlaps that kernel's tail.
+    uint4 wv[R];
+    float sc[R];
+#pragma unroll
+    for (int i = 0; i < R; i++) {
+        const int64_t kr = wrow0 + lane + 32 * i;
+        const bool ok = kr < k_end;
+        wv[i] = ok ? ldg_stream(nibc + kr) : make_uint4(0u, 0u, 0u, 0u);
+        sc[i] = ok ? __half2float(sclc[kr]) : 0.0f;
+    }
+    griddep_launch_dependents();
+    griddep_wait();
 
     for (int r0 = r_begin; r0 < r_end; r0 += B) {
-        uint64_t acc[B][16];
+        if (r0 != r_begin) {
 #pragma unroll
-        for (int b = 0; b < B; b++)
-#pragma unroll
-            for (int j = 0; j < 16; j++) acc[b][j] = 0ull;
-
-        uint4 wv[R];
-        float sc[R];
+            for (int i = 0; i < R; i++) {
+                const int64_t kr = wrow0 + lane + 32 * i;
+                const bool ok = kr < k_end;
+                wv[i] = ok ? ldg_stream(nibc + kr) : make_uint4(0u, 0u, 0u, 0u);
+                sc[i] = ok ? __half2float(sclc[kr]) : 0.0f;
+            }
+        }
         float xs[R][B];
 #pragma unroll
         for (int i = 0; i < R; i++) {
             const int64_t kr = wrow0 + lane + 32 * i;
             const bool ok = kr < k_end;
-            wv[i] = ok ? ldg_stream(nibc + kr) : make_uint4(0u, 0u, 0u, 0u);
-            sc[i] = ok ? __half2float(sclc[kr]) : 0.0f;
 #pragma unroll
             for (int b = 0; b < B; b++) {
                 const int r = r0 + b;
-                const float inv = (XM == X_RMSNORM && r < r_end) ? inv_s[r - r_begin] : 0.0f;
-                xs[i][b] = (ok && r < r_end) ? load_x<XM>(a, r, kr, inv) : 0.0f;
+                xs[i][b] = (ok && r < r_end) ? load_x<XM>(a, r, kr) : 0.0f;
+            }
+        }
+        if constexpr (XM == X_RMSNORM) {
+            // rms_norm_f16 (gemv.rs:445-454): inv = 1/sqrt(sum(x^2)/k + 1e-6), the
+            // sum taken from the producer's per-32-column partials by a fixed
+            // shuffle tree (same in every warp, so every CTA agrees)
+            float inv[B];
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const int r = r0 + b;
+                float t = 0.0f;
+                if (r < r_end)
+                    for (int i = lane; i < a.ss_tiles; i += 32) t += __ldcg(a.ss + (int64_t)r * a.ldss + i);
+                t = warp_sum(t);
+                inv[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
+            }
+#pragma unroll
+            for (int i = 0; i < R; i++) {
+                const int64_t kr = wrow0 + lane + 32 * i;
+                const float g = kr < k_end ? __half2float(a.gamma[kr]) : 0.0f;
+#pragma unroll
+                for (int b = 0; b < B; b++) xs[i][b] = __fmul_rn(__fmul_rn(xs[i][b], inv[b]), g);
             }
         }
         if (write_side) {
@@ -161,6 +190,11 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
                     if (kr < k_end && r0 + b < r_end) a.side[(int64_t)(r0 + b) * a.ldside + kr] = xs[i][b];
             }
         }
+        uint64_t acc[B][16];
+#pragma unroll
+        for (int b = 0; b < B; b++)
+#pragma unroll
+            for (int j = 0; j < 16; j++) acc[b][j] = 0ull;
 #pragma unroll
         for (int i = 0; i < R; i++) {
             uint64_t s01[B], s23[B];
@@ -212,81 +246,51 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
             red[warp][b][lane] = v[0];
         }
         __syncthreads();
-        if (a.S == 1) {
-            // whole K in this CTA: finish here
-            const int nitems = (EM == E_SWIGLU) ? B * 32 : items;
-            for (int it = threadIdx.x; it < nitems; it += blockDim.x) {
-                const int l = it & 31;
-                const int b = (it >> 5) % B;
-                const int cc2 = (it >> 5) / B;
-                const int r = r0 + b;
-                float v = 0.0f, u = 0.0f;
-                for (int w = 0; w < WR; w++) v += red[cc2 * WR + w][b][l];
-                if constexpr (EM == E_SWIGLU)
-                    for (int w = 0; w < WR; w++) u += red[WR + w][b][l];
-                if (r < r_end) {
-                    const int64_t grp = (EM == E_SWIGLU) ? (int64_t)blockIdx.x
-                                                         : (int64_t)blockIdx.x * CPC + cc2;
-                    finalize_group<EM>(a, r, grp, l, v, u, n_out);
-                }
-            }
-        } else {
-            for (int it = threadIdx.x; it < items; it += blockDim.x) {
-                const int l = it & 31;
-                const int b = (it >> 5) % B;
-                const int cc2 = (it >> 5) / B;
-                const int r = r0 + b;
-                float v = 0.0f;
-                for (int w = 0; w < WR; w++) v += red[cc2 * WR + w][b][l];
-                if (r < r_end) {
-                    const int64_t col = ((int64_t)blockIdx.x * CPC + cc2) * 32 + l;
-                    __stcg(a.part + ((int64_t)s * a.rows + r) * n32 + col, v);
-                }
-            }
+        // CTA total per (row, column group): warps summed in order
+        for (int it = threadIdx.x; it < CPC * B * 32; it += blockDim.x) {
+            const int l = it & 31;
+            const int b = (it >> 5) % B;
+            const int cc2 = (it >> 5) / B;
+            float v = 0.0f;
+            for (int w = 0; w < WR; w++) v += red[cc2 * WR + w][b][l];
+            if (r0 + b < r_end) cta_red[r0 + b - r_begin][cc2][l] = v;
         }
         __syncthreads();
     }
 
-    // tail columns beyond the last full group stay zero (gemv.rs:846-861)
-    if (EM == E_STORE && a.w.n > n32 && blockIdx.x == 0 && s == 0) {
-        for (int r = r_begin; r < r_end; r++)
-            for (int64_t col = n32 + threadIdx.x; col < a.w.n; col += blockDim.x)
-                a.y[(int64_t)r * a.ldy + col] = 0.0f;
-    }
-
-    if (a.S > 1) {
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            const unsigned t = atomicAdd(&a.tickets[(int64_t)z * gridDim.x + blockIdx.x], 1u);
-            last_flag = (t == (unsigned)(a.S - 1));
-        }
-        __syncthreads();
-        if (!last_flag) return;
-        __threadfence();
-        // last arriver: sum the S partials in split order, then the epilogue
-        const int nitems = (EM == E_SWIGLU) ? B * 32 : items;
-        for (int r0 = r_begin; r0 < r_end; r0 += B) {
-            for (int it = threadIdx.x; it < nitems; it += blockDim.x) {
-                const int l = it & 31;
-                const int b = (it >> 5) % B;
-                const int cc2 = (it >> 5) / B;
-                const int r = r0 + b;
-                if (r >= r_end) continue;  // whole warp shares r: uniform
-                const int64_t col = ((int64_t)blockIdx.x * CPC + cc2) * 32 + l;
-                float v = 0.0f, u = 0.0f;
-                for (int sp = 0; sp < a.S; sp++) {
-                    v += __ldcg(a.part + ((int64_t)sp * a.rows + r) * n32 + col);
-                    if constexpr (EM == E_SWIGLU)
-                        u += __ldcg(a.part + ((int64_t)sp * a.rows + r) * n32 + col + 32);
-                }
-                const int64_t grp = (EM == E_SWIGLU) ? (int64_t)blockIdx.x
-                                                     : (int64_t)blockIdx.x * CPC + cc2;
-                finalize_group<EM>(a, r, grp, l, v, u, n_out);
+    // K-split totals: the cluster's CTAs hold one partial each in shared
+    // memory; rank 0 sums them in rank order over DSMEM.
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = a.S;
+    if (S > 1) cluster.sync();
+    const bool leader = (S == 1) || cluster.block_rank() == 0;
+    if (leader) {
+        constexpr int CO = (EM == E_SWIGLU) ? 1 : CPC;  // output column groups per CTA
+        const int nz = r_end - r_begin;
+        for (int it = threadIdx.x; it < nz * CO * 32; it += blockDim.x) {
+            const int l = it & 31;
+            const int q = it >> 5;
+            const int row = q / CO, cc2 = q % CO;
+            float v = 0.0f, u = 0.0f;
+            for (int rk = 0; rk < S; rk++) {
+                const float *p = (S == 1) ? &cta_red[0][0][0]
+                                          : cluster.map_shared_rank(&cta_red[0][0][0], rk);
+                v += p[(row * CPC + cc2) * 32 + l];
+                if constexpr (EM == E_SWIGLU) u += p[(row * CPC + 1) * 32 + l];
             }
+            const int64_t grp = (EM == E_SWIGLU) ? (int64_t)blockIdx.x
+                                                 : (int64_t)blockIdx.x * CPC + cc2;
+            finalize_group<EM>(a, r_begin + row, grp, l, v, u, n_out);
         }
-        if (threadIdx.x == 0) a.tickets[(int64_t)z * gridDim.x + blockIdx.x] = 0u;
+        // tail columns beyond the last full group stay zero (gemv.rs:846-861)
+        if (EM == E_STORE && a.w.n > n32 && blockIdx.x == 0) {
+            for (int r = r_begin; r < r_end; r++)
+                for (int64_t col = n32 + threadIdx.x; col < a.w.n; col += blockDim.x)
+                    a.y[(int64_t)r * a.ldy + col] = 0.0f;
+        }
     }
+    if (S > 1) cluster.sync();  // peers keep their shared memory until rank 0 is done
+    if (!leader) return;
 
     if (a.gticket) {
         __threadfence();
@@ -323,15 +327,39 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
     }
 }
 
+template <int B, int XM, int EM>
+int launch_one(const GemvArgs &a, const GemvPlan &p, cudaStream_t st) {
+    return launch_ex(k_gemv<B, XM, EM>, p.grid, p.block, 0, st, (unsigned)p.S, a);
+}
+
+template <int B, int XM, int EM>
+int allow_large_clusters() {
+    QORA_CUDA(cudaFuncSetAttribute(k_gemv<B, XM, EM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    return QORA_OK;
+}
+
+template <int XM, int EM>
+int allow_large_clusters_b() {
+    QORA_TRY((allow_large_clusters<1, XM, EM>()));
+    QORA_TRY((allow_large_clusters<2, XM, EM>()));
+    return allow_large_clusters<4, XM, EM>();
+}
+
+template <int XM>
+int allow_large_clusters_e() {
+    QORA_TRY((allow_large_clusters_b<XM, E_STORE>()));
+    QORA_TRY((allow_large_clusters_b<XM, E_BIAS>()));
+    QORA_TRY((allow_large_clusters_b<XM, E_RESID>()));
+    return allow_large_clusters_b<XM, E_SWIGLU>();
+}
+
 template <int XM, int EM>
 int launch_b(const GemvArgs &a, const GemvPlan &p, cudaStream_t st) {
     switch (p.B) {
-        case 1: k_gemv<1, XM, EM><<<p.grid, p.block, 0, st>>>(a); break;
-        case 2: k_gemv<2, XM, EM><<<p.grid, p.block, 0, st>>>(a); break;
-        default: k_gemv<4, XM, EM><<<p.grid, p.block, 0, st>>>(a); break;
+        case 1: return launch_one<1, XM, EM>(a, p, st);
+        case 2: return launch_one<2, XM, EM>(a, p, st);
+        default: return launch_one<4, XM, EM>(a, p, st);
     }
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
 }
 
 template <int XM>
@@ -360,8 +388,10 @@ __global__ void k_repack(const uint8_t *__restrict__ src, const __half *__restri
 
 __global__ void k_embed_rows(EmbDev e, const uint32_t *__restrict__ tok, int64_t ldtok,
                              float *__restrict__ out, int64_t ldout) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int i = blockIdx.x;
-    const uint32_t t = tok[(int64_t)i * ldtok];
+    const uint32_t t = __ldcg(tok + (int64_t)i * ldtok);
     const uint8_t *p = e.packed + (int64_t)t * (e.n >> 1);
     const __half *s = e.scl + (int64_t)t * (e.n >> 5);
     for (int64_t j = threadIdx.x; j < e.n; j += blockDim.x) {
@@ -373,6 +403,8 @@ __global__ void k_embed_rows(EmbDev e, const uint32_t *__restrict__ tok, int64_t
 
 __global__ void k_copy_rowstats(const float *__restrict__ src, int64_t ldsrc, float *__restrict__ dst,
                                 int64_t lddst, int n, float *__restrict__ ss, int64_t ldss) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int r = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     for (int g = warp; g * 32 < n; g += nw) {
@@ -388,6 +420,8 @@ __global__ void k_rmsnorm_rows(const float *__restrict__ x, const __half *__rest
                                int64_t n, float *__restrict__ out) {
     __shared__ float red[32];
     __shared__ float inv;
+    griddep_launch_dependents();
+    griddep_wait();
     const int r = blockIdx.x;
     const float *xr = x + (int64_t)r * n;
     float t = 0.0f;
@@ -407,49 +441,51 @@ __global__ void k_rmsnorm_rows(const float *__restrict__ x, const __half *__rest
 
 }  // namespace
 
+// Clusters of up to kMaxSplit (16) CTAs exceed the portable size (8) and must
+// be enabled per kernel; done once per device context, before any capture.
+int gemv_init() {
+    QORA_TRY(allow_large_clusters_e<X_PLAIN>());
+    QORA_TRY(allow_large_clusters_e<X_RMSNORM>());
+    return allow_large_clusters_e<X_EMBED>();
+}
+
 GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms) {
     GemvPlan p{};
     p.cpc = (emode == E_SWIGLU) ? 2 : 1;
-    p.B = rows >= 4 ? 4 : (rows >= 2 ? 2 : 1);
-    if (rows == 3) p.B = 4;
-    p.rows_per_z = rows <= 16 ? rows : 16;
+    p.B = rows >= 3 ? 4 : rows;
+    p.rows_per_z = std::min(rows, kRowsPerZ);
     p.Z = (rows + p.rows_per_z - 1) / p.rows_per_z;
     const int64_t tiles = C / p.cpc;
+    auto splits = [&](int wr) { return (k + (int64_t)wr * 128 - 1) / ((int64_t)wr * 128); };
     int WR = 8 / p.cpc;
-    const int64_t max_wr_rows = (k + 127) / 128;
-    while (WR > 1 && WR / 2 >= max_wr_rows) WR /= 2;  // do not exceed K
-    int64_t S = (k + WR * 128 - 1) / (WR * 128);
-    while (WR > 1 && tiles * S * p.Z < 2LL * num_sms) {
-        WR /= 2;
-        S = (k + WR * 128 - 1) / (WR * 128);
-    }
+    // Smaller CTAs (more K-splits) until ~2 CTAs per SM, within one cluster.
+    while (WR > 1 && splits(WR / 2) <= kMaxSplit && tiles * splits(WR) * p.Z < 2LL * num_sms) WR /= 2;
+    while (WR > 1 && splits(WR / 2) == splits(WR)) WR /= 2;  // k smaller than the CTA's rows
     p.WR = WR;
-    p.S = (int)S;
+    p.S = (int)splits(WR);
     p.rows_per_cta_k = WR * 128;
     p.grid = dim3((unsigned)tiles, (unsigned)p.S, (unsigned)p.Z);
     p.block = dim3(32 * p.cpc * WR);
-    p.part_floats = p.S > 1 ? (size_t)p.S * rows * C * 32 : 0;
-    p.tickets = (size_t)tiles * p.Z;
     return p;
 }
 
-int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &p, float *part,
-                unsigned *tickets, unsigned *gticket, cudaStream_t st) {
+int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &p, unsigned *gticket,
+                cudaStream_t st) {
     if (a.rows <= 0 || a.rows > kMaxRows)
         return set_error(QORA_ERR_SHAPE, "gemv rows %d outside 1..%d", a.rows, kMaxRows);
-    if (p.S > 1 && (!part || !tickets))
-        return set_error(QORA_ERR_INVALID, "split-K GEMV needs scratch");
-    if (a.gticket == nullptr && (a.amax || a.adv_len)) a.gticket = gticket;
+    if (p.S > kMaxSplit)
+        return set_error(QORA_ERR_UNSUPPORTED, "gemv k=%lld needs %d K-splits (max %d)",
+                         (long long)a.w.k, p.S, kMaxSplit);
+    if ((a.amax || a.adv_len) && !a.gticket) a.gticket = gticket;
     if ((a.amax || a.adv_len) && !a.gticket)
         return set_error(QORA_ERR_INVALID, "global stage needs a ticket");
+    if (!(a.amax || a.adv_len)) a.gticket = nullptr;
     a.B = p.B;
     a.WR = p.WR;
     a.S = p.S;
     a.Z = p.Z;
     a.rows_per_cta_k = p.rows_per_cta_k;
     a.rows_per_z = p.rows_per_z;
-    a.part = part;
-    a.tickets = tickets;
     switch (xmode) {
         case X_PLAIN: return launch_e<X_PLAIN>(a, emode, p, st);
         case X_RMSNORM: return launch_e<X_RMSNORM>(a, emode, p, st);
@@ -475,25 +511,20 @@ int repack_q4(const uint8_t *src_packed, const __half *src_scl, int64_t k, int64
 int launch_embed_rows(const EmbDev &e, const uint32_t *tok, int64_t ldtok, int count, float *out,
                       int64_t ldout, cudaStream_t stream) {
     if (count <= 0) return QORA_OK;
-    k_embed_rows<<<count, 256, 0, stream>>>(e, tok, ldtok, out, ldout);
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
+    return launch_ex(k_embed_rows, dim3(count), dim3(256), 0, stream, 1u, e, tok, ldtok, out, ldout);
 }
 
 int launch_copy_rowstats(const float *src, int64_t ldsrc, float *dst, int64_t lddst, int rows,
                          int n, float *ss, int64_t ldss, cudaStream_t stream) {
     if (rows <= 0) return QORA_OK;
-    k_copy_rowstats<<<rows, 256, 0, stream>>>(src, ldsrc, dst, lddst, n, ss, ldss);
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
+    return launch_ex(k_copy_rowstats, dim3(rows), dim3(256), 0, stream, 1u, src, ldsrc, dst, lddst,
+                     n, ss, ldss);
 }
 
 int launch_rmsnorm_rows(const float *x, const __half *gamma, int64_t n, int rows, float *out,
                         cudaStream_t stream) {
     if (rows <= 0) return QORA_OK;
-    k_rmsnorm_rows<<<rows, 256, 0, stream>>>(x, gamma, n, out);
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
+    return launch_ex(k_rmsnorm_rows, dim3(rows), dim3(256), 0, stream, 1u, x, gamma, n, out);
 }
 
 // Upload reference-layout parts of one fused weight (all with the same k) into

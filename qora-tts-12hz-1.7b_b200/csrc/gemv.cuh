@@ -42,25 +42,28 @@ struct GemvArgs {
     // ---- filled by plan_gemv
     int B = 1, WR = 1, S = 1, Z = 1;
     int rows_per_cta_k = 128, rows_per_z = 0;
-    float *part = nullptr;          // [S][rows][32*C] split-K partials
-    unsigned *tickets = nullptr;    // [tiles * Z]
-    unsigned *gticket = nullptr;    // [1]
+    unsigned *gticket = nullptr;    // [1] arrival counter of the global final stage
 };
 
+constexpr int kRowsPerZ = 16;       // rows one CTA carries through the K loop
+constexpr int kMaxSplit = 16;       // CTAs of one cluster along K
+
+// Tiling of one GEMV: column groups x K-splits (one cluster) x row groups.
 struct GemvPlan {
     int B, WR, S, Z, rows_per_cta_k, rows_per_z, cpc;
     dim3 grid, block;
-    size_t part_floats;   // split-K scratch floats
-    size_t tickets;       // split-K counters
 };
+
+// Per-device one-time kernel attribute setup (large clusters).
+int gemv_init();
 
 // Chooses tiling so that at least ~2 CTAs per SM are launched.
 GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms);
 
-// Launches the fused GEMV; `a` holds everything but the plan fields and the
-// scratch (part / tickets / gticket), which are taken from plan and buffers.
-int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &plan, float *part,
-                unsigned *tickets, unsigned *gticket, cudaStream_t stream);
+// Launches the fused GEMV; `gticket` backs the global final stage (argmax /
+// length advance) when `a` asks for one.
+int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &plan, unsigned *gticket,
+                cudaStream_t stream);
 
 // Repack reference-layout Q4 rows (device copy) into column-group-major
 // chunks at destination chunk index dst_off + c * dst_stride.

@@ -30,6 +30,8 @@ int host_rope_tables(int32_t head_dim, int32_t max_pos, double theta, const int3
 namespace {
 
 __global__ void k_advance(int *len, int *pos, int count, int by) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < count) {
         len[i] += by;
@@ -38,6 +40,8 @@ __global__ void k_advance(int *len, int *pos, int count, int by) {
 }
 
 __global__ void k_fill_i32(int *p, int count, int v) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
     if (i < count) p[i] = v;
 }
@@ -94,12 +98,11 @@ struct LayerDev {
 
 // Activation and scratch buffers sized for `rows` rows.
 struct Work {
-    DevBuf x, ss, qkv, attn, h, logits, part, tickets, gticket, tbest_v, tbest_i, apo, apml, atk;
+    DevBuf x, ss, qkv, attn, h, logits, gticket, tbest_v, tbest_i, apo, apml, atk;
     int rows = 0;
-    size_t part_floats = 0, ntickets = 0;
 
     int alloc(int rows_, int64_t hidden, int64_t qkvn, int64_t qd, int64_t ffn, int64_t vocab,
-              int kvh, int heads, int hd, size_t part_f, size_t tick) {
+              int kvh, int heads, int hd) {
         rows = rows_;
         QORA_TRY(x.alloc((size_t)rows * hidden * 4));
         QORA_TRY(ss.alloc((size_t)rows * (hidden / kGroup) * 4));
@@ -107,11 +110,6 @@ struct Work {
         QORA_TRY(attn.alloc((size_t)rows * qd * 4));
         QORA_TRY(h.alloc((size_t)rows * ffn * 4));
         QORA_TRY(logits.alloc((size_t)rows * vocab * 4));
-        part_floats = part_f;
-        ntickets = tick;
-        QORA_TRY(part.alloc(std::max<size_t>(part_f, 1) * 4));
-        QORA_TRY(tickets.alloc(std::max<size_t>(tick, 1) * 4));
-        QORA_TRY(tickets.zero());
         QORA_TRY(gticket.alloc(64));
         QORA_TRY(gticket.zero());
         QORA_TRY(tbest_v.alloc((size_t)rows * (vocab / kGroup + 1) * 4));
@@ -124,14 +122,6 @@ struct Work {
         return QORA_OK;
     }
 };
-
-// Largest split-K scratch any GEMV of a layer stack needs for `rows` rows.
-static void scratch_need(int64_t k, int64_t C, int rows, int emode, int sms, size_t &pf,
-                         size_t &tk) {
-    const GemvPlan p = plan_gemv(k, C, rows, emode, sms);
-    pf = std::max(pf, p.part_floats);
-    tk = std::max(tk, p.tickets);
-}
 
 }  // namespace qora
 
@@ -182,12 +172,9 @@ struct Launcher {
 
     int gemv(GemvArgs a, int xm, int em) {
         const GemvPlan p = plan_gemv(a.w.k, a.w.C, a.rows, em, ctx->num_sms);
-        if (p.part_floats > w->part_floats || p.tickets > w->ntickets)
-            return set_error(QORA_ERR_INVALID, "internal: GEMV scratch too small");
         if (!a.err) a.err = ctx->err.as<int>();
         count++;
-        return launch_gemv(a, xm, em, p, w->part.as<float>(), w->tickets.as<unsigned>(),
-                           w->gticket.as<unsigned>(), st);
+        return launch_gemv(a, xm, em, p, w->gticket.as<unsigned>(), st);
     }
 };
 
@@ -400,8 +387,7 @@ static int predictor_frame_impl(qora_predictor *p, qora_kv *kv, Launcher &ln, in
                                 const float *x2, uint32_t *codes, int64_t ldcodes, float *logits,
                                 int64_t ldl, const uint32_t *forced, int64_t ldforced) {
     // reset the per-frame cache (code_predictor.rs:227-231)
-    k_fill_i32<<<(B + 255) / 256, 256, 0, ln.st>>>(kv->lens(), B, 0);
-    QORA_LAUNCH_CHECK();
+    QORA_TRY(launch_ex(k_fill_i32, dim3((B + 255) / 256), dim3(256), 0, ln.st, 1u, kv->lens(), B, 0));
     ln.count++;
     // 2-token prefill: [proj(hidden), proj(semantic)]
     QORA_TRY(predictor_project(p, ln, 2 * B, x2, p->Ht, nullptr, nullptr, 0));
@@ -451,8 +437,8 @@ int qora_kv_create(qora_ctx *ctx, int32_t num_layers, int32_t kv_heads, int32_t 
                    int32_t max_pos, int32_t streams, qora_kv **out) {
     if (!ctx || !out || num_layers <= 0 || kv_heads <= 0 || max_pos <= 0 || streams <= 0)
         return set_error(QORA_ERR_INVALID, "qora_kv_create: bad arguments");
-    if (head_dim != 64 && head_dim != 128 && head_dim != 32)
-        return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d (supported: 32, 64, 128)", head_dim);
+    if (head_dim != 64 && head_dim != 128)
+        return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128)", head_dim);
     QORA_CUDA(cudaSetDevice(ctx->device));
     qora_kv *kv = new qora_kv();
     kv->ctx = ctx;
@@ -586,19 +572,9 @@ int qora_talker_create(qora_ctx *ctx, const qora_talker_host *h, int32_t max_bat
                               cudaMemcpy(t->rope_sin.p, s.data(), s.size() * 4, cudaMemcpyHostToDevice)))
             rc = set_error(QORA_ERR_CUDA, "rope upload");
     }
-    if (rc == QORA_OK) {
-        const int rows = kMaxRows;  // prefill chunks use up to kMaxRows rows
-        size_t pf = 0, tk = 0;
-        for (int r : {max_batch, rows}) {
-            scratch_need(t->H, t->qkvn() / kGroup, r, E_STORE, ctx->num_sms, pf, tk);
-            scratch_need(t->qd(), t->H / kGroup, r, E_RESID, ctx->num_sms, pf, tk);
-            scratch_need(t->H, 2 * t->ffn / kGroup, r, E_SWIGLU, ctx->num_sms, pf, tk);
-            scratch_need(t->ffn, t->H / kGroup, r, E_RESID, ctx->num_sms, pf, tk);
-            scratch_need(t->H, t->vocab / kGroup, r, E_STORE, ctx->num_sms, pf, tk);
-        }
-        rc = t->w.alloc(rows, t->H, t->qkvn(), t->qd(), t->ffn, t->vocab, t->kvh, t->heads, t->hd,
-                        pf, tk);
-    }
+    if (rc == QORA_OK)  // prefill chunks use up to kMaxRows rows
+        rc = t->w.alloc(kMaxRows, t->H, t->qkvn(), t->qd(), t->ffn, t->vocab, t->kvh, t->heads,
+                        t->hd);
     if (rc != QORA_OK) {
         delete t;
         return rc;
@@ -634,9 +610,8 @@ int talker_prefill_rows(qora_talker *t, qora_kv *kv, int s0, int ns, int T, cons
         QORA_TRY(run_layer(ln, t->layers[l], t->H, t->heads, t->kvh, t->hd, t->ffn, rows, T,
                            kv->layer(l, s0), kv->lens() + s0, nullptr, t->rope_cos.as<float>(),
                            t->rope_sin.as<float>(), t->rope_max));
-    k_advance<<<(ns + 255) / 256, 256, 0, st>>>(kv->lens() + s0, nullptr, ns, T);
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
+    return launch_ex(k_advance, dim3((ns + 255) / 256), dim3(256), 0, st, 1u, kv->lens() + s0,
+                     (int *)nullptr, ns, T);
 }
 }  // namespace
 
@@ -754,18 +729,9 @@ int qora_predictor_create(qora_ctx *ctx, const qora_predictor_host *h, int32_t m
     }
     if (rc == QORA_OK) {
         const int rows = 2 * max_batch;
-        size_t pf = 0, tk = 0;
         const int64_t qkvn = (int64_t)(p->heads + 2 * p->kvh) * p->hd;
-        for (int r : {max_batch, rows}) {
-            if (p->has_proj) scratch_need(p->Ht, p->H / kGroup, r, E_BIAS, ctx->num_sms, pf, tk);
-            scratch_need(p->H, qkvn / kGroup, r, E_STORE, ctx->num_sms, pf, tk);
-            scratch_need((int64_t)p->heads * p->hd, p->H / kGroup, r, E_RESID, ctx->num_sms, pf, tk);
-            scratch_need(p->H, 2 * p->ffn / kGroup, r, E_SWIGLU, ctx->num_sms, pf, tk);
-            scratch_need(p->ffn, p->H / kGroup, r, E_RESID, ctx->num_sms, pf, tk);
-            scratch_need(p->H, p->vocab / kGroup, r, E_STORE, ctx->num_sms, pf, tk);
-        }
         rc = p->w.alloc(rows, p->H, qkvn, (int64_t)p->heads * p->hd, p->ffn, p->vocab, p->kvh,
-                        p->heads, p->hd, pf, tk);
+                        p->heads, p->hd);
         if (rc == QORA_OK) rc = p->x2.alloc((size_t)rows * p->Ht * 4);
         if (rc == QORA_OK) rc = p->codes.alloc((size_t)max_batch * p->groups * 4);
         if (rc == QORA_OK) rc = p->xe.alloc((size_t)rows * p->Ht * 4);
@@ -891,8 +857,8 @@ int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const ui
         a.ldy = t->vocab;
         QORA_TRY(ln.gemv(a, X_PLAIN, E_STORE));
     }
-    k_fill_i32<<<(e->B + 255) / 256, 256, 0, st>>>(e->pos.as<int>(), e->B, T);
-    QORA_LAUNCH_CHECK();
+    QORA_TRY(launch_ex(k_fill_i32, dim3((e->B + 255) / 256), dim3(256), 0, st, 1u, e->pos.as<int>(),
+                       e->B, T));
     QORA_CUDA(cudaMemcpyAsync(e->rng.p, seeds_host, (size_t)e->B * 8, cudaMemcpyHostToDevice, st));
     QORA_CUDA(cudaMemsetAsync(e->prev.p, 0, e->prev.bytes, st));
     QORA_CUDA(cudaStreamSynchronize(st));

@@ -90,6 +90,8 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
     __shared__ int n_surv;
     __shared__ int out_code;
 
+    griddep_launch_dependents();
+    griddep_wait();
     const int row = blockIdx.x;
     const int V = a.V;
     const int E = (V + kSampleThreads - 1) / kSampleThreads;
@@ -334,6 +336,8 @@ __global__ void __launch_bounds__(kSampleThreads) k_sample(SampleArgs a) {
 }
 
 __global__ void k_frame_embed(FrameEmbedArgs a) {
+    griddep_launch_dependents();
+    griddep_wait();
     const int r = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int64_t n = a.n;
@@ -375,17 +379,13 @@ int launch_sample(const SampleArgs &a, int rows, cudaStream_t st) {
         return set_error(QORA_ERR_UNSUPPORTED, "top_k %d > %d", a.params.top_k, kMaxSurvivors);
     if (!topk && a.params.top_p > 0.0f && a.params.top_p < 1.0f)
         return set_error(QORA_ERR_UNSUPPORTED, "top_p needs 0 < top_k <= %d", kMaxSurvivors);
-    k_sample<<<rows, kSampleThreads, 0, st>>>(a);
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
+    return launch_ex(k_sample, dim3(rows), dim3(kSampleThreads), 0, st, 1u, a);
 }
 
 int launch_frame_embed(const FrameEmbedArgs &a, int rows, cudaStream_t st) {
     if (rows <= 0) return QORA_OK;
     if (a.ngroups > kMaxEmbedGroups) return set_error(QORA_ERR_INVALID, "too many groups");
-    k_frame_embed<<<rows, 256, 0, st>>>(a);
-    QORA_LAUNCH_CHECK();
-    return QORA_OK;
+    return launch_ex(k_frame_embed, dim3(rows), dim3(256), 0, st, 1u, a);
 }
 
 }  // namespace qora
