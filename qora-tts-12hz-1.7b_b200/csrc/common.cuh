@@ -128,6 +128,58 @@ __device__ __forceinline__ uint4 ldg_stream(const uint4 *p) {
     return r;
 }
 
+// ---- shared-memory bulk copies completed on an mbarrier (no multicast) ----
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+// dst (this CTA's shared memory) <- src (global), `bytes` a multiple of 16,
+// both addresses 16-byte aligned; completion is signalled on `bar`.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait for an mbarrier phase: gives up after ~1 s (raising
+// kDevTimeout on `err`) instead of spinning forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, int *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (global_ns() - t0 > 1000000000ull) {
+            if (err) atomicCAS(err, 0, 3);
+            return false;
+        }
+    }
+    return true;
+}
+
 __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -199,12 +251,18 @@ int launch_ex(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaSt
 //               columns 32c+2j (low) and 32c+2j+1 (high), as in gemv.rs)
 //   scl[c][k] : f16 scale of group c in row k
 // A warp reading rows k0..k0+31 of one group reads 512 contiguous bytes.
+//   Each group's rows are padded with zeros to kpad = round_up(k, 128), so a
+//   128-row chunk is always a whole, 16-byte-aligned bulk copy.
 struct Q4Dev {
     const uint4 *nib = nullptr;
     const __half *scl = nullptr;
     int64_t k = 0, n = 0;  // n may exceed 32*C: the tail stays zero (gemv.rs:846-861)
     int64_t C = 0;         // full groups
+    int64_t kpad = 0;      // row stride of one group in nib / scl
 };
+
+constexpr int kChunkRows = 128;  // rows per bulk-copy chunk
+inline int64_t pad_rows(int64_t k) { return (k + kChunkRows - 1) / kChunkRows * kChunkRows; }
 
 // Row-major device copy of an embedding table in the reference layout
 // (row = token): packed[tok][n/2], scales[tok][n/32].
