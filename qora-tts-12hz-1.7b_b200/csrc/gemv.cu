@@ -156,6 +156,7 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
     const uint64_t neg01 = pk2(-8388616.0f, -8388736.0f);    // -(2^23 + 8),    -(2^23 + 8*16)
     const uint64_t neg23 = pk2(-8390656.0f, -8421376.0f);    // -(2^23 + 8*256), -(2^23 + 8*4096)
     bool waited = false;
+    bool timed_out = false;
 
     for (int r0 = r_begin; r0 < r_end; r0 += B) {
         // ---- x rows [k_begin, k_begin + rows_cta) of this batch tile -> shared
@@ -194,7 +195,7 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
 #pragma unroll
             for (int j = 0; j < 16; j++) acc[b][j] = 0ull;
         for (int ch = 0; ch < nch; ch++) {
-            if (!waited) mbar_wait_bounded(&bars[ch], 0, a.err);
+            if (!waited && !mbar_wait_bounded(&bars[ch], 0, a.err)) timed_out = true;
 #pragma unroll
             for (int i = 0; i < kChunkRows / 32; i++) {
                 const int lr = ch * kChunkRows + lane + 32 * i;   // row within the strip
@@ -262,7 +263,7 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
         }
         __syncthreads();
     }
-    if (!waited)  // no rows: still let every copy land before the CTA exits
+    if (!waited || timed_out)  // let every copy land (bounded) before the CTA exits
         for (int ch = 0; ch < nch; ch++) mbar_wait_bounded(&bars[ch], 0, a.err);
 
     // K-split totals: the cluster's CTAs hold one partial each in shared
