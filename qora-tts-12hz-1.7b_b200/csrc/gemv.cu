@@ -163,13 +163,13 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
         if constexpr (XM == X_RMSNORM) {
             // rms_norm_f16 (gemv.rs:445-454): inv = 1/sqrt(sum(x^2)/k + 1e-6); the sum
             // comes from the producer's per-32-column partials (fixed shuffle tree)
-            if (warp < B) {
-                const int r = r0 + warp;
+            for (int b = warp; b < B; b += nw) {
+                const int r = r0 + b;
                 float t = 0.0f;
                 if (r < r_end)
                     for (int i = lane; i < a.ss_tiles; i += 32) t += __ldcg(a.ss + (int64_t)r * a.ldss + i);
                 t = warp_sum(t);
-                if (lane == 0) inv_s[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
+                if (lane == 0) inv_s[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
             }
             __syncthreads();
         }
