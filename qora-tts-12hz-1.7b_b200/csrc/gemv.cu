@@ -8,20 +8,17 @@
 // product and the sum separately; the difference is within the 1e-3
 // chunk-assembly tolerance the reference itself accepts, gemv.rs:806-809).
 //
-// Work decomposition: the weight is stored column-group-major (see Q4Dev).  A
-// warp owns a strip of SR rows of one 32-column group and streams it into
-// shared memory with cp.async.bulk copies of 128-row chunks (2 KB of nibbles
-// + 256 B of scales, completion on one mbarrier per chunk).  Lane l handles
-// rows l, l+32, l+64, l+96 of each chunk.  x is staged once per CTA in shared
-// memory (RMSNorm applied on the way).  Lane partials are combined once per
-// strip by a butterfly reduce-scatter (lane l ends with column l), then
-// across the CTA's warps in fixed order, then across the K-split CTAs of one
-// thread-block cluster by rank 0 over distributed shared memory, in rank
-// order.  The result is deterministic.
+// Work decomposition: the weight is stored column-group-major (see Q4Dev), a
+// warp owns one 32-column group and 128 rows (4 per lane, lanes = consecutive
+// rows, so every load instruction reads 512 contiguous bytes).  Lane partials
+// are combined by a butterfly reduce-scatter (lane l ends with column l),
+// then across the CTA's warps in fixed order, then across the K-split CTAs
+// of one thread-block cluster by rank 0 over distributed shared memory, in
+// rank order.  The result is deterministic.
 //
-// Launch: programmatic dependent launch.  The strip copies (immutable
-// weights) are issued before griddepcontrol.wait, so weight traffic and
-// launch latency overlap the previous kernel.
+// Launch: programmatic dependent launch.  Each CTA fetches its first weight
+// tile (immutable) before griddepcontrol.wait, so weight traffic and launch
+// latency overlap the previous kernel.
 #include <cooperative_groups.h>
 
 #include <algorithm>
@@ -34,6 +31,7 @@ namespace qora {
 
 namespace {
 
+constexpr int kRowsPerLane = 4;
 constexpr uint32_t kMagic = 0x4B000000u;  // 2^23 as f32 bits
 
 // Input element x[r][kr] before the RMSNorm scaling (applied by the caller).
@@ -57,6 +55,16 @@ __device__ __forceinline__ float epilogue_value(const GemvArgs &a, int r, int64_
     if constexpr (EM == E_BIAS) return __fadd_rn(v, a.bias[col]);
     if constexpr (EM == E_RESID) return __fadd_rn(__ldcg(a.y + (int64_t)r * a.ldy + col), v);
     return v;
+}
+
+// Stores a finished residual-stream value and its sum-of-squares partial.
+__device__ __forceinline__ void finalize_resid(const GemvArgs &a, int r, int64_t out_group, int lane,
+                                               float y) {
+    a.y[(int64_t)r * a.ldy + out_group * 32 + lane] = y;
+    if (a.ss_out) {
+        const float sq = warp_sum(__fmul_rn(y, y));
+        if (lane == 0) a.ss_out[(int64_t)r * a.ldss_out + out_group] = sq;
+    }
 }
 
 // Writes the final values for one warp-group (32 columns of one row).
@@ -97,142 +105,138 @@ __device__ __forceinline__ void finalize_group(const GemvArgs &a, int r, int64_t
     }
 }
 
-// Dynamic shared memory layout of k_gemv for nw warps, SR strip rows, B rows.
-__host__ __device__ inline size_t gemv_smem_bytes(int nw, int SR, int B, int rows_cta) {
-    const size_t strips = (size_t)nw * SR * 18;            // 16 B nibbles + 2 B scale per row
-    const size_t bars = (size_t)nw * (SR / kChunkRows) * 8;
-    return ((strips + 15) / 16) * 16 + bars + (size_t)B * rows_cta * 4;
-}
-
 template <int B, int XM, int EM>
 __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
     constexpr int CPC = (EM == E_SWIGLU) ? 2 : 1;
-    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int R = kRowsPerLane;
     __shared__ float red[8][B][32];
     __shared__ float cta_red[kRowsPerZ][CPC][32];
-    __shared__ float inv_s[B];
     __shared__ int last_flag;
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int nw = blockDim.x >> 5;
-    const int WR = a.WR, SR = a.SR, NCH = SR / kChunkRows;
-    const int rows_cta = WR * SR;
+    const int WR = a.WR;
     const int cc = warp / WR, wr = warp % WR;
     const int64_t c = (int64_t)blockIdx.x * CPC + cc;
     const int s = blockIdx.y, z = blockIdx.z;
-    const int64_t k = a.w.k, kp = a.w.kpad;
-    const int64_t k_begin = (int64_t)s * rows_cta;
-    const int64_t strip0 = k_begin + (int64_t)wr * SR;   // first row of this warp's strip
-    const int nch = (int)max((int64_t)0, min((int64_t)NCH, (kp - strip0) / kChunkRows));
+    const int64_t k = a.w.k;
+    const int64_t k_begin = (int64_t)s * a.rows_per_cta_k;
+    const int64_t k_end = min(k, k_begin + (int64_t)a.rows_per_cta_k);
+    const int64_t wrow0 = k_begin + (int64_t)wr * 32 * R;
     const int r_begin = z * a.rows_per_z;
     const int r_end = min(a.rows, r_begin + a.rows_per_z);
     const int64_t C = a.w.C;
     const int64_t n32 = C * 32;
     const int64_t n_out = (EM == E_SWIGLU) ? (C / 2) * 32 : a.w.n;
 
-    uint4 *nib_s = reinterpret_cast<uint4 *>(smem) + (size_t)warp * SR;
-    __half *scl_s = reinterpret_cast<__half *>(smem + (size_t)nw * SR * 16) + (size_t)warp * SR;
-    uint64_t *bars = reinterpret_cast<uint64_t *>(smem + (((size_t)nw * SR * 18 + 15) / 16) * 16) +
-                     (size_t)warp * NCH;
-    float *xs_s = reinterpret_cast<float *>(bars + (size_t)(nw - warp) * NCH);  // [B][rows_cta]
+    const uint4 *nibc = a.w.nib + c * a.w.kpad;
+    const __half *sclc = a.w.scl + c * a.w.kpad;
+    const bool write_side = (XM == X_RMSNORM) && a.side && blockIdx.x == 0 && cc == 0;
+    const uint64_t neg01 = pk2(-8388616.0f, -8388736.0f);    // -(2^23 + 8),    -(2^23 + 8*16)
+    const uint64_t neg23 = pk2(-8390656.0f, -8421376.0f);    // -(2^23 + 8*256), -(2^23 + 8*4096)
 
-    // Stream this warp's strip (immutable weights) into shared memory before
-    // waiting on the previous kernel: the copies overlap its tail.
-    if (lane == 0) {
-        for (int ch = 0; ch < NCH; ch++) mbar_init(&bars[ch], 1);
-        mbar_fence_init();
-        for (int ch = 0; ch < nch; ch++) {
-            const int64_t row = strip0 + (int64_t)ch * kChunkRows;
-            mbar_arrive_expect_tx(&bars[ch], kChunkRows * 18);
-            bulk_g2s(nib_s + ch * kChunkRows, a.w.nib + c * kp + row, kChunkRows * 16, &bars[ch]);
-            bulk_g2s(scl_s + ch * kChunkRows, a.w.scl + c * kp + row, kChunkRows * 2, &bars[ch]);
-        }
+    // Weights are immutable: fetch the first tile before waiting on the
+    // kernel that produces x, so the fetch overlaps that kernel's tail.
+    uint4 wv[R];
+    float sc[R];
+#pragma unroll
+    for (int i = 0; i < R; i++) {
+        const int64_t kr = wrow0 + lane + 32 * i;
+        const bool ok = kr < k_end;
+        wv[i] = ok ? ldg_stream(nibc + kr) : make_uint4(0u, 0u, 0u, 0u);
+        sc[i] = ok ? __half2float(sclc[kr]) : 0.0f;
     }
-    __syncwarp();
     griddep_launch_dependents();
     griddep_wait();
 
-    const bool write_side = (XM == X_RMSNORM) && a.side && blockIdx.x == 0;
-    const uint64_t neg01 = pk2(-8388616.0f, -8388736.0f);    // -(2^23 + 8),    -(2^23 + 8*16)
-    const uint64_t neg23 = pk2(-8390656.0f, -8421376.0f);    // -(2^23 + 8*256), -(2^23 + 8*4096)
-    bool waited = false;
-    bool timed_out = false;
-
     for (int r0 = r_begin; r0 < r_end; r0 += B) {
-        // ---- x rows [k_begin, k_begin + rows_cta) of this batch tile -> shared
+        if (r0 != r_begin) {
+#pragma unroll
+            for (int i = 0; i < R; i++) {
+                const int64_t kr = wrow0 + lane + 32 * i;
+                const bool ok = kr < k_end;
+                wv[i] = ok ? ldg_stream(nibc + kr) : make_uint4(0u, 0u, 0u, 0u);
+                sc[i] = ok ? __half2float(sclc[kr]) : 0.0f;
+            }
+        }
+        float xs[R][B];
+#pragma unroll
+        for (int i = 0; i < R; i++) {
+            const int64_t kr = wrow0 + lane + 32 * i;
+            const bool ok = kr < k_end;
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const int r = r0 + b;
+                xs[i][b] = (ok && r < r_end) ? load_x<XM>(a, r, kr) : 0.0f;
+            }
+        }
         if constexpr (XM == X_RMSNORM) {
-            // rms_norm_f16 (gemv.rs:445-454): inv = 1/sqrt(sum(x^2)/k + 1e-6); the sum
-            // comes from the producer's per-32-column partials (fixed shuffle tree)
-            for (int b = warp; b < B; b += nw) {
+            // rms_norm_f16 (gemv.rs:445-454): inv = 1/sqrt(sum(x^2)/k + 1e-6), the
+            // sum taken from the producer's per-32-column partials by a fixed
+            // shuffle tree (same in every warp, so every CTA agrees)
+            float inv[B];
+#pragma unroll
+            for (int b = 0; b < B; b++) {
                 const int r = r0 + b;
                 float t = 0.0f;
                 if (r < r_end)
                     for (int i = lane; i < a.ss_tiles; i += 32) t += __ldcg(a.ss + (int64_t)r * a.ldss + i);
                 t = warp_sum(t);
-                if (lane == 0) inv_s[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
+                inv[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
             }
-            __syncthreads();
-        }
-        for (int idx = threadIdx.x; idx < B * rows_cta; idx += blockDim.x) {
-            const int b = idx / rows_cta, j = idx - b * rows_cta;
-            const int64_t kr = k_begin + j;
-            const int r = r0 + b;
-            float v = 0.0f;
-            if (kr < k && r < r_end) {
-                v = load_x<XM>(a, r, kr);
-                if constexpr (XM == X_RMSNORM) {
-                    v = __fmul_rn(__fmul_rn(v, inv_s[b]), __half2float(a.gamma[kr]));
-                    if (write_side) a.side[(int64_t)r * a.ldside + kr] = v;
-                }
+#pragma unroll
+            for (int i = 0; i < R; i++) {
+                const int64_t kr = wrow0 + lane + 32 * i;
+                const float g = kr < k_end ? __half2float(a.gamma[kr]) : 0.0f;
+#pragma unroll
+                for (int b = 0; b < B; b++) xs[i][b] = __fmul_rn(__fmul_rn(xs[i][b], inv[b]), g);
             }
-            xs_s[idx] = v;
         }
-        __syncthreads();
-
+        if (write_side) {
+#pragma unroll
+            for (int i = 0; i < R; i++) {
+                const int64_t kr = wrow0 + lane + 32 * i;
+#pragma unroll
+                for (int b = 0; b < B; b++)
+                    if (kr < k_end && r0 + b < r_end) a.side[(int64_t)(r0 + b) * a.ldside + kr] = xs[i][b];
+            }
+        }
         uint64_t acc[B][16];
 #pragma unroll
         for (int b = 0; b < B; b++)
 #pragma unroll
             for (int j = 0; j < 16; j++) acc[b][j] = 0ull;
-        for (int ch = 0; ch < nch; ch++) {
-            if (!waited && !mbar_wait_bounded(&bars[ch], 0, a.err)) timed_out = true;
 #pragma unroll
-            for (int i = 0; i < kChunkRows / 32; i++) {
-                const int lr = ch * kChunkRows + lane + 32 * i;   // row within the strip
-                const uint4 wv = nib_s[lr];
-                const float sc = __half2float(scl_s[lr]);
-                uint64_t s01[B], s23[B];
+        for (int i = 0; i < R; i++) {
+            uint64_t s01[B], s23[B];
 #pragma unroll
-                for (int b = 0; b < B; b++) {
-                    const float sv = __fmul_rn(sc, xs_s[b * rows_cta + wr * SR + lr]);  // gemv.rs:265
-                    s01[b] = pk2(sv, sv * 0.0625f);
-                    s23[b] = pk2(sv * 0.00390625f, sv * 0.000244140625f);
-                }
-                const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+            for (int b = 0; b < B; b++) {
+                const float sv = __fmul_rn(sc[i], xs[i][b]);  // gemv.rs:265
+                s01[b] = pk2(sv, sv * 0.0625f);
+                s23[b] = pk2(sv * 0.00390625f, sv * 0.000244140625f);
+            }
+            const uint32_t words[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
+            for (int q = 0; q < 4; q++) {
 #pragma unroll
-                    for (int h = 0; h < 2; h++) {
-                        const uint32_t v = h ? (words[q] >> 16) : words[q];
-                        // nibble p of v -> 16^p * (q_p - 8) exactly: OR into the
-                        // mantissa of 2^23, subtract 2^23 + 8 * 16^p.
-                        const uint64_t f01 = fadd2(pk2(__uint_as_float((v & 0xFu) | kMagic),
-                                                       __uint_as_float((v & 0xF0u) | kMagic)),
-                                                   neg01);
-                        const uint64_t f23 = fadd2(pk2(__uint_as_float((v & 0xF00u) | kMagic),
-                                                       __uint_as_float((v & 0xF000u) | kMagic)),
-                                                   neg23);
-                        const int j = 4 * q + 2 * h;
+                for (int h = 0; h < 2; h++) {
+                    const uint32_t v = h ? (words[q] >> 16) : words[q];
+                    // nibble p of v -> 16^p * (q_p - 8) exactly: OR into the
+                    // mantissa of 2^23, subtract 2^23 + 8 * 16^p.
+                    const uint64_t f01 = fadd2(pk2(__uint_as_float((v & 0xFu) | kMagic),
+                                                   __uint_as_float((v & 0xF0u) | kMagic)),
+                                               neg01);
+                    const uint64_t f23 = fadd2(pk2(__uint_as_float((v & 0xF00u) | kMagic),
+                                                   __uint_as_float((v & 0xF000u) | kMagic)),
+                                               neg23);
+                    const int j = 4 * q + 2 * h;
 #pragma unroll
-                        for (int b = 0; b < B; b++) {
-                            acc[b][j] = ffma2(s01[b], f01, acc[b][j]);
-                            acc[b][j + 1] = ffma2(s23[b], f23, acc[b][j + 1]);
-                        }
+                    for (int b = 0; b < B; b++) {
+                        acc[b][j] = ffma2(s01[b], f01, acc[b][j]);
+                        acc[b][j + 1] = ffma2(s23[b], f23, acc[b][j + 1]);
                     }
                 }
             }
         }
-        waited = true;
         // butterfly reduce-scatter: lane l ends with the warp total of column l
 #pragma unroll
         for (int b = 0; b < B; b++) {
@@ -263,33 +267,72 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
         }
         __syncthreads();
     }
-    if (!waited || timed_out)  // let every copy land (bounded) before the CTA exits
-        for (int ch = 0; ch < nch; ch++) mbar_wait_bounded(&bars[ch], 0, a.err);
 
     // K-split totals: the cluster's CTAs hold one partial each in shared
     // memory; rank 0 sums them in rank order over DSMEM.
     cg::cluster_group cluster = cg::this_cluster();
     const int S = a.S;
-    if (S > 1) cluster.sync();
     const bool leader = (S == 1) || cluster.block_rank() == 0;
+    constexpr int CO = (EM == E_SWIGLU) ? 1 : CPC;  // output column groups per CTA
+    constexpr int kPre = 4;                          // residual values prefetched per thread
+    const int nz = r_end - r_begin;
+    const int nitems = nz * CO * 32;
+    float yres[kPre];
+    if constexpr (EM == E_RESID) {
+        // the residual does not depend on the K-split partials: load it while
+        // the cluster barrier completes
+        if (leader) {
+#pragma unroll
+            for (int m = 0; m < kPre; m++) {
+                const int it = threadIdx.x + m * blockDim.x;
+                if (it < nitems) {
+                    const int l = it & 31, q = it >> 5;
+                    const int64_t col = ((int64_t)blockIdx.x * CPC + q % CO) * 32 + l;
+                    yres[m] = __ldcg(a.y + (int64_t)(r_begin + q / CO) * a.ldy + col);
+                }
+            }
+        }
+    }
+    if (S > 1) cluster.sync();
     if (leader) {
-        constexpr int CO = (EM == E_SWIGLU) ? 1 : CPC;  // output column groups per CTA
-        const int nz = r_end - r_begin;
-        for (int it = threadIdx.x; it < nz * CO * 32; it += blockDim.x) {
+        auto finish = [&](int it, float yr, bool have_yr) {
             const int l = it & 31;
             const int q = it >> 5;
             const int row = q / CO, cc2 = q % CO;
+            float pv[kMaxSplit], pu[kMaxSplit];
+#pragma unroll
+            for (int rk = 0; rk < kMaxSplit; rk++) {
+                if (rk < S) {
+                    const float *p = (S == 1) ? &cta_red[0][0][0]
+                                              : cluster.map_shared_rank(&cta_red[0][0][0], rk);
+                    pv[rk] = p[(row * CPC + cc2) * 32 + l];
+                    if constexpr (EM == E_SWIGLU) pu[rk] = p[(row * CPC + 1) * 32 + l];
+                }
+            }
             float v = 0.0f, u = 0.0f;
-            for (int rk = 0; rk < S; rk++) {
-                const float *p = (S == 1) ? &cta_red[0][0][0]
-                                          : cluster.map_shared_rank(&cta_red[0][0][0], rk);
-                v += p[(row * CPC + cc2) * 32 + l];
-                if constexpr (EM == E_SWIGLU) u += p[(row * CPC + 1) * 32 + l];
+#pragma unroll
+            for (int rk = 0; rk < kMaxSplit; rk++) {
+                if (rk < S) {
+                    v += pv[rk];
+                    if constexpr (EM == E_SWIGLU) u += pu[rk];
+                }
             }
             const int64_t grp = (EM == E_SWIGLU) ? (int64_t)blockIdx.x
                                                  : (int64_t)blockIdx.x * CPC + cc2;
-            finalize_group<EM>(a, r_begin + row, grp, l, v, u, n_out);
+            if constexpr (EM == E_RESID) {
+                // x[j] += attn_out[j] (talker.rs:334-336)
+                if (!have_yr) yr = __ldcg(a.y + (int64_t)(r_begin + row) * a.ldy + grp * 32 + l);
+                finalize_resid(a, r_begin + row, grp, l, __fadd_rn(yr, v));
+            } else {
+                finalize_group<EM>(a, r_begin + row, grp, l, v, u, n_out);
+            }
+        };
+#pragma unroll
+        for (int m = 0; m < kPre; m++) {
+            const int it = threadIdx.x + m * blockDim.x;
+            if (it < nitems) finish(it, (EM == E_RESID) ? yres[m] : 0.0f, true);
         }
+        for (int it = threadIdx.x + kPre * blockDim.x; it < nitems; it += blockDim.x) finish(it, 0.0f, false);
         // tail columns beyond the last full group stay zero (gemv.rs:846-861)
         if (EM == E_STORE && a.w.n > n32 && blockIdx.x == 0) {
             for (int r = r_begin; r < r_end; r++)
@@ -337,16 +380,12 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
 
 template <int B, int XM, int EM>
 int launch_one(const GemvArgs &a, const GemvPlan &p, cudaStream_t st) {
-    return launch_ex(k_gemv<B, XM, EM>, p.grid, p.block, p.smem, st, (unsigned)p.S, a);
+    return launch_ex(k_gemv<B, XM, EM>, p.grid, p.block, 0, st, (unsigned)p.S, a);
 }
-
-constexpr int kGemvMaxSmem = 200 * 1024;
 
 template <int B, int XM, int EM>
 int allow_large_clusters() {
     QORA_CUDA(cudaFuncSetAttribute(k_gemv<B, XM, EM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-    QORA_CUDA(cudaFuncSetAttribute(k_gemv<B, XM, EM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   kGemvMaxSmem));
     return QORA_OK;
 }
 
@@ -468,38 +507,16 @@ GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms) {
     p.rows_per_z = std::min(rows, kRowsPerZ);
     p.Z = (rows + p.rows_per_z - 1) / p.rows_per_z;
     const int64_t tiles = C / p.cpc;
-    const int64_t kp = pad_rows(k);
-    const int wr_max = 8 / p.cpc;
-    auto splits = [&](int wr, int sr) { return (kp + (int64_t)wr * sr - 1) / ((int64_t)wr * sr); };
-    // Longest strips (fewest reductions) that still give ~2 CTAs per SM and
-    // fit one cluster; shorter strips / fewer warps per CTA otherwise.
-    int best_wr = 1, best_sr = kChunkRows;
-    int64_t best_score = -1;
-    for (int sr = 512; sr >= kChunkRows; sr /= 2) {
-        for (int wr = wr_max; wr >= 1; wr /= 2) {
-            const int64_t S = splits(wr, sr);
-            if (S > kMaxSplit) continue;
-            if (sr > kp && sr > kChunkRows) continue;              // strip longer than K
-            if ((int64_t)wr * sr > kp && wr > 1) continue;        // more warps than rows
-            const int64_t ctas = tiles * S * p.Z;
-            const size_t smem = gemv_smem_bytes(p.cpc * wr, sr, p.B, wr * sr);
-            if (smem > (size_t)kGemvMaxSmem) continue;
-            // prefer enough CTAs, then long strips, then wide CTAs
-            const int64_t enough = std::min<int64_t>(ctas, 2LL * num_sms);
-            const int64_t score = enough * 1000000 + (int64_t)sr * 1000 + wr;
-            if (score > best_score) {
-                best_score = score;
-                best_wr = wr;
-                best_sr = sr;
-            }
-        }
-    }
-    p.WR = best_wr;
-    p.SR = best_sr;
-    p.S = (int)splits(best_wr, best_sr);
+    auto splits = [&](int wr) { return (k + (int64_t)wr * 128 - 1) / ((int64_t)wr * 128); };
+    int WR = 8 / p.cpc;
+    // Smaller CTAs (more K-splits) until ~2 CTAs per SM, within one cluster.
+    while (WR > 1 && splits(WR / 2) <= kMaxSplit && tiles * splits(WR) * p.Z < 2LL * num_sms) WR /= 2;
+    while (WR > 1 && splits(WR / 2) == splits(WR)) WR /= 2;  // k smaller than the CTA's rows
+    p.WR = WR;
+    p.S = (int)splits(WR);
+    p.rows_per_cta_k = WR * 128;
     p.grid = dim3((unsigned)tiles, (unsigned)p.S, (unsigned)p.Z);
-    p.block = dim3(32 * p.cpc * p.WR);
-    p.smem = gemv_smem_bytes(p.cpc * p.WR, p.SR, p.B, p.WR * p.SR);
+    p.block = dim3(32 * p.cpc * WR);
     return p;
 }
 
@@ -516,9 +533,9 @@ int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &p, unsigned *g
     if (!(a.amax || a.adv_len)) a.gticket = nullptr;
     a.B = p.B;
     a.WR = p.WR;
-    a.SR = p.SR;
     a.S = p.S;
     a.Z = p.Z;
+    a.rows_per_cta_k = p.rows_per_cta_k;
     a.rows_per_z = p.rows_per_z;
     switch (xmode) {
         case X_PLAIN: return launch_e<X_PLAIN>(a, emode, p, st);

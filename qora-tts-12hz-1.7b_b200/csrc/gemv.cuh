@@ -40,8 +40,8 @@ struct GemvArgs {
     int adv_T = 0, adv_streams = 0;
     int *err = nullptr;
     // ---- filled by plan_gemv
-    int B = 1, WR = 1, SR = 128, S = 1, Z = 1;
-    int rows_per_z = 0;
+    int B = 1, WR = 1, S = 1, Z = 1;
+    int rows_per_cta_k = 128, rows_per_z = 0;
     unsigned *gticket = nullptr;    // [1] arrival counter of the global final stage
 };
 
@@ -49,12 +49,9 @@ constexpr int kRowsPerZ = 16;       // rows one CTA carries through the K loop
 constexpr int kMaxSplit = 16;       // CTAs of one cluster along K
 
 // Tiling of one GEMV: column groups x K-splits (one cluster) x row groups.
-// A CTA has cpc * WR warps; each warp streams a strip of SR rows of one
-// column group into shared memory; a CTA covers WR * SR rows of K.
 struct GemvPlan {
-    int B, WR, SR, S, Z, rows_per_z, cpc;
+    int B, WR, S, Z, rows_per_cta_k, rows_per_z, cpc;
     dim3 grid, block;
-    size_t smem;   // dynamic shared memory bytes
 };
 
 // Per-device one-time kernel attribute setup (large clusters).
