@@ -105,6 +105,24 @@ __device__ __forceinline__ void finalize_group(const GemvArgs &a, int r, int64_t
     }
 }
 
+// Bulk L2 prefetch of CTA `id`'s share (16-byte aligned pieces) of [p, p+bytes).
+__device__ __forceinline__ void l2_prefetch_share(const void *p, uint64_t bytes, uint64_t id,
+                                                  uint64_t nctas) {
+    if (!p || bytes == 0) return;
+    const uint64_t per = ((bytes + nctas - 1) / nctas + 15) & ~15ull;
+    uint64_t off = id * per;
+    if (off >= bytes) return;
+    uint64_t len = per < bytes - off ? per : bytes - off;
+    const char *base = static_cast<const char *>(p) + off;
+    while (len >= 16) {
+        const uint64_t whole = len & ~15ull;
+        const uint32_t piece = (uint32_t)(whole < (1ull << 20) ? whole : (1ull << 20));
+        prefetch_l2_bulk(base, piece);
+        base += piece;
+        len -= piece;
+    }
+}
+
 template <int B, int XM, int EM>
 __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
     constexpr int CPC = (EM == E_SWIGLU) ? 2 : 1;
@@ -144,6 +162,13 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
         const bool ok = kr < k_end;
         wv[i] = ok ? ldg_stream(nibc + kr) : make_uint4(0u, 0u, 0u, 0u);
         sc[i] = ok ? __half2float(sclc[kr]) : 0.0f;
+    }
+    // Warm L2 with the next GEMV's weights (this grid's share of them).
+    if (threadIdx.x == 0 && (a.pf0_bytes | a.pf1_bytes)) {
+        const uint64_t nctas = (uint64_t)gridDim.x * gridDim.y * gridDim.z;
+        const uint64_t id = ((uint64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+        l2_prefetch_share(a.pf0, a.pf0_bytes, id, nctas);
+        l2_prefetch_share(a.pf1, a.pf1_bytes, id, nctas);
     }
     griddep_launch_dependents();
     griddep_wait();

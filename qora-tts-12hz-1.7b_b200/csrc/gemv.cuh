@@ -39,6 +39,10 @@ struct GemvArgs {
     int *adv_pos = nullptr;         // pos[s] += adv_T
     int adv_T = 0, adv_streams = 0;
     int *err = nullptr;
+    // ---- L2 prefetch of the weights the next kernel will stream (issued
+    // before griddepcontrol.wait; spread over the grid's CTAs)
+    const void *pf0 = nullptr, *pf1 = nullptr;
+    uint64_t pf0_bytes = 0, pf1_bytes = 0;
     // ---- filled by plan_gemv
     int B = 1, WR = 1, S = 1, Z = 1;
     int rows_per_cta_k = 128, rows_per_z = 0;
@@ -53,6 +57,14 @@ struct GemvPlan {
     int B, WR, S, Z, rows_per_cta_k, rows_per_z, cpc;
     dim3 grid, block;
 };
+
+// Point a GEMV's L2 prefetch at the weights of the GEMV that follows it.
+inline void prefetch_next(GemvArgs &a, const Q4Dev &next) {
+    a.pf0 = next.nib;
+    a.pf0_bytes = (uint64_t)next.C * next.kpad * 16;
+    a.pf1 = next.scl;
+    a.pf1_bytes = (uint64_t)next.C * next.kpad * 2;
+}
 
 // Per-device one-time kernel attribute setup (large clusters).
 int gemv_init();

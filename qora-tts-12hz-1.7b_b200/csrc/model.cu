@@ -179,9 +179,11 @@ struct Launcher {
 };
 
 // One decoder layer over `rows` rows (T tokens per stream).
+// `next` is the weight the GEMV after this layer streams (L2 prefetch target).
 static int run_layer(Launcher &ln, const LayerDev &ld, int H, int heads, int kvh, int hd,
                      int64_t ffn, int rows, int T, const KVLayer &kv, const int *len,
-                     const int *pos, const float *rope_cos, const float *rope_sin, int rope_max) {
+                     const int *pos, const float *rope_cos, const float *rope_sin, int rope_max,
+                     const Q4Dev &next) {
     Work &w = *ln.w;
     const int64_t qd = (int64_t)heads * hd, qkvn = qd + 2 * (int64_t)kvh * hd;
     {
@@ -196,6 +198,7 @@ static int run_layer(Launcher &ln, const LayerDev &ld, int H, int heads, int kvh
         a.ss_tiles = H / kGroup;
         a.y = w.qkv.as<float>();
         a.ldy = qkvn;
+        prefetch_next(a, ld.o);
         QORA_TRY(ln.gemv(a, X_RMSNORM, E_STORE));
     }
     AttnArgs at;
@@ -236,6 +239,7 @@ static int run_layer(Launcher &ln, const LayerDev &ld, int H, int heads, int kvh
         a.ldy = H;
         a.ss_out = w.ss.as<float>();
         a.ldss_out = H / kGroup;
+        prefetch_next(a, ld.gu);
         QORA_TRY(ln.gemv(a, X_PLAIN, E_RESID));
     }
     {
@@ -250,6 +254,7 @@ static int run_layer(Launcher &ln, const LayerDev &ld, int H, int heads, int kvh
         a.ss_tiles = H / kGroup;
         a.y = w.h.as<float>();
         a.ldy = ffn;
+        prefetch_next(a, ld.dn);
         QORA_TRY(ln.gemv(a, X_RMSNORM, E_SWIGLU));
     }
     {
@@ -262,6 +267,7 @@ static int run_layer(Launcher &ln, const LayerDev &ld, int H, int heads, int kvh
         a.ldy = H;
         a.ss_out = w.ss.as<float>();
         a.ldss_out = H / kGroup;
+        prefetch_next(a, next);
         QORA_TRY(ln.gemv(a, X_PLAIN, E_RESID));
     }
     return QORA_OK;
@@ -275,7 +281,8 @@ static int talker_forward_step(qora_talker *t, qora_kv *kv, Launcher &ln, int B,
     for (int l = 0; l < t->L; l++)
         QORA_TRY(run_layer(ln, t->layers[l], t->H, t->heads, t->kvh, t->hd, t->ffn, B, 1,
                            kv->layer(l), kv->lens(), pos, t->rope_cos.as<float>(),
-                           t->rope_sin.as<float>(), t->rope_max));
+                           t->rope_sin.as<float>(), t->rope_max,
+                           l + 1 < t->L ? t->layers[l + 1].qkv : t->head));
     GemvArgs a;
     a.w = t->head;
     a.rows = B;
@@ -394,7 +401,8 @@ static int predictor_frame_impl(qora_predictor *p, qora_kv *kv, Launcher &ln, in
     for (int l = 0; l < p->L; l++)
         QORA_TRY(run_layer(ln, p->layers[l], p->H, p->heads, p->kvh, p->hd, p->ffn, 2 * B, 2,
                            kv->layer(l), kv->lens(), nullptr, p->rope_cos.as<float>(),
-                           p->rope_sin.as<float>(), p->rope_max));
+                           p->rope_sin.as<float>(), p->rope_max,
+                           l + 1 < p->L ? p->layers[l + 1].qkv : p->heads_w[0]));
     QORA_TRY(predictor_head(p, ln, B, 0, 2, kv, codes, ldcodes, logits, ldl));
     for (int g = 1; g < p->groups; g++) {
         const uint32_t *tok = forced ? forced + (g - 1) : codes + (g - 1);
@@ -403,7 +411,8 @@ static int predictor_frame_impl(qora_predictor *p, qora_kv *kv, Launcher &ln, in
         for (int l = 0; l < p->L; l++)
             QORA_TRY(run_layer(ln, p->layers[l], p->H, p->heads, p->kvh, p->hd, p->ffn, B, 1,
                                kv->layer(l), kv->lens(), nullptr, p->rope_cos.as<float>(),
-                               p->rope_sin.as<float>(), p->rope_max));
+                               p->rope_sin.as<float>(), p->rope_max,
+                               l + 1 < p->L ? p->layers[l + 1].qkv : p->heads_w[g]));
         QORA_TRY(predictor_head(p, ln, B, g, 1, kv, codes, ldcodes, logits, ldl));
     }
     return QORA_OK;
@@ -609,7 +618,8 @@ int talker_prefill_rows(qora_talker *t, qora_kv *kv, int s0, int ns, int T, cons
     for (int l = 0; l < t->L; l++)
         QORA_TRY(run_layer(ln, t->layers[l], t->H, t->heads, t->kvh, t->hd, t->ffn, rows, T,
                            kv->layer(l, s0), kv->lens() + s0, nullptr, t->rope_cos.as<float>(),
-                           t->rope_sin.as<float>(), t->rope_max));
+                           t->rope_sin.as<float>(), t->rope_max,
+                           l + 1 < t->L ? t->layers[l + 1].qkv : t->head));
     return launch_ex(k_advance, dim3((ns + 255) / 256), dim3(256), 0, st, 1u, kv->lens() + s0,
                      (int *)nullptr, ns, T);
 }
