@@ -32,7 +32,6 @@ namespace qora {
 namespace {
 
 constexpr int kRowsPerLane = 4;
-constexpr uint32_t kMagic = 0x4B000000u;  // 2^23 as f32 bits
 
 // Input element x[r][kr] before the RMSNorm scaling (applied by the caller).
 template <int XM>
@@ -123,8 +122,15 @@ __device__ __forceinline__ void l2_prefetch_share(const void *p, uint64_t bytes,
     }
 }
 
+// Register caps per batch tile so a whole GEMV grid is resident in one wave
+// (B = 1: 64 registers, 4 CTAs of 256 threads per SM).
+template <int B>
+struct GemvOcc {
+    static constexpr int kMinBlocks = B == 1 ? 4 : (B == 2 ? 2 : 1);
+};
+
 template <int B, int XM, int EM>
-__global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
+__global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const GemvArgs a) {
     constexpr int CPC = (EM == E_SWIGLU) ? 2 : 1;
     constexpr int R = kRowsPerLane;
     __shared__ float red[8][B][32];
@@ -149,8 +155,6 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
     const uint4 *nibc = a.w.nib + c * a.w.kpad;
     const __half *sclc = a.w.scl + c * a.w.kpad;
     const bool write_side = (XM == X_RMSNORM) && a.side && blockIdx.x == 0 && cc == 0;
-    const uint64_t neg01 = pk2(-8388616.0f, -8388736.0f);    // -(2^23 + 8),    -(2^23 + 8*16)
-    const uint64_t neg23 = pk2(-8390656.0f, -8421376.0f);    // -(2^23 + 8*256), -(2^23 + 8*4096)
 
     // Weights are immutable: fetch the first tile before waiting on the
     // kernel that produces x, so the fetch overlaps that kernel's tail.
@@ -225,39 +229,44 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
                     if (kr < k_end && r0 + b < r_end) a.side[(int64_t)(r0 + b) * a.ldside + kr] = xs[i][b];
             }
         }
+        // Dequantise-and-accumulate.  A nibble at bit position 4p (p < 4) of a
+        // 16-bit half-word, masked in place (v & 0xF<<4p), read as f32 bits is
+        // exactly q * 2^(4p-149) (subnormal range: linear in q).  With
+        // s' = scale * x * 2^75 (exact power-of-two scaling of gemv.rs:265's
+        // product), fma(s', that, acc) adds s*q*2^(4p-74) with one rounding.
+        // The -8 offset is applied once: sum_k s*(q-8) = sum_k s*q - 8*sum_k s.
         uint64_t acc[B][16];
+        float ssum[B];
 #pragma unroll
-        for (int b = 0; b < B; b++)
+        for (int b = 0; b < B; b++) {
+            ssum[b] = 0.0f;
 #pragma unroll
             for (int j = 0; j < 16; j++) acc[b][j] = 0ull;
+        }
 #pragma unroll
         for (int i = 0; i < R; i++) {
-            uint64_t s01[B], s23[B];
+            uint64_t s2[B];
 #pragma unroll
             for (int b = 0; b < B; b++) {
-                const float sv = __fmul_rn(sc[i], xs[i][b]);  // gemv.rs:265
-                s01[b] = pk2(sv, sv * 0.0625f);
-                s23[b] = pk2(sv * 0.00390625f, sv * 0.000244140625f);
+                const float sp = __fmul_rn(sc[i], __fmul_rn(xs[i][b], 37778931862957161709568.0f));
+                ssum[b] += sp;
+                s2[b] = pk2(sp, sp);
             }
             const uint32_t words[4] = {wv[i].x, wv[i].y, wv[i].z, wv[i].w};
 #pragma unroll
             for (int q = 0; q < 4; q++) {
 #pragma unroll
                 for (int h = 0; h < 2; h++) {
+                    // nibbles 4h..4h+3 of the word (columns 8q+4h..8q+4h+3) at
+                    // bit positions 0..15, where masked bits stay linear
                     const uint32_t v = h ? (words[q] >> 16) : words[q];
-                    // nibble p of v -> 16^p * (q_p - 8) exactly: OR into the
-                    // mantissa of 2^23, subtract 2^23 + 8 * 16^p.
-                    const uint64_t f01 = fadd2(pk2(__uint_as_float((v & 0xFu) | kMagic),
-                                                   __uint_as_float((v & 0xF0u) | kMagic)),
-                                               neg01);
-                    const uint64_t f23 = fadd2(pk2(__uint_as_float((v & 0xF00u) | kMagic),
-                                                   __uint_as_float((v & 0xF000u) | kMagic)),
-                                               neg23);
-                    const int j = 4 * q + 2 * h;
 #pragma unroll
-                    for (int b = 0; b < B; b++) {
-                        acc[b][j] = ffma2(s01[b], f01, acc[b][j]);
-                        acc[b][j + 1] = ffma2(s23[b], f23, acc[b][j + 1]);
+                    for (int pp = 0; pp < 4; pp += 2) {
+                        const uint64_t qd = pk2(__uint_as_float(v & (0xFu << (4 * pp))),
+                                                __uint_as_float(v & (0xFu << (4 * pp + 4))));
+                        const int j = 4 * q + 2 * h + pp / 2;
+#pragma unroll
+                        for (int b = 0; b < B; b++) acc[b][j] = ffma2(s2[b], qd, acc[b][j]);
                     }
                 }
             }
@@ -278,6 +287,11 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
                     v[j] = keep + __shfl_xor_sync(0xffffffffu, send, sft);
                 }
             }
+            // undo the per-position scaling (column l sits at position l % 4 of
+            // its half-word) and apply the offset: y = 2^(74-4p)*acc - 8*2^-75*sum(s')
+            const float stot = warp_sum(ssum[b]);
+            const float up = __int_as_float((127 + 74 - 4 * (lane & 3)) << 23);
+            v[0] = __fsub_rn(__fmul_rn(v[0], up), __fmul_rn(stot, 2.117582368135751e-22f));  // 2^-72
             red[warp][b][lane] = v[0];
         }
         __syncthreads();
@@ -324,22 +338,25 @@ __global__ void __launch_bounds__(256) k_gemv(const GemvArgs a) {
             const int l = it & 31;
             const int q = it >> 5;
             const int row = q / CO, cc2 = q % CO;
-            float pv[kMaxSplit], pu[kMaxSplit];
-#pragma unroll
-            for (int rk = 0; rk < kMaxSplit; rk++) {
-                if (rk < S) {
-                    const float *p = (S == 1) ? &cta_red[0][0][0]
-                                              : cluster.map_shared_rank(&cta_red[0][0][0], rk);
-                    pv[rk] = p[(row * CPC + cc2) * 32 + l];
-                    if constexpr (EM == E_SWIGLU) pu[rk] = p[(row * CPC + 1) * 32 + l];
-                }
-            }
+            // rank-order sum; peer loads issued four at a time
             float v = 0.0f, u = 0.0f;
+            for (int r4 = 0; r4 < S; r4 += 4) {
+                float pv[4], pu[4];
 #pragma unroll
-            for (int rk = 0; rk < kMaxSplit; rk++) {
-                if (rk < S) {
-                    v += pv[rk];
-                    if constexpr (EM == E_SWIGLU) u += pu[rk];
+                for (int j = 0; j < 4; j++) {
+                    if (r4 + j < S) {
+                        const float *p = (S == 1) ? &cta_red[0][0][0]
+                                                  : cluster.map_shared_rank(&cta_red[0][0][0], r4 + j);
+                        pv[j] = p[(row * CPC + cc2) * 32 + l];
+                        if constexpr (EM == E_SWIGLU) pu[j] = p[(row * CPC + 1) * 32 + l];
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    if (r4 + j < S) {
+                        v += pv[j];
+                        if constexpr (EM == E_SWIGLU) u += pu[j];
+                    }
                 }
             }
             const int64_t grp = (EM == E_SWIGLU) ? (int64_t)blockIdx.x
