@@ -107,6 +107,7 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnArgs a) {
     constexpr int NO = (G * HD + kThreads - 1) / kThreads;
     __shared__ float q_s[G][HD];
     __shared__ float kt_s[HD][kTile + 1];
+    __shared__ __align__(16) float v_s[kTile][HD];
     __shared__ float sc_s[G][PARTS][kTile];
     __shared__ float p_s[G][kTile];
     __shared__ float m_s[G], l_s[G], corr_s[G];
@@ -181,15 +182,20 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnArgs a) {
 
     for (int base = p0; base < p1; base += kTile) {
         const int cnt = min(kTile, p1 - base);
-        // K tile, transposed into shared memory
+        // K tile (transposed) and V tile into shared memory; every load of the
+        // tile is in flight at once
         for (int i = threadIdx.x; i < kTile * (HD / 4); i += kThreads) {
             const int pp = i / (HD / 4), d4 = i % (HD / 4);
-            float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (pp < cnt) kv4 = *reinterpret_cast<const float4 *>(krow_base + (int64_t)(base + pp) * HD + 4 * d4);
-            kt_s[4 * d4 + 0][pp] = kv4.x;
-            kt_s[4 * d4 + 1][pp] = kv4.y;
-            kt_s[4 * d4 + 2][pp] = kv4.z;
-            kt_s[4 * d4 + 3][pp] = kv4.w;
+            float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (pp < cnt) {
+                k4 = __ldcg(reinterpret_cast<const float4 *>(krow_base + (int64_t)(base + pp) * HD) + d4);
+                v4 = __ldcg(reinterpret_cast<const float4 *>(vrow_base + (int64_t)(base + pp) * HD) + d4);
+            }
+            kt_s[4 * d4 + 0][pp] = k4.x;
+            kt_s[4 * d4 + 1][pp] = k4.y;
+            kt_s[4 * d4 + 2][pp] = k4.z;
+            kt_s[4 * d4 + 3][pp] = k4.w;
+            reinterpret_cast<float4 *>(&v_s[pp][0])[d4] = v4;
         }
         __syncthreads();
         {
@@ -226,8 +232,8 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnArgs a) {
             if (o < G * HD) {
                 const int hh = o / HD, d = o % HD;
                 float acc = __fmul_rn(o_acc[i], corr_s[hh]);
-                for (int pp = 0; pp < cnt; pp++)
-                    acc = __fmaf_rn(p_s[hh][pp], vrow_base[(int64_t)(base + pp) * HD + d], acc);
+#pragma unroll 8
+                for (int pp = 0; pp < cnt; pp++) acc = __fmaf_rn(p_s[hh][pp], v_s[pp][d], acc);
                 o_acc[i] = acc;
             }
         }

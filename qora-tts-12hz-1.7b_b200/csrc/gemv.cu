@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
     const int64_t k = a.w.k;
     const int64_t k_begin = (int64_t)s * a.rows_per_cta_k;
     const int64_t k_end = min(k, k_begin + (int64_t)a.rows_per_cta_k);
-    const int64_t wrow0 = k_begin + (int64_t)wr * 32 * R;
+    const int64_t wrow0 = k_begin + (int64_t)wr * 32 * R * a.NSUB;
     const int r_begin = z * a.rows_per_z;
     const int r_end = min(a.rows, r_begin + a.rows_per_z);
     const int64_t C = a.w.C;
@@ -178,10 +178,36 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
     griddep_wait();
 
     for (int r0 = r_begin; r0 < r_end; r0 += B) {
-        if (r0 != r_begin) {
+        // rms_norm_f16 (gemv.rs:445-454): inv = 1/sqrt(sum(x^2)/k + 1e-6), the
+        // sum taken from the producer's per-32-column partials by a fixed
+        // shuffle tree (same in every warp, so every CTA agrees)
+        float inv[B];
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            inv[b] = 1.0f;
+            if constexpr (XM == X_RMSNORM) {
+                const int r = r0 + b;
+                float t = 0.0f;
+                if (r < r_end)
+                    for (int i = lane; i < a.ss_tiles; i += 32) t += __ldcg(a.ss + (int64_t)r * a.ldss + i);
+                t = warp_sum(t);
+                inv[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
+            }
+        }
+        uint64_t acc[B][16];
+        float ssum[B];
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            ssum[b] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 16; j++) acc[b][j] = 0ull;
+        }
+        for (int sb = 0; sb < a.NSUB; sb++) {
+        const int64_t srow0 = wrow0 + (int64_t)sb * 32 * R;
+        if (r0 != r_begin || sb != 0) {
 #pragma unroll
             for (int i = 0; i < R; i++) {
-                const int64_t kr = wrow0 + lane + 32 * i;
+                const int64_t kr = srow0 + lane + 32 * i;
                 const bool ok = kr < k_end;
                 wv[i] = ok ? ldg_stream(nibc + kr) : make_uint4(0u, 0u, 0u, 0u);
                 sc[i] = ok ? __half2float(sclc[kr]) : 0.0f;
@@ -190,7 +216,7 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
         float xs[R][B];
 #pragma unroll
         for (int i = 0; i < R; i++) {
-            const int64_t kr = wrow0 + lane + 32 * i;
+            const int64_t kr = srow0 + lane + 32 * i;
             const bool ok = kr < k_end;
 #pragma unroll
             for (int b = 0; b < B; b++) {
@@ -199,22 +225,9 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
             }
         }
         if constexpr (XM == X_RMSNORM) {
-            // rms_norm_f16 (gemv.rs:445-454): inv = 1/sqrt(sum(x^2)/k + 1e-6), the
-            // sum taken from the producer's per-32-column partials by a fixed
-            // shuffle tree (same in every warp, so every CTA agrees)
-            float inv[B];
-#pragma unroll
-            for (int b = 0; b < B; b++) {
-                const int r = r0 + b;
-                float t = 0.0f;
-                if (r < r_end)
-                    for (int i = lane; i < a.ss_tiles; i += 32) t += __ldcg(a.ss + (int64_t)r * a.ldss + i);
-                t = warp_sum(t);
-                inv[b] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
-            }
 #pragma unroll
             for (int i = 0; i < R; i++) {
-                const int64_t kr = wrow0 + lane + 32 * i;
+                const int64_t kr = srow0 + lane + 32 * i;
                 const float g = kr < k_end ? __half2float(a.gamma[kr]) : 0.0f;
 #pragma unroll
                 for (int b = 0; b < B; b++) xs[i][b] = __fmul_rn(__fmul_rn(xs[i][b], inv[b]), g);
@@ -223,7 +236,7 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
         if (write_side) {
 #pragma unroll
             for (int i = 0; i < R; i++) {
-                const int64_t kr = wrow0 + lane + 32 * i;
+                const int64_t kr = srow0 + lane + 32 * i;
 #pragma unroll
                 for (int b = 0; b < B; b++)
                     if (kr < k_end && r0 + b < r_end) a.side[(int64_t)(r0 + b) * a.ldside + kr] = xs[i][b];
@@ -235,14 +248,6 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
         // s' = scale * x * 2^75 (exact power-of-two scaling of gemv.rs:265's
         // product), fma(s', that, acc) adds s*q*2^(4p-74) with one rounding.
         // The -8 offset is applied once: sum_k s*(q-8) = sum_k s*q - 8*sum_k s.
-        uint64_t acc[B][16];
-        float ssum[B];
-#pragma unroll
-        for (int b = 0; b < B; b++) {
-            ssum[b] = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 16; j++) acc[b][j] = 0ull;
-        }
 #pragma unroll
         for (int i = 0; i < R; i++) {
             uint64_t s2[B];
@@ -271,6 +276,7 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
                 }
             }
         }
+        }  // sub-blocks
         // butterfly reduce-scatter: lane l ends with the warp total of column l
 #pragma unroll
         for (int b = 0; b < B; b++) {
@@ -396,18 +402,31 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
         if (!last_flag) return;
         __threadfence();
         if (a.amax) {
-            for (int r = threadIdx.x; r < a.rows; r += blockDim.x) {
-                float bv = __ldcg(a.tbest_v + (int64_t)r * gridDim.x);
-                int bi = __ldcg(a.tbest_i + (int64_t)r * gridDim.x);
-                for (unsigned t = 1; t < gridDim.x; t++) {
+            // argmax over the column tiles, one warp per row: lanes take tiles
+            // lane, lane+32, ...; ties keep the larger index (the last maximum,
+            // code_predictor.rs:336-339)
+            const int nwarps = blockDim.x >> 5;
+            for (int r = warp; r < a.rows; r += nwarps) {
+                float bv = -INFINITY;
+                int bi = -1;
+                for (unsigned t = lane; t < gridDim.x; t += 32) {
                     const float v = __ldcg(a.tbest_v + (int64_t)r * gridDim.x + t);
                     const int i = __ldcg(a.tbest_i + (int64_t)r * gridDim.x + t);
-                    if (v >= bv) {  // later tile holds later indices: last max wins
+                    if (bi < 0 || v > bv || (v == bv && i > bi)) {
                         bv = v;
                         bi = i;
                     }
                 }
-                a.amax[(int64_t)r * a.ldamax] = (uint32_t)bi;
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi > bi))) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) a.amax[(int64_t)r * a.ldamax] = (uint32_t)bi;
             }
         }
         if (a.adv_len) {
@@ -549,14 +568,29 @@ GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms) {
     p.rows_per_z = std::min(rows, kRowsPerZ);
     p.Z = (rows + p.rows_per_z - 1) / p.rows_per_z;
     const int64_t tiles = C / p.cpc;
-    auto splits = [&](int wr) { return (k + (int64_t)wr * 128 - 1) / ((int64_t)wr * 128); };
+    const int64_t kp = pad_rows(k);
+    // Resident warps per SM at this batch tile's register cap (GemvOcc); a
+    // grid larger than ~90 % of that runs in waves, so long ones get more
+    // 128-row sub-blocks per warp instead.
+    const int warps_per_sm = p.B == 1 ? 32 : (p.B == 2 ? 16 : 8);
+    const int64_t cap = (int64_t)num_sms * warps_per_sm * 9 / 10;
+    const int64_t units = tiles * p.cpc * (kp / 128) * p.Z;
+    int nsub = 1;
+    while (nsub < 8 && units / nsub > cap) nsub *= 2;
+    const int64_t wrows = 128LL * nsub;
+    auto splits = [&](int wr) { return (kp + wr * wrows - 1) / (wr * wrows); };
     int WR = 8 / p.cpc;
+    while (WR > 1 && splits(WR / 2) == splits(WR)) WR /= 2;  // not more warps than K needs
     // Smaller CTAs (more K-splits) until ~2 CTAs per SM, within one cluster.
     while (WR > 1 && splits(WR / 2) <= kMaxSplit && tiles * splits(WR) * p.Z < 2LL * num_sms) WR /= 2;
-    while (WR > 1 && splits(WR / 2) == splits(WR)) WR /= 2;  // k smaller than the CTA's rows
+    while (splits(WR) > kMaxSplit && nsub < 64) {  // very long K: longer strips
+        nsub *= 2;
+        WR = 8 / p.cpc;
+    }
+    p.NSUB = nsub;
     p.WR = WR;
-    p.S = (int)splits(WR);
-    p.rows_per_cta_k = WR * 128;
+    p.S = (int)((kp + WR * 128LL * nsub - 1) / (WR * 128LL * nsub));
+    p.rows_per_cta_k = WR * 128 * nsub;
     p.grid = dim3((unsigned)tiles, (unsigned)p.S, (unsigned)p.Z);
     p.block = dim3(32 * p.cpc * WR);
     return p;
@@ -577,6 +611,7 @@ int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &p, unsigned *g
     a.WR = p.WR;
     a.S = p.S;
     a.Z = p.Z;
+    a.NSUB = p.NSUB;
     a.rows_per_cta_k = p.rows_per_cta_k;
     a.rows_per_z = p.rows_per_z;
     switch (xmode) {

@@ -44,7 +44,7 @@ struct GemvArgs {
     const void *pf0 = nullptr, *pf1 = nullptr;
     uint64_t pf0_bytes = 0, pf1_bytes = 0;
     // ---- filled by plan_gemv
-    int B = 1, WR = 1, S = 1, Z = 1;
+    int B = 1, WR = 1, S = 1, Z = 1, NSUB = 1;
     int rows_per_cta_k = 128, rows_per_z = 0;
     unsigned *gticket = nullptr;    // [1] arrival counter of the global final stage
 };
@@ -54,7 +54,7 @@ constexpr int kMaxSplit = 16;       // CTAs of one cluster along K
 
 // Tiling of one GEMV: column groups x K-splits (one cluster) x row groups.
 struct GemvPlan {
-    int B, WR, S, Z, rows_per_cta_k, rows_per_z, cpc;
+    int B, WR, S, Z, NSUB, rows_per_cta_k, rows_per_z, cpc;
     dim3 grid, block;
 };
 
