@@ -22,6 +22,7 @@ from __future__ import annotations
 import argparse
 import json
 import os
+import re
 import statistics
 import subprocess
 import sys
@@ -51,6 +52,8 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
+    ap.add_argument("--profile-case", default=None, choices=["gemv"],
+                    help="small fixed workload for an ncu capture instead of the bench")
     return ap.parse_args()
 
 
@@ -392,9 +395,13 @@ def run_ours(args):
         achieved = byts / (gms / 1000.0) / 1e9
         traffic = None
         try:
-            with open(os.path.join(ROOT, "profiles", "roofline_traffic.json")) as f:
-                traffic = json.load(f).get("k_gemv_talker_b1_bytes_per_launch")
-        except Exception:
+            # DRAM bytes per algorithmic byte from the committed ncu capture of
+            # k_gemv (profiles/k_gemv_b1_2048x6144.md), scaled to this launch mix
+            with open(os.path.join(ROOT, "profiles", "k_gemv_b1_2048x6144.md")) as f:
+                m = re.search(r"dram_traffic_per_algorithmic_byte:\s*([0-9.]+)", f.read())
+            if m:
+                traffic = round(float(m.group(1)) * byts / n_launch)
+        except OSError:
             pass
         roof = {"bound": "hbm", "kernel": "k_gemv (talker Q4 GEMVs, batch 1, back-to-back)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -439,8 +446,33 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def profile_case_gemv():
+    """ncu case: the isolated batch-1 Q4 GEMV on the talker gate/up shape
+    (in 2048 x out 6144, 7.08 MB of Q4 weights).  24 weight copies (170 MB >
+    126 MB L2) are swept twice without a graph; capture launches 25.. (second
+    sweep), whose weights have left L2."""
+    import torch
+    import qora_b200 as qb
+    from qora_b200 import engine as E
+    torch.cuda.set_device(0)
+    ctx = E.Context(0)
+    w = qb.synth_q4(4242 + 2048 + 6144, 0.02, 2048, 6144)
+    devs = [E.DeviceQ4(ctx, w) for _ in range(24)]
+    x = torch.randn(1, 2048, device="cuda")
+    y = torch.empty(1, 6144, device="cuda")
+    for _ in range(2):
+        for d in devs:
+            d.gemv(x, y)
+    torch.cuda.synchronize()
+    ctx.check_device_error()
+    print(json.dumps({"profile_case": "gemv", "launches": 2 * len(devs), "k": 2048, "n": 6144}))
+
+
 def main():
     args = parse()
+    if args.profile_case == "gemv":
+        profile_case_gemv()
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
