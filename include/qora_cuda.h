@@ -149,6 +149,22 @@ int qora_kv_layer_ptrs(qora_kv *kv, int32_t layer, float **k, float **v, int32_t
 /* Copy one layer's K and V slabs (all streams, [stream][kv_head][max_pos][head_dim])
  * into caller device buffers (KV snapshot of the reference's RawKvCache). */
 int qora_kv_export_layer(qora_kv *kv, int32_t layer, float *k_out, float *v_out, void *stream);
+/* KV-cache append + attend of one decoder layer for streams 0..B-1, T = 1
+ * (the attention block of the decode step, talker.rs:285-331 and
+ * code_predictor.rs:461-498; apply_qk_norm talker.rs:89-99; split RoPE
+ * rope.rs:79-92).  qkv [B][(num_heads + 2*kv_heads)*head_dim]: the raw q | k | v
+ * projections of this layer (read only).  q and k get the per-head RMS norm
+ * (q_norm / k_norm: f16 [head_dim]) and RoPE at positions[b] (int32 [B]) from
+ * rope_cos / rope_sin ([rope_max_pos][head_dim/2] f32); k and v are written at
+ * the stream's cache length; out [B][num_heads*head_dim] = softmax(q.k /
+ * sqrt(head_dim)) . v over length+1 positions.  advance != 0 adds one to each
+ * stream's length afterwards (the cache has one length per stream for all
+ * layers: advance once per step, on the last layer).  num_heads / kv_heads is
+ * 1, 2 or 4.  The first call on a cache allocates its split-merge scratch. */
+int qora_kv_attend(qora_kv *kv, int32_t layer, const float *qkv, int32_t num_heads,
+                   const uint16_t *q_norm, const uint16_t *k_norm, const float *rope_cos,
+                   const float *rope_sin, int32_t rope_max_pos, const int32_t *positions,
+                   int32_t B, int32_t advance, float *out, void *stream);
 
 /* ------------------------------------------------------------ talker.rs */
 int qora_talker_create(qora_ctx *ctx, const qora_talker_host *host, int32_t max_batch,

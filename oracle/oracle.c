@@ -522,6 +522,36 @@ static void attend_one(const float *q, const float *kc, const float *vc, int64_t
     }
 }
 
+/* The attention block of one decode step of one layer, from the raw q / k / v
+ * projections (talker.rs:285-331; code_predictor.rs:461-498): qk-norm
+ * (talker.rs:89-99), split RoPE at `position` (rope.rs:79-92), append k / v
+ * at the layer's cache length, attend over length + 1 positions.  q / k / v
+ * are not modified; returns -1 past the cache, -2 past the RoPE table. */
+int oq_attend_step(const float *q_raw, const float *k_raw, const float *v_raw, int32_t heads,
+                   int32_t kv_heads, int32_t hd, const uint16_t *q_norm, const uint16_t *k_norm,
+                   const float *rope_cos, const float *rope_sin, int64_t rope_len,
+                   int64_t position, oq_kv *kv, int32_t layer, float *out) {
+    int32_t qd = heads * hd, kd = kv_heads * hd;
+    int64_t offset = kv->len[layer];
+    if (offset + 1 > kv->max_pos) return -1;
+    if ((position + 1) * (int64_t)(hd / 2) > rope_len) return -2;
+    float *q = (float *)malloc(sizeof(float) * (size_t)qd);
+    float *kn = (float *)malloc(sizeof(float) * (size_t)kd);
+    float *scores = (float *)malloc(sizeof(float) * (size_t)(offset + 1));
+    memcpy(q, q_raw, sizeof(float) * (size_t)qd);
+    memcpy(kn, k_raw, sizeof(float) * (size_t)kd);
+    oq_qk_norm(q, heads, hd, q_norm);
+    oq_qk_norm(kn, kv_heads, hd, k_norm);
+    oq_apply_rope_split(q, heads, hd, position, rope_cos, rope_sin, rope_len);
+    oq_apply_rope_split(kn, kv_heads, hd, position, rope_cos, rope_sin, rope_len);
+    memcpy(kv->k[layer] + offset * kd, kn, sizeof(float) * (size_t)kd);
+    memcpy(kv->v[layer] + offset * kd, v_raw, sizeof(float) * (size_t)kd);
+    kv->len[layer] = (int32_t)(offset + 1);
+    attend_one(q, kv->k[layer], kv->v[layer], offset + 1, heads, kv_heads, hd, out, scores);
+    free(q); free(kn); free(scores);
+    return 0;
+}
+
 typedef struct {
     int32_t hidden, heads, kv_heads, hd, ffn;
     const float *rope_cos, *rope_sin;

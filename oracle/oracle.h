@@ -123,6 +123,13 @@ float *oq_kv_k(oq_kv *kv, int32_t layer);
 float *oq_kv_v(oq_kv *kv, int32_t layer);
 int oq_kv_copy(oq_kv *dst, const oq_kv *src);
 
+/* Attention block of one decode step of one layer from raw q/k/v projections
+ * (talker.rs:285-331): qk-norm, split RoPE at `position`, append, attend. */
+int oq_attend_step(const float *q_raw, const float *k_raw, const float *v_raw, int32_t heads,
+                   int32_t kv_heads, int32_t hd, const uint16_t *q_norm, const uint16_t *k_norm,
+                   const float *rope_cos, const float *rope_sin, int64_t rope_len,
+                   int64_t position, oq_kv *kv, int32_t layer, float *out);
+
 /* ---- talker.rs ----------------------------------------------------------- */
 /* forward_with_embedding (talker.rs:263-360): out_hidden[hidden], out_logits[vocab]. */
 int oq_talker_step(const oq_talker *t, const float *embedding, oq_kv *kv, int64_t position,

@@ -101,6 +101,8 @@ def lib():
             "oq_kv_v": (vp, [vp, i32]),
             "oq_kv_copy": (C.c_int, [vp, vp]),
             "oq_talker_step": (C.c_int, [vp, vp, vp, i64, vp, vp]),
+            "oq_attend_step": (C.c_int, [vp, vp, vp, i32, i32, i32, vp, vp, vp, vp, i64, i64, vp,
+                                         i32, vp]),
             "oq_talker_prefill": (C.c_int, [vp, vp, i64, vp, i64, vp]),
             "oq_codec_head": (None, [vp, vp, vp]),
             "oq_embed_codec_token": (None, [vp, C.c_uint32, vp]),
@@ -547,6 +549,18 @@ def sample_probs(logits, params: SampleParams, prev, temperature=None):
     t = params.temperature if temperature is None else temperature
     lib().oq_sample_probs(ptr(logits), logits.size, C.byref(params), ptr(prev), prev.size, t,
                           ptr(out))
+    return out
+
+
+def attend_step(kv: "KV", layer: int, q, k, v, heads: int, kv_heads: int, hd: int, q_norm, k_norm,
+                rope_cos, rope_sin, position: int):
+    """Attention block of one decode step of one layer (talker.rs:285-331)."""
+    q, k, v = (np.ascontiguousarray(a, np.float32) for a in (q, k, v))
+    out = np.zeros(heads * hd, np.float32)
+    rc = lib().oq_attend_step(ptr(q), ptr(k), ptr(v), heads, kv_heads, hd, ptr(q_norm), ptr(k_norm),
+                              ptr(rope_cos), ptr(rope_sin), rope_cos.size, position, kv.h, layer,
+                              ptr(out))
+    assert rc == 0, rc
     return out
 
 

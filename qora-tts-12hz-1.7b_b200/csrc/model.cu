@@ -20,6 +20,7 @@
 
 #include "attention.cuh"
 #include "gemv.cuh"
+#include "kv.cuh"
 #include "sampler.cuh"
 
 namespace qora {
@@ -126,25 +127,6 @@ struct Work {
 }  // namespace qora
 
 using namespace qora;
-
-// ------------------------------------------------------------------------- KV
-struct qora_kv {
-    qora_ctx *ctx = nullptr;
-    int layers = 0, kvh = 0, hd = 0, max_pos = 0, streams = 0;
-    DevBuf k, v, len;
-    size_t layer_elems() const { return (size_t)streams * kvh * max_pos * hd; }
-    KVLayer layer(int l, int stream0 = 0) const {
-        KVLayer L;
-        const size_t off = (size_t)l * layer_elems() + (size_t)stream0 * kvh * max_pos * hd;
-        L.k = k.as<float>() + off;
-        L.v = v.as<float>() + off;
-        L.kv_heads = kvh;
-        L.head_dim = hd;
-        L.max_pos = max_pos;
-        return L;
-    }
-    int *lens() const { return len.as<int>(); }
-};
 
 // --------------------------------------------------------------------- talker
 struct qora_talker {

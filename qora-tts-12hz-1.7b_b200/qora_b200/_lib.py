@@ -82,6 +82,8 @@ SIGNATURES = {
     "qora_kv_copy_stream": (C.c_int, [_vp, _i32, _vp, _i32, _vp]),
     "qora_kv_layer_ptrs": (C.c_int, [_vp, _i32, _PP, _PP, _PP]),
     "qora_kv_export_layer": (C.c_int, [_vp, _i32, _vp, _vp, _vp]),
+    "qora_kv_attend": (C.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32,
+                                  _vp, _vp]),
     "qora_talker_create": (C.c_int, [_vp, _vp, _i32, _PP]),
     "qora_talker_destroy": (None, [_vp]),
     "qora_talker_step": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),

@@ -149,6 +149,22 @@ class KvCache:
         _lib.call("qora_kv_export_layer", self.h, layer, _dp(k), _dp(v), _stream(stream))
         return k, v
 
+    def attend(self, layer: int, qkv: torch.Tensor, num_heads: int, q_norm: torch.Tensor,
+               k_norm: torch.Tensor, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
+               positions: torch.Tensor, advance: bool = False, out: torch.Tensor | None = None,
+               stream=None) -> torch.Tensor:
+        """KV append + attend of one layer (talker.rs:285-331): qkv [B][q|k|v] raw
+        projections; q_norm / k_norm f16 bits as int16 tensors; rope tables
+        [max_pos * head_dim/2] f32; positions int32 [B].  Returns [B][num_heads*head_dim]."""
+        B = qkv.shape[0]
+        out = out if out is not None else torch.empty(B, num_heads * self.head_dim,
+                                                      device=qkv.device)
+        rope_max_pos = rope_cos.numel() // (self.head_dim // 2)
+        _lib.call("qora_kv_attend", self.h, layer, _dp(qkv), num_heads, _dp(q_norm), _dp(k_norm),
+                  _dp(rope_cos), _dp(rope_sin), rope_max_pos, _dp(positions), B,
+                  1 if advance else 0, _dp(out), _stream(stream))
+        return out
+
 
 class Talker:
     """TalkerWeights on the device (talker.rs)."""

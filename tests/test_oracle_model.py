@@ -104,3 +104,34 @@ def test_frame_loop_runs(orc, tiny):
         assert np.array_equal(st["prev"], codes)
         seen.append(codes)
     assert tkv.len(0) == 7
+
+
+def test_attend_step_matches_numpy(orc):
+    """oq_attend_step (the attention block, talker.rs:285-331) vs the float64
+    numpy restatement over a growing cache."""
+    import np_ref
+    heads, kvh, hd, steps = 4, 2, 64, 9
+    rng = np.random.default_rng(3)
+    qn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float16).view(np.uint16)
+    kn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float16).view(np.uint16)
+    cos, sin = orc.rope_tables(hd, 64, 1e6)
+    kv = orc.KV(1, kvh, hd, 16)
+    K, V = [], []
+    for s in range(steps):
+        q = rng.standard_normal(heads * hd).astype(np.float32)
+        k = rng.standard_normal(kvh * hd).astype(np.float32)
+        v = rng.standard_normal(kvh * hd).astype(np.float32)
+        pos = 5 + 2 * s
+        got = orc.attend_step(kv, 0, q, k, v, heads, kvh, hd, qn, kn, cos, sin, pos)
+        qr = np_ref.rope(np_ref.qknorm(q.astype(np.float64), heads, hd, qn), heads, hd, pos)
+        kr = np_ref.rope(np_ref.qknorm(k.astype(np.float64), kvh, hd, kn), kvh, hd, pos)
+        K.append(kr.reshape(kvh, hd))
+        V.append(v.astype(np.float64).reshape(kvh, hd))
+        Ks, Vs = np.stack(K), np.stack(V)
+        ref = np.zeros(heads * hd)
+        for h in range(heads):
+            sc = Ks[:, h // (heads // kvh)] @ qr[h * hd:(h + 1) * hd] / np.sqrt(hd)
+            p = np.exp(sc - sc.max())
+            ref[h * hd:(h + 1) * hd] = (p / p.sum()) @ Vs[:, h // (heads // kvh)]
+        assert np.max(np.abs(got - ref)) < 1e-5
+    assert kv.len(0) == steps
