@@ -165,6 +165,22 @@ int qora_kv_attend(qora_kv *kv, int32_t layer, const float *qkv, int32_t num_hea
                    const uint16_t *q_norm, const uint16_t *k_norm, const float *rope_cos,
                    const float *rope_sin, int32_t rope_max_pos, const int32_t *positions,
                    int32_t B, int32_t advance, float *out, void *stream);
+/* No counterpart in the reference (its CPU path allocates freely).  Same
+ * arguments and results as qora_kv_attend, but allocates no device memory:
+ * for callers that cannot let a library call cudaMalloc, such as a real-time
+ * audio loop that must not stall on an allocation, or an application whose
+ * own memory manager already holds the GPU's memory.  The split-merge scratch
+ * is a fixed ~1.1 MB array in the library's static device memory, present on
+ * every GPU that loads the library until the process exits.  Limit:
+ * B * num_heads * head_dim <= 16384 (the talker's 16 x 128 heads: B <= 8) and
+ * B * kv_heads <= 512; larger calls return QORA_ERR_UNSUPPORTED.  The first
+ * call on each device looks up the array's device address (make that first
+ * call before any stream capture).  All calls share the array: calls that
+ * overlap on the GPU race, so issue them on one stream. */
+int qora_kv_attend_noalloc(qora_kv *kv, int32_t layer, const float *qkv, int32_t num_heads,
+                           const uint16_t *q_norm, const uint16_t *k_norm, const float *rope_cos,
+                           const float *rope_sin, int32_t rope_max_pos, const int32_t *positions,
+                           int32_t B, int32_t advance, float *out, void *stream);
 
 /* ------------------------------------------------------------ talker.rs */
 int qora_talker_create(qora_ctx *ctx, const qora_talker_host *host, int32_t max_batch,

@@ -84,6 +84,8 @@ SIGNATURES = {
     "qora_kv_export_layer": (C.c_int, [_vp, _i32, _vp, _vp, _vp]),
     "qora_kv_attend": (C.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32, _i32,
                                   _vp, _vp]),
+    "qora_kv_attend_noalloc": (C.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
+                                          _i32, _vp, _vp]),
     "qora_talker_create": (C.c_int, [_vp, _vp, _i32, _PP]),
     "qora_talker_destroy": (None, [_vp]),
     "qora_talker_step": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),

@@ -152,15 +152,18 @@ class KvCache:
     def attend(self, layer: int, qkv: torch.Tensor, num_heads: int, q_norm: torch.Tensor,
                k_norm: torch.Tensor, rope_cos: torch.Tensor, rope_sin: torch.Tensor,
                positions: torch.Tensor, advance: bool = False, out: torch.Tensor | None = None,
-               stream=None) -> torch.Tensor:
+               stream=None, noalloc: bool = False) -> torch.Tensor:
         """KV append + attend of one layer (talker.rs:285-331): qkv [B][q|k|v] raw
         projections; q_norm / k_norm f16 bits as int16 tensors; rope tables
-        [max_pos * head_dim/2] f32; positions int32 [B].  Returns [B][num_heads*head_dim]."""
+        [max_pos * head_dim/2] f32; positions int32 [B].  Returns [B][num_heads*head_dim].
+        noalloc: use qora_kv_attend_noalloc, which allocates no device memory
+        (its scratch is a fixed static array; B * num_heads * head_dim <= 16384)."""
         B = qkv.shape[0]
         out = out if out is not None else torch.empty(B, num_heads * self.head_dim,
                                                       device=qkv.device)
         rope_max_pos = rope_cos.numel() // (self.head_dim // 2)
-        _lib.call("qora_kv_attend", self.h, layer, _dp(qkv), num_heads, _dp(q_norm), _dp(k_norm),
+        entry = "qora_kv_attend_noalloc" if noalloc else "qora_kv_attend"
+        _lib.call(entry, self.h, layer, _dp(qkv), num_heads, _dp(q_norm), _dp(k_norm),
                   _dp(rope_cos), _dp(rope_sin), rope_max_pos, _dp(positions), B,
                   1 if advance else 0, _dp(out), _stream(stream))
         return out
