@@ -24,6 +24,8 @@ struct AttnArgs {
     int rope_max_pos = 0;
     const int *pos = nullptr;       // RoPE position of token 0 per stream; NULL => cache length
     const int *len = nullptr;       // cache length per stream before this call
+    int pos_static = -1;            // >= 0: RoPE position of token 0 for every stream (overrides pos)
+    int len_static = -1;            // >= 0: cache length for every stream (overrides len)
     KVLayer kv;
     bool preappended = false;       // q/k already normed+roped and K/V appended
     float *out = nullptr;           // [rows][heads*hd]

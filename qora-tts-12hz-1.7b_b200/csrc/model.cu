@@ -21,6 +21,7 @@
 #include "attention.cuh"
 #include "gemv.cuh"
 #include "kv.cuh"
+#include "model.cuh"
 #include "sampler.cuh"
 
 namespace qora {
@@ -57,92 +58,48 @@ int upload_f16(const uint16_t *h, int64_t n, DevBuf &buf) {
 }  // namespace
 
 // --------------------------------------------------------------------- layers
-struct LayerDev {
-    DevBuf qkv_nib, qkv_scl, o_nib, o_scl, gu_nib, gu_scl, dn_nib, dn_scl;
-    Q4Dev qkv, o, gu, dn;
-    DevBuf q_norm, k_norm, in_norm, post_norm;
-
-    int upload(const qora_layer_host &h, int64_t hidden, int heads, int kvh, int hd, int64_t ffn) {
-        const int64_t qd = (int64_t)heads * hd, kd = (int64_t)kvh * hd;
-        if (h.q_proj.k != hidden || h.q_proj.n != qd || h.k_proj.n != kd || h.v_proj.n != kd ||
-            h.o_proj.k != qd || h.o_proj.n != hidden || h.gate_proj.n != ffn ||
-            h.up_proj.n != ffn || h.down_proj.k != ffn || h.down_proj.n != hidden)
-            return set_error(QORA_ERR_SHAPE, "layer weight shapes do not match the config");
-        {   // fused [q | k | v]
-            const qora_q4_host parts[3] = {h.q_proj, h.k_proj, h.v_proj};
-            const int64_t offs[3] = {0, qd / kGroup, (qd + kd) / kGroup};
-            const int64_t strides[3] = {1, 1, 1};
-            QORA_TRY(upload_q4_parts(parts, offs, strides, 3, hidden, (qd + 2 * kd) / kGroup,
-                                     qkv_nib, qkv_scl, qkv, nullptr));
-        }
-        {
-            const int64_t off = 0, st = 1;
-            QORA_TRY(upload_q4_parts(&h.o_proj, &off, &st, 1, qd, hidden / kGroup, o_nib, o_scl, o,
-                                     nullptr));
-            QORA_TRY(upload_q4_parts(&h.down_proj, &off, &st, 1, ffn, hidden / kGroup, dn_nib,
-                                     dn_scl, dn, nullptr));
-        }
-        {   // gate/up interleaved by 32-column group: g0 u0 g1 u1 ...
-            const qora_q4_host parts[2] = {h.gate_proj, h.up_proj};
-            const int64_t offs[2] = {0, 1};
-            const int64_t strides[2] = {2, 2};
-            QORA_TRY(upload_q4_parts(parts, offs, strides, 2, hidden, 2 * ffn / kGroup, gu_nib,
-                                     gu_scl, gu, nullptr));
-        }
-        QORA_TRY(upload_f16(h.q_norm, hd, q_norm));
-        QORA_TRY(upload_f16(h.k_norm, hd, k_norm));
-        QORA_TRY(upload_f16(h.input_norm, hidden, in_norm));
-        QORA_TRY(upload_f16(h.post_attn_norm, hidden, post_norm));
-        return QORA_OK;
+int LayerDev::upload(const qora_layer_host &h, int64_t hidden, int heads, int kvh, int hd,
+                     int64_t ffn) {
+    const int64_t qd = (int64_t)heads * hd, kd = (int64_t)kvh * hd;
+    if (h.q_proj.k != hidden || h.q_proj.n != qd || h.k_proj.n != kd || h.v_proj.n != kd ||
+        h.o_proj.k != qd || h.o_proj.n != hidden || h.gate_proj.n != ffn ||
+        h.up_proj.n != ffn || h.down_proj.k != ffn || h.down_proj.n != hidden)
+        return set_error(QORA_ERR_SHAPE, "layer weight shapes do not match the config");
+    {   // fused [q | k | v]
+        const qora_q4_host parts[3] = {h.q_proj, h.k_proj, h.v_proj};
+        const int64_t offs[3] = {0, qd / kGroup, (qd + kd) / kGroup};
+        const int64_t strides[3] = {1, 1, 1};
+        QORA_TRY(upload_q4_parts(parts, offs, strides, 3, hidden, (qd + 2 * kd) / kGroup,
+                                 qkv_nib, qkv_scl, qkv, nullptr));
     }
-};
+    {
+        const int64_t off = 0, st = 1;
+        QORA_TRY(upload_q4_parts(&h.o_proj, &off, &st, 1, qd, hidden / kGroup, o_nib, o_scl, o,
+                                 nullptr));
+        QORA_TRY(upload_q4_parts(&h.down_proj, &off, &st, 1, ffn, hidden / kGroup, dn_nib,
+                                 dn_scl, dn, nullptr));
+    }
+    {   // gate/up interleaved by 32-column group: g0 u0 g1 u1 ...
+        const qora_q4_host parts[2] = {h.gate_proj, h.up_proj};
+        const int64_t offs[2] = {0, 1};
+        const int64_t strides[2] = {2, 2};
+        QORA_TRY(upload_q4_parts(parts, offs, strides, 2, hidden, 2 * ffn / kGroup, gu_nib,
+                                 gu_scl, gu, nullptr));
+    }
+    QORA_TRY(upload_f16(h.q_norm, hd, q_norm));
+    QORA_TRY(upload_f16(h.k_norm, hd, k_norm));
+    QORA_TRY(upload_f16(h.input_norm, hidden, in_norm));
+    QORA_TRY(upload_f16(h.post_attn_norm, hidden, post_norm));
+    return QORA_OK;
+}
 
 // Activation and scratch buffers sized for `rows` rows.
-struct Work {
-    DevBuf x, ss, qkv, attn, h, logits, gticket, tbest_v, tbest_i, apo, apml, atk;
-    int rows = 0;
-
-    int alloc(int rows_, int64_t hidden, int64_t qkvn, int64_t qd, int64_t ffn, int64_t vocab,
-              int kvh, int heads, int hd) {
-        rows = rows_;
-        QORA_TRY(x.alloc((size_t)rows * hidden * 4));
-        QORA_TRY(ss.alloc((size_t)rows * (hidden / kGroup) * 4));
-        QORA_TRY(qkv.alloc((size_t)rows * qkvn * 4));
-        QORA_TRY(attn.alloc((size_t)rows * qd * 4));
-        QORA_TRY(h.alloc((size_t)rows * ffn * 4));
-        QORA_TRY(logits.alloc((size_t)rows * vocab * 4));
-        QORA_TRY(gticket.alloc(64));
-        QORA_TRY(gticket.zero());
-        QORA_TRY(tbest_v.alloc((size_t)rows * (vocab / kGroup + 1) * 4));
-        QORA_TRY(tbest_i.alloc((size_t)rows * (vocab / kGroup + 1) * 4));
-        QORA_TRY(apo.alloc(attn_part_o_floats(rows, kvh, heads, hd) * 4));
-        QORA_TRY(apml.alloc(attn_part_ml_floats(rows, kvh, heads) * 4));
-        QORA_TRY(atk.alloc((size_t)rows * kvh * 4));
-        QORA_TRY(atk.zero());
-        QORA_CUDA(cudaDeviceSynchronize());
-        return QORA_OK;
-    }
-};
 
 }  // namespace qora
 
 using namespace qora;
 
 // --------------------------------------------------------------------- talker
-struct qora_talker {
-    qora_ctx *ctx = nullptr;
-    int L = 0, H = 0, heads = 0, kvh = 0, hd = 0, ffn = 0, vocab = 0, rope_max = 0;
-    std::vector<LayerDev> layers;
-    DevBuf ce_packed, ce_scl, head_nib, head_scl, final_norm, rope_cos, rope_sin;
-    EmbDev codec_emb;
-    Q4Dev head;
-    int max_batch = 0;
-    Work w;
-
-    int64_t qd() const { return (int64_t)heads * hd; }
-    int64_t kd() const { return (int64_t)kvh * hd; }
-    int64_t qkvn() const { return qd() + 2 * kd(); }
-};
 
 namespace qora {
 
@@ -288,23 +245,6 @@ static int talker_forward_step(qora_talker *t, qora_kv *kv, Launcher &ln, int B,
 }  // namespace qora
 
 // ------------------------------------------------------------------ predictor
-struct qora_predictor {
-    qora_ctx *ctx = nullptr;
-    int L = 0, H = 0, heads = 0, kvh = 0, hd = 0, ffn = 0, vocab = 0, groups = 0, rope_max = 0;
-    int64_t Ht = 0;  // talker hidden (input / embedding width)
-    std::vector<LayerDev> layers;
-    bool has_proj = false;
-    DevBuf proj_nib, proj_scl, proj_bias, final_norm, rope_cos, rope_sin;
-    Q4Dev proj;
-    std::vector<DevBuf> emb_packed, emb_scl, head_nib, head_scl;
-    std::vector<EmbDev> embs;
-    std::vector<Q4Dev> heads_w;
-    int max_batch = 0;
-    Work w;
-    DevBuf x2;     // [rows][2][Ht]: talker hidden | semantic embedding
-    DevBuf codes;  // [rows][groups] internal code buffer
-    DevBuf xe;     // identity-projection staging [rows][Ht]
-};
 
 namespace qora {
 
@@ -403,21 +343,6 @@ static int predictor_frame_impl(qora_predictor *p, qora_kv *kv, Launcher &ln, in
 }  // namespace qora
 
 // --------------------------------------------------------------------- engine
-struct qora_engine {
-    qora_talker *t = nullptr;
-    qora_predictor *p = nullptr;
-    int B = 0, max_pos = 0;
-    qora_sample_params params{};
-    qora_kv *tkv = nullptr, *pkv = nullptr;
-    DevBuf logits, codes, prev, rng, pos, text;
-    bool use_graph = false;
-    cudaGraph_t graph = nullptr;
-    cudaGraphExec_t exec = nullptr;
-    const float *graph_text = nullptr;
-    uint32_t *graph_codes = nullptr;
-    int kernels = kEngineKernelsUnknown;
-    cudaStream_t cap_stream = nullptr;
-};
 
 // =========================================================================
 // extern "C" entry points
