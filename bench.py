@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
-    ap.add_argument("--profile-case", default=None, choices=["gemv"],
+    ap.add_argument("--profile-case", default=None, choices=["gemv", "frame_trace"],
                     help="small fixed workload for an ncu capture instead of the bench")
     return ap.parse_args()
 
@@ -468,10 +468,60 @@ def profile_case_gemv():
     print(json.dumps({"profile_case": "gemv", "launches": 2 * len(devs), "k": 2048, "n": 6144}))
 
 
+def profile_case_frame_trace():
+    """Per-op stamps of the persistent frame kernel (batch 1, 1.7B dims, 64-token
+    prefill): one JSON line with the phase split of a frame.  Phases per op, on
+    the SM running the op's first item: wait (previous op's signal -> this op's
+    dependency met), input (input vector built), items (GEMV / attention /
+    sampler work), signal (completion counter)."""
+    import torch
+    import qora_b200 as qb
+    from qora_b200 import engine as E
+    torch.cuda.set_device(0)
+    cfg = qb.ModelConfig()
+    ctx = E.Context(0)
+    talker = E.Talker(ctx, qb.synth_talker(cfg), max_batch=1)
+    pred = E.CodePredictor(ctx, qb.synth_predictor(cfg), max_batch=1)
+    eng = E.Engine(talker, pred, 1, PREFILL + 16)
+    x = qb.synth_normal(1000, 1.0, PREFILL * cfg.t_hidden).reshape(1, PREFILL, cfg.t_hidden)
+    eng.prefill(x, [1000])
+    text = torch.from_numpy(qb.synth_normal(77, 1.0, cfg.t_hidden).reshape(1, cfg.t_hidden)).cuda()
+    codes = torch.zeros(1, 16, dtype=torch.int32, device="cuda")
+    for _ in range(3):
+        eng.frame(text, codes)
+    eng.trace(True)
+    for _ in range(2):
+        eng.frame(text, codes)
+    ops, st = eng.trace(False)
+    ctx.check_device_error()
+    st = st.astype(np.int64)
+    n = len(ops)
+    wait = np.r_[0, st[1:, 0] - st[:-1, 3]]
+    phases = {"wait": wait, "input": st[:, 1] - st[:, 0], "items": st[:, 2] - st[:, 1],
+              "signal": st[:, 3] - st[:, 2]}
+    total = int(st[-1, 3] - st[0, 0])
+    names = {0: "gemv", 1: "attention", 2: "sampler"}
+    by_type = {}
+    for t, nm in names.items():
+        m = ops == t
+        if m.any():
+            by_type[nm] = {"ops": int(m.sum()),
+                           **{k: round(float(v[m].mean()) / 1000.0, 3) for k, v in phases.items()}}
+    # the talker part: ops after the last predictor head
+    print(json.dumps({"profile_case": "frame_trace", "ops": n, "frame_us": round(total / 1000.0, 1),
+                      "us_per_op": round(total / n / 1000.0, 3),
+                      "phase_share": {k: round(float(v.sum()) / total, 3) for k, v in phases.items()},
+                      "mean_us_by_type": by_type,
+                      "talker_us": round(float(st[-1, 3] - st[n - 5 * cfg.t_layers - 1, 0]) / 1000.0, 1)}))
+
+
 def main():
     args = parse()
     if args.profile_case == "gemv":
         profile_case_gemv()
+        return
+    if args.profile_case == "frame_trace":
+        profile_case_frame_trace()
         return
     if args.impl == "reference":
         run_reference(args)

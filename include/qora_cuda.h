@@ -246,6 +246,21 @@ int qora_engine_frame_host(qora_engine *e, const float *text_host, uint32_t *cod
                            void *stream);
 /* Capture one frame into a CUDA graph (enable=1) and replay it per frame. */
 int qora_engine_use_graph(qora_engine *e, int32_t enable);
+/* Run each frame as ONE launch of the persistent frame kernel (enable = 1, the
+ * default where supported) or as the sequence of per-op kernels (enable = 0).
+ * The persistent kernel needs B = 1, an input projection, head_dim 64 or 128,
+ * heads / kv_heads of 1, 2 or 4, widths <= 6144 and vocab <= 4096;
+ * QORA_ERR_UNSUPPORTED otherwise (the per-op path then stays in use). */
+int qora_engine_use_persistent(qora_engine *e, int32_t enable);
+/* Per-op timing of the persistent frame kernel (a profiling aid, no
+ * reference counterpart).  enable != 0 makes later frames record, for each op,
+ * four globaltimer stamps (ns) taken on the SM that runs the op's first item:
+ * dependency met, input built, items done, completion signalled.  With
+ * ops_host / stamps_host non-NULL it first copies the last recorded frame:
+ * op types (0 GEMV, 1 attention, 2 sampler) into ops_host[capacity] and the
+ * stamps into stamps_host[capacity][4].  *n_ops receives the op count. */
+int qora_engine_trace(qora_engine *e, int32_t enable, int32_t capacity, int32_t *n_ops,
+                      int32_t *ops_host, uint64_t *stamps_host);
 /* Number of kernels one frame launches (for launch accounting). */
 int qora_engine_kernels_per_frame(qora_engine *e, int32_t *count);
 /* Device pointers of the engine state: logits [B][vocab], hidden [B][hidden],

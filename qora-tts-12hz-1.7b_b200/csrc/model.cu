@@ -21,6 +21,7 @@
 #include "attention.cuh"
 #include "gemv.cuh"
 #include "kv.cuh"
+#include "frame.cuh"
 #include "model.cuh"
 #include "sampler.cuh"
 
@@ -728,6 +729,7 @@ int qora_engine_create(qora_talker *t, qora_predictor *p, int32_t B, int32_t max
 
 void qora_engine_destroy(qora_engine *e) {
     if (!e) return;
+    frame_program_destroy(e->frame);
     if (e->exec) cudaGraphExecDestroy(e->exec);
     if (e->graph) cudaGraphDestroy(e->graph);
     qora_kv_destroy(e->tkv);
@@ -855,6 +857,15 @@ int engine_frame_kernels(qora_engine *e, const float *text, uint32_t *codes_out,
 int qora_engine_frame(qora_engine *e, const float *text, uint32_t *codes, void *stream) {
     if (!e || !text) return set_error(QORA_ERR_INVALID, "qora_engine_frame: bad arguments");
     cudaStream_t st = as_stream(stream);
+    if (e->persistent && frame_supported(e)) {
+        // one launch for the whole frame (frame.cu)
+        if (!e->frame) QORA_TRY(frame_build(e, &e->frame));
+        QORA_TRY(frame_launch(e->frame, text, st));
+        if (codes && codes != e->codes.as<uint32_t>())
+            QORA_CUDA(cudaMemcpyAsync(codes, e->codes.p, (size_t)e->B * 16 * 4, cudaMemcpyDeviceToDevice, st));
+        e->kernels = 1;
+        return QORA_OK;
+    }
     if (!e->use_graph) {
         int n = 0;
         QORA_TRY(engine_frame_kernels(e, text, codes, st, &n));
@@ -908,6 +919,39 @@ int qora_engine_frame_host(qora_engine *e, const float *text_host, uint32_t *cod
 int qora_engine_use_graph(qora_engine *e, int32_t enable) {
     if (!e) return set_error(QORA_ERR_INVALID, "null engine");
     e->use_graph = enable != 0;
+    return QORA_OK;
+}
+
+int qora_engine_use_persistent(qora_engine *e, int32_t enable) {
+    if (!e) return set_error(QORA_ERR_INVALID, "null engine");
+    if (enable && !frame_supported(e))
+        return set_error(QORA_ERR_UNSUPPORTED,
+                         "persistent frame kernel: needs batch 1, an input projection, head_dim 64/128, "
+                         "heads/kv_heads 1/2/4, widths <= 6144 and vocab <= 4096");
+    e->persistent = enable != 0;
+    return QORA_OK;
+}
+
+int qora_engine_trace(qora_engine *e, int32_t enable, int32_t capacity, int32_t *n_ops,
+                      int32_t *ops_host, uint64_t *stamps_host) {
+    if (!e) return set_error(QORA_ERR_INVALID, "null engine");
+    if (!e->persistent || !frame_supported(e))
+        return set_error(QORA_ERR_UNSUPPORTED, "tracing needs the persistent frame kernel");
+    if (!e->frame) QORA_TRY(frame_build(e, &e->frame));
+    FrameProgram *fp = e->frame;
+    const int n = (int)fp->ops.size();
+    if (n_ops) *n_ops = n;
+    if (ops_host || stamps_host) {
+        if (capacity < n) return set_error(QORA_ERR_SHAPE, "trace capacity %d < %d ops", capacity, n);
+        if (ops_host)
+            for (int i = 0; i < n; i++) ops_host[i] = fp->ops[i].type;
+        if (stamps_host) {
+            QORA_CUDA(cudaDeviceSynchronize());
+            QORA_CUDA(cudaMemcpy(stamps_host, fp->d_trace.p, (size_t)n * fk::kTraceFields * 8,
+                                 cudaMemcpyDeviceToHost));
+        }
+    }
+    fp->trace = enable != 0;
     return QORA_OK;
 }
 

@@ -103,6 +103,8 @@ SIGNATURES = {
     "qora_engine_frame": (C.c_int, [_vp, _vp, _vp, _vp]),
     "qora_engine_frame_host": (C.c_int, [_vp, _vp, _vp, _vp]),
     "qora_engine_use_graph": (C.c_int, [_vp, _i32]),
+    "qora_engine_use_persistent": (C.c_int, [_vp, _i32]),
+    "qora_engine_trace": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "qora_engine_kernels_per_frame": (C.c_int, [_vp, C.POINTER(C.c_int32)]),
     "qora_engine_state": (C.c_int, [_vp, _PP, _PP, _PP, _PP, _PP]),
 }

@@ -319,6 +319,22 @@ class Engine:
         s = np.ascontiguousarray(np.asarray(seeds, np.uint64).reshape(self.B))
         _lib.call("qora_engine_prefill", self.h, x.ctypes.data, T, s.ctypes.data, _stream(stream))
 
+    def use_persistent(self, enable: bool = True):
+        """One persistent-kernel launch per frame (default where supported) or
+        the per-op kernel sequence."""
+        _lib.call("qora_engine_use_persistent", self.h, 1 if enable else 0)
+
+    def trace(self, enable: bool = True):
+        """Turns per-op stamps of the persistent frame kernel on/off and returns
+        the last recorded frame: (op types int32 [n], stamps uint64 [n][4] ns)."""
+        n = C.c_int32()
+        _lib.call("qora_engine_trace", self.h, 1 if enable else 0, 0, C.byref(n), None, None)
+        ops = np.zeros(n.value, np.int32)
+        st = np.zeros((n.value, 4), np.uint64)
+        _lib.call("qora_engine_trace", self.h, 1 if enable else 0, n.value, C.byref(n),
+                  ops.ctypes.data, st.ctypes.data)
+        return ops, st
+
     def use_graph(self, enable: bool = True):
         _lib.call("qora_engine_use_graph", self.h, 1 if enable else 0)
 
@@ -336,7 +352,28 @@ class Engine:
         _lib.call("qora_engine_kernels_per_frame", self.h, C.byref(n))
         return n.value
 
-    def state(self):
+    def state(self) -> dict:
+        """Copies of the device state (qora_engine_state): logits [B][vocab],
+        hidden [B][hidden] (the talker's final-normed output, the predictor's
+        next input), prev [B][16], rng [B], positions [B]."""
         ptrs = [C.c_void_p() for _ in range(5)]
         _lib.call("qora_engine_state", self.h, *[C.byref(p) for p in ptrs])
-        return [p.value for p in ptrs]
+        c, B = self.talker.cfg, self.B
+        hid = _device_view(ptrs[1].value, (B, 2, c.t_hidden), "<f4")[:, 0]
+        return {"logits": _device_view(ptrs[0].value, (B, c.t_vocab), "<f4").clone(),
+                "hidden": hid.clone(),
+                "prev": _device_view(ptrs[2].value, (B, 16), "<i4").clone(),
+                "rng": _device_view(ptrs[3].value, (B,), "<i8").clone(),
+                "positions": _device_view(ptrs[4].value, (B,), "<i4").clone()}
+
+
+class _CudaArray:
+    """A raw device pointer described by __cuda_array_interface__ (no copy)."""
+
+    def __init__(self, ptr: int, shape, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr,
+                                         "data": (ptr, False), "version": 3, "strides": None}
+
+
+def _device_view(ptr: int, shape, typestr: str) -> torch.Tensor:
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device="cuda")
