@@ -496,23 +496,30 @@ def profile_case_frame_trace():
     ctx.check_device_error()
     st = st.astype(np.int64)
     n = len(ops)
-    wait = np.r_[0, st[1:, 0] - st[:-1, 3]]
+    wait = np.r_[0, st[1:, 0] - st[:-1, 3]]  # slot_wait (col 4) is part of items
     phases = {"wait": wait, "input": st[:, 1] - st[:, 0], "items": st[:, 2] - st[:, 1],
-              "signal": st[:, 3] - st[:, 2]}
+              "signal": st[:, 3] - st[:, 2], "slot_wait": st[:, 4]}
     total = int(st[-1, 3] - st[0, 0])
-    names = {0: "gemv", 1: "attention", 2: "sampler"}
-    by_type = {}
-    for t, nm in names.items():
-        m = ops == t
-        if m.any():
-            by_type[nm] = {"ops": int(m.sum()),
-                           **{k: round(float(v[m].mean()) / 1000.0, 3) for k, v in phases.items()}}
-    # the talker part: ops after the last predictor head
+    # op labels in program order (frame.cu frame_build)
+    layer = ["qkv", "attn", "o", "gate_up", "down"]
+    labels = ["sample"]
+    for tk in range(cfg.p_groups + 1):
+        labels += ["p_proj"] + ["p_" + x for x in layer] * cfg.p_layers + (["p_head"] if tk else [])
+    labels += ["t_" + x for x in layer] * cfg.t_layers + ["t_head"]
+    assert len(labels) == n, (len(labels), n)
+    labels = np.array(labels)
+    by_label = {}
+    for lb in dict.fromkeys(labels.tolist()):
+        m = labels == lb
+        by_label[lb] = {"ops": int(m.sum()),
+                        **{k: round(float(v[m].mean()) / 1000.0, 3) for k, v in phases.items()}}
+    t0 = n - 5 * cfg.t_layers - 1
     print(json.dumps({"profile_case": "frame_trace", "ops": n, "frame_us": round(total / 1000.0, 1),
                       "us_per_op": round(total / n / 1000.0, 3),
-                      "phase_share": {k: round(float(v.sum()) / total, 3) for k, v in phases.items()},
-                      "mean_us_by_type": by_type,
-                      "talker_us": round(float(st[-1, 3] - st[n - 5 * cfg.t_layers - 1, 0]) / 1000.0, 1)}))
+                      "talker_us": round(float(st[-1, 3] - st[t0, 0]) / 1000.0, 1),
+                      "phase_share": {k: round(float(v.sum()) / total, 3) for k, v in phases.items()
+                                      if k != "slot_wait"},
+                      "mean_us_by_op": by_label}))
 
 
 def main():

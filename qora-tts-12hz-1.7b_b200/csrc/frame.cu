@@ -179,17 +179,32 @@ __device__ __forceinline__ float block_sum(float v, FrameSmem &S, int tid) {
     return t;
 }
 
-// Argmax of src[0..n); ties keep the larger index (the last maximum,
-// code_predictor.rs:336-339).  Identical on every SM.
+// Argmax of src[0..n) (n a multiple of 4, <= 4096); ties keep the larger
+// index (the last maximum, code_predictor.rs:336-339).  Identical on every SM.
 __device__ int block_argmax(const FrameParams &P, const float *src, int n, FrameSmem &S, int tid) {
+    constexpr int U = 4;  // float4s per thread: 4 * 4 * 256 = 4096
+    const float4 *s4 = reinterpret_cast<const float4 *>(src);
+    float4 v[U];
+#pragma unroll
+    for (int m = 0; m < U; m++) {
+        const int i = tid + m * kNT;
+        if (4 * i < n) v[m] = __ldcg(s4 + i);
+    }
     float bv = -INFINITY;
     int bi = -1;
-    for (int i = tid; i < n; i += kNT) {
-        const float v = __ldcg(src + i);
-        if (v != v) raise_error(P.err, kDevNaN);
-        if (bi < 0 || v > bv || (v == bv && i > bi)) {
-            bv = v;
-            bi = i;
+#pragma unroll
+    for (int m = 0; m < U; m++) {
+        const int i = tid + m * kNT;
+        if (4 * i < n) {
+            const float e[4] = {v[m].x, v[m].y, v[m].z, v[m].w};
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                if (e[c] != e[c]) raise_error(P.err, kDevNaN);
+                if (bi < 0 || e[c] > bv || (e[c] == bv && 4 * i + c > bi)) {
+                    bv = e[c];
+                    bi = 4 * i + c;
+                }
+            }
         }
     }
 #pragma unroll
@@ -206,14 +221,14 @@ __device__ int block_argmax(const FrameParams &P, const float *src, int n, Frame
         S.bidx[tid >> 5] = bi;
     }
     csync();
-    float v = -INFINITY;
+    float best = -INFINITY;
     int idx = -1;
 #pragma unroll
     for (int w = 0; w < kNT / 32; w++) {
         const int oi = S.bidx[w];
         const float ov = S.bred[w];
-        if (oi >= 0 && (idx < 0 || ov > v || (ov == v && oi > idx))) {
-            v = ov;
+        if (oi >= 0 && (idx < 0 || ov > best || (ov == best && oi > idx))) {
+            best = ov;
             idx = oi;
         }
     }
@@ -221,11 +236,21 @@ __device__ int block_argmax(const FrameParams &P, const float *src, int n, Frame
     return idx < 0 ? 0 : idx;
 }
 
-// embed_lookup_q4 (gemv.rs:425-433): scale * (q - 8) of column j of row `code`.
-__device__ __forceinline__ float emb_value(const EmbDev &e, uint32_t code, int64_t j) {
-    const uint8_t byte = e.packed[(int64_t)code * (e.n >> 1) + (j >> 1)];
-    const int q = (j & 1) ? (byte >> 4) : (byte & 15);
-    return __fmul_rn(__half2float(e.scl[(int64_t)code * (e.n >> 5) + (j >> 5)]), (float)(q - 8));
+// The 8 values of columns 8w..8w+7 of embedding row `code`: nibble word w
+// and its group scale, dequantised as embed_lookup_q4 (gemv.rs:425-433):
+// scale * (q - 8).
+struct EmbWord {
+    uint32_t w;
+    float sc;
+};
+__device__ __forceinline__ EmbWord emb_word(const EmbDev &e, uint32_t code, int w) {
+    EmbWord r;
+    r.w = __ldg(reinterpret_cast<const uint32_t *>(e.packed + (int64_t)code * (e.n >> 1)) + w);
+    r.sc = __half2float(e.scl[(int64_t)code * (e.n >> 5) + (w >> 2)]);
+    return r;
+}
+__device__ __forceinline__ float emb_at(const EmbWord &e, int c) {
+    return __fmul_rn(e.sc, (float)((int)((e.w >> (4 * c)) & 15u) - 8));
 }
 
 // Writes this SM's slice of x (the participating SMs partition [0, K)).
@@ -241,33 +266,62 @@ __device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &
                             bool leader, int j0, int n_items, int grid) {
     float *xs = S.u.xs;
     const int K = d.K;
-    float ss = 0.0f;  // sum of squares for the RMSNorm
     switch (d.in_mode) {
         case IN_VEC: {
-            // K is a multiple of 32: whole float4s, a thread's loads all in flight together
+            // x in 8-float chunks (K is a multiple of 32); every load of the
+            // thread (x, gamma, one sum-of-squares partial) in flight together
+            constexpr int U = kXMax / 8 / kNT;
             const float4 *src = reinterpret_cast<const float4 *>(d.in);
-            float4 *dst = reinterpret_cast<float4 *>(xs);
-            const int K4 = K >> 2;
-            constexpr int U = kXMax / 4 / kNT;
-            float4 v[U];
+            const uint4 *gm = reinterpret_cast<const uint4 *>(d.gamma);
+            const int K8 = K >> 3;
+            float4 v[U][2];
+            uint4 gv[U];
 #pragma unroll
             for (int m = 0; m < U; m++) {
-                const int i = tid + m * kNT;
-                if (i < K4) v[m] = __ldcg(src + i);
+                const int w = tid + m * kNT;
+                if (w < K8) {
+                    v[m][0] = __ldcg(src + 2 * w);
+                    v[m][1] = __ldcg(src + 2 * w + 1);
+                    if (d.gamma) gv[m] = __ldg(gm + w);
+                }
             }
+            const float ssp = (d.gamma && tid < (K >> 5)) ? __ldcg(d.ss_in + tid) : 0.0f;
+            float inv = 1.0f;
+            if (d.gamma) {
+                // the producer's per-32-column sums of squares (K / 32 <= kNT of
+                // them), summed by the fixed block tree: rms_norm_f16's
+                // inv = 1 / sqrt(sum(x^2) / K + 1e-6)
+                const float ssum = block_sum(ssp, S, tid);
+                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, (float)K), 1e-6f)));
+            }
+            const bool pre_save = d.save && !d.save_normed;
 #pragma unroll
             for (int m = 0; m < U; m++) {
-                const int i = tid + m * kNT;
-                if (i < K4) dst[i] = v[m];
+                const int w = tid + m * kNT;
+                if (w < K8) {
+                    float e[8] = {v[m][0].x, v[m][0].y, v[m][0].z, v[m][0].w,
+                                  v[m][1].x, v[m][1].y, v[m][1].z, v[m][1].w};
+                    if (pre_save) {
+                        // this SM's slice of the un-normalised input
+                        const int parts = min(n_items, grid);
+                        const int lo = (int)((int64_t)j0 * K / parts), hi = (int)((int64_t)(j0 + 1) * K / parts);
+#pragma unroll
+                        for (int c = 0; c < 8; c++)
+                            if (8 * w + c >= lo && 8 * w + c < hi) __stcg(d.save + 8 * w + c, e[c]);
+                    }
+                    if (d.gamma) {
+                        const __half *gh = reinterpret_cast<const __half *>(&gv[m]);
+#pragma unroll
+                        for (int c = 0; c < 8; c++) e[c] = __fmul_rn(__fmul_rn(e[c], inv), __half2float(gh[c]));
+                    }
+                    reinterpret_cast<float4 *>(xs)[2 * w] = make_float4(e[0], e[1], e[2], e[3]);
+                    reinterpret_cast<float4 *>(xs)[2 * w + 1] = make_float4(e[4], e[5], e[6], e[7]);
+                }
             }
             for (int k = K + tid; k < d.kpad; k += kNT) xs[k] = 0.0f;
-            if (d.gamma) {
-                // the producer's per-32-column sums of squares, in column order
-                float t = 0.0f;
-                for (int g = 0; g < (K >> 5); g++) t += __ldcg(d.ss_in + g);
-                ss = t;
-            }
-            break;
+            csync();
+            if (d.save && d.save_normed) save_slice(d, xs, j0, n_items, grid, tid);
+            return;
         }
         case IN_EMB: {
             uint32_t code;
@@ -277,7 +331,16 @@ __device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &
             } else {
                 code = __ldcg(d.code_src);
             }
-            for (int k = tid; k < d.kpad; k += kNT) xs[k] = k < K ? emb_value(d.emb, code, k) : 0.0f;
+            for (int w = tid; w < (d.kpad >> 3); w += kNT) {
+                float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                if (8 * w < K) {
+                    const EmbWord e = emb_word(d.emb, code, w);
+#pragma unroll
+                    for (int c = 0; c < 8; c++) o[c] = emb_at(e, c);
+                }
+                reinterpret_cast<float4 *>(xs)[2 * w] = make_float4(o[0], o[1], o[2], o[3]);
+                reinterpret_cast<float4 *>(xs)[2 * w + 1] = make_float4(o[4], o[5], o[6], o[7]);
+            }
             break;
         }
         case IN_FRAME: {
@@ -288,19 +351,36 @@ __device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &
                 for (int g = 1; g < fe.ngroups; g++) __stcg(fe.prev + g, __ldcg(fe.codes + g));
                 __stcg(fe.prev + fe.ngroups, last);
             }
-            uint32_t cg[kMaxEmbedGroups];
-            for (int g = 0; g < fe.ngroups; g++) cg[g] = g + 1 < fe.ngroups ? __ldcg(fe.codes + g + 1) : last;
             const uint32_t c0 = __ldcg(fe.codes);
-            for (int k = tid; k < d.kpad; k += kNT) {
-                float v = 0.0f;
-                if (k < K) {
-                    // (E_talker[c0] + (sum_g E_g[c_{g+1}])) + text, as the engine's frame embed
-                    float acc = 0.0f;
-                    for (int g = 0; g < fe.ngroups; g++) acc = __fadd_rn(acc, emb_value(fe.pred[g], cg[g], k));
-                    acc = __fadd_rn(emb_value(fe.talker, c0, k), acc);
-                    v = __fadd_rn(acc, __ldcg(P.text + k));
+            for (int w = tid; w < (d.kpad >> 3); w += kNT) {
+                float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                if (8 * w < K) {
+                    // every load of the 8 columns in flight before the sums
+                    EmbWord e[kMaxEmbedGroups];
+#pragma unroll
+                    for (int g = 0; g < kMaxEmbedGroups; g++) {
+                        if (g < fe.ngroups) {
+                            const uint32_t cg = g + 1 < fe.ngroups ? __ldcg(fe.codes + g + 1) : last;
+                            e[g] = emb_word(fe.pred[g], cg, w);
+                        }
+                    }
+                    const EmbWord et = emb_word(fe.talker, c0, w);
+                    const float4 t0 = __ldcg(reinterpret_cast<const float4 *>(P.text) + 2 * w);
+                    const float4 t1 = __ldcg(reinterpret_cast<const float4 *>(P.text) + 2 * w + 1);
+                    const float tx[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
+#pragma unroll
+                    for (int c = 0; c < 8; c++) {
+                        // (E_talker[c0] + (sum_g E_g[c_{g+1}])) + text, as the engine's frame embed
+                        float acc = 0.0f;
+#pragma unroll
+                        for (int g = 0; g < kMaxEmbedGroups; g++)
+                            if (g < fe.ngroups) acc = __fadd_rn(acc, emb_at(e[g], c));
+                        acc = __fadd_rn(emb_at(et, c), acc);
+                        o[c] = __fadd_rn(acc, tx[c]);
+                    }
                 }
-                xs[k] = v;
+                reinterpret_cast<float4 *>(xs)[2 * w] = make_float4(o[0], o[1], o[2], o[3]);
+                reinterpret_cast<float4 *>(xs)[2 * w + 1] = make_float4(o[4], o[5], o[6], o[7]);
             }
             break;
         }
@@ -308,13 +388,25 @@ __device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &
     csync();
     if (d.save && !d.save_normed) save_slice(d, xs, j0, n_items, grid, tid);
     if (d.gamma) {
-        if (d.in_mode != IN_VEC) {
-            float t = 0.0f;
-            for (int k = tid; k < K; k += kNT) t += __fmul_rn(xs[k], xs[k]);
-            ss = block_sum(t, S, tid);
-        }
+        constexpr int U = kXMax / 8 / kNT;
+        const uint4 *gm = reinterpret_cast<const uint4 *>(d.gamma);
+        uint4 gv[U];
+#pragma unroll
+        for (int m = 0; m < U; m++)
+            if (tid + m * kNT < (K >> 3)) gv[m] = __ldg(gm + tid + m * kNT);
+        float t = 0.0f;
+        for (int k = tid; k < K; k += kNT) t += __fmul_rn(xs[k], xs[k]);
+        const float ss = block_sum(t, S, tid);
         const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-6f)));
-        for (int k = tid; k < K; k += kNT) xs[k] = __fmul_rn(__fmul_rn(xs[k], inv), __half2float(d.gamma[k]));
+#pragma unroll
+        for (int m = 0; m < U; m++) {
+            const int w = tid + m * kNT;
+            if (w < (K >> 3)) {
+                const __half *gh = reinterpret_cast<const __half *>(&gv[m]);
+#pragma unroll
+                for (int c = 0; c < 8; c++) xs[8 * w + c] = __fmul_rn(__fmul_rn(xs[8 * w + c], inv), __half2float(gh[c]));
+            }
+        }
         csync();
     }
     if (d.save && d.save_normed) save_slice(d, xs, j0, n_items, grid, tid);
@@ -323,7 +415,8 @@ __device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &
 // The items of one GEMV op on this SM, G groups per unit, all K rows each.
 template <int G>
 __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef &op, FrameSmem &S,
-                           int tid, int cta, int grid, uint32_t &q, int &rbuf) {
+                           int tid, int cta, int grid, uint32_t &q, int &rbuf, bool tr, int op_i) {
+    uint64_t waited = 0, slots = 0;
     const int lane = tid & 31, warp = tid >> 5;
     constexpr int CR = G == 1 ? 1024 : 512;
     const float *xs = S.u.xs;
@@ -341,7 +434,12 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
             const int slot = q % kSlots;
             // on a failed wait the thread skips the slot but keeps to the
             // block's barrier sequence; the op ends with a uniform abort check
+            const uint64_t tw = tr ? global_ns() : 0;
             const bool ok = mbar_wait_or_abort(&S.full[slot], (q / kSlots) & 1, S, P);
+            if (tr) {
+                waited += global_ns() - tw;
+                slots++;
+            }
             const uint4 *nb = reinterpret_cast<const uint4 *>(S.nib[slot]);
             const __half *sb = reinterpret_cast<const __half *>(S.scl[slot]);
             for (int lr = tid; ok && lr < rows; lr += kNT) {
@@ -424,6 +522,10 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
         }
         rbuf ^= 1;
     }
+    if (tr) {
+        P.trace[(int64_t)op_i * kTraceFields + 4] = waited;
+        P.trace[(int64_t)op_i * kTraceFields + 5] = slots;
+    }
 }
 
 template <int HD, int G>
@@ -485,8 +587,8 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
                 const GemvDesc &d = P.gemv[op.idx];
                 build_input(P, d, S, tid, j0 == 0, j0, op.n_items, grid);
                 stamp(P, i, 1, tr);
-                if (d.G == 1) gemv_items<1>(P, d, op, S, tid, cta, grid, q, rbuf);
-                else gemv_items<2>(P, d, op, S, tid, cta, grid, q, rbuf);
+                if (d.G == 1) gemv_items<1>(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);
+                else gemv_items<2>(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);
                 csync();
                 if (*(volatile int *)&S.abort) return;
                 if (d.adv_len && j0 == 0 && tid == 0) {

@@ -16,7 +16,7 @@ constexpr int kSlots = 9;              // weight ring slots per SM
 constexpr int kSlotNib = 16384;        // nibble bytes per slot (1024 rows of one group)
 constexpr int kSlotScl = 2048;         // scale bytes per slot
 constexpr int kXMax = 6144;            // widest GEMV input (talker down projection)
-constexpr int kTraceFields = 4;
+constexpr int kTraceFields = 6;
 
 enum OpType : int { OP_GEMV = 0, OP_ATTN = 1, OP_SAMPLE = 2 };
 enum InMode : int {
@@ -87,9 +87,9 @@ struct FrameParams {
     unsigned *done = nullptr;            // [n_ops] completion counters (zeroed per launch)
     int *abort_flag = nullptr;
     int *err = nullptr;
-    unsigned long long *trace = nullptr; // optional [n_ops][4] globaltimer stamps of each op's
-                                         // item-0 SM: dependency met, input built, items done,
-                                         // signalled
+    unsigned long long *trace = nullptr; // optional [n_ops][6] of each op's item-0 SM: globaltimer
+                                         // stamps (dependency met, input built, items done,
+                                         // signalled), ns spent waiting for weight slots, slots
 };
 
 }  // namespace fk
