@@ -498,7 +498,8 @@ def profile_case_frame_trace():
     n = len(ops)
     wait = np.r_[0, st[1:, 0] - st[:-1, 3]]  # slot_wait (col 4) is part of items
     phases = {"wait": wait, "input": st[:, 1] - st[:, 0], "items": st[:, 2] - st[:, 1],
-              "signal": st[:, 3] - st[:, 2], "slot_wait": st[:, 4]}
+              "signal": st[:, 3] - st[:, 2], "slot_wait": st[:, 4] / 1.965,
+              "compute": st[:, 5] / 1.965, "reduce": st[:, 6] / 1.965}
     total = int(st[-1, 3] - st[0, 0])
     # op labels in program order (frame.cu frame_build)
     layer = ["qkv", "attn", "o", "gate_up", "down"]
@@ -518,7 +519,7 @@ def profile_case_frame_trace():
                       "us_per_op": round(total / n / 1000.0, 3),
                       "talker_us": round(float(st[-1, 3] - st[t0, 0]) / 1000.0, 1),
                       "phase_share": {k: round(float(v.sum()) / total, 3) for k, v in phases.items()
-                                      if k != "slot_wait"},
+                                      if k not in ("slot_wait", "compute", "reduce")},
                       "mean_us_by_op": by_label}))
 
 

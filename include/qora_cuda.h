@@ -255,11 +255,12 @@ int qora_engine_use_persistent(qora_engine *e, int32_t enable);
 /* Per-op timing of the persistent frame kernel (a profiling aid, no
  * reference counterpart).  enable != 0 makes later frames record, for each op,
  * on the SM that runs the op's first item: four globaltimer stamps (ns:
- * dependency met, input built, items done, completion signalled), the ns its
- * GEMV items waited for weight slots and the number of slots.  With
- * ops_host / stamps_host non-NULL it first copies the last recorded frame:
- * op types (0 GEMV, 1 attention, 2 sampler) into ops_host[capacity] and the
- * records into stamps_host[capacity][6].  *n_ops receives the op count. */
+ * dependency met, input built, items done, completion signalled), then the
+ * SM cycles its GEMV items spent waiting for weight slots, computing and
+ * reducing, and the number of slots.  With ops_host / stamps_host non-NULL
+ * it first copies the last recorded frame: op types (0 GEMV, 1 attention,
+ * 2 sampler) into ops_host[capacity] and the records into
+ * stamps_host[capacity][8].  *n_ops receives the op count. */
 int qora_engine_trace(qora_engine *e, int32_t enable, int32_t capacity, int32_t *n_ops,
                       int32_t *ops_host, uint64_t *stamps_host);
 /* Number of kernels one frame launches (for launch accounting). */

@@ -12,7 +12,7 @@ struct KVLayer {
     int kv_heads = 0, head_dim = 0, max_pos = 0;
 };
 
-struct AttnArgs {
+struct alignas(16) AttnArgs {
     // raw projections, row r = stream * T + t: [q (heads*hd) | k (kvh*hd) | v (kvh*hd)]
     float *qkv = nullptr;
     int64_t ldqkv = 0;

@@ -70,7 +70,15 @@ struct alignas(128) FrameSmem {
     int bidx[kNT / 32];
     uint64_t full[kSlots], empty[kSlots];
     int abort;
+    // the current op's descriptor, staged from global memory while thread 0
+    // waits for the op's dependency
+    union alignas(16) Desc {
+        GemvDesc g;
+        AttnArgs a;
+        uint4 words[1];
+    } desc;
 };
+static_assert(sizeof(GemvDesc) % 16 == 0 && sizeof(AttnArgs) % 16 == 0, "descriptor staging");
 
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kNT) : "memory"); }
 
@@ -412,15 +420,46 @@ __device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &
     if (d.save && d.save_normed) save_slice(d, xs, j0, n_items, grid, tid);
 }
 
+// One weight row of one 32-column group: acc += s' * nibbles, with
+// s' = f32(scale) * x * 2^75 (gemv.rs:265 times an exact power of two).  A
+// nibble at bit 4p of a half-word, read as f32 bits, is q * 2^(4p-149):
+// linear in q, so one packed FMA handles two columns.
+__device__ __forceinline__ void row_fma(uint64_t (&acc)[16], float &ssum, float sp, const uint4 wv) {
+    ssum += sp;
+    const uint64_t s2 = pk2(sp, sp);
+    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+    for (int w4 = 0; w4 < 4; w4++) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t v = h ? (words[w4] >> 16) : words[w4];
+#pragma unroll
+            for (int pp = 0; pp < 4; pp += 2) {
+                const uint64_t qd = pk2(__uint_as_float(v & (0xFu << (4 * pp))),
+                                        __uint_as_float(v & (0xFu << (4 * pp + 4))));
+                const int jj = 4 * w4 + 2 * h + pp / 2;
+                acc[jj] = ffma2(s2, qd, acc[jj]);
+            }
+        }
+    }
+}
+
 // The items of one GEMV op on this SM, G groups per unit, all K rows each.
 template <int G>
 __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef &op, FrameSmem &S,
                            int tid, int cta, int grid, uint32_t &q, int &rbuf, bool tr, int op_i) {
-    uint64_t waited = 0, slots = 0;
+    uint64_t waited = 0, slots = 0, comp = 0, redc = 0;
     const int lane = tid & 31, warp = tid >> 5;
     constexpr int CR = G == 1 ? 1024 : 512;
     const float *xs = S.u.xs;
     for (int u = first_item(cta, op.rot, grid); u < op.n_items; u += grid) {
+        // the epilogue's residual / bias values, fetched while the item computes
+        float pre = 0.0f;
+        if (G == 1 && warp == 0) {
+            const int64_t col = (int64_t)u * 32 + lane;
+            if (d.out_mode == OUT_RESID) pre = __ldcg(d.resid + col);
+            else if (d.bias) pre = __ldg(d.bias + col);
+        }
         uint64_t acc[G][16];
         float ssum[G];
 #pragma unroll
@@ -434,46 +473,28 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
             const int slot = q % kSlots;
             // on a failed wait the thread skips the slot but keeps to the
             // block's barrier sequence; the op ends with a uniform abort check
-            const uint64_t tw = tr ? global_ns() : 0;
+            const long long tw = tr ? clock64() : 0;
             const bool ok = mbar_wait_or_abort(&S.full[slot], (q / kSlots) & 1, S, P);
+            long long tc = 0;
             if (tr) {
-                waited += global_ns() - tw;
+                tc = clock64();
+                waited += (uint64_t)(tc - tw);
                 slots++;
             }
             const uint4 *nb = reinterpret_cast<const uint4 *>(S.nib[slot]);
             const __half *sb = reinterpret_cast<const __half *>(S.scl[slot]);
             for (int lr = tid; ok && lr < rows; lr += kNT) {
-                // s' = f32(scale) * x * 2^75 (gemv.rs:265 times an exact power of two)
                 const float x75 = __fmul_rn(xs[c0 + lr], 37778931862957161709568.0f);
 #pragma unroll
-                for (int g = 0; g < G; g++) {
-                    const float sp = __fmul_rn(__half2float(sb[g * rows + lr]), x75);
-                    ssum[g] += sp;
-                    const uint64_t s2 = pk2(sp, sp);
-                    const uint4 wv = nb[g * rows + lr];
-                    const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-                    for (int w4 = 0; w4 < 4; w4++) {
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            // nibbles at bit 4p of a half-word read as f32 bits are
-                            // q * 2^(4p-149): linear in q, one FMA per two columns
-                            const uint32_t v = h ? (words[w4] >> 16) : words[w4];
-#pragma unroll
-                            for (int pp = 0; pp < 4; pp += 2) {
-                                const uint64_t qd = pk2(__uint_as_float(v & (0xFu << (4 * pp))),
-                                                        __uint_as_float(v & (0xFu << (4 * pp + 4))));
-                                const int jj = 4 * w4 + 2 * h + pp / 2;
-                                acc[g][jj] = ffma2(s2, qd, acc[g][jj]);
-                            }
-                        }
-                    }
-                }
+                for (int g = 0; g < G; g++)
+                    row_fma(acc[g], ssum[g], __fmul_rn(__half2float(sb[g * rows + lr]), x75), nb[g * rows + lr]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&S.empty[slot]);
+            if (tr) comp += (uint64_t)(clock64() - tc);
             q++;
         }
+        const long long tr0 = tr ? clock64() : 0;
         // butterfly reduce-scatter: lane l ends with the warp's total of column l
 #pragma unroll
         for (int g = 0; g < G; g++) {
@@ -511,8 +532,8 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
             } else {
                 const int64_t col = (int64_t)u * 32 + lane;
                 float o = y[0];
-                if (d.out_mode == OUT_RESID) o = __fadd_rn(__ldcg(d.resid + col), o);  // x += attn / mlp
-                if (d.bias) o = __fadd_rn(o, d.bias[col]);
+                if (d.out_mode == OUT_RESID) o = __fadd_rn(pre, o);  // x += attn / mlp
+                else if (d.bias) o = __fadd_rn(o, pre);
                 __stcg(d.out + col, o);
                 if (d.ss_out) {
                     const float sq = warp_sum(__fmul_rn(o, o));
@@ -521,10 +542,13 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
             }
         }
         rbuf ^= 1;
+        if (tr) redc += (uint64_t)(clock64() - tr0);
     }
     if (tr) {
         P.trace[(int64_t)op_i * kTraceFields + 4] = waited;
-        P.trace[(int64_t)op_i * kTraceFields + 5] = slots;
+        P.trace[(int64_t)op_i * kTraceFields + 5] = comp;
+        P.trace[(int64_t)op_i * kTraceFields + 6] = redc;
+        P.trace[(int64_t)op_i * kTraceFields + 7] = slots;
     }
 }
 
@@ -540,7 +564,7 @@ __device__ __forceinline__ void attn_items(const AttnArgs &a, const OpRef &op, A
 
 __device__ void run_attn(const FrameParams &P, const OpRef &op, FrameSmem &S, int tid, int cta,
                          int grid) {
-    const AttnArgs &a = P.attn[op.idx];
+    const AttnArgs &a = S.desc.a;
     const int G = a.heads / a.kv_heads;
     if (a.kv.head_dim == 128) {
         if (G == 1) attn_items<128, 1>(a, op, S.u.a128_1, tid, cta, grid);
@@ -562,6 +586,14 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
         const int j0 = first_item(cta, op.rot, grid);
         const bool tr = P.trace && j0 == 0 && tid == 0;
         if (j0 < op.n_items) {
+            // stage the descriptor (immutable) while thread 0 polls below;
+            // the barrier after the poll publishes it
+            if (op.type != OP_SAMPLE) {
+                const uint4 *src = op.type == OP_GEMV ? reinterpret_cast<const uint4 *>(P.gemv + op.idx)
+                                                      : reinterpret_cast<const uint4 *>(P.attn + op.idx);
+                const int nw = (op.type == OP_GEMV ? (int)sizeof(GemvDesc) : (int)sizeof(AttnArgs)) / 16;
+                if (tid >= 32 && tid - 32 < nw) S.desc.words[tid - 32] = __ldg(src + (tid - 32));
+            }
             if (i > 0) {
                 // every SM has finished op i-1 (bounded wait, abort-aware)
                 if (tid == 0) {
@@ -579,12 +611,12 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
                         }
                     }
                 }
-                csync();
-                if (*(volatile int *)&S.abort) return;
             }
+            csync();
+            if (*(volatile int *)&S.abort) return;
             stamp(P, i, 0, tr);
             if (op.type == OP_GEMV) {
-                const GemvDesc &d = P.gemv[op.idx];
+                const GemvDesc &d = S.desc.g;
                 build_input(P, d, S, tid, j0 == 0, j0, op.n_items, grid);
                 stamp(P, i, 1, tr);
                 if (d.G == 1) gemv_items<1>(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);

@@ -16,7 +16,7 @@ constexpr int kSlots = 9;              // weight ring slots per SM
 constexpr int kSlotNib = 16384;        // nibble bytes per slot (1024 rows of one group)
 constexpr int kSlotScl = 2048;         // scale bytes per slot
 constexpr int kXMax = 6144;            // widest GEMV input (talker down projection)
-constexpr int kTraceFields = 6;
+constexpr int kTraceFields = 8;
 
 enum OpType : int { OP_GEMV = 0, OP_ATTN = 1, OP_SAMPLE = 2 };
 enum InMode : int {
@@ -33,7 +33,7 @@ enum OutMode : int {
 // One GEMV op: y = epilogue(prologue(x) @ W) over `units` column units of G
 // 32-column groups each; item j = unit j covers all K rows, so every output
 // is final when its item ends.
-struct GemvDesc {
+struct alignas(16) GemvDesc {
     const uint4 *nib = nullptr;
     const __half *scl = nullptr;
     int kpad = 0, K = 0, units = 0, G = 1;
@@ -87,9 +87,10 @@ struct FrameParams {
     unsigned *done = nullptr;            // [n_ops] completion counters (zeroed per launch)
     int *abort_flag = nullptr;
     int *err = nullptr;
-    unsigned long long *trace = nullptr; // optional [n_ops][6] of each op's item-0 SM: globaltimer
+    unsigned long long *trace = nullptr; // optional [n_ops][8] of each op's item-0 SM: globaltimer
                                          // stamps (dependency met, input built, items done,
-                                         // signalled), ns spent waiting for weight slots, slots
+                                         // signalled); thread 0's SM cycles waiting for weight
+                                         // slots, computing, reducing; slots consumed
 };
 
 }  // namespace fk

@@ -326,12 +326,13 @@ class Engine:
 
     def trace(self, enable: bool = True):
         """Turns per-op stamps of the persistent frame kernel on/off and returns
-        the last recorded frame: op types int32 [n] and uint64 [n][6]: four
-        globaltimer stamps (ns), ns waited for weight slots, slots consumed."""
+        the last recorded frame: op types int32 [n] and uint64 [n][8]: four
+        globaltimer stamps (ns); SM cycles waiting for weight slots, computing
+        and reducing; slots consumed."""
         n = C.c_int32()
         _lib.call("qora_engine_trace", self.h, 1 if enable else 0, 0, C.byref(n), None, None)
         ops = np.zeros(n.value, np.int32)
-        st = np.zeros((n.value, 6), np.uint64)
+        st = np.zeros((n.value, 8), np.uint64)
         _lib.call("qora_engine_trace", self.h, 1 if enable else 0, n.value, C.byref(n),
                   ops.ctypes.data, st.ctypes.data)
         return ops, st

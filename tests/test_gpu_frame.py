@@ -113,7 +113,7 @@ def test_trace_records_every_op(E, ctx, orc):
     stamps = st[:, :4].astype(np.int64)
     assert np.all(stamps > 0) and np.all(np.diff(stamps, axis=1) >= 0)
     gemv = ops == 0
-    assert np.all(st[gemv, 5] > 0)          # every GEMV op's item 0 consumed weight slots
+    assert np.all(st[gemv, 7] > 0)          # every GEMV op's item 0 consumed weight slots
 
 
 @pytest.mark.parametrize("hd", [128, 64])
