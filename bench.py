@@ -494,13 +494,18 @@ def profile_case_frame_trace():
         eng.frame(text, codes)
     ops, st = eng.trace(False)
     ctx.check_device_error()
-    st = st.astype(np.int64)
+    st = st.astype(np.uint64)
     n = len(ops)
-    wait = np.r_[0, st[1:, 0] - st[:-1, 3]]  # slot_wait (col 4) is part of items
-    phases = {"wait": wait, "input": st[:, 1] - st[:, 0], "items": st[:, 2] - st[:, 1],
-              "signal": st[:, 3] - st[:, 2], "slot_wait": st[:, 4] / 1.965,
-              "compute": st[:, 5] / 1.965, "reduce": st[:, 6] / 1.965}
-    total = int(st[-1, 3] - st[0, 0])
+    ready0 = (~st[:, 0]).astype(np.int64)          # earliest input ready over SMs
+    ready1, done, start = (st[:, k].astype(np.int64) for k in (1, 2, 3))
+    t_begin = int(min(start.min(), ready0.min()))
+    total = int(done.max() - t_begin)
+    prev_done = np.r_[t_begin, done[:-1]]
+    phases = {"gap": ready0 - prev_done,            # previous op done everywhere -> first input ready
+              "spread": ready1 - ready0,            # first -> last SM with its input ready
+              "work": done - ready1,                # last input ready -> last item done
+              "slot_wait": st[:, 4].astype(np.int64) / 1.965,
+              "compute": st[:, 5].astype(np.int64) / 1.965, "reduce": st[:, 6].astype(np.int64) / 1.965}
     # op labels in program order (frame.cu frame_build)
     layer = ["qkv", "attn", "o", "gate_up", "down"]
     labels = ["sample"]
@@ -517,9 +522,9 @@ def profile_case_frame_trace():
     t0 = n - 5 * cfg.t_layers - 1
     print(json.dumps({"profile_case": "frame_trace", "ops": n, "frame_us": round(total / 1000.0, 1),
                       "us_per_op": round(total / n / 1000.0, 3),
-                      "talker_us": round(float(st[-1, 3] - st[t0, 0]) / 1000.0, 1),
+                      "talker_us": round(float(done[-1] - done[t0 - 1]) / 1000.0, 1),
                       "phase_share": {k: round(float(v.sum()) / total, 3) for k, v in phases.items()
-                                      if k not in ("slot_wait", "compute", "reduce")},
+                                      if k in ("gap", "spread", "work")},
                       "mean_us_by_op": by_label}))
 
 

@@ -253,12 +253,13 @@ int qora_engine_use_graph(qora_engine *e, int32_t enable);
  * QORA_ERR_UNSUPPORTED otherwise (the per-op path then stays in use). */
 int qora_engine_use_persistent(qora_engine *e, int32_t enable);
 /* Per-op timing of the persistent frame kernel (a profiling aid, no
- * reference counterpart).  enable != 0 makes later frames record, for each op,
- * on the SM that runs the op's first item: four globaltimer stamps (ns:
- * dependency met, input built, items done, completion signalled), then the
- * SM cycles its GEMV items spent waiting for weight slots, computing and
- * reducing, and the number of slots.  With ops_host / stamps_host non-NULL
- * it first copies the last recorded frame: op types (0 GEMV, 1 attention,
+ * reference counterpart).  enable != 0 makes later frames record, for each
+ * op, globaltimer ns over the SMs that have items in it: the earliest input
+ * ready (stored bit-complemented), the latest input ready, the latest
+ * completion and the latest start; then, on the SM that runs the op's first
+ * item, the cycles its GEMV items waited for weight slots, computed and
+ * reduced, and the slots consumed.  With ops_host / stamps_host non-NULL it
+ * first copies the last recorded frame: op types (0 GEMV, 1 attention,
  * 2 sampler) into ops_host[capacity] and the records into
  * stamps_host[capacity][8].  *n_ops receives the op count. */
 int qora_engine_trace(qora_engine *e, int32_t enable, int32_t capacity, int32_t *n_ops,

@@ -35,6 +35,14 @@ struct alignas(16) AttnArgs {
     float *part_ml = nullptr;       // [rows][kvh][kAttnMaxSplit][G][2]
     unsigned *tickets = nullptr;    // [rows][kvh]
     int *err = nullptr;
+    // tagged input / output (persistent frame kernel): when qkv_t is set the
+    // q | k | v rows are read from tagged words carrying qkv_tag, and when
+    // out_t is set the output is written as tagged words carrying out_tag
+    const uint64_t *qkv_t = nullptr;
+    uint32_t qkv_tag = 0, out_tag = 0;
+    uint64_t *out_t = nullptr;
+    uint32_t tag_base = 0;          // added to qkv_tag and out_tag
+    int *abort_flag = nullptr;
 };
 
 // qk-norm + RoPE + append for T tokens per stream (used when T > 1).

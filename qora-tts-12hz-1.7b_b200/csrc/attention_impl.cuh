@@ -123,11 +123,21 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
         for (int it = warp; it < G + 2; it += NT / 32) {
             if (it >= G && !appender) continue;
             float v[J];
-            const float *src = it < G ? row + (int64_t)(kvh * G + it) * HD
-                                      : (it == G ? row + (int64_t)(a.heads + kvh) * HD
-                                                 : row + (int64_t)(a.heads + a.kv_heads + kvh) * HD);
+            const int64_t off = it < G ? (int64_t)(kvh * G + it) * HD
+                                       : (it == G ? (int64_t)(a.heads + kvh) * HD
+                                                  : (int64_t)(a.heads + a.kv_heads + kvh) * HD);
+            if (a.qkv_t) {
+                bool all[J];
 #pragma unroll
-            for (int j = 0; j < J; j++) v[j] = __ldcg(src + lane + 32 * j);
+                for (int j = 0; j < J; j++) all[j] = true;
+                // acquire: the K/V rows read below were appended by earlier ops
+                poll_tagged<J, true>(a.qkv_t + (int64_t)r * a.ldqkv + off + lane, 32, a.tag_base + a.qkv_tag,
+                                     v, all, a.err, a.abort_flag);
+            } else {
+                const float *src = row + off;
+#pragma unroll
+                for (int j = 0; j < J; j++) v[j] = __ldcg(src + lane + 32 * j);
+            }
             if (it < G) {
                 norm_rope_head<HD>(v, a.q_gamma, cr, sr, true, lane);
 #pragma unroll
@@ -217,10 +227,15 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
 
     const int64_t out_base = (int64_t)r * a.ldout + (int64_t)kvh * G * HD;
     if (nsplit == 1) {
+        if (a.out_t) fence_acq_rel_gpu();  // the K/V append is published before the output
 #pragma unroll
         for (int i = 0; i < NO; i++) {
             const int o = tid + i * NT;
-            if (o < G * HD) a.out[out_base + o] = __fdiv_rn(o_acc[i], l_s[o / HD]);
+            if (o < G * HD) {
+                const float y = __fdiv_rn(o_acc[i], l_s[o / HD]);
+                if (a.out_t) st_relaxed_u64(a.out_t + out_base + o, tag_pack(y, a.tag_base + a.out_tag));
+                else a.out[out_base + o] = y;
+            }
         }
         return;
     }
@@ -255,7 +270,9 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
             L = __fmaf_rn(__ldcg(a.part_ml + ((slot + sp) * G + hh) * 2 + 1), w, L);
             O = __fmaf_rn(__ldcg(a.part_o + (slot + sp) * (G * HD) + o), w, O);
         }
-        a.out[out_base + o] = __fdiv_rn(O, L);
+        const float y = __fdiv_rn(O, L);
+        if (a.out_t) st_relaxed_u64(a.out_t + out_base + o, tag_pack(y, a.tag_base + a.out_tag));
+        else a.out[out_base + o] = y;
     }
     if (tid == 0) a.tickets[(int64_t)r * a.kv_heads + kvh] = 0u;
 }

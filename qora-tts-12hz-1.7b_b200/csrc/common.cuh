@@ -184,6 +184,104 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) 
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// ---- tagged values: one 64-bit word = (tag << 32) | float bits, written and
+// read with single-copy-atomic relaxed accesses.  A reader that sees the
+// expected tag sees that writer's value (no separate flag, no counter).
+__device__ __forceinline__ uint64_t tag_pack(float v, uint32_t tag) {
+    return ((uint64_t)tag << 32) | __float_as_uint(v);
+}
+__device__ __forceinline__ uint64_t ld_relaxed_u64(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_relaxed_u64(uint64_t *p, uint64_t v) {
+    asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+// Orders this thread's earlier accesses before its later ones at GPU scope:
+// after a poll it is the acquire half, before tagged stores the release half.
+__device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+
+__device__ __forceinline__ uint64_t global_ns_t() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits (bounded, ~2 s) until base[k * stride] carries `tag` for every k < N
+// (pred[k] false skips an element) and returns the values in out[].  On
+// timeout, or when *abort is set by another waiter, it raises kDevTimeout,
+// sets *abort and returns what it has: the caller keeps to its barrier
+// sequence and checks the abort state afterwards.  While nothing has
+// arrived it spins on one word only, to keep idle waiters off the L2.
+// ACQ adds an acquire fence at the end, for callers that go on to read
+// plain data the writers published before their tagged stores.
+template <int N, bool ACQ = false>
+__device__ __forceinline__ bool poll_tagged(const uint64_t *base, int64_t stride, uint32_t tag,
+                                            float (&out)[N], const bool (&pred)[N], int *err,
+                                            int *abort) {
+    uint32_t pending = 0;
+    int gate = -1;
+#pragma unroll
+    for (int k = 0; k < N; k++)
+        if (pred[k]) {
+            pending |= 1u << k;
+            gate = k;
+        }
+    uint64_t t0 = 0;
+    bool ok = true;
+    for (int it = 0; pending; it++) {
+        if (it > 0 && gate >= 0) {
+            // cheap wait: the last requested word first
+            if ((uint32_t)(ld_relaxed_u64(base + gate * stride) >> 32) != tag) {
+                __nanosleep(128);  // idle waiters stay off the L2
+                if (it == 1) t0 = global_ns_t();
+                if ((it & 15) == 15) {
+                    if (*(volatile int *)abort) {
+                        ok = false;
+                        break;
+                    }
+                    if (global_ns_t() - t0 > 2000000000ull) {
+                        if (err) atomicCAS(err, 0, 3);
+                        atomicExch(abort, 1);
+                        ok = false;
+                        break;
+                    }
+                }
+                continue;
+            }
+            gate = -1;
+        }
+        uint64_t v[N];
+#pragma unroll
+        for (int k = 0; k < N; k++)
+            if (pending & (1u << k)) v[k] = ld_relaxed_u64(base + k * stride);
+#pragma unroll
+        for (int k = 0; k < N; k++) {
+            if ((pending & (1u << k)) && (uint32_t)(v[k] >> 32) == tag) {
+                out[k] = __uint_as_float((uint32_t)v[k]);
+                pending &= ~(1u << k);
+            }
+        }
+        if (!pending) break;
+        if (it == 0) t0 = global_ns_t();
+        if ((it & 15) == 15) {
+            if (*(volatile int *)abort) {
+                ok = false;
+                break;
+            }
+            if (global_ns_t() - t0 > 2000000000ull) {
+                if (err) atomicCAS(err, 0, 3);
+                atomicExch(abort, 1);
+                ok = false;
+                break;
+            }
+        }
+    }
+    if (ACQ) fence_acq_rel_gpu();
+    return ok;
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

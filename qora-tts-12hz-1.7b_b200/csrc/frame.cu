@@ -8,9 +8,20 @@
 // Why: at batch 1 the frame is ~570 dependent steps whose weights (~1.5 GB of
 // Q4 passes) would stream in ~0.2 ms, but as separate launches every step
 // costs a kernel boundary (~6 us).  Here one CTA per SM walks the same op
-// list; op i starts on an SM once every SM has finished op i-1 (a per-op
-// arrival counter in global memory, bounded spin), so a step costs one
-// counter round trip instead of a launch.
+// list and the steps are chained through the data itself: every activation
+// an op publishes is a tagged 64-bit word (value | tag << 32, tag unique to
+// the op and the launch), and a consumer polls exactly the words it needs
+// until they carry its producer's tag.  A step then costs one store-to-load
+// trip through L2 - no counters, no separate flag, no per-op fence of its
+// own.  The only plain data read back within a launch is the K/V cache: an
+// attention op fences (release) between its K/V append and its tagged
+// output, and fences (acquire) after polling its q/k/v, before it reads the
+// cache through L2.  Every op consumes its producer's whole
+// output (or, for attention, its head's q/k/v, whose consumer needs all of
+// attention's output), so by the time any SM overwrites a buffer every
+// reader of its previous contents has finished.  The one op whose data does
+// not reach back to its predecessor (the semantic pass's projection needs
+// only the sampled code) waits on the previous pass's output explicitly.
 //
 // Weight streaming is decoupled from that chain.  Each SM's share of every
 // GEMV is known in advance (item j of op i runs on SM (j + rot_i) % grid),
@@ -18,24 +29,24 @@
 // the SM's weight slices into a ring of shared-memory slots with
 // cp.async.bulk (no multicast), signalling an mbarrier per slot; the compute
 // warps consume slots in the same order and release them.  Weights are
-// immutable, so the stream never waits on activations: while the compute
-// warps wait for op i-1 to finish everywhere, the ring is already filling
-// with op i, i+1, ... weights.
+// immutable, so the stream never waits on activations.
 //
 // Every GEMV item is one column unit (32 output columns, or a gate/up pair)
 // over all K rows, so it ends with final values and applies its epilogue
 // itself: residual add (plus the per-32-column sum of squares the next
 // RMSNorm needs), bias, or silu(gate) * up.  An SM that has items in an op
-// reads that op's whole input vector (<= 6144 floats, from L2) into shared
-// memory and applies the RMSNorm prologue from those sums of squares, summed
-// in the same fixed order on every SM.  The attention and sampler ops run the
-// same device code as the standalone kernels (attention_impl.cuh,
-// sampler_impl.cuh).
+// polls that op's whole input vector (<= 6144 values) into shared memory and
+// applies the RMSNorm prologue from those sums of squares, summed in the
+// same fixed order on every SM.  The attention and sampler ops run the same
+// device code as the standalone kernels (attention_impl.cuh,
+// sampler_impl.cuh).  Each op's descriptor is staged into shared memory with
+// cp.async while the previous op runs.
 //
 // Every wait is bounded (~2 s of globaltimer); a timeout raises kDevTimeout,
 // sets a global abort flag that every other waiter polls, and the kernel
 // drains its own in-flight bulk copies before returning.
 #include <algorithm>
+#include <cstddef>
 #include <cstring>
 
 #include "attention_impl.cuh"
@@ -48,6 +59,10 @@ namespace fk {
 namespace {
 
 constexpr uint64_t kWaitNs = 2000000000ull;  // bounded waits: 2 s
+
+constexpr int kMaxOps = 640;                 // op table held in shared memory
+constexpr int kChunkRows = kSlotNib / 16;    // weight rows of one group per slot
+constexpr int kDescWords = 24;               // 384-byte descriptor slots
 
 template <int HD, int G>
 using ASmem = attn::AttnSmem<HD, G, kNT>;
@@ -65,28 +80,27 @@ struct alignas(128) FrameSmem {
         ASmem<64, 4> a64_4;
         samp::SampleSmem<kNT, 1> samp;
     } u;
-    float red[2][kNT / 32][2][32];     // per-item cross-warp reduction (double buffered)
+    float red[2][kNT / 32][32];        // per-group cross-warp reduction (double buffered)
     float bred[kNT / 32];              // block reductions
     int bidx[kNT / 32];
     uint64_t full[kSlots], empty[kSlots];
     int abort;
-    // the current op's descriptor, staged from global memory while thread 0
-    // waits for the op's dependency
+    uint32_t codes_s[kMaxEmbedGroups];  // the frame's codes (talker frame input)
+    // two descriptor slots: the current op's and the next op's (staged with
+    // cp.async while the current op runs)
     union alignas(16) Desc {
         GemvDesc g;
         AttnArgs a;
-        uint4 words[1];
-    } desc;
+        uint4 words[kDescWords];
+    } desc[2];
+    OpRef ops[kMaxOps];
 };
-static_assert(sizeof(GemvDesc) % 16 == 0 && sizeof(AttnArgs) % 16 == 0, "descriptor staging");
+static_assert(sizeof(GemvDesc) <= 16 * kDescWords && sizeof(AttnArgs) <= 16 * kDescWords,
+              "descriptor staging slots");
+static_assert(sizeof(OpRef) == 16, "op table staging");
 
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kNT) : "memory"); }
 
-__device__ __forceinline__ unsigned ld_acquire(const unsigned *p) {
-    unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
 __device__ __forceinline__ int ld_volatile(const int *p) {
     int v;
     asm volatile("ld.volatile.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -95,14 +109,24 @@ __device__ __forceinline__ int ld_volatile(const int *p) {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit_wait() {
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+}
 
 __device__ __forceinline__ int first_item(int cta, int rot, int grid) {
     int j = (cta - rot) % grid;
     return j < 0 ? j + grid : j;
 }
 
-__device__ __forceinline__ void stamp(const FrameParams &P, int op, int field, bool on) {
-    if (on) P.trace[(int64_t)op * kTraceFields + field] = global_ns();
+// Across SMs: field 0 keeps the earliest time (stored complemented, so a
+// max does it), fields 1-3 the latest.
+__device__ __forceinline__ void stamp_all(const FrameParams &P, int op, int field, bool on) {
+    if (!on) return;
+    const unsigned long long t = global_ns();
+    atomicMax(P.trace + (int64_t)op * kTraceFields + field, field == 0 ? ~t : t);
 }
 
 // Sets the abort state everywhere after a failed or timed-out wait.
@@ -112,7 +136,7 @@ __device__ __forceinline__ void raise_abort(const FrameParams &P, FrameSmem &S, 
     S.abort = 1;
 }
 
-// Bounded mbarrier wait that also gives up when the CTA aborted.
+// Bounded mbarrier wait that also gives up when the CTA or the grid aborted.
 __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parity, FrameSmem &S,
                                                    const FrameParams &P) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -120,7 +144,10 @@ __device__ __forceinline__ bool mbar_wait_or_abort(uint64_t *bar, uint32_t parit
     for (int it = 0;; it++) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63) == 63) {
-            if (*(volatile int *)&S.abort) return false;
+            if (*(volatile int *)&S.abort || ld_volatile(P.abort_flag)) {
+                S.abort = 1;
+                return false;
+            }
             if (global_ns() - t0 > kWaitNs) {
                 raise_abort(P, S, kDevTimeout);
                 return false;
@@ -136,28 +163,29 @@ __device__ void producer(const FrameParams &P, FrameSmem &S, int cta, int grid) 
     uint32_t q = 0;
     bool ok = true;
     for (int i = 0; i < P.n_ops && ok; i++) {
-        const OpRef op = P.ops[i];
+        const OpRef op = S.ops[i];
         if (op.type != OP_GEMV) continue;
+        const int u0 = first_item(cta, op.rot, grid);
+        if (u0 >= op.n_items) continue;
         const GemvDesc &d = P.gemv[op.idx];
         const int G = d.G, kpad = d.kpad;
-        const int CR = G == 1 ? 1024 : 512;
-        for (int u = first_item(cta, op.rot, grid); u < op.n_items && ok; u += grid) {
-            for (int c0 = 0; c0 < kpad; c0 += CR) {
-                const int rows = min(CR, kpad - c0);
-                const int slot = q % kSlots;
-                if (q >= kSlots && !mbar_wait_or_abort(&S.empty[slot], ((q / kSlots) - 1) & 1, S, P)) {
-                    ok = false;
-                    break;
+        const uint4 *nib = d.nib;
+        const __half *scl = d.scl;
+        for (int u = u0; u < op.n_items && ok; u += grid) {
+            for (int g = 0; g < G && ok; g++) {  // a unit's groups one after the other
+                const int64_t grp = (int64_t)u * G + g;
+                for (int c0 = 0; c0 < kpad; c0 += kChunkRows) {
+                    const int rows = min(kChunkRows, kpad - c0);
+                    const int slot = q % kSlots;
+                    if (q >= kSlots && !mbar_wait_or_abort(&S.empty[slot], ((q / kSlots) - 1) & 1, S, P)) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&S.full[slot], (uint32_t)(rows * 18));
+                    bulk_g2s(S.nib[slot], nib + grp * kpad + c0, (uint32_t)rows * 16, &S.full[slot]);
+                    bulk_g2s(S.scl[slot], scl + grp * kpad + c0, (uint32_t)rows * 2, &S.full[slot]);
+                    q++;
                 }
-                mbar_arrive_expect_tx(&S.full[slot], (uint32_t)(G * rows * 18));
-                for (int g = 0; g < G; g++) {
-                    const int64_t grp = (int64_t)u * G + g;
-                    bulk_g2s(S.nib[slot] + g * rows * 16, d.nib + grp * kpad + c0, (uint32_t)rows * 16,
-                             &S.full[slot]);
-                    bulk_g2s(S.scl[slot] + g * rows * 2, d.scl + grp * kpad + c0, (uint32_t)rows * 2,
-                             &S.full[slot]);
-                }
-                q++;
             }
         }
     }
@@ -187,32 +215,99 @@ __device__ __forceinline__ float block_sum(float v, FrameSmem &S, int tid) {
     return t;
 }
 
-// Argmax of src[0..n) (n a multiple of 4, <= 4096); ties keep the larger
-// index (the last maximum, code_predictor.rs:336-339).  Identical on every SM.
-__device__ int block_argmax(const FrameParams &P, const float *src, int n, FrameSmem &S, int tid) {
-    constexpr int U = 4;  // float4s per thread: 4 * 4 * 256 = 4096
-    const float4 *s4 = reinterpret_cast<const float4 *>(src);
-    float4 v[U];
+// Polls dst[i] = value of src[i] for i = i0 + tid + m * kNT (m < U, i < n)
+// until every word carries `tag` (bounded; on failure the CTA aborts after
+// its barrier sequence).  GEMV inputs are all tagged, so no fence follows.
+template <int U>
+__device__ __forceinline__ void poll_to_smem(const FrameParams &P, FrameSmem &S, const uint64_t *src,
+                                             int i0, int n, uint32_t tag, float *dst, int tid) {
+    uint32_t pending = 0;
+    int gate = -1;
 #pragma unroll
-    for (int m = 0; m < U; m++) {
-        const int i = tid + m * kNT;
-        if (4 * i < n) v[m] = __ldcg(s4 + i);
+    for (int m = 0; m < U; m++)
+        if (i0 + tid + m * kNT < n) {
+            pending |= 1u << m;
+            gate = m;
+        }
+    uint64_t t0 = global_ns();
+    for (int it = 0; pending; it++) {
+        if (it > 0 && gate >= 0) {
+            // cheap wait while nothing has arrived: one word, then the rest
+            if ((uint32_t)(ld_relaxed_u64(src + i0 + tid + gate * kNT) >> 32) != tag) {
+                __nanosleep(128);  // idle waiters stay off the L2
+                if ((it & 15) == 15) {
+                    if (ld_volatile(P.abort_flag)) {
+                        S.abort = 1;
+                        break;
+                    }
+                    if (global_ns() - t0 > kWaitNs) {
+                        raise_abort(P, S, kDevTimeout);
+                        break;
+                    }
+                }
+                continue;
+            }
+            gate = -1;
+        }
+        uint64_t v[U];
+#pragma unroll
+        for (int m = 0; m < U; m++)
+            if (pending & (1u << m)) v[m] = ld_relaxed_u64(src + i0 + tid + m * kNT);
+#pragma unroll
+        for (int m = 0; m < U; m++) {
+            if ((pending & (1u << m)) && (uint32_t)(v[m] >> 32) == tag) {
+                dst[i0 + tid + m * kNT] = __uint_as_float((uint32_t)v[m]);
+                pending &= ~(1u << m);
+            }
+        }
+        if (!pending) break;
+        if ((it & 15) == 15) {
+            if (ld_volatile(P.abort_flag)) {
+                S.abort = 1;
+                break;
+            }
+            if (global_ns() - t0 > kWaitNs) {
+                raise_abort(P, S, kDevTimeout);
+                break;
+            }
+        }
     }
+}
+
+// A tagged word loaded early (w) or, if it did not carry `tag` yet, polled
+// until it does.
+__device__ __forceinline__ float settle_word(const FrameParams &P, FrameSmem &S, const uint64_t *p,
+                                             uint64_t w, uint32_t tag) {
+    if ((uint32_t)(w >> 32) == tag) return __uint_as_float((uint32_t)w);
+    float v[1] = {0.0f};
+    const bool pr[1] = {true};
+    if (!poll_tagged<1>(p, 0, tag, v, pr, P.err, P.abort_flag)) S.abort = 1;
+    return v[0];
+}
+
+// Polls the tagged vector src[0..n) (n <= kXMax) into dst.
+__device__ __forceinline__ void poll_vector(const FrameParams &P, FrameSmem &S, const uint64_t *src,
+                                            int n, uint32_t tag, float *dst, int tid) {
+    constexpr int UH = kXMax / kNT / 2;  // two rounds of loads at most
+    poll_to_smem<UH>(P, S, src, 0, n, tag, dst, tid);
+    if (n > UH * kNT) poll_to_smem<UH>(P, S, src, UH * kNT, n, tag, dst, tid);
+}
+
+// Argmax over the tagged logits src[0..n) (n <= kXMax, staged through xs);
+// ties keep the larger index (the last maximum, code_predictor.rs:336-339).
+// Identical on every SM.
+__device__ int block_argmax(const FrameParams &P, const uint64_t *src, int n, uint32_t tag,
+                            FrameSmem &S, int tid) {
+    float *xs = S.u.xs;
+    poll_vector(P, S, src, n, tag, xs, tid);
     float bv = -INFINITY;
     int bi = -1;
-#pragma unroll
-    for (int m = 0; m < U; m++) {
-        const int i = tid + m * kNT;
-        if (4 * i < n) {
-            const float e[4] = {v[m].x, v[m].y, v[m].z, v[m].w};
-#pragma unroll
-            for (int c = 0; c < 4; c++) {
-                if (e[c] != e[c]) raise_error(P.err, kDevNaN);
-                if (bi < 0 || e[c] > bv || (e[c] == bv && 4 * i + c > bi)) {
-                    bv = e[c];
-                    bi = 4 * i + c;
-                }
-            }
+    for (int i = tid; i < n; i += kNT) {
+        const float v = xs[i];
+        if (v != v) raise_error(P.err, kDevNaN);
+        if (bi < 0 || v > bv || (v == bv && i > bi)) {
+            bv = v;
+            bi = i;
         }
     }
 #pragma unroll
@@ -261,91 +356,84 @@ __device__ __forceinline__ float emb_at(const EmbWord &e, int c) {
     return __fmul_rn(e.sc, (float)((int)((e.w >> (4 * c)) & 15u) - 8));
 }
 
-// Writes this SM's slice of x (the participating SMs partition [0, K)).
-__device__ __forceinline__ void save_slice(const GemvDesc &d, const float *xs, int j0, int n_items,
-                                           int grid, int tid) {
+// This SM's slice of [0, K) (the SMs with items in the op partition it).
+__device__ __forceinline__ void my_slice(int K, int j0, int n_items, int grid, int &lo, int &hi) {
     const int parts = min(n_items, grid);
-    const int a = (int)((int64_t)j0 * d.K / parts), b = (int)((int64_t)(j0 + 1) * d.K / parts);
-    for (int k = a + tid; k < b; k += kNT) __stcg(d.save + k, xs[k]);
+    lo = (int)((int64_t)j0 * K / parts);
+    hi = (int)((int64_t)(j0 + 1) * K / parts);
+}
+
+constexpr int kGammaPre = 8;  // gamma values per thread fetched before the input wait
+
+// Applies rms_norm_f16 (gemv.rs:445-454) to xs[0..K) in place:
+// x * (1 / sqrt(ss / K + 1e-6)) * gamma.  The first kGammaPre values per
+// thread come from gm[] (prefetched by the caller).
+__device__ __forceinline__ void norm_strided(float *xs, const __half *gamma, int K, float ss,
+                                             const float (&gm)[kGammaPre], int tid) {
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-6f)));
+#pragma unroll
+    for (int m = 0; m < kGammaPre; m++) {
+        const int k = tid + m * kNT;
+        if (k < K) xs[k] = __fmul_rn(__fmul_rn(xs[k], inv), gm[m]);
+    }
+    for (int k = tid + kGammaPre * kNT; k < K; k += kNT)
+        xs[k] = __fmul_rn(__fmul_rn(xs[k], inv), __half2float(__ldg(gamma + k)));
 }
 
 // Builds the GEMV input x[0..kpad) in shared memory (rows >= K are zero).
-__device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &S, int tid,
+__device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &S, int tid,
                             bool leader, int j0, int n_items, int grid) {
     float *xs = S.u.xs;
     const int K = d.K;
+    // gamma is immutable: its first loads go out before any wait
+    float gm[kGammaPre];
+#pragma unroll
+    for (int m = 0; m < kGammaPre; m++) {
+        const int k = tid + m * kNT;
+        gm[m] = (d.gamma && k < K) ? __half2float(__ldg(d.gamma + k)) : 0.0f;
+    }
+    if (d.dep) {
+        // ordering only: the values land in xs and are overwritten below
+        poll_vector(P, S, d.dep, d.dep_n, P.tag_base + d.dep_tag, xs, tid);
+        csync();
+    }
+    for (int k = K + tid; k < d.kpad; k += kNT) xs[k] = 0.0f;
+    float ss = 0.0f;
     switch (d.in_mode) {
         case IN_VEC: {
-            // x in 8-float chunks (K is a multiple of 32); every load of the
-            // thread (x, gamma, one sum-of-squares partial) in flight together
-            constexpr int U = kXMax / 8 / kNT;
-            const float4 *src = reinterpret_cast<const float4 *>(d.in);
-            const uint4 *gm = reinterpret_cast<const uint4 *>(d.gamma);
-            const int K8 = K >> 3;
-            float4 v[U][2];
-            uint4 gv[U];
-#pragma unroll
-            for (int m = 0; m < U; m++) {
-                const int w = tid + m * kNT;
-                if (w < K8) {
-                    v[m][0] = __ldcg(src + 2 * w);
-                    v[m][1] = __ldcg(src + 2 * w + 1);
-                    if (d.gamma) gv[m] = __ldg(gm + w);
-                }
+            float ssp = 0.0f;
+            // the sum-of-squares word goes out with the input loads
+            const bool has_ss = d.gamma && tid < (K >> 5);
+            const uint64_t ssw = has_ss ? ld_relaxed_u64(d.ss_in + tid) : 0ull;
+            if (d.in_plain) {
+                for (int k = tid; k < K; k += kNT) xs[k] = __ldcg(d.in_plain + k);
+            } else {
+                poll_vector(P, S, d.in, K, P.tag_base + d.in_tag, xs, tid);
             }
-            const float ssp = (d.gamma && tid < (K >> 5)) ? __ldcg(d.ss_in + tid) : 0.0f;
-            float inv = 1.0f;
-            if (d.gamma) {
-                // the producer's per-32-column sums of squares (K / 32 <= kNT of
-                // them), summed by the fixed block tree: rms_norm_f16's
-                // inv = 1 / sqrt(sum(x^2) / K + 1e-6)
-                const float ssum = block_sum(ssp, S, tid);
-                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ssum, (float)K), 1e-6f)));
-            }
-            const bool pre_save = d.save && !d.save_normed;
-#pragma unroll
-            for (int m = 0; m < U; m++) {
-                const int w = tid + m * kNT;
-                if (w < K8) {
-                    float e[8] = {v[m][0].x, v[m][0].y, v[m][0].z, v[m][0].w,
-                                  v[m][1].x, v[m][1].y, v[m][1].z, v[m][1].w};
-                    if (pre_save) {
-                        // this SM's slice of the un-normalised input
-                        const int parts = min(n_items, grid);
-                        const int lo = (int)((int64_t)j0 * K / parts), hi = (int)((int64_t)(j0 + 1) * K / parts);
-#pragma unroll
-                        for (int c = 0; c < 8; c++)
-                            if (8 * w + c >= lo && 8 * w + c < hi) __stcg(d.save + 8 * w + c, e[c]);
-                    }
-                    if (d.gamma) {
-                        const __half *gh = reinterpret_cast<const __half *>(&gv[m]);
-#pragma unroll
-                        for (int c = 0; c < 8; c++) e[c] = __fmul_rn(__fmul_rn(e[c], inv), __half2float(gh[c]));
-                    }
-                    reinterpret_cast<float4 *>(xs)[2 * w] = make_float4(e[0], e[1], e[2], e[3]);
-                    reinterpret_cast<float4 *>(xs)[2 * w + 1] = make_float4(e[4], e[5], e[6], e[7]);
-                }
-            }
-            for (int k = K + tid; k < d.kpad; k += kNT) xs[k] = 0.0f;
+            if (has_ss) ssp = settle_word(P, S, d.ss_in + tid, ssw, P.tag_base + d.ss_tag);
             csync();
-            if (d.save && d.save_normed) save_slice(d, xs, j0, n_items, grid, tid);
-            return;
+            if (d.gamma) ss = block_sum(ssp, S, tid);
+            break;
         }
         case IN_EMB: {
             uint32_t code;
             if (d.amax_src) {
-                code = (uint32_t)block_argmax(P, d.amax_src, d.amax_n, S, tid);
-                if (leader && tid == 0 && d.code_dst) __stcg(d.code_dst, code);
-            } else {
-                code = __ldcg(d.code_src);
-            }
-            for (int w = tid; w < (d.kpad >> 3); w += kNT) {
-                float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                if (8 * w < K) {
-                    const EmbWord e = emb_word(d.emb, code, w);
-#pragma unroll
-                    for (int c = 0; c < 8; c++) o[c] = emb_at(e, c);
+                code = (uint32_t)block_argmax(P, d.amax_src, d.amax_n, P.tag_base + d.amax_tag, S, tid);
+                if (leader && tid == 0 && d.code_dst) {
+                    st_relaxed_u64(d.code_dst, tag_pack(__uint_as_float(code), P.tag_base + d.out_tag));
                 }
+            } else {
+                float c[1];
+                const bool pr[1] = {true};
+                if (!poll_tagged<1>(d.code_src, 0, P.tag_base + d.code_tag, c, pr, P.err, P.abort_flag))
+                    S.abort = 1;
+                code = __float_as_uint(c[0]);
+            }
+            for (int w = tid; w < (K >> 3); w += kNT) {
+                const EmbWord e = emb_word(d.emb, code, w);
+                float o[8];
+#pragma unroll
+                for (int c = 0; c < 8; c++) o[c] = emb_at(e, c);
                 reinterpret_cast<float4 *>(xs)[2 * w] = make_float4(o[0], o[1], o[2], o[3]);
                 reinterpret_cast<float4 *>(xs)[2 * w + 1] = make_float4(o[4], o[5], o[6], o[7]);
             }
@@ -353,40 +441,61 @@ __device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &
         }
         case IN_FRAME: {
             const FrameEmbed &fe = P.fe;
-            const uint32_t last = (uint32_t)block_argmax(P, d.amax_src, d.amax_n, S, tid);
-            if (leader && tid == 0) {
-                __stcg(fe.codes + fe.ngroups, last);
-                for (int g = 1; g < fe.ngroups; g++) __stcg(fe.prev + g, __ldcg(fe.codes + g));
-                __stcg(fe.prev + fe.ngroups, last);
-            }
-            const uint32_t c0 = __ldcg(fe.codes);
-            for (int w = tid; w < (d.kpad >> 3); w += kNT) {
-                float o[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                if (8 * w < K) {
-                    // every load of the 8 columns in flight before the sums
-                    EmbWord e[kMaxEmbedGroups];
-#pragma unroll
-                    for (int g = 0; g < kMaxEmbedGroups; g++) {
-                        if (g < fe.ngroups) {
-                            const uint32_t cg = g + 1 < fe.ngroups ? __ldcg(fe.codes + g + 1) : last;
-                            e[g] = emb_word(fe.pred[g], cg, w);
-                        }
+            const uint32_t last =
+                (uint32_t)block_argmax(P, d.amax_src, d.amax_n, P.tag_base + d.amax_tag, S, tid);
+            // codes 0 .. ngroups-1, each tagged by the op that produced it:
+            // thread g polls code g
+            if (tid < fe.ngroups) {
+                const uint32_t tg = P.tag_base + fe.code_tag[tid];
+                const uint64_t t0 = global_ns();
+                for (int it = 0;; it++) {
+                    const uint64_t w = ld_relaxed_u64(fe.codes_t + tid);
+                    if ((uint32_t)(w >> 32) == tg) {
+                        S.codes_s[tid] = (uint32_t)w;
+                        break;
                     }
-                    const EmbWord et = emb_word(fe.talker, c0, w);
-                    const float4 t0 = __ldcg(reinterpret_cast<const float4 *>(P.text) + 2 * w);
-                    const float4 t1 = __ldcg(reinterpret_cast<const float4 *>(P.text) + 2 * w + 1);
-                    const float tx[8] = {t0.x, t0.y, t0.z, t0.w, t1.x, t1.y, t1.z, t1.w};
-#pragma unroll
-                    for (int c = 0; c < 8; c++) {
-                        // (E_talker[c0] + (sum_g E_g[c_{g+1}])) + text, as the engine's frame embed
-                        float acc = 0.0f;
-#pragma unroll
-                        for (int g = 0; g < kMaxEmbedGroups; g++)
-                            if (g < fe.ngroups) acc = __fadd_rn(acc, emb_at(e[g], c));
-                        acc = __fadd_rn(emb_at(et, c), acc);
-                        o[c] = __fadd_rn(acc, tx[c]);
+                    if ((it & 15) == 15 && (ld_volatile(P.abort_flag) || global_ns() - t0 > kWaitNs)) {
+                        raise_abort(P, S, kDevTimeout);
+                        S.codes_s[tid] = 0;
+                        break;
                     }
                 }
+            }
+            csync();
+            uint32_t cg[kMaxEmbedGroups];
+#pragma unroll
+            for (int g = 0; g < kMaxEmbedGroups; g++) cg[g] = g < fe.ngroups ? S.codes_s[g] : 0u;
+            if (leader && tid == 0) {
+                // the frame's codes for the host and the repetition-penalty window
+                for (int g = 0; g < fe.ngroups; g++) fe.codes[g] = cg[g];
+                fe.codes[fe.ngroups] = last;
+                for (int g = 1; g < fe.ngroups; g++) fe.prev[g] = cg[g];
+                fe.prev[fe.ngroups] = last;
+            }
+            for (int w = tid; w < (K >> 3); w += kNT) {
+                const EmbWord et = emb_word(fe.talker, cg[0], w);
+                const float4 t0v = __ldcg(reinterpret_cast<const float4 *>(P.text) + 2 * w);
+                const float4 t1v = __ldcg(reinterpret_cast<const float4 *>(P.text) + 2 * w + 1);
+                float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                // (E_talker[c0] + (sum_g E_g[c_{g+1}])) + text, as the engine's
+                // frame embed; tables in two halves, each half's loads in flight together
+#pragma unroll
+                for (int h = 0; h < kMaxEmbedGroups; h += kMaxEmbedGroups / 2) {
+                    EmbWord e[kMaxEmbedGroups / 2];
+#pragma unroll
+                    for (int g = 0; g < kMaxEmbedGroups / 2; g++)
+                        if (h + g < fe.ngroups)
+                            e[g] = emb_word(fe.pred[h + g], h + g + 1 < fe.ngroups ? cg[h + g + 1] : last, w);
+#pragma unroll
+                    for (int g = 0; g < kMaxEmbedGroups / 2; g++)
+                        if (h + g < fe.ngroups)
+#pragma unroll
+                            for (int c = 0; c < 8; c++) acc[c] = __fadd_rn(acc[c], emb_at(e[g], c));
+                }
+                const float tx[8] = {t0v.x, t0v.y, t0v.z, t0v.w, t1v.x, t1v.y, t1v.z, t1v.w};
+                float o[8];
+#pragma unroll
+                for (int c = 0; c < 8; c++) o[c] = __fadd_rn(__fadd_rn(emb_at(et, c), acc[c]), tx[c]);
                 reinterpret_cast<float4 *>(xs)[2 * w] = make_float4(o[0], o[1], o[2], o[3]);
                 reinterpret_cast<float4 *>(xs)[2 * w + 1] = make_float4(o[4], o[5], o[6], o[7]);
             }
@@ -394,30 +503,27 @@ __device__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &
         }
     }
     csync();
-    if (d.save && !d.save_normed) save_slice(d, xs, j0, n_items, grid, tid);
-    if (d.gamma) {
-        constexpr int U = kXMax / 8 / kNT;
-        const uint4 *gm = reinterpret_cast<const uint4 *>(d.gamma);
-        uint4 gv[U];
-#pragma unroll
-        for (int m = 0; m < U; m++)
-            if (tid + m * kNT < (K >> 3)) gv[m] = __ldg(gm + tid + m * kNT);
+    if (d.in_mode != IN_VEC && d.gamma) {
         float t = 0.0f;
         for (int k = tid; k < K; k += kNT) t += __fmul_rn(xs[k], xs[k]);
-        const float ss = block_sum(t, S, tid);
-        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), 1e-6f)));
-#pragma unroll
-        for (int m = 0; m < U; m++) {
-            const int w = tid + m * kNT;
-            if (w < (K >> 3)) {
-                const __half *gh = reinterpret_cast<const __half *>(&gv[m]);
-#pragma unroll
-                for (int c = 0; c < 8; c++) xs[8 * w + c] = __fmul_rn(__fmul_rn(xs[8 * w + c], inv), __half2float(gh[c]));
-            }
-        }
+        ss = block_sum(t, S, tid);
+    }
+    if (d.save) {
+        // this SM's slice of the un-normalised input, published as tagged words
+        int lo, hi;
+        my_slice(K, j0, n_items, grid, lo, hi);
+        for (int k = lo + tid; k < hi; k += kNT) st_relaxed_u64(d.save + k, tag_pack(xs[k], P.tag_base + d.out_tag));
+    }
+    if (d.gamma) {
+        csync();  // the save above read xs before it is normalised
+        norm_strided(xs, d.gamma, K, ss, gm, tid);
         csync();
     }
-    if (d.save && d.save_normed) save_slice(d, xs, j0, n_items, grid, tid);
+    if (d.save_plain) {
+        int lo, hi;
+        my_slice(K, j0, n_items, grid, lo, hi);
+        for (int k = lo + tid; k < hi; k += kNT) __stcg(d.save_plain + k, xs[k]);
+    }
 }
 
 // One weight row of one 32-column group: acc += s' * nibbles, with
@@ -444,63 +550,58 @@ __device__ __forceinline__ void row_fma(uint64_t (&acc)[16], float &ssum, float 
     }
 }
 
-// The items of one GEMV op on this SM, G groups per unit, all K rows each.
-template <int G>
+// The items of one GEMV op on this SM: each unit's G groups (1, or the
+// gate / up pair) in turn, all K rows each.
 __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef &op, FrameSmem &S,
                            int tid, int cta, int grid, uint32_t &q, int &rbuf, bool tr, int op_i) {
     uint64_t waited = 0, slots = 0, comp = 0, redc = 0;
     const int lane = tid & 31, warp = tid >> 5;
-    constexpr int CR = G == 1 ? 1024 : 512;
     const float *xs = S.u.xs;
+    const uint32_t otag = P.tag_base + d.out_tag;
     for (int u = first_item(cta, op.rot, grid); u < op.n_items; u += grid) {
-        // the epilogue's residual / bias values, fetched while the item computes
+        // the epilogue's residual / bias value, fetched while the item computes
         float pre = 0.0f;
-        if (G == 1 && warp == 0) {
+        uint64_t prew = 0;
+        if (warp == 0) {
             const int64_t col = (int64_t)u * 32 + lane;
-            if (d.out_mode == OUT_RESID) pre = __ldcg(d.resid + col);
+            if (d.out_mode == OUT_RESID) prew = ld_relaxed_u64(d.resid + col);  // checked at the epilogue
             else if (d.bias) pre = __ldg(d.bias + col);
         }
-        uint64_t acc[G][16];
-        float ssum[G];
+        float y[2] = {0.0f, 0.0f};  // warp 0: the unit's group totals, lane = column
+        for (int g = 0; g < d.G; g++) {
+            uint64_t acc[16];
+            float ssum = 0.0f;
 #pragma unroll
-        for (int g = 0; g < G; g++) {
-            ssum[g] = 0.0f;
-#pragma unroll
-            for (int i = 0; i < 16; i++) acc[g][i] = 0ull;
-        }
-        for (int c0 = 0; c0 < d.kpad; c0 += CR) {
-            const int rows = min(CR, d.kpad - c0);
-            const int slot = q % kSlots;
-            // on a failed wait the thread skips the slot but keeps to the
-            // block's barrier sequence; the op ends with a uniform abort check
-            const long long tw = tr ? clock64() : 0;
-            const bool ok = mbar_wait_or_abort(&S.full[slot], (q / kSlots) & 1, S, P);
-            long long tc = 0;
-            if (tr) {
-                tc = clock64();
-                waited += (uint64_t)(tc - tw);
-                slots++;
+            for (int i = 0; i < 16; i++) acc[i] = 0ull;
+            for (int c0 = 0; c0 < d.kpad; c0 += kChunkRows) {
+                const int rows = min(kChunkRows, d.kpad - c0);
+                const int slot = q % kSlots;
+                const long long tw = tr ? clock64() : 0;
+                // on a failed wait the thread skips the slot but keeps to the
+                // block's barrier sequence; the op ends with a uniform abort check
+                const bool ok = mbar_wait_or_abort(&S.full[slot], (q / kSlots) & 1, S, P);
+                long long tc = 0;
+                if (tr) {
+                    tc = clock64();
+                    waited += (uint64_t)(tc - tw);
+                    slots++;
+                }
+                const uint4 *nb = reinterpret_cast<const uint4 *>(S.nib[slot]);
+                const __half *sb = reinterpret_cast<const __half *>(S.scl[slot]);
+                for (int lr = tid; ok && lr < rows; lr += kNT) {
+                    const float x75 = __fmul_rn(xs[c0 + lr], 37778931862957161709568.0f);
+                    row_fma(acc, ssum, __fmul_rn(__half2float(sb[lr]), x75), nb[lr]);
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&S.empty[slot]);
+                if (tr) comp += (uint64_t)(clock64() - tc);
+                q++;
             }
-            const uint4 *nb = reinterpret_cast<const uint4 *>(S.nib[slot]);
-            const __half *sb = reinterpret_cast<const __half *>(S.scl[slot]);
-            for (int lr = tid; ok && lr < rows; lr += kNT) {
-                const float x75 = __fmul_rn(xs[c0 + lr], 37778931862957161709568.0f);
-#pragma unroll
-                for (int g = 0; g < G; g++)
-                    row_fma(acc[g], ssum[g], __fmul_rn(__half2float(sb[g * rows + lr]), x75), nb[g * rows + lr]);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&S.empty[slot]);
-            if (tr) comp += (uint64_t)(clock64() - tc);
-            q++;
-        }
-        const long long tr0 = tr ? clock64() : 0;
-        // butterfly reduce-scatter: lane l ends with the warp's total of column l
-#pragma unroll
-        for (int g = 0; g < G; g++) {
+            const long long tr0 = tr ? clock64() : 0;
+            // butterfly reduce-scatter: lane l ends with the warp's total of column l
             float v[32];
 #pragma unroll
-            for (int i = 0; i < 16; i++) upk2(acc[g][i], v[2 * i], v[2 * i + 1]);
+            for (int i = 0; i < 16; i++) upk2(acc[i], v[2 * i], v[2 * i + 1]);
 #pragma unroll
             for (int sft = 16; sft >= 1; sft >>= 1) {
                 const bool upper = (lane & sft) != 0;
@@ -512,37 +613,39 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
                 }
             }
             // column l sits at nibble position l % 4: y = 2^(74-4p) acc - 8 * 2^-75 * sum(s')
-            const float stot = warp_sum(ssum[g]);
+            const float stot = warp_sum(ssum);
             const float up = __int_as_float((127 + 74 - 4 * (lane & 3)) << 23);
-            S.red[rbuf][warp][g][lane] = __fsub_rn(__fmul_rn(v[0], up), __fmul_rn(stot, 2.117582368135751e-22f));
-        }
-        csync();
-        if (warp == 0) {
-            float y[G];
-#pragma unroll
-            for (int g = 0; g < G; g++) {
+            S.red[rbuf][warp][lane] = __fsub_rn(__fmul_rn(v[0], up), __fmul_rn(stot, 2.117582368135751e-22f));
+            csync();
+            if (warp == 0) {
                 float t = 0.0f;
 #pragma unroll
-                for (int w = 0; w < kNT / 32; w++) t += S.red[rbuf][w][g][lane];
-                y[g] = t;
+                for (int w = 0; w < kNT / 32; w++) t += S.red[rbuf][w][lane];
+                if (g == 0) y[0] = t;
+                else y[1] = t;
             }
-            if constexpr (G == 2) {
+            rbuf ^= 1;
+            if (tr) redc += (uint64_t)(clock64() - tr0);
+        }
+        if (warp == 0) {
+            if (d.out_mode == OUT_SWIGLU) {
                 // SwiGLU unit: group 2u is gate, 2u+1 is up (talker.rs:341-345)
-                __stcg(d.out + (int64_t)u * 32 + lane, __fmul_rn(silu_ref(y[0]), y[1]));
+                st_relaxed_u64(d.out + (int64_t)u * 32 + lane, tag_pack(__fmul_rn(silu_ref(y[0]), y[1]), otag));
             } else {
                 const int64_t col = (int64_t)u * 32 + lane;
                 float o = y[0];
-                if (d.out_mode == OUT_RESID) o = __fadd_rn(pre, o);  // x += attn / mlp
-                else if (d.bias) o = __fadd_rn(o, pre);
-                __stcg(d.out + col, o);
+                if (d.out_mode == OUT_RESID)  // x += attn / mlp
+                    o = __fadd_rn(settle_word(P, S, d.resid + col, prew, P.tag_base + d.resid_tag), o);
+                else if (d.bias)
+                    o = __fadd_rn(o, pre);
+                if (d.out) st_relaxed_u64(d.out + col, tag_pack(o, otag));
+                else __stcg(d.out_plain + col, o);
                 if (d.ss_out) {
                     const float sq = warp_sum(__fmul_rn(o, o));
-                    if (lane == 0) __stcg(d.ss_out + u, sq);
+                    if (lane == 0) st_relaxed_u64(d.ss_out + u, tag_pack(sq, otag));
                 }
             }
         }
-        rbuf ^= 1;
-        if (tr) redc += (uint64_t)(clock64() - tr0);
     }
     if (tr) {
         P.trace[(int64_t)op_i * kTraceFields + 4] = waited;
@@ -562,9 +665,8 @@ __device__ __forceinline__ void attn_items(const AttnArgs &a, const OpRef &op, A
     }
 }
 
-__device__ void run_attn(const FrameParams &P, const OpRef &op, FrameSmem &S, int tid, int cta,
-                         int grid) {
-    const AttnArgs &a = S.desc.a;
+__device__ __noinline__ void run_attn(const AttnArgs &a, const OpRef &op, FrameSmem &S, int tid, int cta,
+                                     int grid) {
     const int G = a.heads / a.kv_heads;
     if (a.kv.head_dim == 128) {
         if (G == 1) attn_items<128, 1>(a, op, S.u.a128_1, tid, cta, grid);
@@ -577,72 +679,87 @@ __device__ void run_attn(const FrameParams &P, const OpRef &op, FrameSmem &S, in
     }
 }
 
+// The sampler op (kept out of line: cold code, its own register budget).
+__device__ __noinline__ void run_sample(const FrameParams &P, FrameSmem &S, int tid) {
+    samp::sample_row<kNT, 1>(P.sample, 0, tid, S.u.samp);
+}
+
+// Next op after `i` that has items on this SM (n_ops if none).
+__device__ __forceinline__ int next_op(const FrameSmem &S, int i, int n_ops, int cta, int grid) {
+    for (int k = i + 1; k < n_ops; k++)
+        if (first_item(cta, S.ops[k].rot, grid) < S.ops[k].n_items) return k;
+    return n_ops;
+}
+
+// Threads 32.. start copying op i's descriptor into slot b (cp.async).
+__device__ __forceinline__ void stage_issue(const FrameParams &P, FrameSmem &S, int i, int b, int tid) {
+    const OpRef &op = S.ops[i];
+    if (op.type == OP_SAMPLE) return;
+    const uint4 *src = op.type == OP_GEMV ? reinterpret_cast<const uint4 *>(P.gemv + op.idx)
+                                          : reinterpret_cast<const uint4 *>(P.attn + op.idx);
+    const int nw = (op.type == OP_GEMV ? (int)sizeof(GemvDesc) : (int)sizeof(AttnArgs)) / 16;
+    const int k = tid - 32;
+    if (k >= 0 && k < nw) cp_async16(&S.desc[b].words[k], src + k);
+}
+
+// The staging threads wait for their copies; attention descriptors get this
+// launch's tag base (the thread that copied that word patches it).
+__device__ __forceinline__ void stage_wait(const FrameParams &P, FrameSmem &S, int i, int b, int tid) {
+    const OpRef &op = S.ops[i];
+    if (op.type == OP_SAMPLE) return;
+    const int nw = (op.type == OP_GEMV ? (int)sizeof(GemvDesc) : (int)sizeof(AttnArgs)) / 16;
+    const int k = tid - 32;
+    if (k >= 0 && k < nw) {
+        cp_async_commit_wait();
+        if (op.type == OP_ATTN && k == (int)(offsetof(AttnArgs, tag_base) / 16))
+            S.desc[b].a.tag_base = P.tag_base;
+    }
+}
+
 __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, int grid) {
-    const unsigned target = (unsigned)grid;
     uint32_t q = 0;
-    int rbuf = 0;
-    for (int i = 0; i < P.n_ops; i++) {
-        const OpRef op = P.ops[i];
+    int rbuf = 0, b = 0;
+    int i = next_op(S, -1, P.n_ops, cta, grid);
+    if (i < P.n_ops) stage_issue(P, S, i, b, tid);
+    while (i < P.n_ops) {
+        const OpRef op = S.ops[i];
         const int j0 = first_item(cta, op.rot, grid);
         const bool tr = P.trace && j0 == 0 && tid == 0;
-        if (j0 < op.n_items) {
-            // stage the descriptor (immutable) while thread 0 polls below;
-            // the barrier after the poll publishes it
-            if (op.type != OP_SAMPLE) {
-                const uint4 *src = op.type == OP_GEMV ? reinterpret_cast<const uint4 *>(P.gemv + op.idx)
-                                                      : reinterpret_cast<const uint4 *>(P.attn + op.idx);
-                const int nw = (op.type == OP_GEMV ? (int)sizeof(GemvDesc) : (int)sizeof(AttnArgs)) / 16;
-                if (tid >= 32 && tid - 32 < nw) S.desc.words[tid - 32] = __ldg(src + (tid - 32));
+        const bool ta = P.trace && tid == 0;  // every SM: across-SM stamps
+        stage_wait(P, S, i, b, tid);
+        csync();
+        const int nx = next_op(S, i, P.n_ops, cta, grid);
+        if (nx < P.n_ops) stage_issue(P, S, nx, b ^ 1, tid);  // lands while op i runs
+        stamp_all(P, i, 3, ta);
+        if (op.type == OP_GEMV) {
+            const GemvDesc &d = S.desc[b].g;
+            build_input(P, d, S, tid, j0 == 0, j0, op.n_items, grid);
+            stamp_all(P, i, 0, ta);
+            stamp_all(P, i, 1, ta);
+            gemv_items(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);
+            if (d.adv_len && j0 == 0 && tid == 0) {
+                // end of the talker step: the cache and RoPE position advance
+                d.adv_len[0] += 1;
+                d.adv_pos[0] += 1;
             }
-            if (i > 0) {
-                // every SM has finished op i-1 (bounded wait, abort-aware)
-                if (tid == 0) {
-                    const uint64_t t0 = global_ns();
-                    for (int it = 0; ld_acquire(P.done + i - 1) < target; it++) {
-                        if ((it & 31) == 31) {
-                            if (ld_volatile(P.abort_flag)) {
-                                S.abort = 1;
-                                break;
-                            }
-                            if (global_ns() - t0 > kWaitNs) {
-                                raise_abort(P, S, kDevTimeout);
-                                break;
-                            }
-                        }
-                    }
-                }
+        } else if (op.type == OP_ATTN) {
+            stamp_all(P, i, 0, ta);  // (the q/k/v wait is inside the items)
+            stamp_all(P, i, 1, ta);
+            run_attn(S.desc[b].a, op, S, tid, cta, grid);
+        } else {
+            stamp_all(P, i, 0, ta);
+            stamp_all(P, i, 1, ta);
+            run_sample(P, S, tid);
+            if (tid == 0) {
+                // code 0 for the predictor's semantic pass, tagged
+                st_relaxed_u64(P.code0_t, tag_pack(__uint_as_float((uint32_t)S.u.samp.out_code), P.tag_base + i + 1));
             }
-            csync();
-            if (*(volatile int *)&S.abort) return;
-            stamp(P, i, 0, tr);
-            if (op.type == OP_GEMV) {
-                const GemvDesc &d = S.desc.g;
-                build_input(P, d, S, tid, j0 == 0, j0, op.n_items, grid);
-                stamp(P, i, 1, tr);
-                if (d.G == 1) gemv_items<1>(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);
-                else gemv_items<2>(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);
-                csync();
-                if (*(volatile int *)&S.abort) return;
-                if (d.adv_len && j0 == 0 && tid == 0) {
-                    // end of the talker step: the cache and RoPE position advance
-                    d.adv_len[0] += 1;
-                    d.adv_pos[0] += 1;
-                }
-            } else if (op.type == OP_ATTN) {
-                stamp(P, i, 1, tr);
-                run_attn(P, op, S, tid, cta, grid);
-            } else {
-                stamp(P, i, 1, tr);
-                samp::sample_row<kNT, 1>(P.sample, 0, tid, S.u.samp);
-            }
-            stamp(P, i, 2, tr);
         }
         csync();
-        if (tid == 0) {
-            __threadfence();
-            atomicAdd(P.done + i, 1u);
-        }
-        stamp(P, i, 3, tr);
+        stamp_all(P, i, 2, ta);
+        if (*(volatile int *)&S.abort) return;
+        b ^= 1;
+        i = nx;
     }
 }
 
@@ -658,6 +775,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_frame(const __grid_constant__ F
         S.abort = 0;
         mbar_fence_init();
     }
+    for (int i = tid; i < P.n_ops; i += kThreads)
+        reinterpret_cast<uint4 *>(S.ops)[i] = __ldg(reinterpret_cast<const uint4 *>(P.ops) + i);
     __syncthreads();
     if (tid >= kNT) {
         if (tid == kNT) producer(P, S, blockIdx.x, gridDim.x);
@@ -696,7 +815,8 @@ struct Builder {
     int grid;
     int64_t items_total = 0;
 
-    void push(int type, int idx, int n_items) {
+    // appends an op; returns its tag (op index + 1, relative to the launch)
+    uint32_t push(int type, int idx, int n_items) {
         OpRef r;
         r.type = type;
         r.idx = idx;
@@ -704,20 +824,24 @@ struct Builder {
         r.rot = (int)(items_total % grid);
         items_total += n_items;
         fp->ops.push_back(r);
+        return (uint32_t)fp->ops.size();
     }
-    void gemv(GemvDesc d, const Q4Dev &w, int G) {
+    uint32_t next_tag() const { return (uint32_t)fp->ops.size() + 1; }
+    uint32_t gemv(GemvDesc d, const Q4Dev &w, int G) {
         d.nib = w.nib;
         d.scl = w.scl;
         d.kpad = (int)w.kpad;
         d.K = (int)w.k;
         d.G = G;
         d.units = (int)(w.C / G);
+        d.out_tag = next_tag();
         fp->gemv.push_back(d);
-        push(OP_GEMV, (int)fp->gemv.size() - 1, d.units);
+        return push(OP_GEMV, (int)fp->gemv.size() - 1, d.units);
     }
-    void attn(const AttnArgs &a, int per_head) {
+    uint32_t attn(AttnArgs a, int per_head) {
+        a.out_tag = next_tag();
         fp->attn.push_back(a);
-        push(OP_ATTN, (int)fp->attn.size() - 1, a.kv_heads * per_head);
+        return push(OP_ATTN, (int)fp->attn.size() - 1, a.kv_heads * per_head);
     }
 };
 
@@ -732,44 +856,56 @@ int frame_build(qora_engine *e, FrameProgram **out) {
     fp->smem = sizeof(FrameSmem);
     int rc = QORA_OK;
 
-    // ---- activation buffers (one allocation, 256-byte aligned pieces)
+    // ---- tagged activation buffers (8 bytes per value) and attention scratch
     const int Hm = std::max(t->H, p->H);
     const int qkvm = (int)std::max(t->qkvn(), (int64_t)(p->heads + 2 * p->kvh) * p->hd);
     const int qdm = (int)std::max(t->qd(), (int64_t)p->heads * p->hd);
     const int ffm = std::max(t->ffn, p->ffn);
     const int kvh_m = std::max(t->kvh, p->kvh);
     size_t off = 0;
-    auto take = [&](size_t floats) {
+    auto take = [&](size_t bytes) {
         const size_t o = off;
-        off += (floats * 4 + 255) / 256 * 256;
+        off += (bytes + 255) / 256 * 256;
         return o;
     };
-    const size_t o_qkv = take(qkvm), o_attn = take(qdm), o_xa = take(Hm), o_xb = take(Hm),
-                 o_ssa = take(Hm / 32), o_ssb = take(Hm / 32), o_h = take(ffm),
-                 o_head = take(p->vocab),
-                 o_apo = take(std::max(attn_part_o_floats(1, t->kvh, t->heads, t->hd),
-                                       attn_part_o_floats(1, p->kvh, p->heads, p->hd))),
-                 o_apml = take(std::max(attn_part_ml_floats(1, t->kvh, t->heads),
-                                        attn_part_ml_floats(1, p->kvh, p->heads))),
-                 o_atk = take(kvh_m);
+    const size_t o_qkv = take(8 * qkvm), o_attn = take(8 * qdm), o_xa = take(8 * Hm),
+                 o_xb = take(8 * Hm), o_ssa = take(8 * (Hm / 32)), o_ssb = take(8 * (Hm / 32)),
+                 o_h = take(8 * ffm), o_head = take(8 * p->vocab), o_codes = take(8 * 16),
+                 o_apo = take(4 * std::max(attn_part_o_floats(1, t->kvh, t->heads, t->hd),
+                                           attn_part_o_floats(1, p->kvh, p->heads, p->hd))),
+                 o_apml = take(4 * std::max(attn_part_ml_floats(1, t->kvh, t->heads),
+                                            attn_part_ml_floats(1, p->kvh, p->heads))),
+                 o_atk = take(4 * kvh_m);
     rc = fp->bufs.alloc(off);
-    if (rc == QORA_OK) rc = fp->bufs.zero();
+    if (rc == QORA_OK) rc = fp->bufs.zero();  // tag 0 never matches
     if (rc != QORA_OK) {
         delete fp;
         return rc;
     }
     char *base = fp->bufs.as<char>();
-    float *qkv = (float *)(base + o_qkv), *attn_out = (float *)(base + o_attn);
-    float *xa = (float *)(base + o_xa), *xb = (float *)(base + o_xb);
-    float *ssa = (float *)(base + o_ssa), *ssb = (float *)(base + o_ssb);
-    float *hbuf = (float *)(base + o_h), *head = (float *)(base + o_head);
+    uint64_t *qkv = (uint64_t *)(base + o_qkv), *attn_out = (uint64_t *)(base + o_attn);
+    uint64_t *xa = (uint64_t *)(base + o_xa), *xb = (uint64_t *)(base + o_xb);
+    uint64_t *ssa = (uint64_t *)(base + o_ssa), *ssb = (uint64_t *)(base + o_ssb);
+    uint64_t *hbuf = (uint64_t *)(base + o_h), *head = (uint64_t *)(base + o_head);
+    uint64_t *codes_t = (uint64_t *)(base + o_codes);
     float *apo = (float *)(base + o_apo), *apml = (float *)(base + o_apml);
     unsigned *atk = (unsigned *)(base + o_atk);
+    rc = fp->d_abort.alloc(16);
+    if (rc == QORA_OK) rc = fp->d_abort.zero();
+    if (rc != QORA_OK) {
+        delete fp;
+        return rc;
+    }
+    int *abort_flag = fp->d_abort.as<int>();
 
     Builder B{fp, fp->grid};
     uint32_t *codes = e->codes.as<uint32_t>();
     uint32_t *prev = e->prev.as<uint32_t>();
     float *hidden = p->x2.as<float>();  // row 0: the talker's final-normed hidden
+
+    // the op that last wrote each tagged buffer (its tag)
+    uint32_t tag_xa = 0, tag_ssa = 0;
+    uint32_t code_tag[16] = {};
 
     // ---- op 0: code 0 = sample_token(logits)
     SampleArgs sa;
@@ -786,23 +922,28 @@ int frame_build(qora_engine *e, FrameProgram **out) {
     sa.prev_update = prev;
     sa.ldprev_update = 16;
     sa.err = ctx->err.as<int>();
-    B.push(OP_SAMPLE, 0, 1);
+    code_tag[0] = B.push(OP_SAMPLE, 0, 1);
 
     // One decoder layer (talker.rs:275-349).  The residual stream enters in xa
     // (sums of squares in ssa) unless `first` supplies the QKV input itself;
     // attention adds into xb (ssb), the MLP back into xa (ssa).
-    auto layer = [&](const LayerDev &ld, int H, int heads, int kvh, int hd, const GemvDesc *first,
-                     AttnArgs at, int per_head) {
+    auto layer = [&](const LayerDev &ld, int heads, int kvh, int hd, const GemvDesc *first, AttnArgs at,
+                     int per_head) {
         const int qkvn = (heads + 2 * kvh) * hd;
         GemvDesc q = first ? *first : GemvDesc();
         if (!first) {
             q.in = xa;
+            q.in_tag = tag_xa;
             q.ss_in = ssa;
+            q.ss_tag = tag_ssa;
         }
         q.gamma = ld.in_norm.as<__half>();
         q.out = qkv;
-        B.gemv(q, ld.qkv, 1);
-        at.qkv = qkv;
+        const uint32_t tag_qkv = B.gemv(q, ld.qkv, 1);
+        if (first && first->save == xa) tag_xa = tag_qkv;  // the frame input, saved by this op
+        at.qkv = nullptr;
+        at.qkv_t = qkv;
+        at.qkv_tag = tag_qkv;
         at.ldqkv = qkvn;
         at.heads = heads;
         at.kv_heads = kvh;
@@ -810,35 +951,42 @@ int frame_build(qora_engine *e, FrameProgram **out) {
         at.streams = 1;
         at.q_gamma = ld.q_norm.as<__half>();
         at.k_gamma = ld.k_norm.as<__half>();
-        at.out = attn_out;
+        at.out = nullptr;
+        at.out_t = attn_out;
         at.ldout = (int64_t)heads * hd;
         at.part_o = apo;
         at.part_ml = apml;
         at.tickets = atk;
         at.err = ctx->err.as<int>();
-        B.attn(at, per_head);
+        at.abort_flag = abort_flag;
+        const uint32_t tag_attn = B.attn(at, per_head);
         GemvDesc o;
         o.in = attn_out;
+        o.in_tag = tag_attn;
         o.out_mode = OUT_RESID;
         o.resid = xa;
+        o.resid_tag = tag_xa;
         o.out = xb;
         o.ss_out = ssb;
-        B.gemv(o, ld.o, 1);
+        const uint32_t tag_xb = B.gemv(o, ld.o, 1);
         GemvDesc gu;
         gu.in = xb;
+        gu.in_tag = tag_xb;
         gu.ss_in = ssb;
+        gu.ss_tag = tag_xb;
         gu.gamma = ld.post_norm.as<__half>();
         gu.out_mode = OUT_SWIGLU;
         gu.out = hbuf;
-        B.gemv(gu, ld.gu, 2);
+        const uint32_t tag_h = B.gemv(gu, ld.gu, 2);
         GemvDesc dn;
         dn.in = hbuf;
+        dn.in_tag = tag_h;
         dn.out_mode = OUT_RESID;
         dn.resid = xb;
+        dn.resid_tag = tag_xb;
         dn.out = xa;
         dn.ss_out = ssa;
-        B.gemv(dn, ld.dn, 1);
-        (void)H;
+        tag_xa = tag_ssa = B.gemv(dn, ld.dn, 1);
     };
 
     // ---- predictor: 16 single-token passes (hidden, semantic, codes 1..14);
@@ -848,40 +996,52 @@ int frame_build(qora_engine *e, FrameProgram **out) {
     pat.rope_cos = p->rope_cos.as<float>();
     pat.rope_sin = p->rope_sin.as<float>();
     pat.rope_max_pos = p->rope_max;
+    uint32_t tag_head = 0;
     for (int tk = 0; tk <= p->groups; tk++) {
         GemvDesc pr;  // project_input (code_predictor.rs:51-61) into the residual stream
         if (tk == 0) {
             pr.in_mode = IN_VEC;
-            pr.in = hidden;
+            pr.in_plain = hidden;
         } else if (tk == 1) {
             pr.in_mode = IN_EMB;
-            pr.code_src = codes;
+            pr.code_src = codes_t;
+            pr.code_tag = code_tag[0];
             pr.emb = t->codec_emb;
+            // this pass needs only code 0, so it waits for the first pass's last
+            // output before reusing its buffers and its cache position
+            pr.dep = xa;
+            pr.dep_tag = tag_xa;
+            pr.dep_n = p->H;
         } else {
             pr.in_mode = IN_EMB;
             pr.amax_src = head;
+            pr.amax_tag = tag_head;
             pr.amax_n = p->vocab;
-            pr.code_dst = codes + (tk - 1);
+            pr.code_dst = codes_t + (tk - 1);
             pr.emb = p->embs[tk - 2];
         }
         pr.out = xa;
         pr.ss_out = ssa;
         pr.bias = p->proj_bias.as<float>();
-        B.gemv(pr, p->proj, 1);
+        const uint32_t tg = B.gemv(pr, p->proj, 1);
+        if (tk >= 2) code_tag[tk - 1] = tg;
+        tag_xa = tag_ssa = tg;
         for (int l = 0; l < p->L; l++) {
             AttnArgs at = pat;
             at.kv = e->pkv->layer(l);
             at.pos_static = tk;
             at.len_static = tk;
-            layer(p->layers[l], p->H, p->heads, p->kvh, p->hd, nullptr, at, 1);
+            layer(p->layers[l], p->heads, p->kvh, p->hd, nullptr, at, 1);
         }
         if (tk >= 1) {
             GemvDesc hd;
             hd.in = xa;
+            hd.in_tag = tag_xa;
             hd.ss_in = ssa;
+            hd.ss_tag = tag_ssa;
             hd.gamma = p->final_norm.as<__half>();
             hd.out = head;
-            B.gemv(hd, p->heads_w[tk - 1], 1);
+            tag_head = B.gemv(hd, p->heads_w[tk - 1], 1);
         }
     }
 
@@ -899,21 +1059,23 @@ int frame_build(qora_engine *e, FrameProgram **out) {
             GemvDesc fr;
             fr.in_mode = IN_FRAME;
             fr.amax_src = head;
+            fr.amax_tag = tag_head;
             fr.amax_n = p->vocab;
             fr.save = xa;  // the frame input is the residual stream for layer 0's attention add
-            layer(t->layers[l], t->H, t->heads, t->kvh, t->hd, &fr, at, kAttnMaxSplit);
+            layer(t->layers[l], t->heads, t->kvh, t->hd, &fr, at, kAttnMaxSplit);
         } else {
-            layer(t->layers[l], t->H, t->heads, t->kvh, t->hd, nullptr, at, kAttnMaxSplit);
+            layer(t->layers[l], t->heads, t->kvh, t->hd, nullptr, at, kAttnMaxSplit);
         }
     }
     {
         GemvDesc hd;  // final norm + apply_codec_head (talker.rs:353-359, 647-649)
         hd.in = xa;
+        hd.in_tag = tag_xa;
         hd.ss_in = ssa;
+        hd.ss_tag = tag_ssa;
         hd.gamma = t->final_norm.as<__half>();
-        hd.save = hidden;
-        hd.save_normed = 1;
-        hd.out = e->logits.as<float>();
+        hd.save_plain = hidden;
+        hd.out_plain = e->logits.as<float>();
         hd.adv_len = e->tkv->lens();
         hd.adv_pos = e->pos.as<int>();
         B.gemv(hd, t->head, 1);
@@ -924,15 +1086,20 @@ int frame_build(qora_engine *e, FrameProgram **out) {
     for (int g = 0; g < p->groups; g++) fe.pred[g] = p->embs[g];
     fe.ngroups = p->groups;
     fe.n = t->H;
+    fe.codes_t = codes_t;
+    for (int g = 0; g < 16; g++) fe.code_tag[g] = code_tag[g];
     fe.codes = codes;
     fe.prev = prev;
 
     // ---- device copies
     const size_t nops = fp->ops.size();
+    if (nops > (size_t)kMaxOps || nops + 1 >= kTagStride) {
+        delete fp;
+        return set_error(QORA_ERR_UNSUPPORTED, "frame program has %zu ops (max %d)", nops, kMaxOps);
+    }
     rc = fp->d_ops.alloc(nops * sizeof(OpRef));
     if (rc == QORA_OK) rc = fp->d_gemv.alloc(fp->gemv.size() * sizeof(GemvDesc));
     if (rc == QORA_OK) rc = fp->d_attn.alloc(fp->attn.size() * sizeof(AttnArgs));
-    if (rc == QORA_OK) rc = fp->d_done.alloc((nops + 1) * sizeof(unsigned));
     if (rc == QORA_OK) rc = fp->d_trace.alloc(nops * kTraceFields * sizeof(unsigned long long));
     if (rc == QORA_OK && (cudaMemcpy(fp->d_ops.p, fp->ops.data(), nops * sizeof(OpRef), cudaMemcpyHostToDevice) ||
                           cudaMemcpy(fp->d_gemv.p, fp->gemv.data(), fp->gemv.size() * sizeof(GemvDesc),
@@ -959,9 +1126,9 @@ int frame_build(qora_engine *e, FrameProgram **out) {
     P.gemv = fp->d_gemv.as<GemvDesc>();
     P.attn = fp->d_attn.as<AttnArgs>();
     P.sample = sa;
+    P.code0_t = codes_t;
     P.fe = fe;
-    P.done = fp->d_done.as<unsigned>();
-    P.abort_flag = reinterpret_cast<int *>(fp->d_done.as<unsigned>() + nops);
+    P.abort_flag = abort_flag;
     P.err = ctx->err.as<int>();
     *out = fp;
     return QORA_OK;
@@ -971,8 +1138,12 @@ int frame_launch(FrameProgram *fp, const float *text, cudaStream_t st) {
     FrameParams P = fp->params;
     P.text = text;
     P.trace = fp->trace ? fp->d_trace.as<unsigned long long>() : nullptr;
-    // counters and the abort flag start each frame at zero
-    QORA_CUDA(cudaMemsetAsync(fp->d_done.p, 0, fp->d_done.bytes, st));
+    // tags unique to this launch (a stale word from an earlier launch never matches)
+    fp->epoch++;
+    if ((uint32_t)(fp->epoch * kTagStride) == 0) fp->epoch++;
+    P.tag_base = fp->epoch * kTagStride;
+    QORA_CUDA(cudaMemsetAsync(fp->d_abort.p, 0, 4, st));
+    if (fp->trace) QORA_CUDA(cudaMemsetAsync(fp->d_trace.p, 0, fp->d_trace.bytes, st));
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(fp->grid);
     cfg.blockDim = dim3(kThreads);

@@ -17,6 +17,7 @@ constexpr int kSlotNib = 16384;        // nibble bytes per slot (1024 rows of on
 constexpr int kSlotScl = 2048;         // scale bytes per slot
 constexpr int kXMax = 6144;            // widest GEMV input (talker down projection)
 constexpr int kTraceFields = 8;
+constexpr uint32_t kTagStride = 2048;  // tags per launch (ops + 1 <= kTagStride)
 
 enum OpType : int { OP_GEMV = 0, OP_ATTN = 1, OP_SAMPLE = 2 };
 enum InMode : int {
@@ -32,29 +33,42 @@ enum OutMode : int {
 
 // One GEMV op: y = epilogue(prologue(x) @ W) over `units` column units of G
 // 32-column groups each; item j = unit j covers all K rows, so every output
-// is final when its item ends.
+// is final when its item ends.  Activations passed between ops are tagged
+// words (value | tag << 32, tag = the producing op's tag); a consumer polls
+// the words it needs until they carry the producer's tag.
 struct alignas(16) GemvDesc {
     const uint4 *nib = nullptr;
     const __half *scl = nullptr;
     int kpad = 0, K = 0, units = 0, G = 1;
     // input
     int in_mode = IN_VEC;
-    const float *in = nullptr;
+    const uint64_t *in = nullptr;        // IN_VEC: tagged x[K]
+    const float *in_plain = nullptr;     // IN_VEC: plain x[K] written by an earlier launch
+    uint32_t in_tag = 0;
     const __half *gamma = nullptr;       // RMSNorm prologue (rms_norm_f16, gemv.rs:445-454)
-    const float *ss_in = nullptr;        // IN_VEC + gamma: per-32-column sums of squares of `in`
-    float *save = nullptr;               // materialise x (before, or after the norm)
-    int save_normed = 0;
-    const float *amax_src = nullptr;     // IN_EMB / IN_FRAME: logits for the argmax
+    const uint64_t *ss_in = nullptr;     // with gamma: tagged per-32-column sums of squares of x
+    uint32_t ss_tag = 0;
+    uint64_t *save = nullptr;            // materialise x as tagged words (before the norm)
+    float *save_plain = nullptr;         // materialise x plain (after the norm)
+    const uint64_t *amax_src = nullptr;  // IN_EMB / IN_FRAME: tagged logits for the argmax
     int amax_n = 0;
-    uint32_t *code_dst = nullptr;        // where the argmax code is stored
-    const uint32_t *code_src = nullptr;  // IN_EMB without amax_src: the code to look up
+    uint32_t amax_tag = 0;
+    uint64_t *code_dst = nullptr;        // tagged slot for the argmax code
+    const uint64_t *code_src = nullptr;  // IN_EMB without amax_src: tagged code to look up
+    uint32_t code_tag = 0;
     EmbDev emb;                          // IN_EMB table
+    const uint64_t *dep = nullptr;       // extra ordering input: wait until dep[0..dep_n) carry
+    uint32_t dep_tag = 0;                // dep_tag before writing (an op whose data input does
+    int dep_n = 0;                       // not already imply its predecessors are done)
     // output
     int out_mode = OUT_STORE;
-    float *out = nullptr;
-    const float *resid = nullptr;        // OUT_RESID
+    uint64_t *out = nullptr;             // tagged output
+    float *out_plain = nullptr;          // plain output (read by the next launch)
+    uint32_t out_tag = 0;
+    const uint64_t *resid = nullptr;     // OUT_RESID: tagged residual stream
+    uint32_t resid_tag = 0;
     const float *bias = nullptr;         // optional, OUT_STORE
-    float *ss_out = nullptr;             // per-32-column sums of squares of the output
+    uint64_t *ss_out = nullptr;          // tagged per-32-column sums of squares of the output
     int *adv_len = nullptr;              // end of frame: len[0] += 1, pos[0] += 1
     int *adv_pos = nullptr;
 };
@@ -65,7 +79,9 @@ struct FrameEmbed {
     EmbDev pred[kMaxEmbedGroups];        // acoustic tables
     int ngroups = 0;
     int64_t n = 0;
-    uint32_t *codes = nullptr;           // [16]: code 0 .. code ngroups
+    const uint64_t *codes_t = nullptr;   // [16] tagged codes 0 .. ngroups-1
+    uint32_t code_tag[16] = {};          // the tag of each tagged code
+    uint32_t *codes = nullptr;           // [16]: plain codes of the frame (for the host)
     uint32_t *prev = nullptr;            // [16]: previous-code window (repetition penalty)
 };
 
@@ -82,15 +98,17 @@ struct FrameParams {
     const GemvDesc *gemv = nullptr;
     const AttnArgs *attn = nullptr;
     SampleArgs sample;
+    uint64_t *code0_t = nullptr;         // tagged code 0 (the sampler's output)
     FrameEmbed fe;
     const float *text = nullptr;         // [hidden] text row of this frame
-    unsigned *done = nullptr;            // [n_ops] completion counters (zeroed per launch)
+    uint32_t tag_base = 0;               // op i of this launch tags its outputs tag_base + i + 1
     int *abort_flag = nullptr;
     int *err = nullptr;
-    unsigned long long *trace = nullptr; // optional [n_ops][8] of each op's item-0 SM: globaltimer
-                                         // stamps (dependency met, input built, items done,
-                                         // signalled); thread 0's SM cycles waiting for weight
-                                         // slots, computing, reducing; slots consumed
+    unsigned long long *trace = nullptr; // optional [n_ops][8] (zeroed per launch): globaltimer
+                                         // ns over the SMs with items: ~earliest input ready, latest
+                                         // input ready, latest done, latest start; then on the
+                                         // item-0 SM: cycles waiting for weight slots, computing,
+                                         // reducing, and slots consumed
 };
 
 }  // namespace fk
@@ -100,7 +118,8 @@ struct FrameProgram {
     std::vector<fk::OpRef> ops;
     std::vector<fk::GemvDesc> gemv;
     std::vector<AttnArgs> attn;
-    DevBuf d_ops, d_gemv, d_attn, d_done, bufs, d_trace;
+    DevBuf d_ops, d_gemv, d_attn, d_abort, bufs, d_trace;
+    uint32_t epoch = 0;                  // launches so far (tags of launch e start at e * kTagStride)
     fk::FrameParams params;
     int grid = 0;
     size_t smem = 0;

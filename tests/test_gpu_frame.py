@@ -110,10 +110,11 @@ def test_trace_records_every_op(E, ctx, orc):
     L_t, L_p, G = cfg.t_layers, cfg.p_layers, cfg.p_groups
     assert len(ops) == 1 + (G + 1) * (1 + 5 * L_p) + G + 5 * L_t + 1
     assert ops[0] == 2 and (ops == 1).sum() == (G + 1) * L_p + L_t
-    stamps = st[:, :4].astype(np.int64)
-    assert np.all(stamps > 0) and np.all(np.diff(stamps, axis=1) >= 0)
-    gemv = ops == 0
-    assert np.all(st[gemv, 7] > 0)          # every GEMV op's item 0 consumed weight slots
+    ready0 = (~st[:, 0]).astype(np.int64)
+    ready1, done = st[:, 1].astype(np.int64), st[:, 2].astype(np.int64)
+    assert np.all(st[:, 2] > 0) and np.all(ready1[ops == 0] >= ready0[ops == 0])
+    assert np.all(done[ops == 0] >= ready1[ops == 0])
+    assert np.all(st[ops == 0, 7] > 0)      # every GEMV op's item 0 consumed weight slots
 
 
 @pytest.mark.parametrize("hd", [128, 64])
