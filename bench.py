@@ -52,7 +52,7 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
-    ap.add_argument("--profile-case", default=None, choices=["gemv", "frame_trace"],
+    ap.add_argument("--profile-case", default=None, choices=["gemv", "frame_trace", "batch_frame"],
                     help="small fixed workload for an ncu capture instead of the bench")
     return ap.parse_args()
 
@@ -528,10 +528,35 @@ def profile_case_frame_trace():
                       "mean_us_by_op": by_label}))
 
 
+def profile_case_batch_frame(B):
+    """ncu case: one frame of B streams (1.7B dims, 64-token prefill, graph
+    replay after 3 warm-up frames), bracketed by cudaProfilerStart/Stop so
+    that `ncu --profile-from-start off` captures exactly that frame."""
+    import torch
+    import qora_b200 as qb
+    from qora_b200 import engine as E
+    torch.cuda.set_device(0)
+    cfg = qb.ModelConfig()
+    ctx = E.Context(0)
+    talker = E.Talker(ctx, qb.synth_talker(cfg), max_batch=B)
+    pred = E.CodePredictor(ctx, qb.synth_predictor(cfg), max_batch=B)
+    eng, text, codes = engine_rate(E, talker, pred, torch, qb, B, 1, 3, 3000)
+    torch.cuda.profiler.start()
+    eng.frame(text, codes)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ctx.check_device_error()
+    print(json.dumps({"profile_case": "batch_frame", "batch": B,
+                      "kernels_per_frame": eng.kernels_per_frame()}))
+
+
 def main():
     args = parse()
     if args.profile_case == "gemv":
         profile_case_gemv()
+        return
+    if args.profile_case == "batch_frame":
+        profile_case_batch_frame(args.batch)
         return
     if args.profile_case == "frame_trace":
         profile_case_frame_trace()

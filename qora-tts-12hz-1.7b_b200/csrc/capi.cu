@@ -211,6 +211,8 @@ int qora_ctx_check_device_error(qora_ctx *ctx, void *stream) {
         case kDevRange: return set_error(QORA_ERR_RANGE, "device: position past RoPE table or KV capacity");
         case kDevNaN: return set_error(QORA_ERR_INVALID, "device: NaN reached argmax/sampler");
         case kDevTimeout: return set_error(QORA_ERR_TIMEOUT, "device: bounded wait expired");
+        case kDevF16Range:
+            return set_error(QORA_ERR_RANGE, "device: GEMV input value outside the f16 operand range");
     }
     return set_error(QORA_ERR_CUDA, "device error code %d", v);
 }
@@ -261,7 +263,6 @@ void qora_q4_weight_destroy(qora_w4 *w) { delete w; }
 
 static int generic_gemv(qora_ctx *ctx, const qora_w4 *w, const float *x, float *y, int rows,
                         cudaStream_t st) {
-    const GemvPlan p = plan_gemv(w->dev.k, w->dev.C, rows, E_STORE, ctx->num_sms);
     GemvArgs a;
     a.w = w->dev;
     a.rows = rows;
@@ -270,6 +271,7 @@ static int generic_gemv(qora_ctx *ctx, const qora_w4 *w, const float *x, float *
     a.y = y;
     a.ldy = w->dev.n;
     a.err = ctx->err.as<int>();
+    const GemvPlan p = plan_gemv_for(a, X_PLAIN, E_STORE, ctx->num_sms);
     return launch_gemv(a, X_PLAIN, E_STORE, p, nullptr, st);
 }
 

@@ -48,6 +48,7 @@ enum DeviceError : int {
     kDevRange = 1,   // position past the RoPE table or KV capacity
     kDevNaN = 2,     // NaN logits reached an argmax / sampler
     kDevTimeout = 3, // bounded wait expired
+    kDevF16Range = 4,// an input row value outside the f16 range of the tensor-core GEMV operands
 };
 
 // ------------------------------------------------------------ device memory
@@ -357,6 +358,8 @@ struct Q4Dev {
     int64_t k = 0, n = 0;  // n may exceed 32*C: the tail stays zero (gemv.rs:846-861)
     int64_t C = 0;         // full groups
     int64_t kpad = 0;      // row stride of one group in nib / scl
+    int mma_exp = -1;      // tensor-core path: scales are used as scale * 2^mma_exp in f16
+                           // (chosen at upload so 8 * max scale * 2^mma_exp <= 2^15); -1: unusable
 };
 
 constexpr int kChunkRows = 128;  // rows per bulk-copy chunk

@@ -19,108 +19,18 @@
 // Launch: programmatic dependent launch.  Each CTA fetches its first weight
 // tile (immutable) before griddepcontrol.wait, so weight traffic and launch
 // latency overlap the previous kernel.
-#include <cooperative_groups.h>
-
 #include <algorithm>
+#include <cmath>
 
-#include "gemv.cuh"
-
-namespace cg = cooperative_groups;
+#include "gemv_impl.cuh"
 
 namespace qora {
 
 namespace {
 
+using namespace gemv_detail;
+
 constexpr int kRowsPerLane = 4;
-
-// Input element x[r][kr] before the RMSNorm scaling (applied by the caller).
-template <int XM>
-__device__ __forceinline__ float load_x(const GemvArgs &a, int r, int64_t kr) {
-    if constexpr (XM == X_PLAIN || XM == X_RMSNORM) {
-        return __ldcg(a.x + (int64_t)r * a.ldx + kr);
-    } else {
-        // embed_lookup_q4 (gemv.rs:425-433): scale * (q - 8)
-        const uint32_t t = __ldcg(a.tok + (int64_t)r * a.ldtok);
-        const uint8_t byte = a.emb.packed[(int64_t)t * (a.emb.n >> 1) + (kr >> 1)];
-        const int q = (kr & 1) ? (byte >> 4) : (byte & 15);
-        const float sc = __half2float(a.emb.scl[(int64_t)t * (a.emb.n >> 5) + (kr >> 5)]);
-        return __fmul_rn(sc, (float)(q - 8));
-    }
-}
-
-// Epilogue value for one (row, column) result.
-template <int EM>
-__device__ __forceinline__ float epilogue_value(const GemvArgs &a, int r, int64_t col, float v) {
-    if constexpr (EM == E_BIAS) return __fadd_rn(v, a.bias[col]);
-    if constexpr (EM == E_RESID) return __fadd_rn(__ldcg(a.y + (int64_t)r * a.ldy + col), v);
-    return v;
-}
-
-// Stores a finished residual-stream value and its sum-of-squares partial.
-__device__ __forceinline__ void finalize_resid(const GemvArgs &a, int r, int64_t out_group, int lane,
-                                               float y) {
-    a.y[(int64_t)r * a.ldy + out_group * 32 + lane] = y;
-    if (a.ss_out) {
-        const float sq = warp_sum(__fmul_rn(y, y));
-        if (lane == 0) a.ss_out[(int64_t)r * a.ldss_out + out_group] = sq;
-    }
-}
-
-// Writes the final values for one warp-group (32 columns of one row).
-// For E_SWIGLU, v is the gate sum and u the up sum (silu(gate) * up, talker.rs:344).
-template <int EM>
-__device__ __forceinline__ void finalize_group(const GemvArgs &a, int r, int64_t out_group,
-                                               int lane, float v, float u, int64_t n_out) {
-    const int64_t col = out_group * 32 + lane;
-    float y;
-    if constexpr (EM == E_SWIGLU) {
-        y = __fmul_rn(silu_ref(v), u);
-    } else {
-        y = epilogue_value<EM>(a, r, col, v);
-    }
-    if (col < n_out) a.y[(int64_t)r * a.ldy + col] = y;
-    if (a.ss_out) {
-        const float sq = warp_sum(__fmul_rn(y, y));
-        if (lane == 0) a.ss_out[(int64_t)r * a.ldss_out + out_group] = sq;
-    }
-    if (a.tbest_v) {
-        // per-tile argmax, last index on ties (code_predictor.rs:336-339)
-        float bv = y;
-        int bi = (int)col;
-        if (y != y) raise_error(a.err, kDevNaN);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi > bi)) {
-                bv = ov;
-                bi = oi;
-            }
-        }
-        if (lane == 0) {
-            a.tbest_v[(int64_t)r * gridDim.x + blockIdx.x] = bv;
-            a.tbest_i[(int64_t)r * gridDim.x + blockIdx.x] = bi;
-        }
-    }
-}
-
-// Bulk L2 prefetch of CTA `id`'s share (16-byte aligned pieces) of [p, p+bytes).
-__device__ __forceinline__ void l2_prefetch_share(const void *p, uint64_t bytes, uint64_t id,
-                                                  uint64_t nctas) {
-    if (!p || bytes == 0) return;
-    const uint64_t per = ((bytes + nctas - 1) / nctas + 15) & ~15ull;
-    uint64_t off = id * per;
-    if (off >= bytes) return;
-    uint64_t len = per < bytes - off ? per : bytes - off;
-    const char *base = static_cast<const char *>(p) + off;
-    while (len >= 16) {
-        const uint64_t whole = len & ~15ull;
-        const uint32_t piece = (uint32_t)(whole < (1ull << 20) ? whole : (1ull << 20));
-        prefetch_l2_bulk(base, piece);
-        base += piece;
-        len -= piece;
-    }
-}
 
 // Register caps per batch tile so a whole GEMV grid is resident in one wave
 // (B = 1: 64 registers, 4 CTAs of 256 threads per SM).
@@ -148,9 +58,6 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
     const int64_t wrow0 = k_begin + (int64_t)wr * 32 * R * a.NSUB;
     const int r_begin = z * a.rows_per_z;
     const int r_end = min(a.rows, r_begin + a.rows_per_z);
-    const int64_t C = a.w.C;
-    const int64_t n32 = C * 32;
-    const int64_t n_out = (EM == E_SWIGLU) ? (C / 2) * 32 : a.w.n;
 
     const uint4 *nibc = a.w.nib + c * a.w.kpad;
     const __half *sclc = a.w.scl + c * a.w.kpad;
@@ -313,130 +220,7 @@ __global__ void __launch_bounds__(256, GemvOcc<B>::kMinBlocks) k_gemv(const Gemv
         __syncthreads();
     }
 
-    // K-split totals: the cluster's CTAs hold one partial each in shared
-    // memory; rank 0 sums them in rank order over DSMEM.
-    cg::cluster_group cluster = cg::this_cluster();
-    const int S = a.S;
-    const bool leader = (S == 1) || cluster.block_rank() == 0;
-    constexpr int CO = (EM == E_SWIGLU) ? 1 : CPC;  // output column groups per CTA
-    constexpr int kPre = 4;                          // residual values prefetched per thread
-    const int nz = r_end - r_begin;
-    const int nitems = nz * CO * 32;
-    float yres[kPre];
-    if constexpr (EM == E_RESID) {
-        // the residual does not depend on the K-split partials: load it while
-        // the cluster barrier completes
-        if (leader) {
-#pragma unroll
-            for (int m = 0; m < kPre; m++) {
-                const int it = threadIdx.x + m * blockDim.x;
-                if (it < nitems) {
-                    const int l = it & 31, q = it >> 5;
-                    const int64_t col = ((int64_t)blockIdx.x * CPC + q % CO) * 32 + l;
-                    yres[m] = __ldcg(a.y + (int64_t)(r_begin + q / CO) * a.ldy + col);
-                }
-            }
-        }
-    }
-    if (S > 1) cluster.sync();
-    if (leader) {
-        auto finish = [&](int it, float yr, bool have_yr) {
-            const int l = it & 31;
-            const int q = it >> 5;
-            const int row = q / CO, cc2 = q % CO;
-            // rank-order sum; peer loads issued four at a time
-            float v = 0.0f, u = 0.0f;
-            for (int r4 = 0; r4 < S; r4 += 4) {
-                float pv[4], pu[4];
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    if (r4 + j < S) {
-                        const float *p = (S == 1) ? &cta_red[0][0][0]
-                                                  : cluster.map_shared_rank(&cta_red[0][0][0], r4 + j);
-                        pv[j] = p[(row * CPC + cc2) * 32 + l];
-                        if constexpr (EM == E_SWIGLU) pu[j] = p[(row * CPC + 1) * 32 + l];
-                    }
-                }
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    if (r4 + j < S) {
-                        v += pv[j];
-                        if constexpr (EM == E_SWIGLU) u += pu[j];
-                    }
-                }
-            }
-            const int64_t grp = (EM == E_SWIGLU) ? (int64_t)blockIdx.x
-                                                 : (int64_t)blockIdx.x * CPC + cc2;
-            if constexpr (EM == E_RESID) {
-                // x[j] += attn_out[j] (talker.rs:334-336)
-                if (!have_yr) yr = __ldcg(a.y + (int64_t)(r_begin + row) * a.ldy + grp * 32 + l);
-                finalize_resid(a, r_begin + row, grp, l, __fadd_rn(yr, v));
-            } else {
-                finalize_group<EM>(a, r_begin + row, grp, l, v, u, n_out);
-            }
-        };
-#pragma unroll
-        for (int m = 0; m < kPre; m++) {
-            const int it = threadIdx.x + m * blockDim.x;
-            if (it < nitems) finish(it, (EM == E_RESID) ? yres[m] : 0.0f, true);
-        }
-        for (int it = threadIdx.x + kPre * blockDim.x; it < nitems; it += blockDim.x) finish(it, 0.0f, false);
-        // tail columns beyond the last full group stay zero (gemv.rs:846-861)
-        if (EM == E_STORE && a.w.n > n32 && blockIdx.x == 0) {
-            for (int r = r_begin; r < r_end; r++)
-                for (int64_t col = n32 + threadIdx.x; col < a.w.n; col += blockDim.x)
-                    a.y[(int64_t)r * a.ldy + col] = 0.0f;
-        }
-    }
-    if (S > 1) cluster.sync();  // peers keep their shared memory until rank 0 is done
-    if (!leader) return;
-
-    if (a.gticket) {
-        __threadfence();
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            const unsigned t = atomicAdd(a.gticket, 1u);
-            last_flag = (t == (unsigned)(gridDim.x * gridDim.z - 1));
-        }
-        __syncthreads();
-        if (!last_flag) return;
-        __threadfence();
-        if (a.amax) {
-            // argmax over the column tiles, one warp per row: lanes take tiles
-            // lane, lane+32, ...; ties keep the larger index (the last maximum,
-            // code_predictor.rs:336-339)
-            const int nwarps = blockDim.x >> 5;
-            for (int r = warp; r < a.rows; r += nwarps) {
-                float bv = -INFINITY;
-                int bi = -1;
-                for (unsigned t = lane; t < gridDim.x; t += 32) {
-                    const float v = __ldcg(a.tbest_v + (int64_t)r * gridDim.x + t);
-                    const int i = __ldcg(a.tbest_i + (int64_t)r * gridDim.x + t);
-                    if (bi < 0 || v > bv || (v == bv && i > bi)) {
-                        bv = v;
-                        bi = i;
-                    }
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) {
-                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                    if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi > bi))) {
-                        bv = ov;
-                        bi = oi;
-                    }
-                }
-                if (lane == 0) a.amax[(int64_t)r * a.ldamax] = (uint32_t)bi;
-            }
-        }
-        if (a.adv_len) {
-            for (int st = threadIdx.x; st < a.adv_streams; st += blockDim.x) {
-                a.adv_len[st] += a.adv_T;
-                if (a.adv_pos) a.adv_pos[st] += a.adv_T;
-            }
-        }
-        if (threadIdx.x == 0) *a.gticket = 0u;
-    }
+    gemv_final<EM, CPC, kRowsPerZ>(a, cta_red, r_begin, r_end, last_flag);
 }
 
 template <int B, int XM, int EM>
@@ -558,7 +342,13 @@ __global__ void k_rmsnorm_rows(const float *__restrict__ x, const __half *__rest
 int gemv_init() {
     QORA_TRY(allow_large_clusters_e<X_PLAIN>());
     QORA_TRY(allow_large_clusters_e<X_RMSNORM>());
-    return allow_large_clusters_e<X_EMBED>();
+    QORA_TRY(allow_large_clusters_e<X_EMBED>());
+    return gemv_mma_init();
+}
+
+GemvPlan plan_gemv_for(const GemvArgs &a, int xmode, int emode, int num_sms) {
+    if (gemv_mma_eligible(a, xmode, emode)) return plan_gemv_mma(a.w.k, a.w.C, a.rows, emode, num_sms);
+    return plan_gemv(a.w.k, a.w.C, a.rows, emode, num_sms);
 }
 
 GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms) {
@@ -614,6 +404,11 @@ int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &p, unsigned *g
     a.NSUB = p.NSUB;
     a.rows_per_cta_k = p.rows_per_cta_k;
     a.rows_per_z = p.rows_per_z;
+    if (p.mma) {
+        if (!gemv_mma_eligible(a, xmode, emode))
+            return set_error(QORA_ERR_INVALID, "tensor-core GEMV plan for an ineligible launch");
+        return launch_gemv_mma(a, xmode, emode, p, st);
+    }
     switch (xmode) {
         case X_PLAIN: return launch_e<X_PLAIN>(a, emode, p, st);
         case X_RMSNORM: return launch_e<X_RMSNORM>(a, emode, p, st);
@@ -655,6 +450,27 @@ int launch_rmsnorm_rows(const float *x, const __half *gamma, int64_t n, int rows
     return launch_ex(k_rmsnorm_rows, dim3(rows), dim3(256), 0, stream, 1u, x, gamma, n, out);
 }
 
+// Exponent E of the tensor-core operand scaling: the largest E in [0, 15] with
+// max|scale| * 2^E <= 2^12, so every (q - 8) * scale * 2^E (|q - 8| <= 8) stays
+// within 2^15 in f16 while small scales move away from the f16 subnormals.
+// -1 when a scale is not finite or too large for the f16 operands.
+static int mma_scale_exponent(const qora_q4_host *parts, int nparts) {
+    uint16_t mx = 0;  // |scale| bits: ordered like the values for finite f16
+    for (int i = 0; i < nparts; i++) {
+        const int64_t cnt = parts[i].k * (parts[i].n / kGroup);
+        for (int64_t j = 0; j < cnt; j++) mx = std::max<uint16_t>(mx, parts[i].scales[j] & 0x7FFFu);
+    }
+    if (mx >= 0x7C00u) return -1;  // inf / NaN
+    const int ex = mx >> 10;
+    const float m = ex ? (1.0f + (float)(mx & 0x3FF) / 1024.0f) * std::ldexp(1.0f, ex - 15)
+                       : (float)(mx & 0x3FF) * std::ldexp(1.0f, -24);
+    if (m == 0.0f) return 15;
+    if (m > 4096.0f) return -1;
+    int e = 15;
+    while (e > 0 && m * std::ldexp(1.0f, e) > 4096.0f) e--;
+    return e;
+}
+
 // Upload reference-layout parts of one fused weight (all with the same k) into
 // a column-group-major buffer of C_total groups: part i's group c lands at
 // group offs[i] + c * strides[i].
@@ -686,6 +502,7 @@ int upload_q4_parts(const qora_q4_host *parts, const int64_t *offs, const int64_
     out.scl = scl.as<__half>();
     out.k = k;
     out.kpad = kp;
+    out.mma_exp = mma_scale_exponent(parts, nparts);
     out.C = C_total;
     out.n = C_total * kGroup;
     return QORA_OK;

@@ -55,8 +55,11 @@ constexpr int kMaxSplit = 16;       // CTAs of one cluster along K
 // Tiling of one GEMV: column groups x K-splits (one cluster) x row groups.
 struct GemvPlan {
     int B, WR, S, Z, NSUB, rows_per_cta_k, rows_per_z, cpc;
+    bool mma;                       // k_gemv_mma (tensor cores, batches of kMmaMinRows rows or more)
     dim3 grid, block;
 };
+
+constexpr int kMmaMinRows = 8;      // from this many rows on, the tensor-core kernel serves batches
 
 // Point a GEMV's L2 prefetch at the weights of the GEMV that follows it.
 inline void prefetch_next(GemvArgs &a, const Q4Dev &next) {
@@ -69,8 +72,20 @@ inline void prefetch_next(GemvArgs &a, const Q4Dev &next) {
 // Per-device one-time kernel attribute setup (large clusters).
 int gemv_init();
 
-// Chooses tiling so that at least ~2 CTAs per SM are launched.
+// Chooses tiling so that at least ~2 CTAs per SM are launched (CUDA-core kernel).
 GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms);
+
+// Tensor-core kernel (gemv_mma.cu): whether a launch qualifies (rows >=
+// kMmaMinRows, plain or RMSNorm input, aligned rows, k % 32 == 0, C % 4 == 0,
+// weight scales within the f16 operand range), its tiling, its launcher.
+int gemv_mma_init();
+bool gemv_mma_eligible(const GemvArgs &a, int xmode, int emode);
+GemvPlan plan_gemv_mma(int64_t k, int64_t C, int rows, int emode, int num_sms);
+int launch_gemv_mma(const GemvArgs &a, int xmode, int emode, const GemvPlan &p, cudaStream_t st);
+
+// The plan for one launch: the tensor-core kernel where it qualifies, else
+// the CUDA-core kernel.
+GemvPlan plan_gemv_for(const GemvArgs &a, int xmode, int emode, int num_sms);
 
 // Launches the fused GEMV; `gticket` backs the global final stage (argmax /
 // length advance) when `a` asks for one.

@@ -1,0 +1,594 @@
+// Tensor-core Q4 GEMV for batched rows (sm_100a, tcgen05).
+//
+// The batched step of the reference's gemv / gemm (gemv.rs:149-162, 290-412)
+// is a dense contraction once 8 or more rows share the weights:
+//     y[r][j] = sum_k x[r][k] * (q[k][j] - 8) * scale[k][j/32]
+// One CTA computes a 128-column tile (four 32-column groups) for 32 rows over
+// a slice of K, as D[column][row] = A[column][k] * B[row][k]: A = the
+// dequantised weights, written by the CUDA cores straight into tensor memory;
+// B = the input rows, in shared memory; D accumulated in tensor memory.
+//
+// Exactness of the operands (f16, kind::f16, f32 accumulate):
+//   * the scale is pre-multiplied by 2^E (E per weight matrix, chosen at
+//     upload so that 8 * scale * 2^E <= 2^15) and split as s = sa + sb, sa
+//     the top 8 significant bits and sb the 3-bit remainder; (q - 8) * sa and
+//     (q - 8) * sb are then exact f16 values (<= 11 and <= 6 significant bits),
+//     so A1 + A2 = 2^E (q - 8) scale exactly;
+//   * x is split as xh = f16(x), xl = f16(x - xh) (22 significant bits);
+//   * D = A1 [xh; xl] (one N = 64 MMA: the xh and xl products side by side)
+//     + A2 xh (A2 xl, ~2^-19 relative, is dropped); the epilogue adds the two
+//     halves and multiplies by 2^-E.
+// The relative error per product is ~2^-17: far inside the 1e-3 tolerance the
+// reference accepts for its own chunked summation (gemv.rs:806-809).
+//
+// Warp roles (192 threads):
+//   warps 0-3  warp g converts column group g (TMEM lanes 32 g ..): raw nibbles
+//              + scales -> A1 / A2 in tensor memory; and x rows 8 g .. 8 g + 7
+//              -> B (hi / lo) in shared memory, RMSNorm prologue applied; then
+//              reads the accumulator back and sends it to its K-split owner;
+//   warp 4     streams raw weights and x rows into a 4-stage ring with
+//              16-byte cp.async copies (weights are immutable and issued before
+//              the wait on the previous kernel);
+//   warp 5     allocates tensor memory and issues the MMAs (one thread).
+// K-split: the S CTAs of one cluster each own a slice of the 32 rows; every
+// CTA stores its partial sums for a slice into the owner's shared memory, one
+// cluster barrier, then the owner sums the S partials in rank order and
+// applies the epilogue.  Every mbarrier wait is bounded.
+#include "gemv_impl.cuh"
+#include "tc.cuh"
+
+namespace qora {
+
+namespace {
+
+using namespace gemv_detail;
+
+constexpr int kMmaRows = 32;                 // batch rows per CTA (MMA N = 2 x 32: hi / lo)
+constexpr int kMmaGroups = 4;                // 32-column groups per CTA (MMA M = 128)
+constexpr int kStageK = 32;                  // K rows per pipeline stage (two K = 16 MMAs)
+constexpr int kRawStages = 4;
+constexpr int kOpStages = 4;
+constexpr int kConvGroups = 2;               // converter groups: group c takes stages t = c mod 2
+constexpr int kConvWarps = 4 * kConvGroups;
+constexpr int kProdWarp = kConvWarps;
+constexpr int kMmaWarp = kConvWarps + 1;
+constexpr int kMmaThreads = (kConvWarps + 2) * 32;
+// tensor memory columns: D (64: hi then lo products), then per operand stage
+// A1 (16 columns: 32 f16 K values) and A2 (16)
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemA = 64;
+constexpr uint32_t kTmemAStage = 32;
+
+// raw stage (bytes): per-group nibble rows and scales, then x rows; strides
+// padded by 16 bytes so that the groups / rows fall on different banks
+constexpr int kNibGroupStride = kStageK * 16 + 16;
+constexpr int kSclGroupStride = kStageK * 2 + 16;
+constexpr int kXRowStride = kStageK * 4 + 16;
+constexpr int kRawNib = 0;
+constexpr int kRawScl = kRawNib + kMmaGroups * kNibGroupStride;
+constexpr int kRawX = kRawScl + kMmaGroups * kSclGroupStride;
+constexpr int kRawBytes = kRawX + kMmaRows * kXRowStride;
+// operand stage: B = [xh rows; xl rows] (64 x 32 f16) in the canonical K-major
+// layout without swizzle.  Core matrix (8 rows x 8 k) = 128 contiguous bytes;
+// core (row block rb, k block kc) at (rb * 4 + kc) * 128, so LBO (along K) =
+// 128 and SBO (along rows) = 512; the xl rows are row blocks 4-7.
+constexpr int kBTile = kMmaRows * kStageK * 2;  // one of xh / xl
+constexpr int kOpBytes = 2 * kBTile;
+constexpr uint32_t kLBO = 128, kSBO = 512;
+// K-split reduction: 16 units per CTA tile, unit = (output group, chunk of
+// kChunkRows(EM) rows); rank q owns units u with u % S == q (S a power of two
+// <= 16).  Receive buffer: [unit slot][source rank][partial][column][padded
+// chunk rows]; padding keeps float2 stores aligned and the reads 2-way at most.
+constexpr int kUnits = 16;
+constexpr int kRecvFloats = kUnits * 2 * 32 * 6 > kUnits * 32 * 10 ? kUnits * 2 * 32 * 6 : kUnits * 32 * 10;
+constexpr size_t kMmaSmem =
+    128 + (size_t)kOpStages * kOpBytes + (size_t)kRawStages * kRawBytes + (size_t)kRecvFloats * 4;
+
+static_assert(kOpBytes % 128 == 0 && kRawBytes % 16 == 0, "stage alignment");
+static_assert(kMmaRows == 32 && kConvWarps == kConvGroups * kMmaGroups, "one converter warp per column group");
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// 16-byte asynchronous copy global -> shared (L2 only), both addresses 16-byte aligned.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// One arrival on `bar` (counted in its init count) once every cp.async this
+// thread issued before has landed.
+__device__ __forceinline__ void cp_async_arrive(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Bounded wait that also gives up when another role of this CTA aborted.
+// The spin is try_wait alone (it suspends in hardware for a while before
+// failing); the bound (2^31 SM cycles, about a second) and the abort flag
+// are looked at every 32 attempts, with the SM's own cycle counter.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, volatile int *abort_s,
+                                              int *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const long long t0 = clock64();
+    for (uint32_t i = 1;; i++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((i & 31) == 0) {
+            if (*abort_s) return false;
+            if (clock64() - t0 > (1ll << 31)) {
+                raise_error(err, kDevTimeout);
+                *abort_s = 1;
+                return false;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+template <int XM, int EM>
+__global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
+    constexpr int CO = (EM == E_SWIGLU) ? kMmaGroups / 2 : kMmaGroups;  // output groups per CTA
+    constexpr int P = (EM == E_SWIGLU) ? 2 : 1;      // partials per output (gate, up)
+    constexpr int RC = kMmaRows * CO / kUnits;       // rows per reduction unit (8, or 4 for SwiGLU)
+    constexpr int RPAD = RC + 2;                     // padded chunk row stride in the receive buffer
+    constexpr int NCH = kMmaRows / RC;               // row chunks per output group
+    extern __shared__ uint8_t mma_dyn[];
+    __shared__ __align__(8) uint64_t raw_full[kRawStages], raw_empty[kRawStages];
+    __shared__ __align__(8) uint64_t op_full[kOpStages], op_empty[kOpStages], d_full;
+    __shared__ uint32_t tmem_slot;
+    __shared__ float inv_s[kMmaRows];
+    __shared__ int abort_s;
+    __shared__ int last_flag;
+
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)mma_dyn + 127) & ~(uintptr_t)127);
+    uint8_t *op_base = smem;
+    uint8_t *raw_base = smem + kOpStages * kOpBytes;
+    float *recv = reinterpret_cast<float *>(raw_base + kRawStages * kRawBytes);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t c0 = (int64_t)blockIdx.x * kMmaGroups;
+    const int T = (int)(a.w.k / kStageK);
+    const int t_begin = (int)((int64_t)blockIdx.y * T / a.S);
+    const int t_end = (int)((int64_t)(blockIdx.y + 1) * T / a.S);
+    const int nst = t_end - t_begin;
+    const int r_begin = blockIdx.z * kMmaRows;
+    const int r_end = min(a.rows, r_begin + kMmaRows);
+    const int nvalid = r_end - r_begin;
+    volatile int *abort_v = &abort_s;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int S = a.S;
+    const int rank = (S == 1) ? 0 : (int)cluster.block_rank();
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kRawStages; i++) {
+            mbar_init(&raw_full[i], 32);  // one cp.async arrival per producer lane
+            mbar_init(&raw_empty[i], 4);  // the converter group of the stage
+        }
+        for (int i = 0; i < kOpStages; i++) {
+            mbar_init(&op_full[i], 4);
+            mbar_init(&op_empty[i], 1);
+        }
+        mbar_init(&d_full, 1);
+        static_assert(kOpStages % kConvGroups == 0, "a converter group keeps its operand stages");
+        abort_s = 0;
+        mbar_fence_init();
+    }
+    if (warp == kMmaWarp) {
+        tc::tmem_alloc(&tmem_slot, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == kProdWarp) {
+        // ---------------------------------------------------------- producer
+        // 16-byte cp.async per lane (a stage is ~13 coalesced copies per lane);
+        // each lane's arrival on raw_full[b] fires when its copies have landed
+        auto issue_w = [&](int t) {
+            uint8_t *raw = raw_base + (t % kRawStages) * kRawBytes;
+            const int64_t k0 = (int64_t)(t_begin + t) * kStageK;
+#pragma unroll
+            for (int g = 0; g < kMmaGroups; g++)  // row `lane` of each group
+                cp_async16(raw + kRawNib + g * kNibGroupStride + lane * 16, a.w.nib + (c0 + g) * a.w.kpad + k0 + lane);
+            if (lane < kMmaGroups * 4) {  // 64 bytes of scales per group
+                const int g = lane >> 2, part = lane & 3;
+                cp_async16(raw + kRawScl + g * kSclGroupStride + part * 16,
+                           reinterpret_cast<const uint8_t *>(a.w.scl + (c0 + g) * a.w.kpad + k0) + part * 16);
+            }
+        };
+        auto issue_x = [&](int t) {
+            const int b = t % kRawStages;
+            uint8_t *raw = raw_base + b * kRawBytes;
+            const int64_t k0 = (int64_t)(t_begin + t) * kStageK;
+            for (int i = lane; i < nvalid * 8; i += 32) {  // 8 x 16 bytes per row
+                const int r = i >> 3, part = i & 7;
+                cp_async16(raw + kRawX + r * kXRowStride + part * 16,
+                           a.x + (int64_t)(r_begin + r) * a.ldx + k0 + part * 4);
+            }
+            cp_async_arrive(&raw_full[b]);
+        };
+        if (lane == 0 && (a.pf0_bytes | a.pf1_bytes)) {
+            const uint64_t nctas = (uint64_t)gridDim.x * gridDim.y * gridDim.z;
+            const uint64_t id = ((uint64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+            l2_prefetch_share(a.pf0, a.pf0_bytes, id, nctas);
+            l2_prefetch_share(a.pf1, a.pf1_bytes, id, nctas);
+        }
+        // weights of the first stages before the wait on the previous kernel
+        const int pre = min(nst, kRawStages);
+        for (int t = 0; t < pre; t++) issue_w(t);
+        griddep_launch_dependents();
+        griddep_wait();
+        for (int t = 0; t < pre; t++) issue_x(t);
+        for (int t = pre; t < nst; t++) {
+            const int b = t % kRawStages;
+            bool ok = true;
+            if (lane == 0) ok = wait_or_abort(&raw_empty[b], ((t / kRawStages) & 1) ^ 1, abort_v, a.err);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            issue_w(t);
+            issue_x(t);
+        }
+        // every copy this CTA issued lands before the CTA can exit
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncwarp();
+    } else if (warp == kMmaWarp) {
+        // ---------------------------------------------------------- MMA issue
+        griddep_launch_dependents();
+        griddep_wait();
+        if (lane == 0) {
+            constexpr uint32_t id64 = tc::idesc_f16_f32(128, 2 * kMmaRows);
+            constexpr uint32_t id32 = tc::idesc_f16_f32(128, kMmaRows);
+            for (int t = 0; t < nst; t++) {
+                const int o = t % kOpStages;
+                if (!wait_or_abort(&op_full[o], (t / kOpStages) & 1, abort_v, a.err)) break;
+                tc::fence_after_sync();
+                const uint32_t bbase = smem_u32(op_base + o * kOpBytes);
+                const uint32_t abase = tmem + kTmemA + (uint32_t)o * kTmemAStage;
+#pragma unroll
+                for (int j = 0; j < kStageK / 16; j++) {
+                    // K = 16: two 8-k core columns of B, 8 TMEM columns of A
+                    const uint64_t bhl = tc::smem_desc(bbase + (uint32_t)j * 256, kLBO, kSBO);  // xh; xl
+                    tc::mma_f16_ts(tmem, abase + 8 * j, bhl, id64, (t | j) != 0 ? 1u : 0u);
+                    tc::mma_f16_ts(tmem, abase + 16 + 8 * j, bhl, id32, 1u);      // A2 * xh
+                }
+                tc::commit(&op_empty[o]);
+            }
+            tc::commit(&d_full);
+        }
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------------- converters
+        griddep_launch_dependents();
+        griddep_wait();
+        const int64_t k = a.w.k;
+        if constexpr (XM == X_RMSNORM) {
+            // rms_norm_f16 (gemv.rs:445-454): inv from the producer's
+            // per-32-column sums of squares, summed as k_gemv sums them
+            for (int rr = warp; rr < kMmaRows; rr += kConvWarps) {
+                const int r = r_begin + rr;
+                float t = 0.0f;
+                if (r < r_end)
+                    for (int i = lane; i < a.ss_tiles; i += 32) t += __ldcg(a.ss + (int64_t)r * a.ldss + i);
+                t = warp_sum(t);
+                if (lane == 0) inv_s[rr] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
+            }
+            asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+        }
+        // Converter group cgp = warp / 4 takes stages t = cgp, cgp + 2, ...
+        // A role: column 32 g + lane of the tile (TMEM lane 32 g + lane), all
+        // K rows of the stage.  The nibble pair of K rows (2p, 2p+1) is
+        // gathered into one 32-bit word (byte perm) and biased into f16 as
+        // 1024 + q (low nibble) or 1024 + 16 q (high nibble); one f16 FMA gives
+        // q - 8 exactly.
+        const int g = warp & 3, cgp = warp >> 2;
+        const int cq = lane & 7;
+        const uint32_t sel = (uint32_t)(cq >> 1) | ((uint32_t)(4 + (cq >> 1)) << 8);
+        const uint32_t nmask = (cq & 1) ? 0x00F000F0u : 0x000F000Fu;
+        const __half2 m1 = __float2half2_rn((cq & 1) ? 0.0625f : 1.0f);
+        const __half2 c1 = __float2half2_rn((cq & 1) ? -72.0f : -1032.0f);
+        const int E = a.w.mma_exp;
+        const __half2 pw = __float2half2_rn(__int_as_float((127 + E) << 23));
+        const uint32_t a_lane = tmem + ((uint32_t)(32 * g) << 16) + kTmemA;
+        // B role: row r = 8 g + lane % 8, K block kc = lane / 8 (8 values)
+        const bool write_side = (XM == X_RMSNORM) && a.side && blockIdx.x == 0;
+        const int r = 8 * g + (lane & 7), kc = lane >> 3;
+        const bool rvalid = r < nvalid;
+        float inv_r = 1.0f;
+        if constexpr (XM == X_RMSNORM) inv_r = inv_s[r];
+
+        for (int t = cgp; t < nst; t += kConvGroups) {
+            const int b = t % kRawStages, o = t % kOpStages;
+            if (!wait_or_abort(&raw_full[b], (t / kRawStages) & 1, abort_v, a.err)) break;
+            if (!wait_or_abort(&op_empty[o], ((t / kOpStages) & 1) ^ 1, abort_v, a.err)) break;
+            const uint8_t *raw = raw_base + b * kRawBytes;
+            uint8_t *op = op_base + o * kOpBytes;
+            const int64_t k0 = (int64_t)(t_begin + t) * kStageK;
+
+            // ---- A1 / A2 -> tensor memory
+            const uint8_t *nibg = raw + kRawNib + g * kNibGroupStride + (lane >> 3) * 4;
+            uint4 sc4[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                sc4[i] = *reinterpret_cast<const uint4 *>(raw + kRawScl + g * kSclGroupStride + 16 * i);
+            uint32_t A1[16], A2[16];
+#pragma unroll
+            for (int p = 0; p < 16; p++) {
+                const uint32_t w0 = *reinterpret_cast<const uint32_t *>(nibg + (2 * p) * 16);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t *>(nibg + (2 * p + 1) * 16);
+                const uint32_t sw = (p & 3) == 0 ? sc4[p >> 2].x
+                                  : (p & 3) == 1 ? sc4[p >> 2].y
+                                  : (p & 3) == 2 ? sc4[p >> 2].z : sc4[p >> 2].w;
+                const __half2 s2 = __hmul2(u2h(sw), pw);            // exact (power of two)
+                const __half2 sa = u2h(h2u(s2) & 0xFFF8FFF8u);      // top 8 significant bits
+                const __half2 sb = __hsub2(s2, sa);                 // exact remainder
+                const uint32_t pr = __byte_perm(w0, w1, sel);
+                const __half2 q8 = __hfma2(u2h((pr & nmask) | 0x64006400u), m1, c1);
+                A1[p] = h2u(__hmul2(q8, sa));
+                A2[p] = h2u(__hmul2(q8, sb));
+            }
+            tc::st_32x32b_x16(a_lane + (uint32_t)o * kTmemAStage, A1);
+            tc::st_32x32b_x16(a_lane + (uint32_t)o * kTmemAStage + 16, A2);
+
+            // ---- B (hi / lo): row r, k = k0 + 8 kc .. + 7
+            float xv[8];
+            {
+                const float4 *xp = reinterpret_cast<const float4 *>(raw + kRawX + r * kXRowStride + kc * 32);
+                const float4 u0 = xp[0], u1 = xp[1];
+                xv[0] = u0.x; xv[1] = u0.y; xv[2] = u0.z; xv[3] = u0.w;
+                xv[4] = u1.x; xv[5] = u1.y; xv[6] = u1.z; xv[7] = u1.w;
+            }
+            if (!rvalid) {
+#pragma unroll
+                for (int i = 0; i < 8; i++) xv[i] = 0.0f;
+            }
+            if constexpr (XM == X_RMSNORM) {
+                const uint4 gq = __ldg(reinterpret_cast<const uint4 *>(a.gamma + k0 + 8 * kc));
+                const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float2 gf = __half22float2(u2h(gw[i]));
+                    xv[2 * i] = __fmul_rn(__fmul_rn(xv[2 * i], inv_r), gf.x);
+                    xv[2 * i + 1] = __fmul_rn(__fmul_rn(xv[2 * i + 1], inv_r), gf.y);
+                }
+                if (write_side && rvalid) {
+                    float *sp = a.side + (int64_t)(r_begin + r) * a.ldside + k0 + 8 * kc;
+#pragma unroll
+                    for (int i = 0; i < 8; i++) sp[i] = xv[i];
+                }
+            }
+            uint32_t bh[4], bl[4];
+            bool big = false;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                big |= fabsf(xv[2 * i]) > 65504.0f || fabsf(xv[2 * i + 1]) > 65504.0f;
+                const __half2 hh = __floats2half2_rn(xv[2 * i], xv[2 * i + 1]);
+                const float2 hf = __half22float2(hh);
+                bh[i] = h2u(hh);
+                bl[i] = h2u(__floats2half2_rn(__fsub_rn(xv[2 * i], hf.x), __fsub_rn(xv[2 * i + 1], hf.y)));
+            }
+            if (big) raise_error(a.err, kDevF16Range);
+            {
+                const int off = ((r >> 3) * 4 + kc) * 128 + (r & 7) * 16;
+                *reinterpret_cast<uint4 *>(op + off) = make_uint4(bh[0], bh[1], bh[2], bh[3]);
+                *reinterpret_cast<uint4 *>(op + kBTile + off) = make_uint4(bl[0], bl[1], bl[2], bl[3]);
+            }
+            tc::fence_proxy_async_smem();   // B: generic-proxy writes -> tensor-core reads
+            tc::fence_before_sync();        // A: tensor-memory stores -> the MMA thread
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&raw_empty[b]);
+                mbar_arrive(&op_full[o]);
+            }
+        }
+        if (cgp == 0) {
+            // ---- accumulator (column 32 g + lane; xh and xl halves), scaled back
+            // by 2^-E -> the owners of its units
+            const bool ok = wait_or_abort(&d_full, 0, abort_v, a.err);
+            tc::fence_after_sync();
+            float vh[32], vl[32];
+            if (ok) {
+                tc::ld_32x32b_x32(tmem + ((uint32_t)(32 * g) << 16), vh);
+                tc::ld_32x32b_x32(tmem + ((uint32_t)(32 * g) << 16) + kMmaRows, vl);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) vh[i] = vl[i] = 0.0f;
+            }
+            const float unscale = __int_as_float((127 - E) << 23);
+#pragma unroll
+            for (int n = 0; n < kMmaRows; n++) vh[n] = __fmul_rn(__fadd_rn(vh[n], vl[n]), unscale);
+            const int cc2 = (EM == E_SWIGLU) ? (g >> 1) : g;
+            const int hp = (EM == E_SWIGLU) ? (g & 1) : 0;
+#pragma unroll
+            for (int c = 0; c < NCH; c++) {
+                if (c * RC < nvalid) {
+                    const int u = cc2 * NCH + c;
+                    const int owner = u % S, slot = u / S;
+                    float *base = (S == 1) ? recv : cluster.map_shared_rank(recv, owner);
+                    float2 *dst = reinterpret_cast<float2 *>(base + (((slot * S + rank) * P + hp) * 32 + lane) * RPAD);
+#pragma unroll
+                    for (int i = 0; i < RC / 2; i++) dst[i] = make_float2(vh[c * RC + 2 * i], vh[c * RC + 2 * i + 1]);
+                }
+            }
+        }
+    }
+    tc::fence_before_sync();
+    // ---- every partial is in its owner's receive buffer after this barrier
+    if (S > 1) cluster.sync(); else __syncthreads();
+    if (warp == kMmaWarp) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+    // ---- finish this rank's units: rank-order sums, epilogue
+    const int64_t n_out = (EM == E_SWIGLU) ? (a.w.C / 2) * 32 : a.w.n;
+    for (int slot = 0; slot * S + rank < kUnits; slot++) {
+        const int u = slot * S + rank;
+        const int cc2 = u / NCH, c = u % NCH;
+        const int nrow = min(RC, nvalid - c * RC);
+        for (int it = threadIdx.x; it < nrow * 32; it += blockDim.x) {  // whole rows per warp
+            const int l = it & 31, rr = it >> 5;
+            float vsum = 0.0f, usum = 0.0f;
+            for (int j = 0; j < S; j++) {
+                const float *src = recv + (((slot * S + j) * P) * 32 + l) * RPAD + rr;
+                vsum += src[0];
+                if constexpr (EM == E_SWIGLU) usum += src[32 * RPAD];
+            }
+            const int row = c * RC + rr;
+            const int64_t grp = (int64_t)blockIdx.x * CO + cc2;
+            if constexpr (EM == E_RESID) {
+                // x[j] += attn_out[j] (talker.rs:334-336)
+                const float yr = __ldcg(a.y + (int64_t)(r_begin + row) * a.ldy + grp * 32 + l);
+                finalize_resid(a, r_begin + row, grp, l, __fadd_rn(yr, vsum));
+            } else {
+                finalize_group<EM>(a, r_begin + row, grp, l, vsum, usum, n_out, CO);
+            }
+        }
+    }
+    // tail columns beyond the last full group stay zero (gemv.rs:846-861)
+    if (EM == E_STORE && a.w.n > a.w.C * 32 && blockIdx.x == 0 && rank == 0) {
+        for (int rr = r_begin; rr < r_end; rr++)
+            for (int64_t col = a.w.C * 32 + threadIdx.x; col < a.w.n; col += blockDim.x)
+                a.y[(int64_t)rr * a.ldy + col] = 0.0f;
+    }
+    gemv_global_stage(a, last_flag, gridDim.x * CO);
+}
+
+template <int XM, int EM>
+int mma_attrs() {
+    QORA_CUDA(cudaFuncSetAttribute(k_gemv_mma<XM, EM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    QORA_CUDA(cudaFuncSetAttribute(k_gemv_mma<XM, EM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kMmaSmem));
+    // two CTAs per SM need the shared-memory carveout at its maximum
+    QORA_CUDA(cudaFuncSetAttribute(k_gemv_mma<XM, EM>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   (int)cudaSharedmemCarveoutMaxShared));
+    return QORA_OK;
+}
+
+template <int XM>
+int mma_attrs_e() {
+    QORA_TRY((mma_attrs<XM, E_STORE>()));
+    QORA_TRY((mma_attrs<XM, E_BIAS>()));
+    QORA_TRY((mma_attrs<XM, E_RESID>()));
+    return mma_attrs<XM, E_SWIGLU>();
+}
+
+template <int XM>
+int launch_mma_e(const GemvArgs &a, int emode, const GemvPlan &p, cudaStream_t st) {
+    switch (emode) {
+        case E_STORE: return launch_ex(k_gemv_mma<XM, E_STORE>, p.grid, p.block, kMmaSmem, st, (unsigned)p.S, a);
+        case E_BIAS: return launch_ex(k_gemv_mma<XM, E_BIAS>, p.grid, p.block, kMmaSmem, st, (unsigned)p.S, a);
+        case E_RESID: return launch_ex(k_gemv_mma<XM, E_RESID>, p.grid, p.block, kMmaSmem, st, (unsigned)p.S, a);
+        case E_SWIGLU: return launch_ex(k_gemv_mma<XM, E_SWIGLU>, p.grid, p.block, kMmaSmem, st, (unsigned)p.S, a);
+    }
+    return set_error(QORA_ERR_INVALID, "bad epilogue mode %d", emode);
+}
+
+bool mma_disabled_by_env() {
+    static const bool off = [] {
+        const char *v = getenv("QORA_MMA");
+        return v && v[0] == '0';
+    }();
+    return off;
+}
+
+// Clusters of 2^i CTAs (i = 0..4) that can be resident at once, per device:
+// a grid with more clusters than this runs in waves.
+constexpr int kMaxDevices = 64;
+int g_max_clusters[kMaxDevices][5];
+
+// cudaOccupancyMaxActiveClusters counts one CTA of this kernel per SM.  Two
+// fit when each SM sub-partition can hold the registers of the warps two CTAs
+// place on it (the 10 warps of a CTA go 3/3/2/2 over the four 16K-register
+// sub-partitions: 6 warps at most), and then twice as many clusters are
+// resident (measured on 148 SMs: 14 clusters of 16 CTAs where the query
+// reports 7).  Only a performance bound: more clusters than this run in waves.
+int query_max_clusters(int dev) {
+    cudaFuncAttributes fa;
+    QORA_CUDA(cudaFuncGetAttributes(&fa, k_gemv_mma<X_RMSNORM, E_SWIGLU>));
+    const int regs_warp = ((fa.numRegs + 7) / 8) * 8 * 32;
+    const int warps_smsp = 2 * ((kMmaThreads / 32 + 3) / 4);
+    const int per_sm = (warps_smsp * regs_warp <= 16384) ? 2 : 1;
+    for (int i = 0; i < 5; i++) {
+        const int S = 1 << i;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(64, (unsigned)S, 1);
+        cfg.blockDim = dim3(kMmaThreads);
+        cfg.dynamicSmemBytes = kMmaSmem;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 1;
+        attr.val.clusterDim.y = (unsigned)S;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        QORA_CUDA(cudaOccupancyMaxActiveClusters(&n, k_gemv_mma<X_RMSNORM, E_SWIGLU>, &cfg));
+        g_max_clusters[dev][i] = n * per_sm;
+    }
+    return QORA_OK;
+}
+
+}  // namespace
+
+int gemv_mma_init() {
+    QORA_TRY(mma_attrs_e<X_PLAIN>());
+    QORA_TRY(mma_attrs_e<X_RMSNORM>());
+    int dev = 0;
+    QORA_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= kMaxDevices) return set_error(QORA_ERR_UNSUPPORTED, "device id %d", dev);
+    return query_max_clusters(dev);
+}
+
+bool gemv_mma_eligible(const GemvArgs &a, int xmode, int emode) {
+    if (mma_disabled_by_env()) return false;
+    if (a.rows < kMmaMinRows) return false;
+    if (xmode != X_PLAIN && xmode != X_RMSNORM) return false;
+    if (emode < E_STORE || emode > E_SWIGLU) return false;
+    if (a.w.mma_exp < 0 || a.w.k % kStageK != 0 || a.w.C % kMmaGroups != 0) return false;
+    if (a.ldx % 4 != 0 || ((uintptr_t)a.x & 15) != 0) return false;
+    if (xmode == X_RMSNORM && ((uintptr_t)a.gamma & 15) != 0) return false;
+    return true;
+}
+
+GemvPlan plan_gemv_mma(int64_t k, int64_t C, int rows, int emode, int num_sms) {
+    GemvPlan p{};
+    p.mma = true;
+    p.cpc = kMmaGroups;
+    p.B = kMmaRows;
+    p.rows_per_z = kMmaRows;
+    p.Z = (rows + kMmaRows - 1) / kMmaRows;
+    const int64_t tiles = C / kMmaGroups;
+    const int64_t stages = k / kStageK;
+    // about two CTAs per SM: K-split CTAs (one cluster) fill what the column
+    // and row tiles leave
+    const int64_t want = (2LL * num_sms) / std::max<int64_t>(1, tiles * p.Z);
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const int *maxc = (dev >= 0 && dev < kMaxDevices) ? g_max_clusters[dev] : nullptr;
+    // a power of two (the reduction's 16 units split evenly over the ranks);
+    // larger only while all clusters of the grid stay resident at once
+    int64_t S = 1;
+    int lg = 0;
+    while (2 * S <= want && 2 * S <= std::min<int64_t>(kMaxSplit, stages) &&
+           (!maxc || maxc[lg + 1] <= 0 || tiles * p.Z <= maxc[lg + 1])) {
+        S *= 2;
+        lg++;
+    }
+    p.S = (int)S;
+    p.WR = kConvWarps;
+    p.NSUB = 1;
+    p.rows_per_cta_k = (int)((stages + S - 1) / S * kStageK);
+    p.grid = dim3((unsigned)tiles, (unsigned)p.S, (unsigned)p.Z);
+    p.block = dim3(kMmaThreads);
+    (void)emode;
+    return p;
+}
+
+int launch_gemv_mma(const GemvArgs &a, int xmode, int emode, const GemvPlan &p, cudaStream_t st) {
+    switch (xmode) {
+        case X_PLAIN: return launch_mma_e<X_PLAIN>(a, emode, p, st);
+        case X_RMSNORM: return launch_mma_e<X_RMSNORM>(a, emode, p, st);
+    }
+    return set_error(QORA_ERR_INVALID, "tensor-core GEMV: prologue mode %d unsupported", xmode);
+}
+
+}  // namespace qora

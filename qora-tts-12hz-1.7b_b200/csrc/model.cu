@@ -111,7 +111,7 @@ struct Launcher {
     int count = 0;  // kernels launched
 
     int gemv(GemvArgs a, int xm, int em) {
-        const GemvPlan p = plan_gemv(a.w.k, a.w.C, a.rows, em, ctx->num_sms);
+        const GemvPlan p = plan_gemv_for(a, xm, em, ctx->num_sms);
         if (!a.err) a.err = ctx->err.as<int>();
         count++;
         return launch_gemv(a, xm, em, p, w->gticket.as<unsigned>(), st);

@@ -158,3 +158,49 @@ def test_small_k_single_split(E, ctx, orc, k, rows):
     got = _dev(E, ctx, w.packed, w.scales, k, n).gemv(torch.from_numpy(x).cuda()).cpu().numpy()
     for r in range(rows):
         _close(got[r], orc.gemv_single(x[r], w))
+
+
+# Batches of >= 8 rows on 128-column tiles run on the tensor cores (tcgen05,
+# f16 operands split into exact weight halves and hi/lo input halves, f32
+# accumulation): the same 1e-4-of-scale bound as the CUDA-core kernel.
+@pytest.mark.parametrize("k,n,rows", [(2048, 6144, 32), (6144, 2048, 16), (2048, 3072, 8),
+                                      (1024, 2048, 100), (2048, 1024, 512), (1024, 3072, 9)])
+def test_batched_shapes_tensor_core(E, ctx, orc, k, n, rows):
+    import ctypes
+    import torch
+    w = orc.synth_q4(600 + rows, 0.02, k, n)
+    x = orc.synth_normal(601 + rows, 1.0, rows * k).reshape(rows, k)
+    got = _dev(E, ctx, w.packed, w.scales, k, n).gemv(torch.from_numpy(x).cuda()).cpu().numpy()
+    ctx.check_device_error()
+    ref = np.zeros((rows, n), np.float32)
+    ws = w.cstruct()
+    orc.lib().oq_gemm(orc.ptr(x), rows, ctypes.addressof(ws), orc.ptr(ref))
+    for r in range(rows):
+        _close(got[r], ref[r])
+
+
+def test_batched_tensor_core_is_deterministic(E, ctx, orc):
+    import torch
+    k, n, rows = 2048, 2048, 24
+    w = orc.synth_q4(610, 0.02, k, n)
+    x = torch.from_numpy(orc.synth_normal(611, 1.0, rows * k)).cuda().reshape(rows, k)
+    dw = _dev(E, ctx, w.packed, w.scales, k, n)
+    a = dw.gemv(x).cpu().numpy()
+    b = dw.gemv(x).cpu().numpy()
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+
+
+def test_batched_input_outside_f16_range_is_an_error(E, ctx, orc):
+    # the tensor-core operands hold inputs in f16 (hi/lo halves): a value past
+    # the f16 range is reported instead of silently overflowing
+    import torch
+    from qora_b200 import _lib
+    k, n, rows = 1024, 1024, 8
+    w = orc.synth_q4(620, 0.02, k, n)
+    x = orc.synth_normal(621, 1.0, rows * k).reshape(rows, k)
+    x[3, 100] = 1.0e6
+    _dev(E, ctx, w.packed, w.scales, k, n).gemv(torch.from_numpy(x).cuda())
+    with pytest.raises(_lib.QoraError) as ei:
+        ctx.check_device_error()
+    assert ei.value.status == 5   # QORA_ERR_RANGE
+    ctx.check_device_error()      # cleared

@@ -251,3 +251,38 @@ def test_position_past_rope_table_is_an_error(E, ctx, orc, tiny):
     with pytest.raises(Exception):
         ctx.check_device_error()
     ctx.check_device_error()  # cleared
+
+
+def test_engine_batch8_frames_match_oracle(E, ctx, orc):
+    """Eight streams: the talker and predictor projections run on the
+    tensor-core GEMV (>= 8 rows), the output heads (not a multiple of 128
+    columns) on the CUDA-core kernel; frames must equal the oracle's."""
+    import torch
+    import qora_b200
+    cfg = qora_b200.ModelConfig.tiny()
+    om = orc.OracleModel(orc.Model.synth(orc.ModelConfig.tiny()))
+    talker = E.Talker(ctx, qora_b200.synth_talker(cfg), max_batch=8)
+    pred = E.CodePredictor(ctx, qora_b200.synth_predictor(cfg), max_batch=8)
+    B, T, F = 8, 3, 3
+    eng = E.Engine(talker, pred, B, max_pos=32)
+    x = orc.synth_normal(960, 1.0, B * T * cfg.t_hidden).reshape(B, T, cfg.t_hidden)
+    seeds = [1000 + b for b in range(B)]
+    eng.prefill(x, seeds)
+    text = orc.synth_normal(961, 1.0, B * cfg.t_hidden).reshape(B, cfg.t_hidden)
+    params = orc.SampleParams(0.9, 50, 1.0, 1.05)
+    states, kvs = [], []
+    for b in range(B):
+        tkv, pkv = om.talker_kv(32), om.predictor_kv()
+        hdn = om.talker_prefill(x[b], tkv, 0)
+        states.append({"logits": om.codec_head(hdn), "hidden": hdn.copy(),
+                       "prev": np.zeros(16, np.uint32), "rng": seeds[b]})
+        kvs.append((tkv, pkv))
+    tt = _cuda(text)
+    codes = torch.zeros(B, 16, dtype=torch.int32).cuda()
+    for f in range(F):
+        eng.frame(tt, codes)
+        got = codes.cpu().numpy()
+        for b in range(B):
+            ref = om.frame(kvs[b][0], kvs[b][1], params, text[b], T + f, states[b])
+            assert list(got[b]) == list(ref), (f, b)
+    ctx.check_device_error()
