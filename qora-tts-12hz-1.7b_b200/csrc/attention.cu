@@ -78,7 +78,11 @@ template <int HD>
 int launch_attn_hd(const AttnArgs &a, cudaStream_t st) {
     const int G = a.heads / a.kv_heads;
     const int rows = a.streams * a.T;
-    dim3 grid(a.kv_heads, kAttnMaxSplit, rows);
+    // position splits: the kernel uses min(16, ceil(positions / 32)) of them
+    // and positions never exceed the cache capacity, so that bounds the grid
+    // (a short cache such as the predictor's launches one split per row)
+    const int ysplit = std::max(1, std::min(kAttnMaxSplit, (a.kv.max_pos + attn::kTile - 1) / attn::kTile));
+    dim3 grid(a.kv_heads, ysplit, rows);
     switch (G) {
         case 1: return launch_ex(k_attention<HD, 1>, grid, dim3(kThreads), 0, st, 1u, a);
         case 2: return launch_ex(k_attention<HD, 2>, grid, dim3(kThreads), 0, st, 1u, a);

@@ -121,6 +121,16 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, vo
     }
 }
 
+// Shared-memory address of `local` (this CTA) in cluster rank `rank`'s shared memory.
+__device__ __forceinline__ uint32_t cluster_addr(const void *local, int rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
+    return r;
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b) {
+    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
@@ -403,10 +413,31 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
                 if (c * RC < nvalid) {
                     const int u = cc2 * NCH + c;
                     const int owner = u % S, slot = u / S;
-                    float *base = (S == 1) ? recv : cluster.map_shared_rank(recv, owner);
-                    float2 *dst = reinterpret_cast<float2 *>(base + (((slot * S + rank) * P + hp) * 32 + lane) * RPAD);
+                    const float *dst = recv + (((slot * S + rank) * P + hp) * 32 + lane) * RPAD;
+                    const uint32_t da = (S == 1) ? smem_u32(dst) : cluster_addr(dst, owner);
 #pragma unroll
-                    for (int i = 0; i < RC / 2; i++) dst[i] = make_float2(vh[c * RC + 2 * i], vh[c * RC + 2 * i + 1]);
+                    for (int i = 0; i < RC / 2; i++) st_cluster_v2(da + 8 * i, vh[c * RC + 2 * i], vh[c * RC + 2 * i + 1]);
+                }
+            }
+        }
+    }
+    // the residual of this rank's first outputs does not depend on the
+    // partial sums: load it while the cluster barrier completes
+    constexpr int kPre = 4;
+    float yres[kPre];
+    if constexpr (EM == E_RESID) {
+#pragma unroll
+        for (int m = 0; m < kPre; m++) {
+            yres[m] = 0.0f;
+            const int slot = 0;  // the first unit of this rank covers the prefetched items
+            const int u = slot * S + rank;
+            const int it = threadIdx.x + m * blockDim.x;
+            if (u < kUnits) {
+                const int cc2 = u / NCH, c = u % NCH;
+                const int nrow = min(RC, nvalid - c * RC);
+                if (it < nrow * 32) {
+                    const int64_t col = ((int64_t)blockIdx.x * CO + cc2) * 32 + (it & 31);
+                    yres[m] = __ldcg(a.y + (int64_t)(r_begin + c * RC + (it >> 5)) * a.ldy + col);
                 }
             }
         }
@@ -424,7 +455,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
         const int u = slot * S + rank;
         const int cc2 = u / NCH, c = u % NCH;
         const int nrow = min(RC, nvalid - c * RC);
-        for (int it = threadIdx.x; it < nrow * 32; it += blockDim.x) {  // whole rows per warp
+        for (int it = threadIdx.x, m = 0; it < nrow * 32; it += blockDim.x, m++) {  // whole rows per warp
             const int l = it & 31, rr = it >> 5;
             float vsum = 0.0f, usum = 0.0f;
             for (int j = 0; j < S; j++) {
@@ -436,7 +467,15 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
             const int64_t grp = (int64_t)blockIdx.x * CO + cc2;
             if constexpr (EM == E_RESID) {
                 // x[j] += attn_out[j] (talker.rs:334-336)
-                const float yr = __ldcg(a.y + (int64_t)(r_begin + row) * a.ldy + grp * 32 + l);
+                float yr = 0.0f;
+                bool have = false;
+#pragma unroll
+                for (int q = 0; q < kPre; q++)
+                    if (slot == 0 && m == q) {
+                        yr = yres[q];
+                        have = true;
+                    }
+                if (!have) yr = __ldcg(a.y + (int64_t)(r_begin + row) * a.ldy + grp * 32 + l);
                 finalize_resid(a, r_begin + row, grp, l, __fadd_rn(yr, vsum));
             } else {
                 finalize_group<EM>(a, r_begin + row, grp, l, vsum, usum, n_out, CO);
