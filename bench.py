@@ -227,6 +227,26 @@ def _graph_time_ms(torch, fn, reps):
     return e0.elapsed_time(e1) / reps
 
 
+def frame_algorithmic_bytes(cfg, positions):
+    """Algorithmic bytes of one batch-1 frame: talker step (Q4 weights, f16
+    norms, K/V read over `positions` + 1 cached positions and the appended
+    row, the embedding row) plus the predictor's 15 weight passes (one
+    2-token prefill + 14 steps, each with the input projection and one
+    head), Q4 at 0.5625 B per weight."""
+    q4 = 0.5625
+    H, F = cfg.t_hidden, cfg.t_ffn
+    qd, kd = cfg.t_heads * cfg.t_head_dim, cfg.t_kv_heads * cfg.t_head_dim
+    t_w = cfg.t_layers * (H * (qd + 2 * kd) + qd * H + 2 * H * F + F * H) + H * cfg.t_vocab
+    t_norm = 2 * (cfg.t_layers * (2 * H + 2 * cfg.t_head_dim) + H)
+    kv_pos = cfg.t_layers * 2 * kd * 4
+    Hp, Fp = cfg.p_hidden, cfg.p_ffn
+    pq, pk = cfg.p_heads * cfg.p_head_dim, cfg.p_kv_heads * cfg.p_head_dim
+    p_layer = Hp * (pq + 2 * pk) + pq * Hp + 2 * Hp * Fp + Fp * Hp
+    p_pass = cfg.p_layers * p_layer + H * Hp + Hp * cfg.p_vocab
+    return (q4 * t_w + t_norm + kv_pos * (positions + 1) + kv_pos + 1152
+            + q4 * cfg.p_groups * p_pass)
+
+
 def gemv_stream_roofline(E, ctx, tw, torch, reps=5):
     """k_gemv over the whole talker weight set at batch 1, back to back in one
     CUDA graph (197 launches, 796 MB > L2): algorithmic bytes and time."""
@@ -386,29 +406,50 @@ def run_ours(args):
             dist.destroy_process_group()
         return
 
-    # ---- roofline of the dominant kernel (k_gemv over the talker weights, batch 1)
+    # ---- roofline of the dominant kernel: at batch 1 the whole frame is one
+    # k_frame launch (talker step + 15-code predictor + sampler), so its
+    # launch duration is the CUDA-event time per frame measured above
     peak, peak_src = peaks()
-    roof = None
+    roof, gemv_stream = None, None
     if not args.no_roofline:
-        byts, gms = gemv_stream_roofline(E, ctx, tw, torch)
-        n_launch = 7 * len(tw.layers) + 1
-        achieved = byts / (gms / 1000.0) / 1e9
+        pos_avg = PREFILL + W + 0.5 * K  # cache positions during the timed frames
+        fb = frame_algorithmic_bytes(cfg, pos_avg)
+        us = 1000.0 * ms / K
+        achieved = fb / (us * 1e-6) / 1e9
         traffic = None
         try:
-            # DRAM bytes per algorithmic byte from the committed ncu capture of
-            # k_gemv (profiles/k_gemv_b1_2048x6144.md), scaled to this launch mix
+            # DRAM bytes of one k_frame launch from the committed ncu capture
+            # (profiles/k_frame_b1_frame.md, same workload)
+            with open(os.path.join(ROOT, "profiles", "k_frame_b1_frame.md")) as f:
+                m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", f.read())
+            if m:
+                traffic = int(m.group(1))
+        except OSError:
+            pass
+        roof = {"bound": "hbm", "kernel": "k_frame (persistent frame kernel, batch 1)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": traffic,
+                "launches_per_step": kernels, "us_per_launch": round(us, 2),
+                "algorithmic_bytes_per_launch": round(fb),
+                "bytes_model": "talker weights 796,262,400 + norms + KV read 229,376 B x (P+1) + "
+                               "KV write + predictor weight passes (15 x per-pass weights x 0.5625 B)"}
+        # the per-launch Q4 GEMV kernel over the talker weights, back to back
+        byts, gms = gemv_stream_roofline(E, ctx, tw, torch)
+        n_launch = 7 * len(tw.layers) + 1
+        g_ach = byts / (gms / 1000.0) / 1e9
+        g_traffic = None
+        try:
             with open(os.path.join(ROOT, "profiles", "k_gemv_b1_2048x6144.md")) as f:
                 m = re.search(r"dram_traffic_per_algorithmic_byte:\s*([0-9.]+)", f.read())
             if m:
-                traffic = round(float(m.group(1)) * byts / n_launch)
+                g_traffic = round(float(m.group(1)) * byts / n_launch)
         except OSError:
             pass
-        roof = {"bound": "hbm", "kernel": "k_gemv (talker Q4 GEMVs, batch 1, back-to-back)",
-                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                "traffic": traffic, "launches": n_launch,
-                "us_per_launch": round(1000.0 * gms / n_launch, 2),
-                "algorithmic_bytes_per_launch": round(byts / n_launch)}
+        gemv_stream = {"kernel": "k_gemv (talker Q4 GEMVs, batch 1, back-to-back launches)",
+                       "achieved": round(g_ach, 1), "peak": peak, "unit": "GB/s",
+                       "frac": round(g_ach / peak, 4), "traffic": g_traffic, "launches": n_launch,
+                       "us_per_launch": round(1000.0 * gms / n_launch, 2),
+                       "algorithmic_bytes_per_launch": round(byts / n_launch)}
 
     sweep = None if args.no_sweep else gemv_sweep(E, ctx, torch, qb)
 
@@ -435,6 +476,7 @@ def run_ours(args):
         "gpu_launches": int(kernels * K),
         "kernels_per_step": kernels,
         "roofline": roof,
+        "gemv_stream": gemv_stream,
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "batch32": b32,

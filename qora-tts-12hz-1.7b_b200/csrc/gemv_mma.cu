@@ -30,10 +30,11 @@
 //              16-byte cp.async copies (weights are immutable and issued before
 //              the wait on the previous kernel);
 //   warp 5     allocates tensor memory and issues the MMAs (one thread).
-// K-split: the S CTAs of one cluster each own a slice of the 32 rows; every
-// CTA stores its partial sums for a slice into the owner's shared memory, one
-// cluster barrier, then the owner sums the S partials in rank order and
-// applies the epilogue.  Every mbarrier wait is bounded.
+// K-split: the S CTAs of one cluster each own a slice of the outputs; every
+// CTA sends its partial sums for a slice into the owner's shared memory with
+// asynchronous stores that complete on the owner's mbarrier, and the owner,
+// once its bytes are in, sums the S partials in rank order and applies the
+// epilogue.  Every mbarrier wait is bounded.
 #include "gemv_impl.cuh"
 #include "tc.cuh"
 
@@ -67,7 +68,8 @@ constexpr int kXRowStride = kStageK * 4 + 16;
 constexpr int kRawNib = 0;
 constexpr int kRawScl = kRawNib + kMmaGroups * kNibGroupStride;
 constexpr int kRawX = kRawScl + kMmaGroups * kSclGroupStride;
-constexpr int kRawBytes = kRawX + kMmaRows * kXRowStride;
+constexpr int kRawGamma = kRawX + kMmaRows * kXRowStride;   // RMSNorm gamma of the stage (f16)
+constexpr int kRawBytes = kRawGamma + kStageK * 2;
 // operand stage: B = [xh rows; xl rows] (64 x 32 f16) in the canonical K-major
 // layout without swizzle.  Core matrix (8 rows x 8 k) = 128 contiguous bytes;
 // core (row block rb, k block kc) at (rb * 4 + kc) * 128, so LBO (along K) =
@@ -78,9 +80,9 @@ constexpr uint32_t kLBO = 128, kSBO = 512;
 // K-split reduction: 16 units per CTA tile, unit = (output group, chunk of
 // kChunkRows(EM) rows); rank q owns units u with u % S == q (S a power of two
 // <= 16).  Receive buffer: [unit slot][source rank][partial][column][padded
-// chunk rows]; padding keeps float2 stores aligned and the reads 2-way at most.
+// chunk rows] (rows padded by 4: 16-byte remote stores).
 constexpr int kUnits = 16;
-constexpr int kRecvFloats = kUnits * 2 * 32 * 6 > kUnits * 32 * 10 ? kUnits * 2 * 32 * 6 : kUnits * 32 * 10;
+constexpr int kRecvFloats = kUnits * 2 * 32 * 8 > kUnits * 32 * 12 ? kUnits * 2 * 32 * 8 : kUnits * 32 * 12;
 constexpr size_t kMmaSmem =
     128 + (size_t)kOpStages * kOpBytes + (size_t)kRawStages * kRawBytes + (size_t)kRecvFloats * 4;
 
@@ -127,8 +129,24 @@ __device__ __forceinline__ uint32_t cluster_addr(const void *local, int rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(local)), "r"(rank));
     return r;
 }
-__device__ __forceinline__ void st_cluster_v2(uint32_t addr, float a, float b) {
-    asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(a), "f"(b) : "memory");
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c),
+                 "f"(d)
+                 : "memory");
+}
+// Asynchronous 16-byte store into a cluster peer's shared memory; its bytes
+// complete on the peer's mbarrier `bar` (a shared::cluster address too).
+__device__ __forceinline__ void st_async_v4(uint32_t addr, float a, float b, float c, float d, uint32_t bar) {
+    asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                     addr),
+                 "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
@@ -139,11 +157,11 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
     constexpr int CO = (EM == E_SWIGLU) ? kMmaGroups / 2 : kMmaGroups;  // output groups per CTA
     constexpr int P = (EM == E_SWIGLU) ? 2 : 1;      // partials per output (gate, up)
     constexpr int RC = kMmaRows * CO / kUnits;       // rows per reduction unit (8, or 4 for SwiGLU)
-    constexpr int RPAD = RC + 2;                     // padded chunk row stride in the receive buffer
+    constexpr int RPAD = RC + 4;                     // padded chunk row stride in the receive buffer
     constexpr int NCH = kMmaRows / RC;               // row chunks per output group
     extern __shared__ uint8_t mma_dyn[];
     __shared__ __align__(8) uint64_t raw_full[kRawStages], raw_empty[kRawStages];
-    __shared__ __align__(8) uint64_t op_full[kOpStages], op_empty[kOpStages], d_full;
+    __shared__ __align__(8) uint64_t op_full[kOpStages], op_empty[kOpStages], d_full, recv_full;
     __shared__ uint32_t tmem_slot;
     __shared__ float inv_s[kMmaRows];
     __shared__ int abort_s;
@@ -177,6 +195,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
             mbar_init(&op_empty[i], 1);
         }
         mbar_init(&d_full, 1);
+        mbar_init(&recv_full, 1);  // this rank's K-split partials (expect_tx below)
         static_assert(kOpStages % kConvGroups == 0, "a converter group keeps its operand stages");
         abort_s = 0;
         mbar_fence_init();
@@ -189,6 +208,19 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
     __syncthreads();
     tc::fence_after_sync();
     const uint32_t tmem = tmem_slot;
+    // K-split: the cluster's ranks send partial sums into each other's
+    // receive buffers; a rank's mbarriers must be initialised before a peer
+    // stores, which this arrive (released here, waited on before the first
+    // remote store) guarantees.  This rank expects every byte of its units.
+    if (S > 1) {
+        cluster_arrive();
+        if (threadIdx.x == 0) {
+            uint32_t bytes = 0;
+            for (int slot = 0; slot * S + rank < kUnits; slot++)
+                if (((slot * S + rank) % NCH) * RC < nvalid) bytes += (uint32_t)(S * P * 32 * RC * 4);
+            mbar_arrive_expect_tx(&recv_full, bytes);
+        }
+    }
 
     if (warp == kProdWarp) {
         // ---------------------------------------------------------- producer
@@ -205,15 +237,30 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
                 cp_async16(raw + kRawScl + g * kSclGroupStride + part * 16,
                            reinterpret_cast<const uint8_t *>(a.w.scl + (c0 + g) * a.w.kpad + k0) + part * 16);
             }
+            if constexpr (XM == X_RMSNORM) {  // the stage's 32 gamma values (immutable)
+                if (lane >= 28) cp_async16(raw + kRawGamma + (lane - 28) * 16, a.gamma + k0 + (lane - 28) * 8);
+            }
         };
+        // X_EMBED: the token of row `lane` (tokens come from earlier kernels)
+        uint32_t tok = 0;
         auto issue_x = [&](int t) {
             const int b = t % kRawStages;
             uint8_t *raw = raw_base + b * kRawBytes;
             const int64_t k0 = (int64_t)(t_begin + t) * kStageK;
-            for (int i = lane; i < nvalid * 8; i += 32) {  // 8 x 16 bytes per row
-                const int r = i >> 3, part = i & 7;
-                cp_async16(raw + kRawX + r * kXRowStride + part * 16,
-                           a.x + (int64_t)(r_begin + r) * a.ldx + k0 + part * 4);
+            if constexpr (XM == X_EMBED) {
+                // row `lane`: the stage's 16 bytes of nibbles and the 16-byte
+                // block holding its scale (embed_lookup_q4, gemv.rs:425-433)
+                if (lane < nvalid) {
+                    cp_async16(raw + kRawX + lane * kXRowStride, a.emb.packed + (int64_t)tok * (a.emb.n >> 1) + (k0 >> 1));
+                    const int64_t si = (int64_t)tok * (a.emb.n >> 5) + (k0 >> 5);
+                    cp_async16(raw + kRawX + lane * kXRowStride + 16, a.emb.scl + (si & ~(int64_t)7));
+                }
+            } else {
+                for (int i = lane; i < nvalid * 8; i += 32) {  // 8 x 16 bytes per row
+                    const int r = i >> 3, part = i & 7;
+                    cp_async16(raw + kRawX + r * kXRowStride + part * 16,
+                               a.x + (int64_t)(r_begin + r) * a.ldx + k0 + part * 4);
+                }
             }
             cp_async_arrive(&raw_full[b]);
         };
@@ -228,6 +275,13 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
         for (int t = 0; t < pre; t++) issue_w(t);
         griddep_launch_dependents();
         griddep_wait();
+        if constexpr (XM == X_EMBED) {
+            if (lane < nvalid) tok = __ldcg(a.tok + (int64_t)(r_begin + lane) * a.ldtok);
+            if ((int64_t)tok >= a.emb.rows) {  // never read outside the table
+                raise_error(a.err, kDevRange);
+                tok = 0;
+            }
+        }
         for (int t = 0; t < pre; t++) issue_x(t);
         for (int t = pre; t < nst; t++) {
             const int b = t % kRawStages;
@@ -241,6 +295,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
         // every copy this CTA issued lands before the CTA can exit
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncwarp();
+        if (S > 1) cluster_wait();
     } else if (warp == kMmaWarp) {
         // ---------------------------------------------------------- MMA issue
         griddep_launch_dependents();
@@ -266,6 +321,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
             tc::commit(&d_full);
         }
         __syncwarp();
+        if (S > 1) cluster_wait();
     } else {
         // ---------------------------------------------------------- converters
         griddep_launch_dependents();
@@ -303,6 +359,11 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
         const bool write_side = (XM == X_RMSNORM) && a.side && blockIdx.x == 0;
         const int r = 8 * g + (lane & 7), kc = lane >> 3;
         const bool rvalid = r < nvalid;
+        uint32_t tok_r = 0;  // X_EMBED: the token of row r
+        if constexpr (XM == X_EMBED) {
+            if (rvalid) tok_r = __ldcg(a.tok + (int64_t)(r_begin + r) * a.ldtok);
+            if ((int64_t)tok_r >= a.emb.rows) tok_r = 0;  // (reported by the producer)
+        }
         float inv_r = 1.0f;
         if constexpr (XM == X_RMSNORM) inv_r = inv_s[r];
 
@@ -341,7 +402,16 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
 
             // ---- B (hi / lo): row r, k = k0 + 8 kc .. + 7
             float xv[8];
-            {
+            if constexpr (XM == X_EMBED) {
+                // x = scale * (q - 8) (gemv.rs:425-433): exact in f32, and
+                // exact as the f16 hi + lo pair below
+                const uint32_t nb = *reinterpret_cast<const uint32_t *>(raw + kRawX + r * kXRowStride + 4 * kc);
+                const int64_t si = (int64_t)tok_r * (a.emb.n >> 5) + (k0 >> 5);
+                const float sc = __half2float(
+                    *reinterpret_cast<const __half *>(raw + kRawX + r * kXRowStride + 16 + 2 * (int)(si & 7)));
+#pragma unroll
+                for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(sc, (float)((int)((nb >> (4 * i)) & 15u) - 8));
+            } else {
                 const float4 *xp = reinterpret_cast<const float4 *>(raw + kRawX + r * kXRowStride + kc * 32);
                 const float4 u0 = xp[0], u1 = xp[1];
                 xv[0] = u0.x; xv[1] = u0.y; xv[2] = u0.z; xv[3] = u0.w;
@@ -352,7 +422,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
                 for (int i = 0; i < 8; i++) xv[i] = 0.0f;
             }
             if constexpr (XM == X_RMSNORM) {
-                const uint4 gq = __ldg(reinterpret_cast<const uint4 *>(a.gamma + k0 + 8 * kc));
+                const uint4 gq = *reinterpret_cast<const uint4 *>(raw + kRawGamma + 16 * kc);
                 const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
 #pragma unroll
                 for (int i = 0; i < 4; i++) {
@@ -390,6 +460,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
                 mbar_arrive(&op_full[o]);
             }
         }
+        if (cgp != 0 && S > 1) cluster_wait();
         if (cgp == 0) {
             // ---- accumulator (column 32 g + lane; xh and xl halves), scaled back
             // by 2^-E -> the owners of its units
@@ -408,15 +479,26 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
             for (int n = 0; n < kMmaRows; n++) vh[n] = __fmul_rn(__fadd_rn(vh[n], vl[n]), unscale);
             const int cc2 = (EM == E_SWIGLU) ? (g >> 1) : g;
             const int hp = (EM == E_SWIGLU) ? (g & 1) : 0;
+            if (S > 1) cluster_wait();  // every rank's mbarriers are initialised
 #pragma unroll
             for (int c = 0; c < NCH; c++) {
                 if (c * RC < nvalid) {
                     const int u = cc2 * NCH + c;
                     const int owner = u % S, slot = u / S;
                     const float *dst = recv + (((slot * S + rank) * P + hp) * 32 + lane) * RPAD;
-                    const uint32_t da = (S == 1) ? smem_u32(dst) : cluster_addr(dst, owner);
+                    if (S == 1) {
+                        const uint32_t da = smem_u32(dst);
 #pragma unroll
-                    for (int i = 0; i < RC / 2; i++) st_cluster_v2(da + 8 * i, vh[c * RC + 2 * i], vh[c * RC + 2 * i + 1]);
+                        for (int i = 0; i < RC / 4; i++)
+                            st_cluster_v4(da + 16 * i, vh[c * RC + 4 * i], vh[c * RC + 4 * i + 1],
+                                          vh[c * RC + 4 * i + 2], vh[c * RC + 4 * i + 3]);
+                    } else {
+                        const uint32_t da = cluster_addr(dst, owner), ba = cluster_addr(&recv_full, owner);
+#pragma unroll
+                        for (int i = 0; i < RC / 4; i++)
+                            st_async_v4(da + 16 * i, vh[c * RC + 4 * i], vh[c * RC + 4 * i + 1],
+                                        vh[c * RC + 4 * i + 2], vh[c * RC + 4 * i + 3], ba);
+                    }
                 }
             }
         }
@@ -443,12 +525,13 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
         }
     }
     tc::fence_before_sync();
-    // ---- every partial is in its owner's receive buffer after this barrier
-    if (S > 1) cluster.sync(); else __syncthreads();
+    __syncthreads();  // tensor memory read back (S == 1: partials in place)
     if (warp == kMmaWarp) {
         tc::fence_after_sync();
         tc::tmem_dealloc(tmem, kTmemCols);
     }
+    // ---- S > 1: every partial of this rank's units has arrived
+    if (S > 1) wait_or_abort(&recv_full, 0, abort_v, a.err);
     // ---- finish this rank's units: rank-order sums, epilogue
     const int64_t n_out = (EM == E_SWIGLU) ? (a.w.C / 2) * 32 : a.w.n;
     for (int slot = 0; slot * S + rank < kUnits; slot++) {
@@ -571,6 +654,7 @@ int query_max_clusters(int dev) {
 int gemv_mma_init() {
     QORA_TRY(mma_attrs_e<X_PLAIN>());
     QORA_TRY(mma_attrs_e<X_RMSNORM>());
+    QORA_TRY(mma_attrs_e<X_EMBED>());
     int dev = 0;
     QORA_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= kMaxDevices) return set_error(QORA_ERR_UNSUPPORTED, "device id %d", dev);
@@ -580,10 +664,17 @@ int gemv_mma_init() {
 bool gemv_mma_eligible(const GemvArgs &a, int xmode, int emode) {
     if (mma_disabled_by_env()) return false;
     if (a.rows < kMmaMinRows) return false;
-    if (xmode != X_PLAIN && xmode != X_RMSNORM) return false;
+    if (xmode != X_PLAIN && xmode != X_RMSNORM && xmode != X_EMBED) return false;
     if (emode < E_STORE || emode > E_SWIGLU) return false;
     if (a.w.mma_exp < 0 || a.w.k % kStageK != 0 || a.w.C % kMmaGroups != 0) return false;
-    if (a.ldx % 4 != 0 || ((uintptr_t)a.x & 15) != 0) return false;
+    if (xmode == X_EMBED) {
+        // nibble rows and scale rows must be whole 16-byte blocks
+        if (a.emb.n != a.w.k || a.emb.n % 256 != 0 || ((uintptr_t)a.emb.packed & 15) != 0 ||
+            ((uintptr_t)a.emb.scl & 15) != 0 || !a.tok)
+            return false;
+    } else if (a.ldx % 4 != 0 || ((uintptr_t)a.x & 15) != 0) {
+        return false;
+    }
     if (xmode == X_RMSNORM && ((uintptr_t)a.gamma & 15) != 0) return false;
     return true;
 }
@@ -626,6 +717,7 @@ int launch_gemv_mma(const GemvArgs &a, int xmode, int emode, const GemvPlan &p, 
     switch (xmode) {
         case X_PLAIN: return launch_mma_e<X_PLAIN>(a, emode, p, st);
         case X_RMSNORM: return launch_mma_e<X_RMSNORM>(a, emode, p, st);
+        case X_EMBED: return launch_mma_e<X_EMBED>(a, emode, p, st);
     }
     return set_error(QORA_ERR_INVALID, "tensor-core GEMV: prologue mode %d unsupported", xmode);
 }
