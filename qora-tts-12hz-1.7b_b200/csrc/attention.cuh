@@ -26,6 +26,9 @@ struct alignas(16) AttnArgs {
     const int *len = nullptr;       // cache length per stream before this call
     int pos_static = -1;            // >= 0: RoPE position of token 0 for every stream (overrides pos)
     int len_static = -1;            // >= 0: cache length for every stream (overrides len)
+    int stable_len = -1;            // cache rows [0, stable_len) were written before this launch
+                                    // (may be read before the item's inputs arrive); < 0: all of
+                                    // them (a kernel of its own, after griddepcontrol.wait)
     KVLayer kv;
     bool preappended = false;       // q/k already normed+roped and K/V appended
     float *out = nullptr;           // [rows][heads*hd]

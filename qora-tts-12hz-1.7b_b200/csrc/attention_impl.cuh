@@ -54,6 +54,39 @@ __device__ __forceinline__ void norm_rope_head(float (&v)[HD / 32], const __half
     }
 }
 
+// The same with gamma and the RoPE row already in registers (g[j] = gamma
+// element lane + 32 j, c / sn[j] = cos / sin element lane + 32 j, j < HD/64).
+template <int HD>
+__device__ __forceinline__ void norm_rope_head_pre(float (&v)[HD / 32], const float (&g)[HD / 32],
+                                                   const float (&c)[HD / 64], const float (&sn)[HD / 64]) {
+    constexpr int J = HD / 32;
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < J; j++) ss += __fmul_rn(v[j], v[j]);
+    ss = warp_sum(ss);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)HD), 1e-6f)));
+#pragma unroll
+    for (int j = 0; j < J; j++) v[j] = __fmul_rn(__fmul_rn(v[j], inv), g[j]);
+#pragma unroll
+    for (int j = 0; j < J / 2; j++) {
+        const float x1 = v[j], x2 = v[j + J / 2];
+        v[j] = __fsub_rn(__fmul_rn(x1, c[j]), __fmul_rn(x2, sn[j]));
+        v[j + J / 2] = __fadd_rn(__fmul_rn(x2, c[j]), __fmul_rn(x1, sn[j]));
+    }
+}
+
+// Asynchronous global -> shared copies of 16 bytes (L2 only) and 4 bytes.
+__device__ __forceinline__ void attn_cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void attn_cp_async4(void *dst, const void *src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+
 template <int HD>
 __device__ __forceinline__ bool rope_rows(const AttnArgs &a, int b, int t, int L0,
                                           const float *&cr, const float *&sr) {
@@ -110,6 +143,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
     const float *row = a.qkv + (int64_t)r * a.ldqkv;
 
     // ---- prologue: query heads (normed + roped unless pre-appended), append
+    bool staged0 = false;  // the split's first K / V tile is complete in shared memory
     if (a.preappended) {
         for (int i = tid; i < G * HD; i += NT)
             q_s[i / HD][i % HD] = __ldcg(row + (int64_t)(kvh * G) * HD + i);
@@ -120,8 +154,38 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
             return;
         }
         const bool appender = (p1 == Lq);
+        // What does not depend on this op's inputs is requested before waiting
+        // for them: the qk-norm gamma and RoPE row of the warp's head, and the
+        // cached K / V rows of the split's first tile (positions < L0) that were
+        // written before this launch (V as 16-byte pieces, K elements straight
+        // into the transposed tile).  Rows written earlier in this launch are
+        // read only after the inputs: the first tile is then loaded whole after
+        // the barrier below.
+        const int old0 = max(0, min(min(kTile, p1 - p0), L0 - p0));
+        const int stable = a.stable_len < 0 ? L0 : min(L0, a.stable_len);
+        const int pre0 = max(0, min(old0, stable - p0));
+        staged0 = (pre0 == old0);
+        for (int i = tid; i < pre0 * (HD / 4); i += NT) {
+            const int pp = i / (HD / 4), d4 = i % (HD / 4);
+            attn_cp_async16(&v_s[pp][4 * d4], vrow_base + (int64_t)(p0 + pp) * HD + 4 * d4);
+        }
+        for (int i = tid; i < pre0 * HD; i += NT) {
+            const int pp = i / HD, d = i % HD;
+            attn_cp_async4(&kt_s[d][pp], krow_base + (int64_t)(p0 + pp) * HD + d);
+        }
         for (int it = warp; it < G + 2; it += NT / 32) {
             if (it >= G && !appender) continue;
+            float gv[J], cv[J / 2], sv[J / 2];
+            if (it <= G) {
+                const __half *gm = it < G ? a.q_gamma : a.k_gamma;
+#pragma unroll
+                for (int j = 0; j < J; j++) gv[j] = __half2float(gm[lane + 32 * j]);
+#pragma unroll
+                for (int j = 0; j < J / 2; j++) {
+                    cv[j] = cr[lane + 32 * j];
+                    sv[j] = sr[lane + 32 * j];
+                }
+            }
             float v[J];
             const int64_t off = it < G ? (int64_t)(kvh * G + it) * HD
                                        : (it == G ? (int64_t)(a.heads + kvh) * HD
@@ -138,21 +202,33 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
 #pragma unroll
                 for (int j = 0; j < J; j++) v[j] = __ldcg(src + lane + 32 * j);
             }
+            // the new row sits in the split's first tile when L0 - p0 < kTile
+            const int nt = L0 + t - p0;
+            const bool in_tile0 = appender && nt < kTile;
             if (it < G) {
-                norm_rope_head<HD>(v, a.q_gamma, cr, sr, true, lane);
+                norm_rope_head_pre<HD>(v, gv, cv, sv);
 #pragma unroll
                 for (int j = 0; j < J; j++) q_s[it][lane + 32 * j] = v[j];
             } else if (it == G) {
-                norm_rope_head<HD>(v, a.k_gamma, cr, sr, true, lane);
+                norm_rope_head_pre<HD>(v, gv, cv, sv);
                 float *dst = const_cast<float *>(krow_base) + (int64_t)(L0 + t) * HD;
 #pragma unroll
                 for (int j = 0; j < J; j++) dst[lane + 32 * j] = v[j];
+                if (in_tile0) {
+#pragma unroll
+                    for (int j = 0; j < J; j++) kt_s[lane + 32 * j][nt] = v[j];
+                }
             } else {
                 float *dst = const_cast<float *>(vrow_base) + (int64_t)(L0 + t) * HD;
 #pragma unroll
                 for (int j = 0; j < J; j++) dst[lane + 32 * j] = v[j];
+                if (in_tile0) {
+#pragma unroll
+                    for (int j = 0; j < J; j++) v_s[nt][lane + 32 * j] = v[j];
+                }
             }
         }
+        asm volatile("cp.async.wait_all;" ::: "memory");
     }
     if (tid < G) {
         m_s[tid] = -INFINITY;
@@ -168,8 +244,9 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
     for (int base = p0; base < p1; base += kTile) {
         const int cnt = min(kTile, p1 - base);
         // K tile (transposed) and V tile into shared memory; every load of the
-        // tile is in flight at once
-        for (int i = tid; i < kTile * (HD / 4); i += NT) {
+        // tile is in flight at once (a staged first tile is already in place)
+        const bool staged = staged0 && base == p0;
+        for (int i = staged ? kTile * (HD / 4) : tid; i < kTile * (HD / 4); i += NT) {
             const int pp = i / (HD / 4), d4 = i % (HD / 4);
             float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = make_float4(0.f, 0.f, 0.f, 0.f);
             if (pp < cnt) {

@@ -1031,6 +1031,7 @@ int frame_build(qora_engine *e, FrameProgram **out) {
             at.kv = e->pkv->layer(l);
             at.pos_static = tk;
             at.len_static = tk;
+            at.stable_len = 0;  // the predictor cache is refilled within this launch
             layer(p->layers[l], p->heads, p->kvh, p->hd, nullptr, at, 1);
         }
         if (tk >= 1) {
