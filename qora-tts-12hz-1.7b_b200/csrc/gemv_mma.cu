@@ -78,11 +78,16 @@ constexpr int kBTile = kMmaRows * kStageK * 2;  // one of xh / xl
 constexpr int kOpBytes = 2 * kBTile;
 constexpr uint32_t kLBO = 128, kSBO = 512;
 // K-split reduction: 16 units per CTA tile, unit = (output group, chunk of
-// kChunkRows(EM) rows); rank q owns units u with u % S == q (S a power of two
-// <= 16).  Receive buffer: [unit slot][source rank][partial][column][padded
-// chunk rows] (rows padded by 4: 16-byte remote stores).
+// rows); rank q of S owns units u with u % S == q.  Receive buffer: [unit slot
+// u / S][source rank][partial][column][padded chunk rows] (rows padded by 4:
+// 16-byte remote stores): ceil(16 / S) * S (slot, source) pairs, at most
+// kSlotPairs for the splits the planner uses (S <= 12 or S == 16).
 constexpr int kUnits = 16;
-constexpr int kRecvFloats = kUnits * 2 * 32 * 8 > kUnits * 32 * 12 ? kUnits * 2 * 32 * 8 : kUnits * 32 * 12;
+constexpr int kSlotPairs = 24;
+constexpr bool split_ok(int S) { return S >= 1 && (S <= 12 || S == 16); }
+constexpr int kRecvFloats = kSlotPairs * 2 * 32 * 8 > kSlotPairs * 32 * 12 ? kSlotPairs * 2 * 32 * 8
+                                                                           : kSlotPairs * 32 * 12;
+static_assert(split_ok(kMaxSplit), "the largest cluster split");
 constexpr size_t kMmaSmem =
     128 + (size_t)kOpStages * kOpBytes + (size_t)kRawStages * kRawBytes + (size_t)kRecvFloats * 4;
 
@@ -612,10 +617,10 @@ bool mma_disabled_by_env() {
     return off;
 }
 
-// Clusters of 2^i CTAs (i = 0..4) that can be resident at once, per device:
+// Clusters of S CTAs (S = 1..16) that can be resident at once, per device:
 // a grid with more clusters than this runs in waves.
 constexpr int kMaxDevices = 64;
-int g_max_clusters[kMaxDevices][5];
+int g_max_clusters[kMaxDevices][kMaxSplit + 1];
 
 // cudaOccupancyMaxActiveClusters counts one CTA of this kernel per SM.  Two
 // fit when each SM sub-partition can hold the registers of the warps two CTAs
@@ -629,8 +634,9 @@ int query_max_clusters(int dev) {
     const int regs_warp = ((fa.numRegs + 7) / 8) * 8 * 32;
     const int warps_smsp = 2 * ((kMmaThreads / 32 + 3) / 4);
     const int per_sm = (warps_smsp * regs_warp <= 16384) ? 2 : 1;
-    for (int i = 0; i < 5; i++) {
-        const int S = 1 << i;
+    for (int S = 1; S <= kMaxSplit; S++) {
+        g_max_clusters[dev][S] = 0;
+        if (!split_ok(S)) continue;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(64, (unsigned)S, 1);
         cfg.blockDim = dim3(kMmaThreads);
@@ -644,7 +650,7 @@ int query_max_clusters(int dev) {
         cfg.numAttrs = 1;
         int n = 0;
         QORA_CUDA(cudaOccupancyMaxActiveClusters(&n, k_gemv_mma<X_RMSNORM, E_SWIGLU>, &cfg));
-        g_max_clusters[dev][i] = n * per_sm;
+        g_max_clusters[dev][S] = n * per_sm;
     }
     return QORA_OK;
 }
@@ -694,15 +700,10 @@ GemvPlan plan_gemv_mma(int64_t k, int64_t C, int rows, int emode, int num_sms) {
     int dev = 0;
     cudaGetDevice(&dev);
     const int *maxc = (dev >= 0 && dev < kMaxDevices) ? g_max_clusters[dev] : nullptr;
-    // a power of two (the reduction's 16 units split evenly over the ranks);
-    // larger only while all clusters of the grid stay resident at once
+    // the largest split up to `want` whose clusters all stay resident at once
     int64_t S = 1;
-    int lg = 0;
-    while (2 * S <= want && 2 * S <= std::min<int64_t>(kMaxSplit, stages) &&
-           (!maxc || maxc[lg + 1] <= 0 || tiles * p.Z <= maxc[lg + 1])) {
-        S *= 2;
-        lg++;
-    }
+    for (int s = 2; s <= std::min<int64_t>(std::min<int64_t>(want, kMaxSplit), stages); s++)
+        if (split_ok(s) && (!maxc || maxc[s] <= 0 || tiles * p.Z <= maxc[s])) S = s;
     p.S = (int)S;
     p.WR = kConvWarps;
     p.NSUB = 1;
