@@ -213,8 +213,9 @@ __device__ __forceinline__ uint64_t global_ns_t() {
 // (pred[k] false skips an element) and returns the values in out[].  On
 // timeout, or when *abort is set by another waiter, it raises kDevTimeout,
 // sets *abort and returns what it has: the caller keeps to its barrier
-// sequence and checks the abort state afterwards.  While nothing has
-// arrived it spins on one word only, to keep idle waiters off the L2.
+// sequence and checks the abort state afterwards.  Every attempt reloads
+// all pending words (one L2 round trip per attempt), so the values are in
+// hand in the attempt that sees them.
 // ACQ adds an acquire fence at the end, for callers that go on to read
 // plain data the writers published before their tagged stores.
 template <int N, bool ACQ = false>
@@ -222,37 +223,12 @@ __device__ __forceinline__ bool poll_tagged(const uint64_t *base, int64_t stride
                                             float (&out)[N], const bool (&pred)[N], int *err,
                                             int *abort) {
     uint32_t pending = 0;
-    int gate = -1;
 #pragma unroll
     for (int k = 0; k < N; k++)
-        if (pred[k]) {
-            pending |= 1u << k;
-            gate = k;
-        }
+        if (pred[k]) pending |= 1u << k;
     uint64_t t0 = 0;
     bool ok = true;
     for (int it = 0; pending; it++) {
-        if (it > 0 && gate >= 0) {
-            // cheap wait: the last requested word first
-            if ((uint32_t)(ld_relaxed_u64(base + gate * stride) >> 32) != tag) {
-                __nanosleep(128);  // idle waiters stay off the L2
-                if (it == 1) t0 = global_ns_t();
-                if ((it & 15) == 15) {
-                    if (*(volatile int *)abort) {
-                        ok = false;
-                        break;
-                    }
-                    if (global_ns_t() - t0 > 2000000000ull) {
-                        if (err) atomicCAS(err, 0, 3);
-                        atomicExch(abort, 1);
-                        ok = false;
-                        break;
-                    }
-                }
-                continue;
-            }
-            gate = -1;
-        }
         uint64_t v[N];
 #pragma unroll
         for (int k = 0; k < N; k++)

@@ -218,37 +218,17 @@ __device__ __forceinline__ float block_sum(float v, FrameSmem &S, int tid) {
 // Polls dst[i] = value of src[i] for i = i0 + tid + m * kNT (m < U, i < n)
 // until every word carries `tag` (bounded; on failure the CTA aborts after
 // its barrier sequence).  GEMV inputs are all tagged, so no fence follows.
+// Every attempt reloads all of the thread's pending words (one L2 round trip
+// per attempt), so the values are in hand in the attempt that sees them.
 template <int U>
 __device__ __forceinline__ void poll_to_smem(const FrameParams &P, FrameSmem &S, const uint64_t *src,
                                              int i0, int n, uint32_t tag, float *dst, int tid) {
     uint32_t pending = 0;
-    int gate = -1;
 #pragma unroll
     for (int m = 0; m < U; m++)
-        if (i0 + tid + m * kNT < n) {
-            pending |= 1u << m;
-            gate = m;
-        }
+        if (i0 + tid + m * kNT < n) pending |= 1u << m;
     uint64_t t0 = global_ns();
     for (int it = 0; pending; it++) {
-        if (it > 0 && gate >= 0) {
-            // cheap wait while nothing has arrived: one word, then the rest
-            if ((uint32_t)(ld_relaxed_u64(src + i0 + tid + gate * kNT) >> 32) != tag) {
-                __nanosleep(128);  // idle waiters stay off the L2
-                if ((it & 15) == 15) {
-                    if (ld_volatile(P.abort_flag)) {
-                        S.abort = 1;
-                        break;
-                    }
-                    if (global_ns() - t0 > kWaitNs) {
-                        raise_abort(P, S, kDevTimeout);
-                        break;
-                    }
-                }
-                continue;
-            }
-            gate = -1;
-        }
         uint64_t v[U];
 #pragma unroll
         for (int m = 0; m < U; m++)
