@@ -41,6 +41,7 @@ typedef struct qora_kv qora_kv;               /* device KV cache, `streams` slab
 typedef struct qora_talker qora_talker;       /* device TalkerWeights */
 typedef struct qora_predictor qora_predictor; /* device CodePredictorWeights */
 typedef struct qora_engine qora_engine;       /* per-GPU frame-loop state */
+typedef struct qora_model_file qora_model_file; /* a mapped .qora-tts checkpoint */
 
 /* Host view of one Q4 weight in the reference layout (gemv.rs:26-31). */
 typedef struct qora_q4_host {
@@ -181,6 +182,22 @@ int qora_kv_attend_noalloc(qora_kv *kv, int32_t layer, const float *qkv, int32_t
                            const uint16_t *q_norm, const uint16_t *k_norm, const float *rope_cos,
                            const float *rope_sin, int32_t rope_max_pos, const int32_t *positions,
                            int32_t B, int32_t advance, float *out, void *stream);
+
+/* ------------------------------------------------------------ save.rs */
+/* load_model (save.rs:262-409; records gemv.rs:595-687): maps a .qora-tts
+ * checkpoint (Q4 format) read-only and parses its talker and code-predictor
+ * sections; the speech decoder after them is not read.  Every length is
+ * checked against the file; a malformed file, a version other than 1 or an
+ * f16 (format 0) checkpoint is an error.  The RoPE base is recovered from the
+ * stored tables and must reproduce them exactly. */
+int qora_model_file_open(const char *path, qora_model_file **out);
+/* Host views of the file's TalkerWeights / CodePredictorWeights for
+ * qora_talker_create / qora_predictor_create; their pointers stay valid until
+ * qora_model_file_close (nibbles point into the mapping, the small f16 / f32
+ * arrays into aligned copies). */
+int qora_model_file_talker(const qora_model_file *f, qora_talker_host *out);
+int qora_model_file_predictor(const qora_model_file *f, qora_predictor_host *out);
+void qora_model_file_close(qora_model_file *f);
 
 /* ------------------------------------------------------------ talker.rs */
 int qora_talker_create(qora_ctx *ctx, const qora_talker_host *host, int32_t max_batch,

@@ -86,6 +86,10 @@ SIGNATURES = {
                                   _vp, _vp]),
     "qora_kv_attend_noalloc": (C.c_int, [_vp, _i32, _vp, _i32, _vp, _vp, _vp, _vp, _i32, _vp, _i32,
                                           _i32, _vp, _vp]),
+    "qora_model_file_open": (C.c_int, [C.c_char_p, _PP]),
+    "qora_model_file_talker": (C.c_int, [_vp, _vp]),
+    "qora_model_file_predictor": (C.c_int, [_vp, _vp]),
+    "qora_model_file_close": (None, [_vp]),
     "qora_talker_create": (C.c_int, [_vp, _vp, _i32, _PP]),
     "qora_talker_destroy": (None, [_vp]),
     "qora_talker_step": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),

@@ -230,3 +230,47 @@ def synth_predictor(cfg: ModelConfig) -> PredictorWeights:
         lm_heads=[synth_q4(s * 1000 + 940 + g, sg, cfg.p_hidden, cfg.p_vocab)
                   for g in range(cfg.p_groups)],
         final_norm=np.full(cfg.p_hidden, F16_ONE, np.uint16))
+
+
+class _HostView:
+    """Duck-typed stand-in for TalkerWeights / PredictorWeights built from a
+    ModelFile: `cfg` and `host()` are what engine.Talker / CodePredictor use."""
+
+    def __init__(self, owner, cfg: ModelConfig, host):
+        self._owner, self.cfg, self._host = owner, cfg, host
+
+    def host(self):
+        return self._host
+
+
+class ModelFile:
+    """A .qora-tts checkpoint (save.rs:262-409), mapped read-only by the engine
+    library.  `talker` / `predictor` are views for engine.Talker(ctx, view) and
+    engine.CodePredictor(ctx, view); keep this object alive until those are
+    created (the device copies are independent of it afterwards)."""
+
+    def __init__(self, path: str):
+        h = C.c_void_p()
+        _lib.call("qora_model_file_open", str(path).encode(), C.byref(h))
+        self.h = h
+        self.talker_host = _lib.TalkerHost()
+        self.predictor_host = _lib.PredictorHost()
+        _lib.call("qora_model_file_talker", self.h, C.byref(self.talker_host))
+        _lib.call("qora_model_file_predictor", self.h, C.byref(self.predictor_host))
+        t, p = self.talker_host, self.predictor_host
+        self.cfg = ModelConfig(
+            t_layers=t.num_layers, t_hidden=t.hidden, t_heads=t.num_heads, t_kv_heads=t.num_kv_heads,
+            t_head_dim=t.head_dim, t_ffn=t.ffn, t_vocab=t.vocab, t_max_pos=t.rope_max_pos,
+            p_layers=p.num_layers, p_hidden=p.hidden, p_heads=p.num_heads, p_kv_heads=p.num_kv_heads,
+            p_head_dim=p.head_dim, p_ffn=p.ffn, p_vocab=p.vocab, p_groups=p.num_groups,
+            p_max_pos=p.rope_max_pos, rope_theta=t.rope_theta)
+        self.talker = _HostView(self, self.cfg, self.talker_host)
+        self.predictor = _HostView(self, self.cfg, self.predictor_host)
+
+    def close(self):
+        if getattr(self, "h", None):
+            _lib.load().qora_model_file_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
