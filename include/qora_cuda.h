@@ -42,6 +42,7 @@ typedef struct qora_talker qora_talker;       /* device TalkerWeights */
 typedef struct qora_predictor qora_predictor; /* device CodePredictorWeights */
 typedef struct qora_engine qora_engine;       /* per-GPU frame-loop state */
 typedef struct qora_model_file qora_model_file; /* a mapped .qora-tts checkpoint */
+typedef struct qora_text_proj qora_text_proj;   /* device text projection */
 
 /* Host view of one Q4 weight in the reference layout (gemv.rs:26-31). */
 typedef struct qora_q4_host {
@@ -82,6 +83,15 @@ typedef struct qora_predictor_host {
     const qora_q4_host *lm_heads;         /* num_groups x [hidden][vocab] */
     const uint16_t *final_norm;
 } qora_predictor_host;
+
+/* TalkerWeights text path (talker.rs:33-56; loader.rs:280-284). */
+typedef struct qora_text_proj_host {
+    qora_q4_host text_embedding;     /* [text_vocab][text_hidden] */
+    qora_q4_host fc1;                /* text_projection.linear_fc1 [text_hidden][mid] */
+    qora_q4_host fc2;                /* text_projection.linear_fc2 [mid][hidden] */
+    const float *fc1_bias;           /* [mid] */
+    const float *fc2_bias;           /* [hidden] */
+} qora_text_proj_host;
 
 /* TTSParams sampling fields (generate_new.rs:38-79). */
 typedef struct qora_sample_params {
@@ -197,6 +207,8 @@ int qora_model_file_open(const char *path, qora_model_file **out);
  * arrays into aligned copies). */
 int qora_model_file_talker(const qora_model_file *f, qora_talker_host *out);
 int qora_model_file_predictor(const qora_model_file *f, qora_predictor_host *out);
+/* The talker's text embedding and text projection (save.rs:78-82). */
+int qora_model_file_text_proj(const qora_model_file *f, qora_text_proj_host *out);
 void qora_model_file_close(qora_model_file *f);
 
 /* ------------------------------------------------------------ talker.rs */
@@ -219,6 +231,16 @@ int qora_talker_codec_head(qora_talker *t, const float *hidden, int32_t B, float
 /* embed_codec_token (talker.rs:152-154) for B tokens. */
 int qora_talker_embed_codec(qora_talker *t, const uint32_t *tokens, int32_t B, float *out,
                             void *stream);
+
+/* embed_text_token (talker.rs:104-116): text-embedding row -> fc1 + bias ->
+ * SiLU -> fc2 + bias, for a run of prompt tokens.  `tokens` is a HOST array
+ * of `count` text token ids (the tokenizer's output); `out` is device
+ * [count][hidden].  A token >= text_vocab is QORA_ERR_RANGE before any
+ * launch.  One object serves one stream at a time (its scratch is shared). */
+int qora_text_proj_create(qora_ctx *ctx, const qora_text_proj_host *host, qora_text_proj **out);
+void qora_text_proj_destroy(qora_text_proj *tp);
+int qora_text_proj_embed(qora_text_proj *tp, const uint32_t *tokens, int32_t count, float *out,
+                         void *stream);
 
 /* ------------------------------------------------------------ code_predictor.rs */
 int qora_predictor_create(qora_ctx *ctx, const qora_predictor_host *host, int32_t max_batch,

@@ -613,7 +613,7 @@ static int prefill_layer(const layer_dims *d, const oq_layer *lw, float *x, int6
     int32_t H = d->hidden, qd = d->heads * d->hd, kd = d->kv_heads * d->hd;
     if (kv->len[layer] != start_pos) return -3;
     if (start_pos + T > kv->max_pos) return -1;
-    float *xn = (float *)malloc(sizeof(float) * (size_t)(T * H));
+    float *xn = (float *)calloc((size_t)(T * H), sizeof(float));
     float *q = (float *)malloc(sizeof(float) * (size_t)(T * qd));
     float *kn = (float *)malloc(sizeof(float) * (size_t)(T * kd));
     float *vn = (float *)malloc(sizeof(float) * (size_t)(T * kd));
@@ -732,6 +732,20 @@ void oq_codec_head(const oq_talker *t, const float *hidden, float *out_logits) {
 
 void oq_embed_codec_token(const oq_talker *t, uint32_t token, float *out) {
     oq_embed_lookup(&t->codec_embedding, token, out);
+}
+
+void oq_embed_text_token(const oq_text_proj *tp, uint32_t token, float *out) {
+    const int64_t th = tp->text_embedding.n, mid = tp->fc1.n;
+    float *raw = (float *)malloc((size_t)th * sizeof(float));
+    float *h = (float *)malloc((size_t)mid * sizeof(float));
+    oq_embed_lookup(&tp->text_embedding, token, raw);                  /* :107 */
+    oq_gemv(raw, &tp->fc1, h);                                         /* :109 */
+    for (int64_t j = 0; j < mid; j++) h[j] += tp->fc1_bias[j];          /* :110 */
+    for (int64_t j = 0; j < mid; j++) h[j] = oq_silu(h[j]);            /* :112 */
+    oq_gemv(h, &tp->fc2, out);                                         /* :113 */
+    for (int64_t j = 0; j < tp->fc2.n; j++) out[j] += tp->fc2_bias[j]; /* :114 */
+    free(raw);
+    free(h);
 }
 
 /* ======================================================================== */

@@ -141,6 +141,16 @@ int oq_talker_prefill(const oq_talker *t, const float *x, int64_t seq_len, oq_kv
 void oq_codec_head(const oq_talker *t, const float *hidden, float *out_logits);
 void oq_embed_codec_token(const oq_talker *t, uint32_t token, float *out);
 
+/* TalkerWeights text path (talker.rs:33-56, loader.rs:280-284):
+ * text_embedding [text_vocab][text_hidden], text_projection.linear_fc1
+ * [text_hidden][mid] + bias [mid], linear_fc2 [mid][hidden] + bias [hidden]. */
+typedef struct oq_text_proj {
+    oq_q4 text_embedding, fc1, fc2;
+    const float *fc1_bias, *fc2_bias;
+} oq_text_proj;
+/* embed_text_token (talker.rs:104-116): out [fc2.n]. */
+void oq_embed_text_token(const oq_text_proj *tp, uint32_t token, float *out);
+
 /* ---- code_predictor.rs --------------------------------------------------- */
 int oq_predictor_frame(const oq_predictor *p, const float *talker_hidden,
                        const float *semantic_embed, oq_kv *kv, uint32_t *codes_out,

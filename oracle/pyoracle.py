@@ -106,6 +106,7 @@ def lib():
             "oq_talker_prefill": (C.c_int, [vp, vp, i64, vp, i64, vp]),
             "oq_codec_head": (None, [vp, vp, vp]),
             "oq_embed_codec_token": (None, [vp, C.c_uint32, vp]),
+            "oq_embed_text_token": (None, [vp, C.c_uint32, vp]),
             "oq_predictor_frame": (C.c_int, [vp, vp, vp, vp, vp, vp]),
             "oq_predictor_frame_forced": (C.c_int, [vp, vp, vp, vp, vp, vp, vp]),
             "oq_acoustic_embeddings_sum": (None, [vp, vp, vp]),
@@ -215,6 +216,43 @@ def embed_lookup(w: Q4Weight, token: int) -> np.ndarray:
     ws = w.cstruct()
     lib().oq_embed_lookup(C.addressof(ws), token, ptr(out))
     return out
+
+
+class TextProjC(C.Structure):
+    _fields_ = [("text_embedding", Q4), ("fc1", Q4), ("fc2", Q4), ("fc1_bias", C.c_void_p),
+                ("fc2_bias", C.c_void_p)]
+
+
+@dataclass
+class TextProj:
+    """TalkerWeights text path (talker.rs:33-56): text_embedding, fc1 + bias,
+    fc2 + bias."""
+    text_embedding: Q4Weight
+    fc1: Q4Weight
+    fc1_bias: np.ndarray
+    fc2: Q4Weight
+    fc2_bias: np.ndarray
+
+    @staticmethod
+    def synth(seed: int, text_vocab: int, text_hidden: int, hidden: int, sigma: float = 0.02,
+              mid: int | None = None) -> "TextProj":
+        mid = text_hidden if mid is None else mid
+        return TextProj(synth_q4(seed, sigma, text_vocab, text_hidden),
+                        synth_q4(seed + 1, sigma, text_hidden, mid),
+                        synth_normal(seed + 2, sigma, mid),
+                        synth_q4(seed + 3, sigma, mid, hidden),
+                        synth_normal(seed + 4, sigma, hidden))
+
+    def cstruct(self) -> TextProjC:
+        return TextProjC(self.text_embedding.cstruct(), self.fc1.cstruct(), self.fc2.cstruct(),
+                         ptr(self.fc1_bias), ptr(self.fc2_bias))
+
+    def embed_text_token(self, token: int) -> np.ndarray:
+        """embed_text_token (talker.rs:104-116)."""
+        out = np.zeros(self.fc2.n, np.float32)
+        s = self.cstruct()
+        lib().oq_embed_text_token(C.addressof(s), token, ptr(out))
+        return out
 
 
 def rms_norm_f16(x: np.ndarray, gamma_f16: np.ndarray) -> np.ndarray:

@@ -3,7 +3,8 @@
 // reference's Rust loader.
 //
 // Layout (little endian): "QTTS", u32 version (1), u8 format (1 = Q4, 0 = f16),
-// then the talker section (save.rs:300-351), the code-predictor section
+// then the talker section (save.rs:300-351, with the text embedding and text
+// projection the prompt is built from), the code-predictor section
 // (save.rs:353-438) and the speech decoder, which this engine does not use and
 // which is not read.  Arrays are u64 element counts followed by the elements;
 // a weight is u64 k, u64 n, then (Q4) the packed bytes and the f16 scales.
@@ -40,6 +41,7 @@ struct qora_model_file {
     std::vector<qora_q4_host> p_embs, p_heads;
     qora_talker_host talker{};
     qora_predictor_host predictor{};
+    qora_text_proj_host text{};
 };
 
 namespace {
@@ -110,20 +112,6 @@ qora_q4_host read_q4(Cursor &c, qora_model_file *f) {
     return w;
 }
 
-// f16 / f32 arrays that this engine does not use
-void skip_array(Cursor &c, int elem) {
-    const uint64_t n = c.u(8);
-    if (n > (1ull << 40)) c.ok = false;
-    c.bytes(n * (uint64_t)elem);
-}
-void skip_q4(Cursor &c) {
-    const uint64_t k = c.u(8), n = c.u(8);
-    (void)k;
-    (void)n;
-    skip_array(c, 1);  // packed
-    skip_array(c, 2);  // scales
-}
-
 qora_layer_host read_layer(Cursor &c, qora_model_file *f, int hidden, int hd) {
     qora_layer_host l{};
     l.q_proj = read_q4(c, f);
@@ -179,7 +167,7 @@ int parse(qora_model_file *f) {
     qora_talker_host &t = f->talker;
     t.num_layers = (int32_t)c.u(4);
     t.hidden = (int32_t)c.u(4);
-    c.u(4);  // text_hidden_size
+    const uint64_t text_hidden = c.u(4);
     t.num_heads = (int32_t)c.u(4);
     t.num_kv_heads = (int32_t)c.u(4);
     t.head_dim = (int32_t)c.u(4);
@@ -192,11 +180,15 @@ int parse(qora_model_file *f) {
     f->t_layers.resize((size_t)t.num_layers);
     for (int i = 0; i < t.num_layers && c.ok; i++) f->t_layers[(size_t)i] = read_layer(c, f, t.hidden, t.head_dim);
     t.codec_embedding = read_q4(c, f);
-    skip_q4(c);        // text_embedding
-    skip_q4(c);        // text_proj_fc1
-    skip_array(c, 4);  // text_proj_fc1_bias
-    skip_q4(c);        // text_proj_fc2
-    skip_array(c, 4);  // text_proj_fc2_bias
+    qora_text_proj_host &x = f->text;
+    x.text_embedding = read_q4(c, f);
+    x.fc1 = read_q4(c, f);
+    x.fc1_bias = read_f32(c, f, x.fc1.n);
+    x.fc2 = read_q4(c, f);
+    x.fc2_bias = read_f32(c, f, x.fc2.n);
+    if (c.ok && ((uint64_t)x.text_embedding.n != text_hidden || x.fc1.k != x.text_embedding.n ||
+                 x.fc2.k != x.fc1.n || x.fc2.n != t.hidden))
+        return set_error(QORA_ERR_INVALID, "model file: text projection shapes do not chain");
     t.codec_head = read_q4(c, f);
     t.final_norm = read_f16(c, f, t.hidden);
     int64_t tc = 0, ts = 0;
@@ -299,6 +291,12 @@ int qora_model_file_talker(const qora_model_file *f, qora_talker_host *out) {
 int qora_model_file_predictor(const qora_model_file *f, qora_predictor_host *out) {
     if (!f || !out) return set_error(QORA_ERR_INVALID, "qora_model_file_predictor: bad arguments");
     *out = f->predictor;
+    return QORA_OK;
+}
+
+int qora_model_file_text_proj(const qora_model_file *f, qora_text_proj_host *out) {
+    if (!f || !out) return set_error(QORA_ERR_INVALID, "qora_model_file_text_proj: bad arguments");
+    *out = f->text;
     return QORA_OK;
 }
 

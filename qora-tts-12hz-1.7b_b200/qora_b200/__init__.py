@@ -7,9 +7,9 @@ qora_b200.engine (imports torch).
 """
 from . import _lib
 from .weights import (ModelConfig, Q4Weight, LayerWeights, TalkerWeights, PredictorWeights,
-                      ModelFile, quantize_f32_to_q4, synth_q4, synth_normal, synth_talker,
-                      synth_predictor)
+                      TextProjWeights, ModelFile, quantize_f32_to_q4, synth_q4, synth_normal,
+                      synth_talker, synth_predictor, synth_text_proj)
 
 __all__ = ["_lib", "ModelConfig", "Q4Weight", "LayerWeights", "TalkerWeights", "PredictorWeights",
-           "ModelFile",
-           "quantize_f32_to_q4", "synth_q4", "synth_normal", "synth_talker", "synth_predictor"]
+           "TextProjWeights", "ModelFile", "quantize_f32_to_q4", "synth_q4", "synth_normal",
+           "synth_talker", "synth_predictor", "synth_text_proj"]

@@ -51,6 +51,11 @@ class PredictorHost(C.Structure):
                 ("lm_heads", C.c_void_p), ("final_norm", C.c_void_p)]
 
 
+class TextProjHost(C.Structure):
+    _fields_ = [("text_embedding", Q4Host), ("fc1", Q4Host), ("fc2", Q4Host),
+                ("fc1_bias", C.c_void_p), ("fc2_bias", C.c_void_p)]
+
+
 class SampleParams(C.Structure):
     _fields_ = [("temperature", C.c_float), ("top_k", C.c_int32), ("top_p", C.c_float),
                 ("repetition_penalty", C.c_float)]
@@ -89,7 +94,11 @@ SIGNATURES = {
     "qora_model_file_open": (C.c_int, [C.c_char_p, _PP]),
     "qora_model_file_talker": (C.c_int, [_vp, _vp]),
     "qora_model_file_predictor": (C.c_int, [_vp, _vp]),
+    "qora_model_file_text_proj": (C.c_int, [_vp, _vp]),
     "qora_model_file_close": (None, [_vp]),
+    "qora_text_proj_create": (C.c_int, [_vp, _vp, _PP]),
+    "qora_text_proj_destroy": (None, [_vp]),
+    "qora_text_proj_embed": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),
     "qora_talker_create": (C.c_int, [_vp, _vp, _i32, _PP]),
     "qora_talker_destroy": (None, [_vp]),
     "qora_talker_step": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),

@@ -230,6 +230,39 @@ class Talker:
         return out
 
 
+class TextProjection:
+    """The talker's text embedding + text projection on the device
+    (TalkerWeights text path, talker.rs:33-56)."""
+
+    def __init__(self, ctx: Context, w):
+        self.ctx = ctx
+        hs = w.host()
+        self.hidden, self.text_vocab = int(hs.fc2.n), int(hs.text_embedding.k)
+        h = C.c_void_p()
+        _lib.call("qora_text_proj_create", ctx.h, C.byref(hs), C.byref(h))
+        self.h = h
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            _lib.load().qora_text_proj_destroy(self.h)
+            self.h = None
+
+    def embed_text_tokens(self, tokens, out: torch.Tensor | None = None,
+                          stream=None) -> torch.Tensor:
+        """embed_text_token (talker.rs:104-116) for every token id in `tokens`
+        (host ids); returns [len(tokens)][hidden] on the device."""
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
+        if out is None:
+            out = torch.empty(t.size, self.hidden, device=f"cuda:{self.ctx.device}")
+        assert out.numel() == t.size * self.hidden
+        _lib.call("qora_text_proj_embed", self.h, t.ctypes.data, t.size, _dp(out), _stream(stream))
+        return out
+
+    def embed_text_token(self, token: int, stream=None) -> torch.Tensor:
+        """embed_text_token (talker.rs:104-116) for one token: [hidden]."""
+        return self.embed_text_tokens([token], stream=stream)[0]
+
+
 class CodePredictor:
     """CodePredictorWeights on the device (code_predictor.rs)."""
 

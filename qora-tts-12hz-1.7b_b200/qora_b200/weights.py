@@ -204,6 +204,42 @@ class PredictorWeights:
         return n
 
 
+@dataclass
+class TextProjWeights:
+    """TalkerWeights text path (talker.rs:33-56; loader.rs:280-284):
+    text_embedding [text_vocab][text_hidden], text_projection fc1
+    [text_hidden][mid] + bias, fc2 [mid][hidden] + bias."""
+    text_embedding: Q4Weight
+    fc1: Q4Weight
+    fc1_bias: np.ndarray
+    fc2: Q4Weight
+    fc2_bias: np.ndarray
+
+    def host(self) -> _lib.TextProjHost:
+        return _lib.TextProjHost(self.text_embedding.host(), self.fc1.host(), self.fc2.host(),
+                                 _ptr(self.fc1_bias), _ptr(self.fc2_bias))
+
+    @property
+    def hidden(self) -> int:
+        return self.fc2.n
+
+    @property
+    def text_vocab(self) -> int:
+        return self.text_embedding.k
+
+
+def synth_text_proj(seed: int, text_vocab: int, text_hidden: int, hidden: int,
+                    sigma: float = 0.02, mid: int | None = None) -> TextProjWeights:
+    """Random-init text path (seeds seed .. seed+4).  The 1.7B model: text_vocab
+    151936, text_hidden 2048 (config.rs:137-138), mid = text_hidden, hidden 2048."""
+    mid = text_hidden if mid is None else mid
+    return TextProjWeights(synth_q4(seed, sigma, text_vocab, text_hidden),
+                           synth_q4(seed + 1, sigma, text_hidden, mid),
+                           synth_normal(seed + 2, sigma, mid),
+                           synth_q4(seed + 3, sigma, mid, hidden),
+                           synth_normal(seed + 4, sigma, hidden))
+
+
 def synth_talker(cfg: ModelConfig) -> TalkerWeights:
     """Random-init talker.  Seeds: layer i uses cfg.seed*1000 + 10*i (+1..7)."""
     s, sg = cfg.seed, cfg.sigma
@@ -245,8 +281,9 @@ class _HostView:
 
 class ModelFile:
     """A .qora-tts checkpoint (save.rs:262-409), mapped read-only by the engine
-    library.  `talker` / `predictor` are views for engine.Talker(ctx, view) and
-    engine.CodePredictor(ctx, view); keep this object alive until those are
+    library.  `talker` / `predictor` / `text_proj` are views for
+    engine.Talker(ctx, view), engine.CodePredictor(ctx, view) and
+    engine.TextProjection(ctx, view); keep this object alive until those are
     created (the device copies are independent of it afterwards)."""
 
     def __init__(self, path: str):
@@ -266,6 +303,9 @@ class ModelFile:
             p_max_pos=p.rope_max_pos, rope_theta=t.rope_theta)
         self.talker = _HostView(self, self.cfg, self.talker_host)
         self.predictor = _HostView(self, self.cfg, self.predictor_host)
+        self.text_proj_host = _lib.TextProjHost()
+        _lib.call("qora_model_file_text_proj", self.h, C.byref(self.text_proj_host))
+        self.text_proj = _HostView(self, self.cfg, self.text_proj_host)
 
     def close(self):
         if getattr(self, "h", None):

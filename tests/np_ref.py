@@ -48,6 +48,20 @@ def silu(x):
     return x / (1 + np.exp(-x))
 
 
+def embed_text_token(tp, token):
+    """embed_text_token (talker.rs:104-116) in float64: text-embedding row ->
+    fc1 + bias -> SiLU -> fc2 + bias."""
+    raw = deq(tp.text_embedding)[token] if tp.text_embedding.k < 4096 else None
+    if raw is None:  # large tables: dequantise the one row
+        e = tp.text_embedding
+        g = e.n // 32
+        p = e.packed.reshape(e.k, g, 16)[token]
+        q = np.stack([(p & 15).astype(np.int64) - 8, (p >> 4).astype(np.int64) - 8], -1).reshape(-1)
+        raw = q * np.repeat(e.scales.view(np.float16).astype(np.float64).reshape(e.k, g)[token], 32)
+    h = silu(raw @ deq(tp.fc1) + tp.fc1_bias.astype(np.float64))
+    return h @ deq(tp.fc2) + tp.fc2_bias.astype(np.float64)
+
+
 class NpKV:
     def __init__(self, layers):
         self.k = [[] for _ in range(layers)]

@@ -63,9 +63,16 @@ def rope_tables(head_dim, max_pos, theta):
     return cos, sin
 
 
-def write(path, tw, pw, cfg, fmt=1, version=1, theta=None, tail=b"decoder section"):
+def text_proj_for(cfg, text_vocab=64):
+    """A random-init text path that chains with the talker of `cfg`
+    (text_hidden = mid = hidden)."""
     import qora_b200
+    return qora_b200.synth_text_proj(71, text_vocab, cfg.t_hidden, cfg.t_hidden)
+
+
+def write(path, tw, pw, cfg, fmt=1, version=1, theta=None, tail=b"decoder section", text=None):
     theta = cfg.rope_theta if theta is None else theta
+    text = text_proj_for(cfg) if text is None else text
     with open(path, "wb") as f:
         f.write(b"QTTS")
         _u32(f, version)
@@ -73,17 +80,17 @@ def write(path, tw, pw, cfg, fmt=1, version=1, theta=None, tail=b"decoder sectio
         # talker (save.rs:49-88)
         half = cfg.t_head_dim // 2
         sections = [half - 2 * (half // 3), half // 3, half // 3]
-        for v in (cfg.t_layers, cfg.t_hidden, cfg.t_hidden, cfg.t_heads, cfg.t_kv_heads,
+        for v in (cfg.t_layers, cfg.t_hidden, text.text_embedding.n, cfg.t_heads, cfg.t_kv_heads,
                   cfg.t_head_dim, cfg.t_heads // cfg.t_kv_heads, len(sections), *sections):
             _u32(f, v)
         for lw in tw.layers:
             _layer(f, lw)
         _q4(f, tw.codec_embedding)
-        _q4(f, qora_b200.synth_q4(71, 0.02, 8, 32))   # text_embedding
-        _q4(f, qora_b200.synth_q4(72, 0.02, 32, 32))  # text_proj_fc1
-        _f32(f, np.zeros(32, np.float32))
-        _q4(f, qora_b200.synth_q4(73, 0.02, 32, 32))  # text_proj_fc2
-        _f32(f, np.zeros(32, np.float32))
+        _q4(f, text.text_embedding)
+        _q4(f, text.fc1)
+        _f32(f, text.fc1_bias)
+        _q4(f, text.fc2)
+        _f32(f, text.fc2_bias)
         _q4(f, tw.codec_head)
         _f16(f, tw.final_norm)
         for a in rope_tables(cfg.t_head_dim, cfg.t_max_pos, theta):

@@ -42,7 +42,8 @@ def test_reads_back_every_array(model, tmp_path):
     from qora_b200 import _lib
     cfg, tw, pw = model
     path = tmp_path / "tiny.qora-tts"
-    qf.write(path, tw, pw, cfg)
+    text = qora_b200.synth_text_proj(81, 96, cfg.t_hidden, cfg.t_hidden, mid=2 * cfg.t_hidden)
+    qf.write(path, tw, pw, cfg, text=text)
     mf = qora_b200.ModelFile(path)
     c = mf.cfg
     for k in ("t_layers", "t_hidden", "t_heads", "t_kv_heads", "t_head_dim", "t_ffn", "t_vocab",
@@ -68,6 +69,12 @@ def test_reads_back_every_array(model, tmp_path):
         _same_q4(embs[g], pw.codec_embeddings[g])
         _same_q4(heads[g], pw.lm_heads[g])
     assert np.array_equal(_arr(p.final_norm, cfg.p_hidden, np.uint16), pw.final_norm)
+    x = mf.text_proj_host
+    _same_q4(x.text_embedding, text.text_embedding)
+    _same_q4(x.fc1, text.fc1)
+    _same_q4(x.fc2, text.fc2)
+    assert np.array_equal(_arr(x.fc1_bias, text.fc1.n, np.float32), text.fc1_bias)
+    assert np.array_equal(_arr(x.fc2_bias, text.fc2.n, np.float32), text.fc2_bias)
     mf.close()
 
 
@@ -96,6 +103,10 @@ def test_malformed_files_are_errors(model, tmp_path):
     assert _status(bad) == 6
     qf.write(bad, tw, pw, cfg, theta=1e6 + 0.25)   # tables of a non-integer base
     assert _status(bad) == 6
+    import qora_b200
+    text = qora_b200.synth_text_proj(82, 32, cfg.t_hidden, cfg.t_hidden + 32)
+    qf.write(bad, tw, pw, cfg, text=text)          # fc2 output != talker hidden
+    assert _status(bad) == 1
     assert _status(tmp_path / "missing.qora-tts") == 1
     os.remove(bad)
 

@@ -135,3 +135,14 @@ def test_attend_step_matches_numpy(orc):
             ref[h * hd:(h + 1) * hd] = (p / p.sum()) @ Vs[:, h // (heads // kvh)]
         assert np.max(np.abs(got - ref)) < 1e-5
     assert kv.len(0) == steps
+
+
+def test_embed_text_token_matches_numpy(orc):
+    """oq_embed_text_token (talker.rs:104-116) against the float64 restatement,
+    with fc1 widening the text hidden size (mid != text_hidden)."""
+    tp = orc.TextProj.synth(61, text_vocab=50, text_hidden=128, hidden=96, mid=160, sigma=0.05)
+    for tok in (0, 1, 17, 49):
+        got = tp.embed_text_token(tok)
+        ref = np_ref.embed_text_token(tp, tok)
+        assert got.shape == (96,)
+        assert np.max(np.abs(got - ref)) < 1e-5 * max(1.0, np.max(np.abs(ref)))
