@@ -93,6 +93,22 @@ typedef struct qora_text_proj_host {
     const float *fc2_bias;           /* [hidden] */
 } qora_text_proj_host;
 
+/* One row of a talker prompt (generate_new.rs:91-466, 756-768): row =
+ * text + codec, either part optional.
+ *   text  = text_rows[text] (text >= 0; -1: none)
+ *   codec = codes_n == 0:  none
+ *           codes_n == 1:  codec_embedding[codes[0]]
+ *           codes_n == n > 1: codec_embedding[codes[0]] + acoustic_embedding[0][codes[1]]
+ *                         + ... + acoustic_embedding[n-2][codes[n-1]], summed in
+ *                         that order (a reference frame, generate_new.rs:164-169)
+ *           codes_n == -1: the voice embedding (generate_new.rs:214-217, 404-407):
+ *                         values past its length are 0, text included. */
+typedef struct qora_prompt_row {
+    int32_t text;
+    int32_t codes_n;
+    uint32_t codes[16];
+} qora_prompt_row;
+
 /* TTSParams sampling fields (generate_new.rs:38-79). */
 typedef struct qora_sample_params {
     float temperature;         /* 0.9 */
@@ -242,6 +258,16 @@ void qora_text_proj_destroy(qora_text_proj *tp);
 int qora_text_proj_embed(qora_text_proj *tp, const uint32_t *tokens, int32_t count, float *out,
                          void *stream);
 
+/* Prompt assembly (generate_new.rs:91-466): `count` rows described by the
+ * HOST array `rows` into device out [count][hidden]; text_rows is device
+ * [n_text][hidden] (e.g. from qora_text_proj_embed), voice a device vector of
+ * voice_len floats (NULL when no row is a voice row); `p` may be NULL when no
+ * row has more than one code.  Every index is checked before any launch
+ * (QORA_ERR_RANGE). */
+int qora_prompt_assemble(qora_talker *t, qora_predictor *p, const float *text_rows,
+                         int32_t n_text, const float *voice, int32_t voice_len,
+                         const qora_prompt_row *rows, int32_t count, float *out, void *stream);
+
 /* ------------------------------------------------------------ code_predictor.rs */
 int qora_predictor_create(qora_ctx *ctx, const qora_predictor_host *host, int32_t max_batch,
                           qora_predictor **out);
@@ -291,6 +317,12 @@ int qora_engine_use_graph(qora_engine *e, int32_t enable);
  * heads / kv_heads of 1, 2 or 4, widths <= 6144 and vocab <= 4096;
  * QORA_ERR_UNSUPPORTED otherwise (the per-op path then stays in use). */
 int qora_engine_use_persistent(qora_engine *e, int32_t enable);
+/* frame_temperature (generate_new.rs:82-88, used at :608): sets the
+ * temperature of the following frames' first sample_token.  The onset
+ * schedule (onset_frames frames at onset_temperature, then temperature) is a
+ * call at the start and one at frame onset_frames; a captured frame graph is
+ * captured again on the next frame.  NaN is QORA_ERR_INVALID. */
+int qora_engine_set_temperature(qora_engine *e, float temperature);
 /* Per-op timing of the persistent frame kernel (a profiling aid, no
  * reference counterpart).  enable != 0 makes later frames record, for each
  * op, globaltimer ns over the SMs that have items in it: the earliest input

@@ -1141,4 +1141,10 @@ int frame_launch(FrameProgram *fp, const float *text, cudaStream_t st) {
 
 void frame_program_destroy(FrameProgram *p) { delete p; }
 
+// The sampler's arguments travel in the launch parameters, so the next launch
+// picks the new temperature up.
+void frame_program_set_temperature(FrameProgram *p, float temperature) {
+    p->params.sample.params.temperature = temperature;
+}
+
 }  // namespace qora

@@ -405,8 +405,8 @@ int launch_gemv(GemvArgs a, int xmode, int emode, const GemvPlan &p, unsigned *g
     a.rows_per_cta_k = p.rows_per_cta_k;
     a.rows_per_z = p.rows_per_z;
     if (p.mma) {
-        if (!gemv_mma_eligible(a, xmode, emode))
-            return set_error(QORA_ERR_INVALID, "tensor-core GEMV plan for an ineligible launch");
+        if (!gemv_mma_supported(a, xmode, emode))
+            return set_error(QORA_ERR_INVALID, "tensor-core GEMV plan for an unsupported launch");
         return launch_gemv_mma(a, xmode, emode, p, st);
     }
     switch (xmode) {

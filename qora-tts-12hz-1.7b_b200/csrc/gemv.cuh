@@ -80,6 +80,8 @@ GemvPlan plan_gemv(int64_t k, int64_t C, int rows, int emode, int num_sms);
 // weight scales within the f16 operand range), its tiling, its launcher.
 int gemv_mma_init();
 bool gemv_mma_eligible(const GemvArgs &a, int xmode, int emode);
+// The same conditions apart from the row count (any 1..kMaxRows rows run correctly).
+bool gemv_mma_supported(const GemvArgs &a, int xmode, int emode);
 GemvPlan plan_gemv_mma(int64_t k, int64_t C, int rows, int emode, int num_sms);
 int launch_gemv_mma(const GemvArgs &a, int xmode, int emode, const GemvPlan &p, cudaStream_t st);
 

@@ -668,8 +668,11 @@ int gemv_mma_init() {
 }
 
 bool gemv_mma_eligible(const GemvArgs &a, int xmode, int emode) {
+    return a.rows >= kMmaMinRows && gemv_mma_supported(a, xmode, emode);
+}
+
+bool gemv_mma_supported(const GemvArgs &a, int xmode, int emode) {
     if (mma_disabled_by_env()) return false;
-    if (a.rows < kMmaMinRows) return false;
     if (xmode != X_PLAIN && xmode != X_RMSNORM && xmode != X_EMBED) return false;
     if (emode < E_STORE || emode > E_SWIGLU) return false;
     if (a.w.mma_exp < 0 || a.w.k % kStageK != 0 || a.w.C % kMmaGroups != 0) return false;

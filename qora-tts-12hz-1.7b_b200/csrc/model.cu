@@ -922,6 +922,19 @@ int qora_engine_use_graph(qora_engine *e, int32_t enable) {
     return QORA_OK;
 }
 
+int qora_engine_set_temperature(qora_engine *e, float temperature) {
+    if (!e || temperature != temperature) return set_error(QORA_ERR_INVALID, "qora_engine_set_temperature: bad arguments");
+    if (e->params.temperature == temperature) return QORA_OK;
+    e->params.temperature = temperature;
+    if (e->frame) frame_program_set_temperature(e->frame, temperature);
+    // the per-op graph holds the old value in its sampler node: capture again
+    if (e->exec) cudaGraphExecDestroy(e->exec);  // (freed after an in-flight launch completes)
+    if (e->graph) cudaGraphDestroy(e->graph);
+    e->exec = nullptr;
+    e->graph = nullptr;
+    return QORA_OK;
+}
+
 int qora_engine_use_persistent(qora_engine *e, int32_t enable) {
     if (!e) return set_error(QORA_ERR_INVALID, "null engine");
     if (enable && !frame_supported(e))

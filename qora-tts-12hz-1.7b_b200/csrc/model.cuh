@@ -51,6 +51,7 @@ struct Work {
 
 struct FrameProgram;  // persistent frame kernel state (frame.cu)
 void frame_program_destroy(FrameProgram *p);
+void frame_program_set_temperature(FrameProgram *p, float temperature);
 
 }  // namespace qora
 

@@ -7,9 +7,10 @@
 //   -> [fc2 GEMV, bias epilogue] -> out[count][hidden]
 //
 // Up to kMaxRows tokens share one launch sequence, so the fc1 / fc2 weights
-// are streamed once per chunk rather than once per token; chunks of 8 or more
-// tokens run on the tensor-core GEMV.  Token ids arrive from the host (the
-// tokenizer's output) and are range-checked there, before any launch.
+// are streamed once per chunk rather than once per token, on the tensor-core
+// GEMV; each token's row is the same bits whatever else is in the chunk.
+// Token ids arrive from the host (the tokenizer's output) and are
+// range-checked there, before any launch.
 #include <algorithm>
 #include <vector>
 
@@ -43,6 +44,13 @@ int upload_f32(const float *src, int64_t n, DevBuf &buf) {
     return QORA_OK;
 }
 
+// A token's row must not depend on which other tokens share the call: the
+// reference projects one token at a time, and its prefix cache relies on a
+// prompt row coming out the same in the prefix build and in the full build.
+// So every chunk runs the tensor-core GEMV with the K split planned for a
+// single row tile, whatever the chunk's size (its clusters are independent,
+// so any number of row tiles is valid).  Where the tensor-core path does not
+// apply, each token gets its own launch.
 int bias_gemv(qora_text_proj *tp, const Q4Dev &w, int xmode, const float *x, const uint32_t *tok,
               const float *bias, float *y, int rows, cudaStream_t st) {
     GemvArgs a;
@@ -60,8 +68,22 @@ int bias_gemv(qora_text_proj *tp, const Q4Dev &w, int xmode, const float *x, con
     a.y = y;
     a.ldy = w.n;
     a.err = tp->ctx->err.as<int>();
-    const GemvPlan p = plan_gemv_for(a, xmode, E_BIAS, tp->ctx->num_sms);
-    return launch_gemv(a, xmode, E_BIAS, p, nullptr, st);
+    if (gemv_mma_supported(a, xmode, E_BIAS)) {
+        GemvPlan p = plan_gemv_mma(w.k, w.C, 1, E_BIAS, tp->ctx->num_sms);
+        p.Z = (rows + p.rows_per_z - 1) / p.rows_per_z;
+        p.grid.z = (unsigned)p.Z;
+        return launch_gemv(a, xmode, E_BIAS, p, nullptr, st);
+    }
+    for (int r = 0; r < rows; r++) {
+        GemvArgs b = a;
+        b.rows = 1;
+        if (xmode == X_EMBED) b.tok = tok + r;
+        else b.x = x + (int64_t)r * w.k;
+        b.y = y + (int64_t)r * w.n;
+        const GemvPlan p = plan_gemv(w.k, w.C, 1, E_BIAS, tp->ctx->num_sms);
+        QORA_TRY(launch_gemv(b, xmode, E_BIAS, p, nullptr, st));
+    }
+    return QORA_OK;
 }
 
 }  // namespace

@@ -56,6 +56,10 @@ class TextProjHost(C.Structure):
                 ("fc1_bias", C.c_void_p), ("fc2_bias", C.c_void_p)]
 
 
+class PromptRow(C.Structure):
+    _fields_ = [("text", C.c_int32), ("codes_n", C.c_int32), ("codes", C.c_uint32 * 16)]
+
+
 class SampleParams(C.Structure):
     _fields_ = [("temperature", C.c_float), ("top_k", C.c_int32), ("top_p", C.c_float),
                 ("repetition_penalty", C.c_float)]
@@ -99,6 +103,7 @@ SIGNATURES = {
     "qora_text_proj_create": (C.c_int, [_vp, _vp, _PP]),
     "qora_text_proj_destroy": (None, [_vp]),
     "qora_text_proj_embed": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),
+    "qora_prompt_assemble": (C.c_int, [_vp, _vp, _vp, _i32, _vp, _i32, _vp, _i32, _vp, _vp]),
     "qora_talker_create": (C.c_int, [_vp, _vp, _i32, _PP]),
     "qora_talker_destroy": (None, [_vp]),
     "qora_talker_step": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
@@ -117,6 +122,7 @@ SIGNATURES = {
     "qora_engine_frame_host": (C.c_int, [_vp, _vp, _vp, _vp]),
     "qora_engine_use_graph": (C.c_int, [_vp, _i32]),
     "qora_engine_use_persistent": (C.c_int, [_vp, _i32]),
+    "qora_engine_set_temperature": (C.c_int, [_vp, _f32]),
     "qora_engine_trace": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "qora_engine_kernels_per_frame": (C.c_int, [_vp, C.POINTER(C.c_int32)]),
     "qora_engine_state": (C.c_int, [_vp, _PP, _PP, _PP, _PP, _PP]),

@@ -373,6 +373,12 @@ class Engine:
     def use_graph(self, enable: bool = True):
         _lib.call("qora_engine_use_graph", self.h, 1 if enable else 0)
 
+    def set_temperature(self, temperature: float):
+        """The first sample_token's temperature for the following frames
+        (frame_temperature, generate_new.rs:82-88)."""
+        self.params.temperature = temperature
+        _lib.call("qora_engine_set_temperature", self.h, float(temperature))
+
     def frame(self, text: torch.Tensor, codes: torch.Tensor, stream=None):
         """One frame from device buffers: text [B][H] f32 -> codes [B][16] int32."""
         _lib.call("qora_engine_frame", self.h, _dp(text), _dp(codes), _stream(stream))

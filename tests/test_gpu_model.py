@@ -286,3 +286,40 @@ def test_engine_batch8_frames_match_oracle(E, ctx, orc):
             ref = om.frame(kvs[b][0], kvs[b][1], params, text[b], T + f, states[b])
             assert list(got[b]) == list(ref), (f, b)
     ctx.check_device_error()
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_engine_onset_temperature_schedule(E, orc, tiny, B):
+    """frame_temperature (generate_new.rs:82-88): the first frames sample at
+    the onset temperature, then at the base one.  B = 1 runs the persistent
+    frame kernel, B = 2 the per-op kernels in a CUDA graph (captured again
+    after the change)."""
+    import torch
+    from qora_b200 import generate as G
+    cfg, om, talker, pred = tiny
+    T, F = 3, 5
+    sched = G.TTSParams(temperature=1.4, onset_frames=2, onset_temperature=0.05)
+    eng = E.Engine(talker, pred, B, max_pos=32, params=sched.sample_params())
+    eng.use_graph(True)
+    x = orc.synth_normal(960 + B, 1.0, B * T * cfg.t_hidden).reshape(B, T, cfg.t_hidden)
+    seeds = [70 + b for b in range(B)]
+    eng.prefill(x, seeds)
+    text = orc.synth_normal(961, 1.0, B * cfg.t_hidden).reshape(B, cfg.t_hidden)
+    states, kvs = [], []
+    for b in range(B):
+        tkv, pkv = om.talker_kv(32), om.predictor_kv()
+        hdn = om.talker_prefill(x[b], tkv, 0)
+        states.append({"logits": om.codec_head(hdn), "hidden": hdn.copy(),
+                       "prev": np.zeros(16, np.uint32), "rng": seeds[b]})
+        kvs.append((tkv, pkv))
+    tt = _cuda(text)
+    codes = torch.zeros(B, 16, dtype=torch.int32).cuda()
+    for f in range(F):
+        temp = G.frame_temperature(sched, f)
+        eng.set_temperature(temp)
+        eng.frame(tt, codes)
+        got = codes.cpu().numpy()
+        params = orc.SampleParams(temp, sched.top_k, sched.top_p, sched.repetition_penalty)
+        for b in range(B):
+            ref = om.frame(kvs[b][0], kvs[b][1], params, text[b], T + f, states[b])
+            assert list(got[b]) == list(ref), (f, b)

@@ -59,6 +59,23 @@ def test_embed_matches_oracle(E, ctx, orc, vocab, th, mid, hidden):
     ctx.check_device_error()
 
 
+@pytest.mark.parametrize("th,mid,hidden", [(256, 384, 256), (128, 160, 96)])
+def test_rows_do_not_depend_on_the_batch(E, ctx, orc, th, mid, hidden):
+    """A token's row is the same bits alone, in any run and at any position
+    (the reference projects one token at a time; its prefix cache relies on
+    equal rows).  (128, 160, 96) has column groups that are not a multiple of
+    4, so it runs one CUDA-core launch per token."""
+    tp = orc.TextProj.synth(94, 500, th, hidden, mid=mid, sigma=0.05)
+    dev = E.TextProjection(ctx, _device_weights(tp))
+    tokens = np.random.default_rng(1).integers(0, 500, size=45).astype(np.uint32)
+    full = dev.embed_text_tokens(tokens).cpu().numpy()
+    for lo, hi in ((0, 1), (3, 5), (7, 15), (10, 45), (44, 45)):
+        part = dev.embed_text_tokens(tokens[lo:hi]).cpu().numpy()
+        assert np.array_equal(part, full[lo:hi]), (lo, hi)
+    rev = dev.embed_text_tokens(tokens[::-1].copy()).cpu().numpy()
+    assert np.array_equal(rev[::-1], full)
+
+
 def test_long_prompt_is_chunked(E, ctx, orc):
     """600 tokens: one 512-row chunk and one of 88, same rows as the oracle."""
     tp = orc.TextProj.synth(92, 211, 256, 256, sigma=0.05)
