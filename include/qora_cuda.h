@@ -145,7 +145,9 @@ int qora_q4_gemv(qora_ctx *ctx, const qora_w4 *w, const float *x, float *y, int3
 /* gemm (gemv.rs:157, 349-412): seq_len token rows. */
 int qora_q4_gemm(qora_ctx *ctx, const qora_w4 *w, const float *x, int64_t seq_len, float *y,
                  void *stream);
-/* embed_lookup (gemv.rs:165, 415-437): out[i][0..n) = dequantised row tokens[i]. */
+/* embed_lookup (gemv.rs:165, 415-437): out[i][0..n) = dequantised row tokens[i]
+ * (device tokens; one outside the table gives a zero row and QORA_ERR_RANGE at
+ * the next qora_ctx_check_device_error). */
 int qora_q4_embed_rows(qora_ctx *ctx, const qora_w4 *w, const uint32_t *tokens, int32_t count,
                        float *out, void *stream);
 /* rms_norm_f16 (gemv.rs:445-454) over `rows` rows of length n. */
@@ -241,10 +243,20 @@ int qora_talker_step(qora_talker *t, qora_kv *kv, const float *emb, const int32_
  * x [T][hidden], start_pos must equal the stream's cache length. */
 int qora_talker_prefill(qora_talker *t, qora_kv *kv, int32_t kv_stream, const float *x,
                         int32_t T, int32_t start_pos, float *hidden, void *stream);
+/* forward_talker_decode (talker.rs:161-258) for B streams: embeds
+ * tokens_host[b] (a HOST array) through the text projection `tp` when is_text,
+ * else through the codec embedding, runs the talker step at positions[b]
+ * (device int32) and writes the final-normed hidden [B][hidden]; no codec
+ * head.  `tp` may be NULL when is_text == 0.  Out-of-vocabulary tokens are
+ * QORA_ERR_RANGE before any launch. */
+int qora_talker_decode(qora_talker *t, qora_kv *kv, qora_text_proj *tp, const uint32_t *tokens_host,
+                       int32_t is_text, const int32_t *positions, int32_t B, float *hidden,
+                       void *stream);
 /* apply_codec_head (talker.rs:647-649). */
 int qora_talker_codec_head(qora_talker *t, const float *hidden, int32_t B, float *logits,
                            void *stream);
-/* embed_codec_token (talker.rs:152-154) for B tokens. */
+/* embed_codec_token (talker.rs:152-154) for B device tokens (range as
+ * qora_q4_embed_rows). */
 int qora_talker_embed_codec(qora_talker *t, const uint32_t *tokens, int32_t B, float *out,
                             void *stream);
 

@@ -748,6 +748,19 @@ void oq_embed_text_token(const oq_text_proj *tp, uint32_t token, float *out) {
     free(h);
 }
 
+int oq_talker_decode(const oq_talker *t, const oq_text_proj *tp, uint32_t token, int is_text,
+                     oq_kv *kv, int64_t position, float *out_hidden) {
+    float *x = (float *)malloc(sizeof(float) * (size_t)t->hidden);
+    float *logits = (float *)malloc(sizeof(float) * (size_t)t->vocab);
+    if (is_text) oq_embed_text_token(tp, token, x);           /* talker.rs:170-174 */
+    else oq_embed_codec_token(t, token, x);
+    /* talker.rs:176-257 are forward_with_embedding's layers and final norm */
+    const int rc = oq_talker_step(t, x, kv, position, out_hidden, logits);
+    free(x);
+    free(logits);
+    return rc;
+}
+
 /* ======================================================================== */
 /* Code predictor: code_predictor.rs                                         */
 /* ======================================================================== */

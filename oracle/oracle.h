@@ -150,6 +150,11 @@ typedef struct oq_text_proj {
 } oq_text_proj;
 /* embed_text_token (talker.rs:104-116): out [fc2.n]. */
 void oq_embed_text_token(const oq_text_proj *tp, uint32_t token, float *out);
+/* forward_talker_decode (talker.rs:161-258): embed the token (text path when
+ * is_text, else the codec embedding), one talker step at `position`;
+ * out_hidden [hidden] final-normed. */
+int oq_talker_decode(const oq_talker *t, const oq_text_proj *tp, uint32_t token, int is_text,
+                     oq_kv *kv, int64_t position, float *out_hidden);
 
 /* ---- code_predictor.rs --------------------------------------------------- */
 int oq_predictor_frame(const oq_predictor *p, const float *talker_hidden,

@@ -107,6 +107,7 @@ def lib():
             "oq_codec_head": (None, [vp, vp, vp]),
             "oq_embed_codec_token": (None, [vp, C.c_uint32, vp]),
             "oq_embed_text_token": (None, [vp, C.c_uint32, vp]),
+            "oq_talker_decode": (C.c_int, [vp, vp, C.c_uint32, C.c_int, vp, i64, vp]),
             "oq_predictor_frame": (C.c_int, [vp, vp, vp, vp, vp, vp]),
             "oq_predictor_frame_forced": (C.c_int, [vp, vp, vp, vp, vp, vp, vp]),
             "oq_acoustic_embeddings_sum": (None, [vp, vp, vp]),
@@ -513,6 +514,16 @@ class OracleModel:
         rc = lib().oq_talker_step(C.addressof(self.t), ptr(emb), kv.h, position, ptr(h), ptr(lg))
         assert rc == 0, rc
         return h, lg
+
+    def talker_decode(self, token: int, is_text: bool, kv: KV, position: int,
+                      text_proj: "TextProj | None" = None):
+        """forward_talker_decode (talker.rs:161-258): the final-normed hidden."""
+        out = np.zeros(self.m.cfg.t_hidden, np.float32)
+        tps = text_proj.cstruct() if text_proj is not None else None
+        rc = lib().oq_talker_decode(C.addressof(self.t), C.addressof(tps) if tps is not None else None,
+                                    token, 1 if is_text else 0, kv.h, position, ptr(out))
+        assert rc == 0, rc
+        return out
 
     def talker_prefill(self, x, kv: KV, start_pos: int = 0):
         c = self.m.cfg

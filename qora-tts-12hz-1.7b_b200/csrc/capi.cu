@@ -293,7 +293,7 @@ int qora_q4_gemm(qora_ctx *ctx, const qora_w4 *w, const float *x, int64_t seq_le
 int qora_q4_embed_rows(qora_ctx *ctx, const qora_w4 *w, const uint32_t *tokens, int32_t count,
                        float *out, void *stream) {
     if (!ctx || !w || !tokens || !out || count < 0) return set_error(QORA_ERR_INVALID, "bad arguments");
-    return launch_embed_rows(w->emb, tokens, 1, count, out, w->emb.n, as_stream(stream));
+    return launch_embed_rows(w->emb, tokens, 1, count, out, w->emb.n, ctx->err.as<int>(), as_stream(stream));
 }
 
 int qora_rms_norm_f16(qora_ctx *ctx, const float *x, const uint16_t *gamma, int64_t n, int32_t rows,

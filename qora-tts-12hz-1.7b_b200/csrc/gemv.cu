@@ -283,11 +283,16 @@ __global__ void k_repack(const uint8_t *__restrict__ src, const __half *__restri
 }
 
 __global__ void k_embed_rows(EmbDev e, const uint32_t *__restrict__ tok, int64_t ldtok,
-                             float *__restrict__ out, int64_t ldout) {
+                             float *__restrict__ out, int64_t ldout, int *err) {
     griddep_launch_dependents();
     griddep_wait();
     const int i = blockIdx.x;
     const uint32_t t = __ldcg(tok + (int64_t)i * ldtok);
+    if ((int64_t)t >= e.rows) {  // never read outside the table: zeros, and the flag
+        if (threadIdx.x == 0) raise_error(err, kDevRange);
+        for (int64_t j = threadIdx.x; j < e.n; j += blockDim.x) out[(int64_t)i * ldout + j] = 0.0f;
+        return;
+    }
     const uint8_t *p = e.packed + (int64_t)t * (e.n >> 1);
     const __half *s = e.scl + (int64_t)t * (e.n >> 5);
     for (int64_t j = threadIdx.x; j < e.n; j += blockDim.x) {
@@ -432,9 +437,10 @@ int repack_q4(const uint8_t *src_packed, const __half *src_scl, int64_t k, int64
 }
 
 int launch_embed_rows(const EmbDev &e, const uint32_t *tok, int64_t ldtok, int count, float *out,
-                      int64_t ldout, cudaStream_t stream) {
+                      int64_t ldout, int *err, cudaStream_t stream) {
     if (count <= 0) return QORA_OK;
-    return launch_ex(k_embed_rows, dim3(count), dim3(256), 0, stream, 1u, e, tok, ldtok, out, ldout);
+    return launch_ex(k_embed_rows, dim3(count), dim3(256), 0, stream, 1u, e, tok, ldtok, out, ldout,
+                     err);
 }
 
 int launch_copy_rowstats(const float *src, int64_t ldsrc, float *dst, int64_t lddst, int rows,

@@ -100,8 +100,9 @@ int repack_q4(const uint8_t *src_packed, const __half *src_scl, int64_t k, int64
               uint4 *dst_nib, __half *dst_scl, int64_t dst_k_stride, int64_t dst_off,
               int64_t dst_stride, cudaStream_t stream);
 
+// A token outside the table gives a zero row and raises kDevRange on `err`.
 int launch_embed_rows(const EmbDev &e, const uint32_t *tok, int64_t ldtok, int count, float *out,
-                      int64_t ldout, cudaStream_t stream);
+                      int64_t ldout, int *err, cudaStream_t stream);
 
 // Copy rows and write their per-32-column sum-of-squares partials.
 int launch_copy_rowstats(const float *src, int64_t ldsrc, float *dst, int64_t lddst, int rows,

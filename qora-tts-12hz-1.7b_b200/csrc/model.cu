@@ -258,7 +258,7 @@ static int predictor_project(qora_predictor *p, Launcher &ln, int rows, const fl
         const float *src = x;
         int64_t lds = ldx;
         if (emb) {
-            QORA_TRY(launch_embed_rows(*emb, tok, ldtok, rows, p->xe.as<float>(), p->Ht, ln.st));
+            QORA_TRY(launch_embed_rows(*emb, tok, ldtok, rows, p->xe.as<float>(), p->Ht, p->ctx->err.as<int>(), ln.st));
             ln.count++;
             src = p->xe.as<float>();
             lds = p->Ht;
@@ -492,6 +492,8 @@ int qora_talker_create(qora_ctx *ctx, const qora_talker_host *h, int32_t max_bat
     if (rc == QORA_OK)  // prefill chunks use up to kMaxRows rows
         rc = t->w.alloc(kMaxRows, t->H, t->qkvn(), t->qd(), t->ffn, t->vocab, t->kvh, t->heads,
                         t->hd);
+    if (rc == QORA_OK) rc = t->emb_in.alloc((size_t)max_batch * t->H * 4);
+    if (rc == QORA_OK) rc = t->tok_in.alloc((size_t)max_batch * 4);
     if (rc != QORA_OK) {
         delete t;
         return rc;
@@ -512,6 +514,31 @@ int qora_talker_step(qora_talker *t, qora_kv *kv, const float *emb, const int32_
     QORA_TRY(launch_copy_rowstats(emb, t->H, t->w.x.as<float>(), t->H, B, t->H,
                                   t->w.ss.as<float>(), t->H / kGroup, ln.st));
     return talker_forward_step(t, kv, ln, B, positions, hidden, t->H, logits, t->vocab, nullptr);
+}
+
+int qora_talker_decode(qora_talker *t, qora_kv *kv, qora_text_proj *tp, const uint32_t *tokens_host,
+                       int32_t is_text, const int32_t *positions, int32_t B, float *hidden,
+                       void *stream) {
+    if (!t || !kv || !tokens_host || !positions || !hidden || B <= 0 || B > t->max_batch ||
+        (is_text && !tp))
+        return set_error(QORA_ERR_INVALID, "qora_talker_decode: bad arguments");
+    cudaStream_t st = as_stream(stream);
+    float *emb = t->emb_in.as<float>();
+    if (is_text) {  // embed_text_token (talker.rs:171)
+        if (text_proj_hidden(tp) != t->H)
+            return set_error(QORA_ERR_SHAPE, "text projection is %lld wide, talker %d",
+                             (long long)text_proj_hidden(tp), t->H);
+        QORA_TRY(qora_text_proj_embed(tp, tokens_host, B, emb, stream));
+    } else {  // embed_codec_token (talker.rs:173)
+        for (int32_t b = 0; b < B; b++)
+            if ((int64_t)tokens_host[b] >= t->codec_emb.rows)
+                return set_error(QORA_ERR_RANGE, "codec token %u outside the codec vocabulary (%lld)",
+                                 tokens_host[b], (long long)t->codec_emb.rows);
+        QORA_CUDA(cudaMemcpyAsync(t->tok_in.p, tokens_host, (size_t)B * 4, cudaMemcpyHostToDevice, st));
+        QORA_TRY(launch_embed_rows(t->codec_emb, t->tok_in.as<uint32_t>(), 1, B, emb, t->H,
+                                   t->ctx->err.as<int>(), st));
+    }
+    return qora_talker_step(t, kv, emb, positions, B, hidden, nullptr, stream);
 }
 
 namespace {
@@ -574,7 +601,7 @@ int qora_talker_codec_head(qora_talker *t, const float *hidden, int32_t B, float
 int qora_talker_embed_codec(qora_talker *t, const uint32_t *tokens, int32_t B, float *out,
                             void *stream) {
     if (!t || !tokens || !out || B <= 0) return set_error(QORA_ERR_INVALID, "bad arguments");
-    return launch_embed_rows(t->codec_emb, tokens, 1, B, out, t->H, as_stream(stream));
+    return launch_embed_rows(t->codec_emb, tokens, 1, B, out, t->H, t->ctx->err.as<int>(), as_stream(stream));
 }
 
 // --------------------------------------------------------------- predictor

@@ -52,6 +52,7 @@ struct Work {
 struct FrameProgram;  // persistent frame kernel state (frame.cu)
 void frame_program_destroy(FrameProgram *p);
 void frame_program_set_temperature(FrameProgram *p, float temperature);
+int64_t text_proj_hidden(const qora_text_proj *tp);  // output width (text_proj.cu)
 
 }  // namespace qora
 
@@ -64,6 +65,7 @@ struct qora_talker {
     qora::Q4Dev head;
     int max_batch = 0;
     qora::Work w;
+    qora::DevBuf emb_in, tok_in;  // qora_talker_decode: [max_batch][H] input rows, their tokens
 
     int64_t qd() const { return (int64_t)heads * hd; }
     int64_t kd() const { return (int64_t)kvh * hd; }

@@ -31,10 +31,8 @@ namespace {
 // silu (gemv.rs:486-488): x / (1 + exp(-x)), in place over n values.
 __global__ void k_silu(float *h, int64_t n) {
     const int64_t stride = (int64_t)gridDim.x * blockDim.x;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-        const float x = h[i];
-        h[i] = __fdiv_rn(x, __fadd_rn(1.0f, expf(-x)));
-    }
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+        h[i] = silu_ref(h[i]);
 }
 
 int upload_f32(const float *src, int64_t n, DevBuf &buf) {
@@ -87,6 +85,9 @@ int bias_gemv(qora_text_proj *tp, const Q4Dev &w, int xmode, const float *x, con
 }
 
 }  // namespace
+
+int64_t text_proj_hidden(const qora_text_proj *tp) { return tp->H; }
+
 }  // namespace qora
 
 using namespace qora;

@@ -109,6 +109,7 @@ SIGNATURES = {
     "qora_talker_step": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _vp, _vp, _vp]),
     "qora_talker_prefill": (C.c_int, [_vp, _vp, _i32, _vp, _i32, _i32, _vp, _vp]),
     "qora_talker_codec_head": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),
+    "qora_talker_decode": (C.c_int, [_vp, _vp, _vp, _vp, _i32, _vp, _i32, _vp, _vp]),
     "qora_talker_embed_codec": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),
     "qora_predictor_create": (C.c_int, [_vp, _vp, _i32, _PP]),
     "qora_predictor_destroy": (None, [_vp]),

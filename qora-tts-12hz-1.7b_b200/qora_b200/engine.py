@@ -213,6 +213,21 @@ class Talker:
                   _dp(hidden), _stream(stream))
         return hidden
 
+    def forward_talker_decode(self, tokens, is_text: bool, kv: KvCache, positions,
+                              text_proj: "TextProjection | None" = None,
+                              stream=None) -> torch.Tensor:
+        """forward_talker_decode (talker.rs:161-258) for B = len(tokens) streams:
+        embeds each token (text path through `text_proj`, or the codec
+        embedding), runs the step and returns the final-normed hidden [B][H]."""
+        c = self.cfg
+        t = np.ascontiguousarray(np.asarray(tokens, dtype=np.uint32).reshape(-1))
+        dev = f"cuda:{self.ctx.device}"
+        pos = torch.as_tensor(positions, dtype=torch.int32).reshape(-1).to(dev)
+        hidden = torch.empty(t.size, c.t_hidden, device=dev)
+        _lib.call("qora_talker_decode", self.h, kv.h, text_proj.h if text_proj is not None else None,
+                  t.ctypes.data, 1 if is_text else 0, _dp(pos), t.size, _dp(hidden), _stream(stream))
+        return hidden
+
     def apply_codec_head(self, hidden: torch.Tensor, stream=None) -> torch.Tensor:
         """apply_codec_head (talker.rs:647-649)."""
         c = self.cfg

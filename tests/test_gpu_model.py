@@ -323,3 +323,50 @@ def test_engine_onset_temperature_schedule(E, orc, tiny, B):
         for b in range(B):
             ref = om.frame(kvs[b][0], kvs[b][1], params, text[b], T + f, states[b])
             assert list(got[b]) == list(ref), (f, b)
+
+
+def test_talker_decode_teacher_forced(E, ctx, orc, tiny):
+    """forward_talker_decode (talker.rs:161-258) over a mixed text / codec token
+    sequence, device against oracle, then two streams at once."""
+    import qora_b200
+    from qora_b200 import _lib
+    cfg, om, talker, _ = tiny
+    tpo = orc.TextProj.synth(63, 400, cfg.t_hidden, cfg.t_hidden, sigma=0.05)
+    q = lambda w: qora_b200.Q4Weight(w.packed, w.scales, w.k, w.n)
+    tp = E.TextProjection(ctx, qora_b200.TextProjWeights(q(tpo.text_embedding), q(tpo.fc1),
+                                                        tpo.fc1_bias, q(tpo.fc2), tpo.fc2_bias))
+    kv = talker.new_kv(max_pos=16)
+    okv = om.talker_kv(16)
+    seq = [(11, True), (250, False), (399, True), (0, False), (7, True), (cfg.t_vocab - 1, False)]
+    for pos, (tok, is_text) in enumerate(seq):
+        got = talker.forward_talker_decode([tok], is_text, kv, [pos], tp).cpu().numpy()[0]
+        want = om.talker_decode(tok, is_text, okv, pos, tpo)
+        assert _maxerr(got, want) < TOL, pos
+    kv2 = talker.new_kv(max_pos=16, streams=2)
+    got = talker.forward_talker_decode([3, 4], False, kv2, [0, 0]).cpu().numpy()
+    for b, tok in enumerate((3, 4)):
+        want = om.talker_decode(tok, False, om.talker_kv(16), 0)
+        assert _maxerr(got[b], want) < TOL, b
+    with pytest.raises(_lib.QoraError) as ei:
+        talker.forward_talker_decode([cfg.t_vocab], False, kv, [len(seq)])
+    assert ei.value.status == 5
+    with pytest.raises(_lib.QoraError) as ei:
+        talker.forward_talker_decode([1], True, kv, [len(seq)])   # text path, no projection
+    assert ei.value.status == 1
+    ctx.check_device_error()
+
+
+def test_embed_rows_out_of_table_is_flagged(E, ctx, tiny):
+    """A device token past the codec table gives a zero row and a range error
+    at the next device-error check, never a read outside the table."""
+    import torch
+    from qora_b200 import _lib
+    cfg, _, talker, _ = tiny
+    out = talker.embed_codec_token([1, cfg.t_vocab + 5, 2])
+    torch.cuda.synchronize()
+    with pytest.raises(_lib.QoraError) as ei:
+        ctx.check_device_error()
+    assert ei.value.status == 5
+    o = out.cpu().numpy()
+    assert np.all(o[1] == 0.0) and np.any(o[0] != 0.0) and np.any(o[2] != 0.0)
+    ctx.check_device_error()   # the flag was cleared

@@ -146,3 +146,17 @@ def test_embed_text_token_matches_numpy(orc):
         ref = np_ref.embed_text_token(tp, tok)
         assert got.shape == (96,)
         assert np.max(np.abs(got - ref)) < 1e-5 * max(1.0, np.max(np.abs(ref)))
+
+
+def test_talker_decode_is_embed_then_step(orc, tiny):
+    """forward_talker_decode (talker.rs:161-258) = embed (text or codec path)
+    then the layers of forward_with_embedding: same bits as composing them."""
+    m, om, _ = tiny
+    c = m.cfg
+    tp = orc.TextProj.synth(62, 300, c.t_hidden, c.t_hidden)
+    kv_a, kv_b = om.talker_kv(), om.talker_kv()
+    for pos, (tok, is_text) in enumerate([(5, True), (17, False), (299, True), (0, False)]):
+        got = om.talker_decode(tok, is_text, kv_a, pos, tp)
+        emb = tp.embed_text_token(tok) if is_text else om.embed_codec(tok)
+        want, _ = om.talker_step(emb, kv_b, pos)
+        assert np.array_equal(got, want), pos
