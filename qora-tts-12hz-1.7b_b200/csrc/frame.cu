@@ -116,11 +116,14 @@ __device__ __forceinline__ void cp_async_commit_wait() {
     asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
 }
 
-// (rot is kept in [0, grid) by the builder, so no division is needed: this
-// sits on the path between two ops, where an integer division is measurable.)
-__device__ __forceinline__ int first_item(int cta, int rot, int grid) {
-    const int j = cta - rot;
-    return j < 0 ? j + grid : j;
+// This SM's first item of `op` (op.n_items if it has none); its further
+// items follow every op.avail.  (rot is kept in [0, grid) by the builder, so
+// no division is needed: this sits on the path between two ops, where an
+// integer division is measurable.)
+__device__ __forceinline__ int first_item(int cta, const OpRef &op, int grid) {
+    int j = cta - op.rot;
+    if (j < 0) j += grid;
+    return j < op.avail ? j : op.n_items;
 }
 
 // Across SMs: field 0 keeps the earliest time (stored complemented, so a
@@ -167,13 +170,13 @@ __device__ void producer(const FrameParams &P, FrameSmem &S, int cta, int grid) 
     for (int i = 0; i < P.n_ops && ok; i++) {
         const OpRef op = S.ops[i];
         if (op.type != OP_GEMV) continue;
-        const int u0 = first_item(cta, op.rot, grid);
+        const int u0 = first_item(cta, op, grid);
         if (u0 >= op.n_items) continue;
         const GemvDesc &d = P.gemv[op.idx];
         const int G = d.G, kpad = d.kpad;
         const uint4 *nib = d.nib;
         const __half *scl = d.scl;
-        for (int u = u0; u < op.n_items && ok; u += grid) {
+        for (int u = u0; u < op.n_items && ok; u += op.avail) {
             for (int g = 0; g < G && ok; g++) {  // a unit's groups one after the other
                 const int64_t grp = (int64_t)u * G + g;
                 for (int c0 = 0; c0 < kpad; c0 += kChunkRows) {
@@ -339,8 +342,8 @@ __device__ __forceinline__ float emb_at(const EmbWord &e, int c) {
 }
 
 // This SM's slice of [0, K) (the SMs with items in the op partition it).
-__device__ __forceinline__ void my_slice(int K, int j0, int n_items, int grid, int &lo, int &hi) {
-    const int parts = min(n_items, grid);
+__device__ __forceinline__ void my_slice(int K, int j0, int n_items, int avail, int &lo, int &hi) {
+    const int parts = min(n_items, avail);
     lo = (int)((int64_t)j0 * K / parts);
     hi = (int)((int64_t)(j0 + 1) * K / parts);
 }
@@ -364,7 +367,7 @@ __device__ __forceinline__ void norm_strided(float *xs, const __half *gamma, int
 
 // Builds the GEMV input x[0..kpad) in shared memory (rows >= K are zero).
 __device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &S, int tid,
-                            bool leader, int j0, int n_items, int grid) {
+                            bool leader, int j0, int n_items, int avail) {
     float *xs = S.u.xs;
     const int K = d.K;
     // gamma is immutable: its first loads go out before any wait
@@ -493,7 +496,7 @@ __device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d
     if (d.save) {
         // this SM's slice of the un-normalised input, published as tagged words
         int lo, hi;
-        my_slice(K, j0, n_items, grid, lo, hi);
+        my_slice(K, j0, n_items, avail, lo, hi);
         for (int k = lo + tid; k < hi; k += kNT) st_relaxed_u64(d.save + k, tag_pack(xs[k], P.tag_base + d.out_tag));
     }
     if (d.gamma) {
@@ -503,7 +506,7 @@ __device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d
     }
     if (d.save_plain) {
         int lo, hi;
-        my_slice(K, j0, n_items, grid, lo, hi);
+        my_slice(K, j0, n_items, avail, lo, hi);
         for (int k = lo + tid; k < hi; k += kNT) __stcg(d.save_plain + k, xs[k]);
     }
 }
@@ -540,7 +543,7 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
     const int lane = tid & 31, warp = tid >> 5;
     const float *xs = S.u.xs;
     const uint32_t otag = P.tag_base + d.out_tag;
-    for (int u = first_item(cta, op.rot, grid); u < op.n_items; u += grid) {
+    for (int u = first_item(cta, op, grid); u < op.n_items; u += op.avail) {
         // the epilogue's residual / bias value, fetched while the item computes
         float pre = 0.0f;
         uint64_t prew = 0;
@@ -641,7 +644,7 @@ template <int HD, int G>
 __device__ __forceinline__ void attn_items(const AttnArgs &a, const OpRef &op, ASmem<HD, G> &sm,
                                            int tid, int cta, int grid) {
     const int per_head = op.n_items / a.kv_heads;
-    for (int j = first_item(cta, op.rot, grid); j < op.n_items; j += grid) {
+    for (int j = first_item(cta, op, grid); j < op.n_items; j += op.avail) {
         attn::attn_item<HD, G, kNT, 1>(a, j / per_head, j % per_head, 0, tid, sm);
         csync();
     }
@@ -669,7 +672,7 @@ __device__ __noinline__ void run_sample(const FrameParams &P, FrameSmem &S, int 
 // Next op after `i` that has items on this SM (n_ops if none).
 __device__ __forceinline__ int next_op(const FrameSmem &S, int i, int n_ops, int cta, int grid) {
     for (int k = i + 1; k < n_ops; k++)
-        if (first_item(cta, S.ops[k].rot, grid) < S.ops[k].n_items) return k;
+        if (first_item(cta, S.ops[k], grid) < S.ops[k].n_items) return k;
     return n_ops;
 }
 
@@ -705,7 +708,7 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
     if (i < P.n_ops) stage_issue(P, S, i, b, tid);
     while (i < P.n_ops) {
         const OpRef op = S.ops[i];
-        const int j0 = first_item(cta, op.rot, grid);
+        const int j0 = first_item(cta, op, grid);
         const bool tr = P.trace && j0 == 0 && tid == 0;
         const bool ta = P.trace && tid == 0;  // every SM: across-SM stamps
         stage_wait(P, S, i, b, tid);
@@ -715,7 +718,7 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
         stamp_all(P, i, 3, ta);
         if (op.type == OP_GEMV) {
             const GemvDesc &d = S.desc[b].g;
-            build_input(P, d, S, tid, j0 == 0, j0, op.n_items, grid);
+            build_input(P, d, S, tid, j0 == 0, j0, op.n_items, op.avail);
             stamp_all(P, i, 0, ta);
             stamp_all(P, i, 1, ta);
             gemv_items(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);
@@ -797,14 +800,28 @@ struct Builder {
     int grid;
     int64_t items_total = 0;
 
-    // appends an op; returns its tag (op index + 1, relative to the launch)
-    uint32_t push(int type, int idx, int n_items) {
+    int last_rot = 0, last_used = 0;  // the SM window of the previous op
+
+    // appends an op; returns its tag (op index + 1, relative to the launch).
+    // Items go round the SMs continuing where the previous op's ended; with
+    // avail > 0 they are instead spread over the `avail` SMs right after the
+    // previous op's window (which must then be grid - last_used wide).
+    uint32_t push(int type, int idx, int n_items, int avail = 0) {
         OpRef r;
-        r.type = type;
+        r.type = (int16_t)type;
         r.idx = idx;
         r.n_items = n_items;
-        r.rot = (int)(items_total % grid);
-        items_total += n_items;
+        if (avail > 0) {
+            r.rot = (last_rot + last_used) % grid;
+            r.avail = (int16_t)avail;
+            items_total = (int64_t)r.rot + avail;
+        } else {
+            r.rot = (int)(items_total % grid);
+            r.avail = (int16_t)grid;
+            items_total += n_items;
+        }
+        last_rot = r.rot;
+        last_used = std::min(n_items, (int)r.avail);
         fp->ops.push_back(r);
         return (uint32_t)fp->ops.size();
     }
@@ -818,7 +835,15 @@ struct Builder {
         d.units = (int)(w.C / G);
         d.out_tag = next_tag();
         fp->gemv.push_back(d);
-        return push(OP_GEMV, (int)fp->gemv.size() - 1, d.units);
+        // Small single-group items that would spill onto the SMs still
+        // finishing the previous op (whose inputs then arrive late there) go
+        // two to an SM on the free SMs instead: a second item of K <= 1024 rows
+        // costs less than the late start (the predictor's QKV after its down
+        // projection).
+        const int free_sms = grid - last_used;
+        const bool avoid = G == 1 && d.K <= 1024 && !d.save && !d.save_plain && free_sms > 0 &&
+                           d.units > free_sms && d.units <= 2 * free_sms;
+        return push(OP_GEMV, (int)fp->gemv.size() - 1, d.units, avoid ? free_sms : 0);
     }
     uint32_t attn(AttnArgs a, int per_head) {
         a.out_tag = next_tag();

@@ -86,10 +86,11 @@ struct FrameEmbed {
 };
 
 struct OpRef {
-    int type = OP_GEMV;
+    int16_t type = OP_GEMV;
+    int16_t avail = 0;  // SMs the items are spread over (the window starting at rot)
     int idx = 0;        // into the gemv / attn arrays
     int n_items = 0;
-    int rot = 0;        // item j runs on SM (j + rot) % grid
+    int rot = 0;        // item j runs on SM (j % avail + rot) % grid
 };
 
 struct FrameParams {
