@@ -366,7 +366,15 @@ def run_ours(args):
     frames = B * K * world
     value = frames / (ms / 1000.0)
 
-    # ---- end to end through the public host API (pinned host buffers)
+    # ---- end to end through the public host API (pinned host buffers), on the
+    # same workload: the cache is prefilled again (untimed) so these frames sit
+    # at the same positions as the device-resident ones above
+    x = np.stack([qb.synth_normal(1000 + rank * B + b, 1.0, PREFILL * cfg.t_hidden).reshape(PREFILL, cfg.t_hidden)
+                  for b in range(B)])
+    eng.prefill(x, [1000 + rank * B + b for b in range(B)])
+    for _ in range(W):
+        eng.frame(text, codes)
+    torch.cuda.synchronize()
     text_pin = text.cpu().pin_memory()
     codes_pin = torch.zeros(B, 16, dtype=torch.int32).pin_memory()
     text_h, codes_h = text_pin.numpy(), codes_pin.numpy()
