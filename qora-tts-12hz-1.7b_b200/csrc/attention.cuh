@@ -29,6 +29,9 @@ struct alignas(16) AttnArgs {
     int stable_len = -1;            // cache rows [0, stable_len) were written before this launch
                                     // (may be read before the item's inputs arrive); < 0: all of
                                     // them (a kernel of its own, after griddepcontrol.wait)
+    int stable_writer = -1;         // frame kernel: op index of the attention op that wrote row
+                                    // len - 1 in this launch (-1: none); an SM that has waited on
+                                    // the input of a later op may read rows [0, len) early
     KVLayer kv;
     bool preappended = false;       // q/k already normed+roped and K/V appended
     float *out = nullptr;           // [rows][heads*hd]

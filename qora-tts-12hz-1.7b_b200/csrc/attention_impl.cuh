@@ -108,9 +108,11 @@ struct AttnSmem {
     int last_flag;
 };
 
+// `stable_all`: every cache row before this call's new ones is final (the
+// caller knows it), whatever a.stable_len says.
 template <int HD, int G, int NT, int BAR>
 __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split, int r, int tid,
-                                          AttnSmem<HD, G, NT> &sm) {
+                                          AttnSmem<HD, G, NT> &sm, bool stable_all = false) {
     constexpr int J = HD / 32;
     constexpr int PARTS = (NT / 32) / G;   // warps per head in the score phase
     constexpr int DPART = HD / PARTS;
@@ -162,7 +164,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
         // read only after the inputs: the first tile is then loaded whole after
         // the barrier below.
         const int old0 = max(0, min(min(kTile, p1 - p0), L0 - p0));
-        const int stable = a.stable_len < 0 ? L0 : min(L0, a.stable_len);
+        const int stable = (stable_all || a.stable_len < 0) ? L0 : min(L0, a.stable_len);
         const int pre0 = max(0, min(old0, stable - p0));
         staged0 = (pre0 == old0);
         for (int i = tid; i < pre0 * (HD / 4); i += NT) {

@@ -24,8 +24,8 @@
 // only the sampled code) waits on the previous pass's output explicitly.
 //
 // Weight streaming is decoupled from that chain.  Each SM's share of every
-// GEMV is known in advance (item j of op i runs on SM (j + rot_i) % grid),
-// so a producer warp walks the op list ahead of the compute warps and pulls
+// GEMV is known in advance (item j of op i runs on SM (rot_i + j % avail_i)
+// % grid), so a producer warp walks the op list ahead of the compute warps and pulls
 // the SM's weight slices into a ring of shared-memory slots with
 // cp.async.bulk (no multicast), signalling an mbarrier per slot; the compute
 // warps consume slots in the same order and release them.  Weights are
@@ -642,25 +642,33 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
 
 template <int HD, int G>
 __device__ __forceinline__ void attn_items(const AttnArgs &a, const OpRef &op, ASmem<HD, G> &sm,
-                                           int tid, int cta, int grid) {
+                                           int tid, int cta, int grid, bool stable_all) {
     const int per_head = op.n_items / a.kv_heads;
     for (int j = first_item(cta, op, grid); j < op.n_items; j += op.avail) {
-        attn::attn_item<HD, G, kNT, 1>(a, j / per_head, j % per_head, 0, tid, sm);
+        attn::attn_item<HD, G, kNT, 1>(a, j / per_head, j % per_head, 0, tid, sm, stable_all);
         csync();
     }
 }
 
+// last_gemv: the latest GEMV op whose whole input this SM has waited for.
+// Each op's items wait for the previous op's whole output, so every op before
+// last_gemv is complete; if that includes the writer of the cache's last row
+// (its K/V stores precede its release fence and tagged outputs), all cached
+// rows are final and the item may read them before its own inputs arrive.
+// (This SM reads those rows only once they are final, so its L1 holds no
+// stale copy of them.)
 __device__ __noinline__ void run_attn(const AttnArgs &a, const OpRef &op, FrameSmem &S, int tid, int cta,
-                                     int grid) {
+                                     int grid, int last_gemv) {
+    const bool stable_all = a.stable_writer >= 0 && last_gemv > a.stable_writer;
     const int G = a.heads / a.kv_heads;
     if (a.kv.head_dim == 128) {
-        if (G == 1) attn_items<128, 1>(a, op, S.u.a128_1, tid, cta, grid);
-        else if (G == 2) attn_items<128, 2>(a, op, S.u.a128_2, tid, cta, grid);
-        else attn_items<128, 4>(a, op, S.u.a128_4, tid, cta, grid);
+        if (G == 1) attn_items<128, 1>(a, op, S.u.a128_1, tid, cta, grid, stable_all);
+        else if (G == 2) attn_items<128, 2>(a, op, S.u.a128_2, tid, cta, grid, stable_all);
+        else attn_items<128, 4>(a, op, S.u.a128_4, tid, cta, grid, stable_all);
     } else {
-        if (G == 1) attn_items<64, 1>(a, op, S.u.a64_1, tid, cta, grid);
-        else if (G == 2) attn_items<64, 2>(a, op, S.u.a64_2, tid, cta, grid);
-        else attn_items<64, 4>(a, op, S.u.a64_4, tid, cta, grid);
+        if (G == 1) attn_items<64, 1>(a, op, S.u.a64_1, tid, cta, grid, stable_all);
+        else if (G == 2) attn_items<64, 2>(a, op, S.u.a64_2, tid, cta, grid, stable_all);
+        else attn_items<64, 4>(a, op, S.u.a64_4, tid, cta, grid, stable_all);
     }
 }
 
@@ -703,7 +711,7 @@ __device__ __forceinline__ void stage_wait(const FrameParams &P, FrameSmem &S, i
 
 __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, int grid) {
     uint32_t q = 0;
-    int rbuf = 0, b = 0;
+    int rbuf = 0, b = 0, last_gemv = -1;
     int i = next_op(S, -1, P.n_ops, cta, grid);
     if (i < P.n_ops) stage_issue(P, S, i, b, tid);
     while (i < P.n_ops) {
@@ -719,6 +727,7 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
         if (op.type == OP_GEMV) {
             const GemvDesc &d = S.desc[b].g;
             build_input(P, d, S, tid, j0 == 0, j0, op.n_items, op.avail);
+            last_gemv = i;
             stamp_all(P, i, 0, ta);
             stamp_all(P, i, 1, ta);
             gemv_items(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);
@@ -730,7 +739,7 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
         } else if (op.type == OP_ATTN) {
             stamp_all(P, i, 0, ta);  // (the q/k/v wait is inside the items)
             stamp_all(P, i, 1, ta);
-            run_attn(S.desc[b].a, op, S, tid, cta, grid);
+            run_attn(S.desc[b].a, op, S, tid, cta, grid, last_gemv);
         } else {
             stamp_all(P, i, 0, ta);
             stamp_all(P, i, 1, ta);
@@ -934,6 +943,7 @@ int frame_build(qora_engine *e, FrameProgram **out) {
     // One decoder layer (talker.rs:275-349).  The residual stream enters in xa
     // (sums of squares in ssa) unless `first` supplies the QKV input itself;
     // attention adds into xb (ssb), the MLP back into xa (ssa).
+    int last_attn_op = -1;  // op index of the latest attention op (set by layer())
     auto layer = [&](const LayerDev &ld, int heads, int kvh, int hd, const GemvDesc *first, AttnArgs at,
                      int per_head) {
         const int qkvn = (heads + 2 * kvh) * hd;
@@ -967,6 +977,7 @@ int frame_build(qora_engine *e, FrameProgram **out) {
         at.err = ctx->err.as<int>();
         at.abort_flag = abort_flag;
         const uint32_t tag_attn = B.attn(at, per_head);
+        last_attn_op = (int)tag_attn - 1;
         GemvDesc o;
         o.in = attn_out;
         o.in_tag = tag_attn;
@@ -1004,6 +1015,7 @@ int frame_build(qora_engine *e, FrameProgram **out) {
     pat.rope_sin = p->rope_sin.as<float>();
     pat.rope_max_pos = p->rope_max;
     uint32_t tag_head = 0;
+    std::vector<int> prev_attn_op((size_t)p->L, -1);
     for (int tk = 0; tk <= p->groups; tk++) {
         GemvDesc pr;  // project_input (code_predictor.rs:51-61) into the residual stream
         if (tk == 0) {
@@ -1038,8 +1050,12 @@ int frame_build(qora_engine *e, FrameProgram **out) {
             at.kv = e->pkv->layer(l);
             at.pos_static = tk;
             at.len_static = tk;
-            at.stable_len = 0;  // the predictor cache is refilled within this launch
+            at.stable_len = 0;  // the predictor cache is refilled within this launch:
+            // its rows [0, tk) are final once the previous pass's attention op
+            // of this layer (the writer of row tk - 1) is
+            at.stable_writer = tk >= 1 ? prev_attn_op[(size_t)l] : -1;
             layer(p->layers[l], p->heads, p->kvh, p->hd, nullptr, at, 1);
+            prev_attn_op[(size_t)l] = last_attn_op;
         }
         if (tk >= 1) {
             GemvDesc hd;
