@@ -180,6 +180,55 @@ def cpu_frames(model, frames: int, warmup: int, budget_s: float | None = None):
     return done / dt, done, dt, po.lib().oq_pool_workers()
 
 
+class Ranks:
+    """One process per GPU as torchrun starts them (RANK / LOCAL_RANK /
+    WORLD_SIZE / MASTER_* from the environment): the barrier that brackets the
+    timed region and the max over ranks of a device-timed duration.  Replicas
+    only: no collective touches the data path.  backend "nccl" (device
+    tensors) for the bench; "gloo" (CPU tensors) for the host-side tests."""
+
+    def __init__(self, backend: str = "nccl", device=None, timeout_s: int = 300):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.backend, self.device, self.dist = backend, device, None
+        if self.world > 1:
+            import datetime
+            import torch.distributed as dist
+            kw = {"device_id": device} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=timeout_s), **kw)
+            self.dist = dist
+
+    def barrier(self):
+        if self.dist is not None:
+            self.dist.barrier()
+
+    def max(self, v: float) -> float:
+        """The largest of every rank's v (each rank's own time when alone)."""
+        if self.dist is None:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64,
+                         device=self.device if self.backend == "nccl" else "cpu")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def stream_seed(self, base: int, batch: int, b: int) -> int:
+        """Seed of stream b of this rank: every stream of the job distinct."""
+        return base + self.rank * batch + b
+
+    def close(self):
+        if self.dist is not None:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+            self.dist = None
+
+
+def aggregate_rate(units_per_rank: int, world: int, ms_max: float) -> float:
+    """Whole-job rate: the units every rank processed over the slowest rank's time."""
+    return units_per_rank * world / (ms_max / 1000.0)
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -318,16 +367,10 @@ def run_ours(args):
     import qora_b200 as qb
     from qora_b200 import engine as E
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+    ranks = Ranks("nccl", torch.device("cuda", local))
+    world, rank = ranks.world, ranks.rank
 
     K, W, B = args.steps, max(3, args.warmup), args.batch
     cfg = qb.ModelConfig()
@@ -338,19 +381,13 @@ def run_ours(args):
     pred = E.CodePredictor(ctx, pw, max_batch=maxb)
 
     def barrier():
-        if dist is not None:
-            dist.barrier()
+        ranks.barrier()
         torch.cuda.synchronize()
 
-    def max_over_ranks(v):
-        if dist is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    max_over_ranks = ranks.max
 
     # ---- device-resident frame loop (value)
-    eng, text, codes = engine_rate(E, talker, pred, torch, qb, B, K, W, 1000 + rank * B, True)
+    eng, text, codes = engine_rate(E, talker, pred, torch, qb, B, K, W, ranks.stream_seed(1000, B, 0), True)
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
@@ -364,14 +401,14 @@ def run_ours(args):
     kernels = eng.kernels_per_frame()
     ctx.check_device_error()
     frames = B * K * world
-    value = frames / (ms / 1000.0)
+    value = aggregate_rate(B * K, world, ms)
 
     # ---- end to end through the public host API (pinned host buffers), on the
     # same workload: the cache is prefilled again (untimed) so these frames sit
     # at the same positions as the device-resident ones above
-    x = np.stack([qb.synth_normal(1000 + rank * B + b, 1.0, PREFILL * cfg.t_hidden).reshape(PREFILL, cfg.t_hidden)
+    x = np.stack([qb.synth_normal(ranks.stream_seed(1000, B, b), 1.0, PREFILL * cfg.t_hidden).reshape(PREFILL, cfg.t_hidden)
                   for b in range(B)])
-    eng.prefill(x, [1000 + rank * B + b for b in range(B)])
+    eng.prefill(x, [ranks.stream_seed(1000, B, b) for b in range(B)])
     for _ in range(W):
         eng.frame(text, codes)
     torch.cuda.synchronize()
@@ -395,7 +432,7 @@ def run_ours(args):
     if not args.no_batch32:
         K32 = max(10, min(K, 60))
         eng32, text32, codes32 = engine_rate(E, talker, pred, torch, qb, 32, K32, W,
-                                             50000 + rank * 32)
+                                             ranks.stream_seed(50000, 32, 0))
         barrier()
         e0.record(st)
         for _ in range(K32):
@@ -409,9 +446,7 @@ def run_ours(args):
         torch.cuda.synchronize()
 
     if rank != 0:
-        if dist is not None:
-            dist.barrier()
-            dist.destroy_process_group()
+        ranks.close()
         return
 
     # ---- roofline of the dominant kernel: at batch 1 the whole frame is one
@@ -491,9 +526,7 @@ def run_ours(args):
         "gemv_sweep": sweep,
     }
     print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    ranks.close()
 
 
 def profile_case_gemv():
