@@ -314,6 +314,16 @@ void qora_engine_destroy(qora_engine *e);
  * stream), set RNG seeds (seeds_host [B]) and clear the previous-code window. */
 int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const uint64_t *seeds_host,
                         void *stream);
+/* The prefix-cache path of generate_speech (generate_new.rs:509-530): every
+ * stream's cache becomes a copy of stream `prefix_stream` of `prefix` (a
+ * talker cache holding exactly prefix_len positions, e.g. the role prefix,
+ * codec header and ICL reference part prefilled once per run), then
+ * x_host [B][T][hidden] (the text-dependent suffix) is prefilled on top at
+ * positions prefix_len.., as prefill_talker_raw_from does.  A prefix of
+ * another length is QORA_ERR_SHAPE (the reference then prefills in full). */
+int qora_engine_prefill_from(qora_engine *e, const qora_kv *prefix, int32_t prefix_stream,
+                             int32_t prefix_len, const float *x_host, int32_t T,
+                             const uint64_t *seeds_host, void *stream);
 /* Run one frame (device buffers): text [B][hidden] -> codes [B][16]. */
 int qora_engine_frame(qora_engine *e, const float *text, uint32_t *codes, void *stream);
 /* Run one frame from HOST buffers: text_host [B][hidden] in, codes_host [B][16]

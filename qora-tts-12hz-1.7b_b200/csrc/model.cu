@@ -764,14 +764,14 @@ void qora_engine_destroy(qora_engine *e) {
     delete e;
 }
 
-int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const uint64_t *seeds_host,
-                        void *stream) {
-    if (!e || !x_host || !seeds_host || T <= 0 || T >= e->max_pos)
-        return set_error(QORA_ERR_INVALID, "qora_engine_prefill: bad arguments");
+namespace {
+// Prefills T rows per stream on top of each stream's cache (which holds
+// `start` positions), then sets up the first frame: logits, positions, rng.
+int engine_prefill_rows(qora_engine *e, const float *x_host, int32_t T, const uint64_t *seeds_host,
+                        int32_t start, void *stream) {
     qora_talker *t = e->t;
     qora_predictor *p = e->p;
     cudaStream_t st = as_stream(stream);
-    QORA_TRY(qora_kv_reset(e->tkv, nullptr, 0, stream));
     DevBuf xd;
     QORA_TRY(xd.alloc((size_t)e->B * T * t->H * 4));
     QORA_CUDA(cudaMemcpyAsync(xd.p, x_host, xd.bytes, cudaMemcpyHostToDevice, st));
@@ -788,7 +788,7 @@ int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const ui
         } else {
             for (int i = 0; i < ns; i++)
                 QORA_TRY(qora_talker_prefill(t, e->tkv, s0 + i, xd.as<float>() + (int64_t)(s0 + i) * T * t->H,
-                                             T, 0, p->x2.as<float>() + (int64_t)(s0 + i) * 2 * p->Ht, stream));
+                                             T, start, p->x2.as<float>() + (int64_t)(s0 + i) * 2 * p->Ht, stream));
         }
     }
     // first logits (generate_new.rs:473)
@@ -804,11 +804,41 @@ int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const ui
         QORA_TRY(ln.gemv(a, X_PLAIN, E_STORE));
     }
     QORA_TRY(launch_ex(k_fill_i32, dim3((e->B + 255) / 256), dim3(256), 0, st, 1u, e->pos.as<int>(),
-                       e->B, T));
+                       e->B, start + T));
     QORA_CUDA(cudaMemcpyAsync(e->rng.p, seeds_host, (size_t)e->B * 8, cudaMemcpyHostToDevice, st));
     QORA_CUDA(cudaMemsetAsync(e->prev.p, 0, e->prev.bytes, st));
     QORA_CUDA(cudaStreamSynchronize(st));
     return QORA_OK;
+}
+
+}  // namespace
+
+int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const uint64_t *seeds_host,
+                        void *stream) {
+    if (!e || !x_host || !seeds_host || T <= 0 || T >= e->max_pos)
+        return set_error(QORA_ERR_INVALID, "qora_engine_prefill: bad arguments");
+    QORA_TRY(qora_kv_reset(e->tkv, nullptr, 0, stream));
+    return engine_prefill_rows(e, x_host, T, seeds_host, 0, stream);
+}
+
+int qora_engine_prefill_from(qora_engine *e, const qora_kv *prefix, int32_t prefix_stream,
+                             int32_t prefix_len, const float *x_host, int32_t T,
+                             const uint64_t *seeds_host, void *stream) {
+    if (!e || !prefix || !x_host || !seeds_host || T <= 0 || prefix_len < 0 ||
+        prefix_len + T >= e->max_pos || prefix_stream < 0 || prefix_stream >= prefix->streams)
+        return set_error(QORA_ERR_INVALID, "qora_engine_prefill_from: bad arguments");
+    if (prefix->layers != e->t->L || prefix->kvh != e->t->kvh || prefix->hd != e->t->hd ||
+        prefix->max_pos > e->max_pos)
+        return set_error(QORA_ERR_SHAPE, "qora_engine_prefill_from: the prefix cache does not fit the engine");
+    cudaStream_t st = as_stream(stream);
+    int32_t have = -1;
+    QORA_CUDA(cudaMemcpyAsync(&have, prefix->lens() + prefix_stream, 4, cudaMemcpyDeviceToHost, st));
+    QORA_CUDA(cudaStreamSynchronize(st));
+    if (have != prefix_len)  // the reference falls back to a full prefill here (generate_new.rs:307-316)
+        return set_error(QORA_ERR_SHAPE, "qora_engine_prefill_from: prefix holds %d positions, not %d",
+                         have, prefix_len);
+    for (int b = 0; b < e->B; b++) QORA_TRY(qora_kv_copy_stream(e->tkv, b, prefix, prefix_stream, stream));
+    return engine_prefill_rows(e, x_host, T, seeds_host, prefix_len, stream);
 }
 
 namespace {

@@ -119,6 +119,7 @@ SIGNATURES = {
     "qora_engine_create": (C.c_int, [_vp, _vp, _i32, _i32, _vp, _PP]),
     "qora_engine_destroy": (None, [_vp]),
     "qora_engine_prefill": (C.c_int, [_vp, _vp, _i32, _vp, _vp]),
+    "qora_engine_prefill_from": (C.c_int, [_vp, _vp, _i32, _i32, _vp, _i32, _vp, _vp]),
     "qora_engine_frame": (C.c_int, [_vp, _vp, _vp, _vp]),
     "qora_engine_frame_host": (C.c_int, [_vp, _vp, _vp, _vp]),
     "qora_engine_use_graph": (C.c_int, [_vp, _i32]),

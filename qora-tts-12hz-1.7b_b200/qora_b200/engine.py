@@ -367,6 +367,17 @@ class Engine:
         s = np.ascontiguousarray(np.asarray(seeds, np.uint64).reshape(self.B))
         _lib.call("qora_engine_prefill", self.h, x.ctypes.data, T, s.ctypes.data, _stream(stream))
 
+    def prefill_from(self, prefix: KvCache, prefix_len: int, x: np.ndarray, seeds,
+                     prefix_stream: int = 0, stream=None):
+        """The prefix-cache path (generate_new.rs:509-530): every stream starts
+        from a copy of `prefix` (holding prefix_len positions) and prefills the
+        suffix x [B][T][hidden] on top."""
+        x = np.ascontiguousarray(x, np.float32)
+        T = x.shape[1]
+        s = np.ascontiguousarray(np.asarray(seeds, np.uint64).reshape(self.B))
+        _lib.call("qora_engine_prefill_from", self.h, prefix.h, prefix_stream, prefix_len,
+                  x.ctypes.data, T, s.ctypes.data, _stream(stream))
+
     def use_persistent(self, enable: bool = True):
         """One persistent-kernel launch per frame (default where supported) or
         the per-op kernel sequence."""

@@ -370,3 +370,43 @@ def test_embed_rows_out_of_table_is_flagged(E, ctx, tiny):
     o = out.cpu().numpy()
     assert np.all(o[1] == 0.0) and np.any(o[0] != 0.0) and np.any(o[2] != 0.0)
     ctx.check_device_error()   # the flag was cleared
+
+
+@pytest.mark.parametrize("B", [1, 2])
+def test_engine_prefill_from_prefix(E, orc, tiny, B):
+    """The prefix-cache path (generate_new.rs:509-530): a prefix prefilled once,
+    copied into every stream, the suffix prefilled on top; frames equal the
+    oracle's on the same prefix + suffix (whose prefill-from-prefix equals a
+    full prefill bit for bit, tests/test_oracle_model.py)."""
+    import torch
+    from qora_b200 import _lib
+    cfg, om, talker, pred = tiny
+    P0, T, F = 5, 4, 3
+    xp = orc.synth_normal(970, 1.0, P0 * cfg.t_hidden).reshape(P0, cfg.t_hidden)
+    xs = orc.synth_normal(971, 1.0, B * T * cfg.t_hidden).reshape(B, T, cfg.t_hidden)
+    prefix = talker.new_kv(max_pos=32)
+    talker.prefill_talker_raw_from(_cuda(xp), prefix, 0)
+    eng = E.Engine(talker, pred, B, max_pos=32)
+    seeds = [40 + b for b in range(B)]
+    eng.prefill_from(prefix, P0, xs, seeds)
+    text = orc.synth_normal(972, 1.0, B * cfg.t_hidden).reshape(B, cfg.t_hidden)
+    states, kvs = [], []
+    for b in range(B):
+        tkv, pkv = om.talker_kv(32), om.predictor_kv()
+        om.talker_prefill(xp, tkv, 0)
+        hdn = om.talker_prefill(xs[b], tkv, P0)
+        states.append({"logits": om.codec_head(hdn), "hidden": hdn.copy(),
+                       "prev": np.zeros(16, np.uint32), "rng": seeds[b]})
+        kvs.append((tkv, pkv))
+    tt = _cuda(text)
+    codes = torch.zeros(B, 16, dtype=torch.int32).cuda()
+    params = orc.SampleParams(0.9, 50, 1.0, 1.05)
+    for f in range(F):
+        eng.frame(tt, codes)
+        got = codes.cpu().numpy()
+        for b in range(B):
+            ref = om.frame(kvs[b][0], kvs[b][1], params, text[b], P0 + T + f, states[b])
+            assert list(got[b]) == list(ref), (f, b)
+    with pytest.raises(_lib.QoraError) as ei:
+        eng.prefill_from(prefix, P0 + 1, xs, seeds)     # the cache holds P0 positions
+    assert ei.value.status == 2
