@@ -108,10 +108,22 @@ struct Launcher {
     qora_ctx *ctx;
     Work *w;
     cudaStream_t st;
-    int count = 0;  // kernels launched
+    int count = 0;      // kernels launched
+    bool fixed = false; // prefill: a row's rounding must not depend on the rows of its launch
 
     int gemv(GemvArgs a, int xm, int em) {
-        const GemvPlan p = plan_gemv_for(a, xm, em, ctx->num_sms);
+        GemvPlan p;
+        if (fixed && gemv_mma_supported(a, xm, em)) {
+            // the tensor-core kernel with the K split planned for a full
+            // kMaxRows chunk, whatever this launch's row count: the same split
+            // (hence the same bits) for a row in any chunk, as the reference's
+            // prefix cache needs (generate_new.rs:320-322)
+            p = plan_gemv_mma(a.w.k, a.w.C, kMaxRows, em, ctx->num_sms);
+            p.Z = (a.rows + p.rows_per_z - 1) / p.rows_per_z;
+            p.grid.z = (unsigned)p.Z;
+        } else {
+            p = plan_gemv_for(a, xm, em, ctx->num_sms);
+        }
         if (!a.err) a.err = ctx->err.as<int>();
         count++;
         return launch_gemv(a, xm, em, p, w->gticket.as<unsigned>(), st);
@@ -547,6 +559,7 @@ namespace {
 int talker_prefill_rows(qora_talker *t, qora_kv *kv, int s0, int ns, int T, const float *x,
                         cudaStream_t st) {
     Launcher ln{t->ctx, &t->w, st};
+    ln.fixed = true;
     const int rows = ns * T;
     QORA_TRY(launch_copy_rowstats(x, t->H, t->w.x.as<float>(), t->H, rows, t->H,
                                   t->w.ss.as<float>(), t->H / kGroup, st));

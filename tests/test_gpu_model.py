@@ -389,6 +389,15 @@ def test_engine_prefill_from_prefix(E, orc, tiny, B):
     eng = E.Engine(talker, pred, B, max_pos=32)
     seeds = [40 + b for b in range(B)]
     eng.prefill_from(prefix, P0, xs, seeds)
+    # bit-identical to prefilling prefix + suffix in one go (prefill chunks
+    # plan their GEMMs independently of their row count), as the reference's
+    # prefix cache is (generate_new.rs:320-322)
+    full = E.Engine(talker, pred, B, max_pos=32)
+    full.prefill(np.concatenate([np.broadcast_to(xp, (B, P0, cfg.t_hidden)), xs], axis=1), seeds)
+    a, b_ = eng.state(), full.state()
+    assert np.array_equal(a["hidden"].cpu().numpy(), b_["hidden"].cpu().numpy())
+    assert np.array_equal(a["logits"].cpu().numpy(), b_["logits"].cpu().numpy())
+    assert np.array_equal(a["positions"].cpu().numpy(), b_["positions"].cpu().numpy())
     text = orc.synth_normal(972, 1.0, B * cfg.t_hidden).reshape(B, cfg.t_hidden)
     states, kvs = [], []
     for b in range(B):
