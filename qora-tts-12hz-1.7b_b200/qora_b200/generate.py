@@ -175,6 +175,26 @@ def build_trailing_text(text_tokens) -> list:
     return [Row(int(t)) for t in list(text_tokens)[1:]] + [Row(TTS_EOS)]
 
 
+def encode_rows(rows):
+    """The recipes as qora_prompt_row structs (include/qora_cuda.h): returns
+    (the distinct text tokens in ascending order, whose projected rows the
+    structs index, and the struct array)."""
+    toks = sorted({r.text for r in rows if r.text is not None})
+    index = {t: i for i, t in enumerate(toks)}
+    recs = (_lib.PromptRow * max(1, len(rows)))()
+    for i, r in enumerate(rows):
+        if len(r.codes) > 16 or (r.voice and r.codes):
+            raise ValueError(f"row {i}: at most 16 codes, and none with the voice embedding")
+        recs[i].text = -1 if r.text is None else index[r.text]
+        if r.voice:
+            recs[i].codes_n = -1
+        else:
+            recs[i].codes_n = len(r.codes)
+            for g, c in enumerate(r.codes):
+                recs[i].codes[g] = int(c)
+    return toks, recs
+
+
 class PromptAssembler:
     """Builds recipe rows on the device: `text_proj` an engine.TextProjection,
     `talker` an engine.Talker, `predictor` an engine.CodePredictor (needed for
@@ -197,19 +217,9 @@ class PromptAssembler:
         voice=True."""
         import torch
         from .engine import _dp, _stream
-        toks = sorted({r.text for r in rows if r.text is not None})
-        index = {t: i for i, t in enumerate(toks)}
+        toks, recs = encode_rows(rows)
         dev = f"cuda:{self.talker.ctx.device}"
         text = self.text_rows(toks, stream=stream) if toks else None
-        recs = (_lib.PromptRow * max(1, len(rows)))()
-        for i, r in enumerate(rows):
-            recs[i].text = -1 if r.text is None else index[r.text]
-            if r.voice:
-                recs[i].codes_n = -1
-            else:
-                recs[i].codes_n = len(r.codes)
-                for g, c in enumerate(r.codes):
-                    recs[i].codes[g] = int(c)
         out = torch.empty(len(rows), self.hidden, device=dev)
         vlen = 0
         if voice is not None:

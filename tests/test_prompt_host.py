@@ -167,3 +167,24 @@ def test_bad_reference_codes_are_errors():
     ragged[4] = ragged[4][:2]
     with pytest.raises(ValueError):
         G.build_icl_prefix([1, 2], ragged)
+
+
+def test_recipes_encode_as_prompt_rows():
+    """encode_rows: the qora_prompt_row structs the device assembly reads
+    (text index into the sorted distinct tokens, -1 none; codes_n 1 / 16 /
+    0, -1 for the voice row)."""
+    codes = _codes(2, 7)
+    rows = G.build_codec_prefix_voice(2050) + G.build_icl_prefix([9, 5], codes) + [G.Row()]
+    toks, recs = G.encode_rows(rows)
+    assert toks == sorted({G.TTS_PAD, G.TTS_BOS, 9, 5})
+    got = [(recs[i].text, recs[i].codes_n, list(recs[i].codes)[:max(recs[i].codes_n, 0)])
+           for i in range(len(rows))]
+    ix = {t: i for i, t in enumerate(toks)}
+    assert got[0] == (ix[G.TTS_PAD], 1, [G.CODEC_THINK])
+    assert got[4] == (ix[G.TTS_PAD], -1, [])                  # the voice row
+    assert got[5] == (ix[G.TTS_BOS], 1, [G.CODEC_PAD])
+    assert got[6] == (ix[9], 1, [G.CODEC_BOS])                # ICL prefix row 0
+    assert got[7] == (ix[5], 16, [int(codes[g][0]) for g in range(16)])
+    assert got[8] == (-1, 0, [])
+    with pytest.raises(ValueError):
+        G.encode_rows([G.Row(1, tuple(range(17)))])
