@@ -68,3 +68,25 @@ def test_reference_arm_runs_on_rank_zero_only():
                        env=env, capture_output=True, text=True, timeout=120)
     assert p.returncode == 0, p.stderr
     assert p.stdout.strip() == ""
+
+
+def test_algorithmic_bytes_model_matches_the_published_figures():
+    """The roofline's per-unit figures (1.7B dims): talker step weights
+    796,262,400 B (28 x 50,331,648 + 6,291,456 codec-head weights at
+    0.5625 B), predictor weight passes 698,941,440 B (15 passes, head_dim
+    128), 229,376 B of K/V per cached position."""
+    sys.path.insert(0, ROOT)
+    import bench
+    import qora_b200
+    cfg = qora_b200.ModelConfig()
+    q4 = 0.5625
+    talker_w = 28 * 50_331_648 + 6_291_456
+    assert q4 * talker_w == 796_262_400
+    kv_pos = cfg.t_layers * 2 * cfg.t_kv_heads * cfg.t_head_dim * 4
+    assert kv_pos == 229_376
+    norms = 2 * (cfg.t_layers * (2 * cfg.t_hidden + 2 * cfg.t_head_dim) + cfg.t_hidden)
+    for P in (0, 64, 300):
+        total = bench.frame_algorithmic_bytes(cfg, P)
+        pred = total - (796_262_400 + norms + kv_pos * (P + 1) + kv_pos + 1152)
+        assert pred == 698_941_440, (P, pred)
+    assert bench.aggregate_rate(400, 8, 1000.0) == 3200.0
