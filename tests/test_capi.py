@@ -46,6 +46,15 @@ def test_binding_covers_header(lib):
     assert sorted(qora_b200._lib.SIGNATURES) == names
 
 
+def test_documented_rust_binding_covers_header():
+    """The extern "C" block a Rust caller would add declares
+    exactly the header's functions."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    doc = open(os.path.join(root, "INTEGRATION.md")).read()
+    block = doc[doc.index('extern "C" {'):doc.index("/// Turns a status")]
+    assert sorted(set(re.findall(r"pub fn (qora_\w+)", block))) == header_functions()
+
+
 def test_status_strings(lib):
     assert lib.qora_status_string(0) == b"ok"
     assert lib.qora_status_string(2) == b"shape mismatch"
