@@ -119,6 +119,9 @@ typedef struct qora_sample_params {
 
 /* ---------------------------------------------------------------- context */
 int qora_ctx_create(int32_t device, qora_ctx **out);
+/* Releases the caller's reference.  Objects created from the context hold
+ * references of their own, so the context stays valid until the last of them
+ * is destroyed as well. */
 void qora_ctx_destroy(qora_ctx *ctx);
 const char *qora_status_string(int32_t status);
 const char *qora_last_error(void);
@@ -324,14 +327,21 @@ int qora_engine_prefill(qora_engine *e, const float *x_host, int32_t T, const ui
 int qora_engine_prefill_from(qora_engine *e, const qora_kv *prefix, int32_t prefix_stream,
                              int32_t prefix_len, const float *x_host, int32_t T,
                              const uint64_t *seeds_host, void *stream);
-/* Run one frame (device buffers): text [B][hidden] -> codes [B][16]. */
+/* Run one frame (device buffers): text [B][hidden] -> codes [B][16].
+ * On the persistent frame kernel (the default at B = 1) each launch carries
+ * its own synchronisation tags, so the call must not be captured into a CUDA
+ * graph by the caller: under stream capture it returns QORA_ERR_UNSUPPORTED.
+ * The per-op path (qora_engine_use_persistent(e, 0), or B > 1) may be
+ * captured, and qora_engine_use_graph captures it internally. */
 int qora_engine_frame(qora_engine *e, const float *text, uint32_t *codes, void *stream);
 /* Run one frame from HOST buffers: text_host [B][hidden] in, codes_host [B][16]
  * out; both copies are issued on `stream` and the call returns after the
  * codes have landed. */
 int qora_engine_frame_host(qora_engine *e, const float *text_host, uint32_t *codes_host,
                            void *stream);
-/* Capture one frame into a CUDA graph (enable=1) and replay it per frame. */
+/* Capture one frame of the per-op path into a CUDA graph (enable=1) and
+ * replay it per frame (no effect while the persistent frame kernel runs the
+ * frames: that path is one launch per frame already). */
 int qora_engine_use_graph(qora_engine *e, int32_t enable);
 /* Run each frame as ONE launch of the persistent frame kernel (enable = 1, the
  * default where supported) or as the sequence of per-op kernels (enable = 0).

@@ -196,7 +196,7 @@ int qora_ctx_create(int32_t device, qora_ctx **out) {
     return QORA_OK;
 }
 
-void qora_ctx_destroy(qora_ctx *ctx) { delete ctx; }
+void qora_ctx_destroy(qora_ctx *ctx) { qora::CtxRef::drop(ctx); }
 
 int qora_ctx_check_device_error(qora_ctx *ctx, void *stream) {
     if (!ctx) return set_error(QORA_ERR_INVALID, "null ctx");

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -41,6 +42,29 @@ int set_error(int code, const char *fmt, ...);
 #define QORA_LAUNCH_CHECK() QORA_CUDA(cudaGetLastError())
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Makes a device current for the guard's lifetime and gives the caller's
+// current device back afterwards (entry points that launch on an object's
+// device whatever device the calling thread has current).
+class DeviceGuard {
+    int prev_ = -1;
+
+  public:
+    DeviceGuard() = default;
+    DeviceGuard(const DeviceGuard &) = delete;
+    DeviceGuard &operator=(const DeviceGuard &) = delete;
+    int set(int device) {
+        int cur = 0;
+        QORA_CUDA(cudaGetDevice(&cur));
+        if (cur == device) return QORA_OK;
+        QORA_CUDA(cudaSetDevice(device));
+        prev_ = cur;
+        return QORA_OK;
+    }
+    ~DeviceGuard() {
+        if (prev_ >= 0) cudaSetDevice(prev_);
+    }
+};
 
 // Device error flag codes (written by kernels, read by the host).
 enum DeviceError : int {
@@ -351,14 +375,46 @@ struct EmbDev {
 
 }  // namespace qora
 
+// A context is reference counted: the caller's handle (released by
+// qora_ctx_destroy) and every object created from it (weights, caches,
+// models, text projections) each hold one reference, so destroying the
+// context before its objects leaves it alive until the last one is gone.
 struct qora_ctx {
     int device = 0;
     int num_sms = 148;
     qora::DevBuf err;       // device error flag
+    std::atomic<int> refs{1};
 };
 
+namespace qora {
+// An object's reference to its context (retained on assignment, released
+// when the object is destroyed; the last release frees the context).
+class CtxRef {
+    qora_ctx *c_ = nullptr;
+    static void release(qora_ctx *c) {
+        if (c && c->refs.fetch_sub(1) == 1) delete c;
+    }
+
+  public:
+    CtxRef() = default;
+    CtxRef(const CtxRef &) = delete;
+    CtxRef &operator=(const CtxRef &) = delete;
+    ~CtxRef() { release(c_); }
+    CtxRef &operator=(qora_ctx *c) {
+        if (c) c->refs.fetch_add(1);
+        release(c_);
+        c_ = c;
+        return *this;
+    }
+    operator qora_ctx *() const { return c_; }
+    qora_ctx *operator->() const { return c_; }
+    // Drops the caller's own reference (qora_ctx_destroy).
+    static void drop(qora_ctx *c) { release(c); }
+};
+}  // namespace qora
+
 struct qora_w4 {
-    qora_ctx *ctx = nullptr;
+    qora::CtxRef ctx;
     qora::DevBuf nib, scl, rowmajor_packed, rowmajor_scl;
     qora::Q4Dev dev;
     qora::EmbDev emb;  // valid after qora_q4_embed_rows first use (lazy)

@@ -644,6 +644,11 @@ template <int HD, int G>
 __device__ __forceinline__ void attn_items(const AttnArgs &a, const OpRef &op, ASmem<HD, G> &sm,
                                            int tid, int cta, int grid, bool stable_all) {
     const int per_head = op.n_items / a.kv_heads;
+    // Early reads of rows written in this launch: the SM learned that their
+    // writer is complete through relaxed polls only, so an acquire fence
+    // (which also drops any L1 line of the cache, read with cp.async.ca)
+    // comes before the first of those reads.
+    if (stable_all && first_item(cta, op, grid) < op.n_items) fence_acq_rel_gpu();
     for (int j = first_item(cta, op, grid); j < op.n_items; j += op.avail) {
         attn::attn_item<HD, G, kNT, 1>(a, j / per_head, j % per_head, 0, tid, sm, stable_all);
         csync();
@@ -1162,9 +1167,24 @@ int frame_launch(FrameProgram *fp, const float *text, cudaStream_t st) {
     FrameParams P = fp->params;
     P.text = text;
     P.trace = fp->trace ? fp->d_trace.as<unsigned long long>() : nullptr;
-    // tags unique to this launch (a stale word from an earlier launch never matches)
+    // Each launch bakes its tags into its parameters, so a captured launch
+    // replayed from a graph would accept the previous replay's words as its
+    // own: capture is refused (the per-op path is the one to capture).
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    QORA_CUDA(cudaStreamIsCapturing(st, &cs));
+    if (cs != cudaStreamCaptureStatusNone)
+        return set_error(QORA_ERR_UNSUPPORTED,
+                         "the persistent frame kernel cannot be captured in a CUDA graph "
+                         "(qora_engine_use_persistent(e, 0) selects the capturable per-op path)");
+    // tags unique to this launch (a stale word from an earlier launch never
+    // matches).  tag_base = epoch * kTagStride stays below 2^32; before the
+    // epochs start over, every tagged word is cleared back to tag 0, which no
+    // launch uses, so a word left over from an earlier cycle cannot match.
     fp->epoch++;
-    if ((uint32_t)(fp->epoch * kTagStride) == 0) fp->epoch++;
+    if ((uint64_t)fp->epoch * kTagStride >= (1ull << 32)) {
+        QORA_CUDA(cudaMemsetAsync(fp->bufs.p, 0, fp->bufs.bytes, st));
+        fp->epoch = 1;
+    }
     P.tag_base = fp->epoch * kTagStride;
     QORA_CUDA(cudaMemsetAsync(fp->d_abort.p, 0, 4, st));
     if (fp->trace) QORA_CUDA(cudaMemsetAsync(fp->d_trace.p, 0, fp->d_trace.bytes, st));

@@ -5,7 +5,7 @@
 #include "attention.cuh"
 
 struct qora_kv {
-    qora_ctx *ctx = nullptr;
+    qora::CtxRef ctx;
     int layers = 0, kvh = 0, hd = 0, max_pos = 0, streams = 0;
     qora::DevBuf k, v, len;
     // split-merge scratch of qora_kv_attend, sized on its first call

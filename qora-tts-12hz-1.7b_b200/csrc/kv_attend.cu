@@ -66,8 +66,9 @@ extern "C" int qora_kv_attend(qora_kv *kv, int32_t layer, const float *qkv, int3
     AttnArgs at;
     QORA_TRY(kv_attend_args(kv, layer, qkv, num_heads, q_norm, k_norm, rope_cos, rope_sin,
                             rope_max_pos, positions, B, out, at));
+    DeviceGuard dg;  // the cache's device, whatever the calling thread has current
+    QORA_TRY(dg.set(kv->ctx->device));
     if (!kv->attn_po.p || kv->attn_heads != num_heads) {  // first call on this cache: size scratch
-        QORA_CUDA(cudaSetDevice(kv->ctx->device));
         QORA_TRY(kv->attn_po.alloc(attn_part_o_floats(kv->streams, kv->kvh, num_heads, kv->hd) * 4));
         QORA_TRY(kv->attn_pml.alloc(attn_part_ml_floats(kv->streams, kv->kvh, num_heads) * 4));
         QORA_TRY(kv->attn_tk.alloc((size_t)kv->streams * kv->kvh * 4));

@@ -83,6 +83,10 @@ extern "C" int qora_kv_attend_noalloc(qora_kv *kv, int32_t layer, const float *q
                          "floats and %zu counters of scratch; the static array holds %zu + %zu "
                          "and %zu (B * heads * head_dim <= 16384)",
                          B, num_heads, kv->hd, po, pml, tk, kNaPartO, kNaPartML, kNaTickets);
+    // the cache's device is current for the look-up, the clear and the launch,
+    // whatever device the calling thread had current (restored on return)
+    DeviceGuard dg;
+    QORA_TRY(dg.set(kv->ctx->device));
     float *base = nullptr;
     QORA_TRY(scratch_address(kv->ctx->device, &base));
     at.part_o = base;

@@ -49,6 +49,31 @@ __global__ void k_fill_i32(int *p, int count, int v) {
     if (i < count) p[i] = v;
 }
 
+// Prefix snapshot / restore (generate_new.rs:317-355): rows [0, len) of one
+// source stream, every (layer, kv head), into `ndst` destination streams
+// dst0.., and their lengths.  Only the source's live rows move; the source
+// length is read on the device, so the copy needs no host round trip.
+// grid (layers * kvh, ndst, row chunks); K and V rows are head_dim floats.
+__global__ void k_kv_copy_rows(const float *sk, const float *sv, size_t s_layer, size_t s_base,
+                               int s_max_pos, float *dk, float *dv, size_t d_layer, int d_max_pos,
+                               int dst0, int kvh, int hd, const int *src_len, int *dst_len) {
+    griddep_launch_dependents();
+    griddep_wait();
+    const int l = blockIdx.x / kvh, h = blockIdx.x % kvh;
+    const int ds = dst0 + blockIdx.y;
+    const int len = min(__ldcg(src_len), min(s_max_pos, d_max_pos));
+    const size_t so = l * s_layer + s_base + (size_t)h * s_max_pos * hd;
+    const size_t dof = l * d_layer + ((size_t)ds * kvh + h) * d_max_pos * hd;
+    const int n4 = len * hd / 4;  // head_dim is a multiple of 4
+    const float4 *k4 = reinterpret_cast<const float4 *>(sk + so), *v4 = reinterpret_cast<const float4 *>(sv + so);
+    float4 *dk4 = reinterpret_cast<float4 *>(dk + dof), *dv4 = reinterpret_cast<float4 *>(dv + dof);
+    for (int i = blockIdx.z * blockDim.x + threadIdx.x; i < n4; i += gridDim.z * blockDim.x) {
+        dk4[i] = __ldcg(k4 + i);
+        dv4[i] = __ldcg(v4 + i);
+    }
+    if (blockIdx.x == 0 && blockIdx.z == 0 && threadIdx.x == 0) dst_len[ds] = __ldcg(src_len);
+}
+
 int upload_f16(const uint16_t *h, int64_t n, DevBuf &buf) {
     if (!h) return set_error(QORA_ERR_INVALID, "null norm vector");
     QORA_TRY(buf.alloc((size_t)n * 2));
@@ -416,25 +441,26 @@ int qora_kv_lengths_host(qora_kv *kv, int32_t *len_host, void *stream) {
     return QORA_OK;
 }
 
-int qora_kv_copy_stream(qora_kv *dst, int32_t ds, const qora_kv *src, int32_t ss, void *stream) {
+namespace qora {
+// Copies stream `ss` of `src` into streams [ds, ds + n) of `dst` (live rows only).
+int kv_copy_streams(qora_kv *dst, int32_t ds, int32_t n, const qora_kv *src, int32_t ss,
+                    cudaStream_t st) {
     if (!dst || !src || dst->layers != src->layers || dst->kvh != src->kvh || dst->hd != src->hd ||
-        dst->max_pos < src->max_pos || ds < 0 || ds >= dst->streams || ss < 0 || ss >= src->streams)
+        dst->max_pos < src->max_pos || ds < 0 || n <= 0 || ds + n > dst->streams || ss < 0 ||
+        ss >= src->streams)
         return set_error(QORA_ERR_INVALID, "qora_kv_copy_stream: incompatible caches");
-    cudaStream_t st = as_stream(stream);
-    const size_t row = (size_t)src->hd * 4;
-    for (int l = 0; l < src->layers; l++) {
-        KVLayer a = dst->layer(l, ds), b = src->layer(l, ss);
-        for (int h = 0; h < src->kvh; h++) {
-            QORA_CUDA(cudaMemcpyAsync(a.k + (size_t)h * dst->max_pos * dst->hd,
-                                      b.k + (size_t)h * src->max_pos * src->hd,
-                                      row * src->max_pos, cudaMemcpyDeviceToDevice, st));
-            QORA_CUDA(cudaMemcpyAsync(a.v + (size_t)h * dst->max_pos * dst->hd,
-                                      b.v + (size_t)h * src->max_pos * src->hd,
-                                      row * src->max_pos, cudaMemcpyDeviceToDevice, st));
-        }
-    }
-    QORA_CUDA(cudaMemcpyAsync(dst->lens() + ds, src->lens() + ss, 4, cudaMemcpyDeviceToDevice, st));
-    return QORA_OK;
+    const size_t s_base = (size_t)ss * src->kvh * src->max_pos * src->hd;
+    // row chunks: enough CTAs to keep HBM busy for a long prefix
+    const int chunks = std::max(1, std::min(64, src->max_pos * src->hd / 4 / 256 / 4));
+    return launch_ex(k_kv_copy_rows, dim3(src->layers * src->kvh, n, chunks), dim3(256), 0, st, 1u,
+                     src->k.as<float>(), src->v.as<float>(), src->layer_elems(), s_base,
+                     src->max_pos, dst->k.as<float>(), dst->v.as<float>(), dst->layer_elems(),
+                     dst->max_pos, ds, src->kvh, src->hd, src->lens() + ss, dst->lens());
+}
+}  // namespace qora
+
+int qora_kv_copy_stream(qora_kv *dst, int32_t ds, const qora_kv *src, int32_t ss, void *stream) {
+    return kv_copy_streams(dst, ds, 1, src, ss, as_stream(stream));
 }
 
 int qora_kv_layer_ptrs(qora_kv *kv, int32_t layer, float **k, float **v, int32_t **len) {
@@ -850,7 +876,7 @@ int qora_engine_prefill_from(qora_engine *e, const qora_kv *prefix, int32_t pref
     if (have != prefix_len)  // the reference falls back to a full prefill here (generate_new.rs:307-316)
         return set_error(QORA_ERR_SHAPE, "qora_engine_prefill_from: prefix holds %d positions, not %d",
                          have, prefix_len);
-    for (int b = 0; b < e->B; b++) QORA_TRY(qora_kv_copy_stream(e->tkv, b, prefix, prefix_stream, stream));
+    QORA_TRY(kv_copy_streams(e->tkv, 0, e->B, prefix, prefix_stream, st));
     return engine_prefill_rows(e, x_host, T, seeds_host, prefix_len, stream);
 }
 

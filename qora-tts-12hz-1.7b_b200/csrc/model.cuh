@@ -57,7 +57,7 @@ int64_t text_proj_hidden(const qora_text_proj *tp);  // output width (text_proj.
 }  // namespace qora
 
 struct qora_talker {
-    qora_ctx *ctx = nullptr;
+    qora::CtxRef ctx;
     int L = 0, H = 0, heads = 0, kvh = 0, hd = 0, ffn = 0, vocab = 0, rope_max = 0;
     std::vector<qora::LayerDev> layers;
     qora::DevBuf ce_packed, ce_scl, head_nib, head_scl, final_norm, rope_cos, rope_sin;
@@ -73,7 +73,7 @@ struct qora_talker {
 };
 
 struct qora_predictor {
-    qora_ctx *ctx = nullptr;
+    qora::CtxRef ctx;
     int L = 0, H = 0, heads = 0, kvh = 0, hd = 0, ffn = 0, vocab = 0, groups = 0, rope_max = 0;
     int64_t Ht = 0;  // talker hidden (input / embedding width)
     std::vector<qora::LayerDev> layers;

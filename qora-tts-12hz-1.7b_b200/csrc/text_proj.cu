@@ -18,7 +18,7 @@
 #include "gemv.cuh"
 
 struct qora_text_proj {
-    qora_ctx *ctx = nullptr;
+    qora::CtxRef ctx;
     int64_t vocab = 0, th = 0, mid = 0, H = 0;
     qora::DevBuf emb_packed, emb_scl, fc1_nib, fc1_scl, fc2_nib, fc2_scl, b1, b2, tok, h;
     qora::EmbDev emb;

@@ -34,13 +34,14 @@ class Context:
 
     def __init__(self, device: int = 0):
         self.device = device
+        self._L = _lib.load()
         h = C.c_void_p()
         _lib.call("qora_ctx_create", device, C.byref(h))
         self.h = h
 
     def close(self):
         if getattr(self, "h", None):
-            _lib.load().qora_ctx_destroy(self.h)
+            self._L.qora_ctx_destroy(self.h)
             self.h = None
 
     def __del__(self):
@@ -57,13 +58,14 @@ class DeviceQ4:
     def __init__(self, ctx: Context, w: Q4Weight):
         self.ctx, self.k, self.n = ctx, w.k, w.n
         hs = w.host()
+        self._L = _lib.load()
         h = C.c_void_p()
         _lib.call("qora_q4_weight_upload", ctx.h, C.byref(hs), C.byref(h))
         self.h = h
 
     def __del__(self):
         if getattr(self, "h", None):
-            _lib.load().qora_q4_weight_destroy(self.h)
+            self._L.qora_q4_weight_destroy(self.h)
             self.h = None
 
     def gemv(self, x: torch.Tensor, out: torch.Tensor | None = None, stream=None) -> torch.Tensor:
@@ -117,13 +119,14 @@ class KvCache:
                  streams: int = 1):
         self.ctx, self.layers, self.kv_heads, self.head_dim = ctx, layers, kv_heads, head_dim
         self.max_pos, self.streams = max_pos, streams
+        self._L = _lib.load()
         h = C.c_void_p()
         _lib.call("qora_kv_create", ctx.h, layers, kv_heads, head_dim, max_pos, streams, C.byref(h))
         self.h = h
 
     def __del__(self):
         if getattr(self, "h", None):
-            _lib.load().qora_kv_destroy(self.h)
+            self._L.qora_kv_destroy(self.h)
             self.h = None
 
     def reset(self, ids=None, stream=None):
@@ -175,6 +178,7 @@ class Talker:
     def __init__(self, ctx: Context, w: TalkerWeights, max_batch: int = 1):
         self.ctx, self.cfg = ctx, w.cfg
         hs = w.host()
+        self._L = _lib.load()
         h = C.c_void_p()
         _lib.call("qora_talker_create", ctx.h, C.byref(hs), max_batch, C.byref(h))
         self.h = h
@@ -182,7 +186,7 @@ class Talker:
 
     def __del__(self):
         if getattr(self, "h", None):
-            _lib.load().qora_talker_destroy(self.h)
+            self._L.qora_talker_destroy(self.h)
             self.h = None
 
     def new_kv(self, max_pos: int | None = None, streams: int = 1) -> KvCache:
@@ -253,13 +257,14 @@ class TextProjection:
         self.ctx = ctx
         hs = w.host()
         self.hidden, self.text_vocab = int(hs.fc2.n), int(hs.text_embedding.k)
+        self._L = _lib.load()
         h = C.c_void_p()
         _lib.call("qora_text_proj_create", ctx.h, C.byref(hs), C.byref(h))
         self.h = h
 
     def __del__(self):
         if getattr(self, "h", None):
-            _lib.load().qora_text_proj_destroy(self.h)
+            self._L.qora_text_proj_destroy(self.h)
             self.h = None
 
     def embed_text_tokens(self, tokens, out: torch.Tensor | None = None,
@@ -284,13 +289,14 @@ class CodePredictor:
     def __init__(self, ctx: Context, w: PredictorWeights, max_batch: int = 1):
         self.ctx, self.cfg = ctx, w.cfg
         hs = w.host()
+        self._L = _lib.load()
         h = C.c_void_p()
         _lib.call("qora_predictor_create", ctx.h, C.byref(hs), max_batch, C.byref(h))
         self.h = h
 
     def __del__(self):
         if getattr(self, "h", None):
-            _lib.load().qora_predictor_destroy(self.h)
+            self._L.qora_predictor_destroy(self.h)
             self.h = None
 
     def new_kv(self, streams: int = 1) -> KvCache:
@@ -351,6 +357,7 @@ class Engine:
                  params: _lib.SampleParams | None = None):
         self.talker, self.predictor, self.B = talker, predictor, batch
         self.params = params or default_params()
+        self._L = _lib.load()
         h = C.c_void_p()
         _lib.call("qora_engine_create", talker.h, predictor.h, batch, max_pos,
                   C.byref(self.params), C.byref(h))
@@ -358,7 +365,7 @@ class Engine:
 
     def __del__(self):
         if getattr(self, "h", None):
-            _lib.load().qora_engine_destroy(self.h)
+            self._L.qora_engine_destroy(self.h)
             self.h = None
 
     def prefill(self, x: np.ndarray, seeds, stream=None):

@@ -46,12 +46,11 @@ def test_binding_covers_header(lib):
     assert sorted(qora_b200._lib.SIGNATURES) == names
 
 
-def test_documented_rust_binding_covers_header():
-    """The extern "C" block a Rust caller would add declares
-    exactly the header's functions."""
-    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-    doc = open(os.path.join(root, "INTEGRATION.md")).read()
-    block = doc[doc.index('extern "C" {'):doc.index("/// Turns a status")]
+def test_rust_binding_covers_header():
+    """The extern "C" block a Rust caller would add (include/qora_cuda_ffi.rs)
+    declares exactly the header's functions."""
+    src = open(os.path.join(ROOT, "include", "qora_cuda_ffi.rs")).read()
+    block = src[src.index('extern "C" {'):src.index("/// Turns a status")]
     assert sorted(set(re.findall(r"pub fn (qora_\w+)", block))) == header_functions()
 
 
