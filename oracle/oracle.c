@@ -475,6 +475,8 @@ void oq_kv_reset(oq_kv *kv) {
     for (int32_t l = 0; l < kv->num_layers; l++) kv->len[l] = 0;
 }
 int32_t oq_kv_len(const oq_kv *kv, int32_t layer) { return kv->len[layer]; }
+int32_t oq_kv_max_pos(const oq_kv *kv) { return kv->max_pos; }
+void oq_kv_set_len(oq_kv *kv, int32_t layer, int32_t len) { kv->len[layer] = len; }
 float *oq_kv_k(oq_kv *kv, int32_t layer) { return kv->k[layer]; }
 float *oq_kv_v(oq_kv *kv, int32_t layer) { return kv->v[layer]; }
 

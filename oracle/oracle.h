@@ -119,6 +119,8 @@ oq_kv *oq_kv_create(int32_t num_layers, int32_t kv_heads, int32_t head_dim, int3
 void oq_kv_destroy(oq_kv *kv);
 void oq_kv_reset(oq_kv *kv);
 int32_t oq_kv_len(const oq_kv *kv, int32_t layer);
+int32_t oq_kv_max_pos(const oq_kv *kv);
+void oq_kv_set_len(oq_kv *kv, int32_t layer, int32_t len);
 float *oq_kv_k(oq_kv *kv, int32_t layer);
 float *oq_kv_v(oq_kv *kv, int32_t layer);
 int oq_kv_copy(oq_kv *dst, const oq_kv *src);
@@ -137,6 +139,14 @@ int oq_talker_step(const oq_talker *t, const float *embedding, oq_kv *kv, int64_
 /* prefill_talker_raw_from (talker.rs:379-482): returns final-normed last hidden. */
 int oq_talker_prefill(const oq_talker *t, const float *x, int64_t seq_len, oq_kv *kv,
                       int64_t start_pos, float *out_hidden);
+/* Long sequences (oracle_long.c): the same values as oq_gemm and
+ * oq_talker_prefill, blocked and run on every host core.
+ * oq_talker_prefill_rows also returns every row's final-normed hidden
+ * (out_hidden_rows [seq_len][hidden]) and, when out_logits_rows is not NULL,
+ * every row's codec-head logits [seq_len][vocab]. */
+void oq_gemm_long(const float *x, int64_t seq_len, const oq_q4 *w, float *out);
+int oq_talker_prefill_rows(const oq_talker *t, const float *x, int64_t seq_len, oq_kv *kv,
+                           int64_t start_pos, float *out_hidden_rows, float *out_logits_rows);
 /* apply_codec_head (talker.rs:647-649). */
 void oq_codec_head(const oq_talker *t, const float *hidden, float *out_logits);
 void oq_embed_codec_token(const oq_talker *t, uint32_t token, float *out);

@@ -104,6 +104,8 @@ def lib():
             "oq_attend_step": (C.c_int, [vp, vp, vp, i32, i32, i32, vp, vp, vp, vp, i64, i64, vp,
                                          i32, vp]),
             "oq_talker_prefill": (C.c_int, [vp, vp, i64, vp, i64, vp]),
+            "oq_gemm_long": (None, [vp, i64, vp, vp]),
+            "oq_talker_prefill_rows": (C.c_int, [vp, vp, i64, vp, i64, vp, vp]),
             "oq_codec_head": (None, [vp, vp, vp]),
             "oq_embed_codec_token": (None, [vp, C.c_uint32, vp]),
             "oq_embed_text_token": (None, [vp, C.c_uint32, vp]),
@@ -182,6 +184,15 @@ def gemv(x: np.ndarray, w: Q4Weight, workers: int = 0) -> np.ndarray:
     out = np.zeros(w.n, np.float32)
     ws = w.cstruct()
     lib().oq_gemv_workers(ptr(x), C.addressof(ws), ptr(out), workers)
+    return out
+
+
+def gemm_long(x: np.ndarray, w: Q4Weight) -> np.ndarray:
+    """oq_gemm_long: the bits of gemm (per-row single pass), blocked over rows."""
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, w.k)
+    out = np.zeros((x.shape[0], w.n), np.float32)
+    ws = w.cstruct()
+    lib().oq_gemm_long(ptr(x), x.shape[0], C.addressof(ws), ptr(out))
     return out
 
 
@@ -533,6 +544,21 @@ class OracleModel:
         rc = lib().oq_talker_prefill(C.addressof(self.t), ptr(x), T, kv.h, start_pos, ptr(h))
         assert rc == 0, rc
         return h
+
+    def talker_prefill_rows(self, x, kv: KV, start_pos: int = 0, logits: bool = False):
+        """The prefill of `x` [T][hidden] on top of kv (oracle_long.c: the
+        values of talker_prefill, blocked and on every host core), returning
+        every row's final-normed hidden [T][hidden] and, with logits=True,
+        every row's codec-head logits [T][vocab]."""
+        c = self.m.cfg
+        x = np.ascontiguousarray(x, np.float32).reshape(-1, c.t_hidden)
+        T = x.shape[0]
+        h = np.zeros((T, c.t_hidden), np.float32)
+        lg = np.zeros((T, c.t_vocab), np.float32) if logits else None
+        rc = lib().oq_talker_prefill_rows(C.addressof(self.t), ptr(x), T, kv.h, start_pos, ptr(h),
+                                          ptr(lg) if logits else None)
+        assert rc == 0, rc
+        return (h, lg) if logits else h
 
     def codec_head(self, hidden):
         out = np.zeros(self.m.cfg.t_vocab, np.float32)
