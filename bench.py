@@ -22,7 +22,6 @@ from __future__ import annotations
 import argparse
 import json
 import os
-import re
 import statistics
 import subprocess
 import sys
@@ -52,7 +51,9 @@ def parse():
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
-    ap.add_argument("--profile-case", default=None, choices=["gemv", "frame_trace", "batch_frame"],
+    ap.add_argument("--no-config3", action="store_true")
+    ap.add_argument("--profile-case", default=None,
+                    choices=["gemv", "frame_trace", "batch_frame", "attn_decode"],
                     help="small fixed workload for an ncu capture instead of the bench")
     return ap.parse_args()
 
@@ -346,11 +347,93 @@ def gemv_sweep(E, ctx, torch, qb):
     return out
 
 
-def engine_rate(E, talker, pred, torch, qb, B, K, W, seed0, with_e2e=False):
+def config3_rate(E, ctx, tw, torch, qb, K, W, seed0, peak):
+    """Config 3: 32 streams, each with its own cache.
+    Times the 2048-token N(0,1) prefill of all 32 streams (per stream, 512-row
+    chunks), tops every cache up to 4064 positions with a second prefill (an
+    ICL prompt of that length fills the same cache), then times K batched
+    decode steps (forward_with_embedding for the 32 streams) at positions
+    4064 .. 4064+K-1 and, on its own, the decode attention of one layer over
+    that cache (qora_kv_attend without advancing: the same append slot and
+    the same K/V read every call)."""
+    cfg = tw.cfg
+    S, P1, P2 = 32, 2048, 4064
+    H = cfg.t_hidden
+    talker = E.Talker(ctx, tw, max_batch=S)
+    kv = talker.new_kv(max_pos=P2 + K + W + 8, streams=S)
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    xs = [torch.from_numpy(qb.synth_normal(seed0 + s, 1.0, P1 * H).reshape(P1, H)).cuda() for s in range(S)]
+    torch.cuda.synchronize()
+    e0.record(st)
+    for s in range(S):
+        talker.prefill_talker_raw_from(xs[s], kv, 0, kv_stream=s)
+    e1.record(st)
+    torch.cuda.synchronize()
+    prefill_ms = e0.elapsed_time(e1)
+    del xs
+    for s in range(S):
+        x2 = torch.from_numpy(qb.synth_normal(seed0 + 100 + s, 1.0, (P2 - P1) * H).reshape(P2 - P1, H)).cuda()
+        talker.prefill_talker_raw_from(x2, kv, P1, kv_stream=s)
+    emb = torch.from_numpy(qb.synth_normal(seed0 + 999, 1.0, S * H).reshape(S, H)).cuda()
+    pos = P2
+    for _ in range(W):
+        talker.forward_with_embedding(emb, kv, [pos] * S)
+        pos += 1
+    torch.cuda.synchronize()
+    p_start = pos
+    e0.record(st)
+    for _ in range(K):
+        talker.forward_with_embedding(emb, kv, [pos] * S)
+        pos += 1
+    e1.record(st)
+    torch.cuda.synchronize()
+    step_ms = e0.elapsed_time(e1) / K
+    # the decode attention of layer 0 alone, over the cache as it stands
+    c = cfg
+    qkv = torch.randn(S, (c.t_heads + 2 * c.t_kv_heads) * c.t_head_dim, device="cuda")
+    lw = tw.layers[0]
+    qn = torch.from_numpy(lw.q_norm.view(np.int16).copy()).cuda()
+    kn = torch.from_numpy(lw.k_norm.view(np.int16).copy()).cuda()
+    cos, sin = E.build_mrope_tables(c.t_head_dim, c.t_max_pos, c.rope_theta, [24, 20, 20])
+    cos, sin = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    posd = torch.full((S,), pos, dtype=torch.int32, device="cuda")
+    out = torch.empty(S, c.t_heads * c.t_head_dim, device="cuda")
+    reps = 20
+    for _ in range(3):
+        kv.attend(0, qkv, c.t_heads, qn, kn, cos, sin, posd, out=out)
+    torch.cuda.synchronize()
+    e0.record(st)
+    for _ in range(reps):
+        kv.attend(0, qkv, c.t_heads, qn, kn, cos, sin, posd, out=out)
+    e1.record(st)
+    torch.cuda.synchronize()
+    attn_us = 1000.0 * e0.elapsed_time(e1) / reps
+    P = pos  # cached positions read per stream (+1 appended row)
+    kv_bytes = S * c.t_kv_heads * (P + 1) * c.t_head_dim * 4 * 2
+    io_bytes = S * 4 * ((c.t_heads + 2 * c.t_kv_heads) * c.t_head_dim + c.t_heads * c.t_head_dim)
+    attn_gbs = (kv_bytes + io_bytes) / (attn_us * 1e-6) / 1e9
+    ctx.check_device_error()
+    del kv, talker
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    return {"streams": S, "prefill_tokens_per_stream": P1,
+            "prefill_ms_all_streams": round(prefill_ms, 1),
+            "prefill_tokens_per_s": round(S * P1 / (prefill_ms / 1000.0), 1),
+            "decode_positions": [p_start, p_start + K - 1], "decode_steps": K,
+            "ms_per_step": round(step_ms, 3), "stream_steps_per_s": round(S / (step_ms / 1000.0), 1),
+            "attention": {"kernel": "k_attention (decode, 32 streams, one layer)",
+                          "positions": P + 1, "us_per_launch": round(attn_us, 2),
+                          "algorithmic_bytes_per_launch": int(kv_bytes + io_bytes),
+                          "achieved": round(attn_gbs, 1), "peak": peak, "unit": "GB/s",
+                          "frac": round(attn_gbs / peak, 4)}}
+
+
+def engine_rate(E, talker, pred, torch, qb, B, K, W, seed0, with_e2e=False, prefill=PREFILL):
     cfg = talker.cfg
-    max_pos = PREFILL + W + (2 * K if with_e2e else K) + 8
+    max_pos = prefill + W + (2 * K if with_e2e else K) + 8
     eng = E.Engine(talker, pred, B, max_pos)
-    x = np.stack([qb.synth_normal(seed0 + b, 1.0, PREFILL * cfg.t_hidden).reshape(PREFILL, cfg.t_hidden)
+    x = np.stack([qb.synth_normal(seed0 + b, 1.0, prefill * cfg.t_hidden).reshape(prefill, cfg.t_hidden)
                   for b in range(B)])
     eng.prefill(x, [seed0 + b for b in range(B)])
     eng.use_graph(True)
@@ -360,6 +443,66 @@ def engine_rate(E, talker, pred, torch, qb, B, K, W, seed0, with_e2e=False):
         eng.frame(text, codes)
     torch.cuda.synchronize()
     return eng, text, codes
+
+
+# DRAM bytes per launch from the committed ncu captures (text copied here,
+# never read at run time): k_frame on the bench's batch-1 frame workload, and
+# k_gemv's DRAM bytes per algorithmic byte on the talker gate/up shape.
+KFRAME_DRAM_BYTES = 937957888        # profiles/k_frame_b1_frame.md
+KGEMV_DRAM_PER_ALG_BYTE = 1.0058     # profiles/k_gemv_b1_2048x6144.md
+
+
+def predictor_rate(E, ctx, qb, torch, hd, frames):
+    """Config 2: the code predictor alone at batch 1 -
+    one generate_acoustic_codes per frame (2-token prefill + 14 steps, 15
+    heads with argmax), the per-op kernels of a frame captured in one CUDA
+    graph and replayed; talker hidden N(0,1) (seed 7), semantic row from a
+    codec-embedding-shaped table."""
+    cfg = qb.ModelConfig(p_head_dim=hd)
+    pw = qb.synth_predictor(cfg)
+    pred = E.CodePredictor(ctx, pw, max_batch=1)
+    kv = pred.new_kv()
+    hid = torch.from_numpy(qb.synth_normal(7, 1.0, cfg.t_hidden)).cuda().reshape(1, -1)
+    sem = torch.from_numpy(qb.synth_normal(8, 1.0, cfg.t_hidden)).cuda().reshape(1, -1)
+    codes = torch.zeros(1, cfg.p_groups, dtype=torch.int32, device="cuda")
+    from qora_b200 import _lib
+
+    def run():
+        _lib.call("qora_predictor_frame", pred.h, kv.h, hid.data_ptr(), sem.data_ptr(), 1,
+                  codes.data_ptr(), None, None, torch.cuda.current_stream().cuda_stream)
+
+    ms = _graph_time_ms(torch, run, frames)
+    del pred, kv
+    return {"head_dim": hd, "frames": frames, "ms_per_frame": round(ms, 4),
+            "frames_per_s": round(1000.0 / ms, 1)}
+
+
+def talker_step_rate(E, ctx, tw, torch, qb, steps=256, prefill=32):
+    """Config 0: the talker alone at batch 1 - a 32-token
+    prefill, then `steps` forward_with_embedding steps (per-op kernels of one
+    step captured in a CUDA graph; each replay appends a position, so the
+    replays walk positions 32 .. 32 + steps - 1 as config 0 does)."""
+    cfg = tw.cfg
+    talker = E.Talker(ctx, tw, max_batch=1)
+    kv = talker.new_kv(max_pos=prefill + steps + 8)
+    x = torch.from_numpy(qb.synth_normal(42, 1.0, prefill * cfg.t_hidden).reshape(prefill, -1)).cuda()
+    emb = torch.from_numpy(qb.synth_normal(43, 1.0, cfg.t_hidden)).cuda().reshape(1, -1)
+    pos = torch.full((1,), prefill, dtype=torch.int32, device="cuda")
+    hidden = torch.empty(1, cfg.t_hidden, device="cuda")
+    logits = torch.empty(1, cfg.t_vocab, device="cuda")
+    from qora_b200 import _lib
+
+    def run():
+        _lib.call("qora_talker_step", talker.h, kv.h, emb.data_ptr(), pos.data_ptr(), 1,
+                  hidden.data_ptr(), logits.data_ptr(), torch.cuda.current_stream().cuda_stream)
+
+    talker.prefill_talker_raw_from(x, kv, 0)
+    # _graph_time_ms runs one eager step and one replay before timing: start the
+    # timed replays two positions in, and time steps - 2 of them
+    ms = _graph_time_ms(torch, run, steps - 2)
+    del talker, kv
+    return {"prefill_tokens": prefill, "steps": steps, "ms_per_step": round(ms, 4),
+            "steps_per_s": round(1000.0 / ms, 1)}
 
 
 def run_ours(args):
@@ -379,25 +522,31 @@ def run_ours(args):
     maxb = max(B, 1 if args.no_batch32 else 32)
     talker = E.Talker(ctx, tw, max_batch=maxb)
     pred = E.CodePredictor(ctx, pw, max_batch=maxb)
+    peak, peak_src = peaks()
 
     def barrier():
         ranks.barrier()
         torch.cuda.synchronize()
 
     max_over_ranks = ranks.max
-
-    # ---- device-resident frame loop (value)
-    eng, text, codes = engine_rate(E, talker, pred, torch, qb, B, K, W, ranks.stream_seed(1000, B, 0), True)
     st = torch.cuda.current_stream()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    with ClockSampler(local) as clk:
+
+    def timed_frames(eng, text, codes, n):
+        barrier()
         e0.record(st)
-        for _ in range(K):
+        for _ in range(n):
             eng.frame(text, codes)
         e1.record(st)
         torch.cuda.synchronize()
-    ms = max_over_ranks(e0.elapsed_time(e1))
+        return max_over_ranks(e0.elapsed_time(e1))
+
+    # the clock sampler runs across every timed GPU leg below
+    clk = ClockSampler(local).__enter__()
+
+    # ---- device-resident frame loop (value)
+    eng, text, codes = engine_rate(E, talker, pred, torch, qb, B, K, W, ranks.stream_seed(1000, B, 0), True)
+    ms = timed_frames(eng, text, codes, K)
     kernels = eng.kernels_per_frame()
     ctx.check_device_error()
     frames = B * K * world
@@ -427,51 +576,49 @@ def run_ours(args):
     del eng
     torch.cuda.synchronize()
 
-    # ---- batch 32
-    b32 = None
+    # ---- batch 32 (same positions), then batch 1 and 32 at config 4's mean
+    # cache position (1000 frames after a 64-token prefill: ~564)
+    b32, c4 = None, None
     if not args.no_batch32:
         K32 = max(10, min(K, 60))
         eng32, text32, codes32 = engine_rate(E, talker, pred, torch, qb, 32, K32, W,
                                              ranks.stream_seed(50000, 32, 0))
-        barrier()
-        e0.record(st)
-        for _ in range(K32):
-            eng32.frame(text32, codes32)
-        e1.record(st)
-        torch.cuda.synchronize()
-        ms32 = max_over_ranks(e0.elapsed_time(e1))
+        ms32 = timed_frames(eng32, text32, codes32, K32)
         b32 = {"value": 32 * K32 * world / (ms32 / 1000.0), "unit": "frames/s", "steps": K32,
-               "ms_per_step": ms32 / K32}
+               "ms_per_step": ms32 / K32, "positions": [PREFILL + W, PREFILL + W + K32 - 1]}
         del eng32
         torch.cuda.synchronize()
+        c4 = {"positions_from": 564}
+        for bb, kk in ((1, K), (32, K32)):
+            e4, t4, c4d = engine_rate(E, talker, pred, torch, qb, bb, kk, W,
+                                      ranks.stream_seed(90000, bb, 0), prefill=564 - W)
+            m4 = timed_frames(e4, t4, c4d, kk)
+            c4[f"b{bb}"] = {"value": round(bb * kk * world / (m4 / 1000.0), 2), "unit": "frames/s",
+                            "ms_per_step": round(m4 / kk, 4), "steps": kk}
+            del e4
+            torch.cuda.synchronize()
+        c4["note"] = ("config 4's per-GPU step at its mean cache position (the cache is "
+                      "prefilled to 564 - warm-up positions instead of decoding 500 frames)")
 
     if rank != 0:
+        clk.__exit__(None, None, None)
         ranks.close()
         return
 
     # ---- roofline of the dominant kernel: at batch 1 the whole frame is one
     # k_frame launch (talker step + 15-code predictor + sampler), so its
     # launch duration is the CUDA-event time per frame measured above
-    peak, peak_src = peaks()
     roof, gemv_stream = None, None
     if not args.no_roofline:
         pos_avg = PREFILL + W + 0.5 * K  # cache positions during the timed frames
         fb = frame_algorithmic_bytes(cfg, pos_avg)
         us = 1000.0 * ms / K
         achieved = fb / (us * 1e-6) / 1e9
-        traffic = None
-        try:
-            # DRAM bytes of one k_frame launch from the committed ncu capture
-            # (profiles/k_frame_b1_frame.md, same workload)
-            with open(os.path.join(ROOT, "profiles", "k_frame_b1_frame.md")) as f:
-                m = re.search(r"dram_bytes_per_launch:\s*([0-9]+)", f.read())
-            if m:
-                traffic = int(m.group(1))
-        except OSError:
-            pass
         roof = {"bound": "hbm", "kernel": "k_frame (persistent frame kernel, batch 1)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "peak_source": peak_src, "traffic": traffic,
+                "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                "traffic": KFRAME_DRAM_BYTES,
+                "traffic_source": "ncu capture of one launch on this workload (profiles/k_frame_b1_frame.md)",
                 "launches_per_step": kernels, "us_per_launch": round(us, 2),
                 "algorithmic_bytes_per_launch": round(fb),
                 "bytes_model": "talker weights 796,262,400 + norms + KV read 229,376 B x (P+1) + "
@@ -480,21 +627,25 @@ def run_ours(args):
         byts, gms = gemv_stream_roofline(E, ctx, tw, torch)
         n_launch = 7 * len(tw.layers) + 1
         g_ach = byts / (gms / 1000.0) / 1e9
-        g_traffic = None
-        try:
-            with open(os.path.join(ROOT, "profiles", "k_gemv_b1_2048x6144.md")) as f:
-                m = re.search(r"dram_traffic_per_algorithmic_byte:\s*([0-9.]+)", f.read())
-            if m:
-                g_traffic = round(float(m.group(1)) * byts / n_launch)
-        except OSError:
-            pass
         gemv_stream = {"kernel": "k_gemv (talker Q4 GEMVs, batch 1, back-to-back launches)",
                        "achieved": round(g_ach, 1), "peak": peak, "unit": "GB/s",
-                       "frac": round(g_ach / peak, 4), "traffic": g_traffic, "launches": n_launch,
+                       "frac": round(g_ach / peak, 4),
+                       "traffic": round(KGEMV_DRAM_PER_ALG_BYTE * byts / n_launch),
+                       "traffic_source": "DRAM bytes per algorithmic byte of the ncu capture "
+                                         "profiles/k_gemv_b1_2048x6144.md, scaled to the launch mix",
+                       "launches": n_launch,
                        "us_per_launch": round(1000.0 * gms / n_launch, 2),
                        "algorithmic_bytes_per_launch": round(byts / n_launch)}
 
     sweep = None if args.no_sweep else gemv_sweep(E, ctx, torch, qb)
+
+    cfg3 = cfg2 = cfg0 = None
+    if world == 1 and not args.no_config3:
+        cfg3 = config3_rate(E, ctx, tw, torch, qb, max(5, min(K, 20)), 3, 42, peak)
+    if world == 1 and not args.no_sweep:
+        cfg2 = [predictor_rate(E, ctx, qb, torch, hd, 64) for hd in (64, 128)]
+        cfg0 = talker_step_rate(E, ctx, tw, torch, qb)
+    clk.__exit__(None, None, None)
 
     cpu = None
     if world == 1 and not args.no_cpu:
@@ -510,11 +661,14 @@ def run_ours(args):
         "vs_baseline": round(value / REF_FRAMES_PER_S, 2), "dtype": "f32 (Q4 weights)",
         "data": "synthetic: random-init N(0,0.02) Q4 weights, N(0,1) prefill and text rows",
         "config": {"workload": "frame loop: talker step + 15-code predictor + top-k 50 sampling "
-                               "(one CUDA graph per frame)",
+                               "(one persistent-kernel launch per batch-1 frame)",
                    "batch_per_gpu": B, "prefill_tokens": PREFILL, "talker_layers": cfg.t_layers,
                    "predictor_head_dim": cfg.p_head_dim, "parallelism": f"replicas x{world}",
                    "l2": "per-frame weight stream 0.95 GB > 126 MB L2, no flush",
-                   "vs_baseline_ref": "README.md:280 0.35 s/frame (laptop CPU)"},
+                   "vs_baseline_ref": "README.md:280 0.35 s/frame (laptop CPU)",
+                   "reference_arm": "one CPU process on rank 0 (the reference is a single-host "
+                                    "CPU program); at N > 1 the arms' ratio compares N GPUs "
+                                    "with that one process"},
         "e2e": {k: (round(v, 2) if isinstance(v, float) else v) for k, v in e2e.items()},
         "gpu_launches": int(kernels * K),
         "kernels_per_step": kernels,
@@ -523,6 +677,10 @@ def run_ours(args):
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "batch32": b32,
+        "config4_positions": c4,
+        "config3": cfg3,
+        "config2_predictor": cfg2,
+        "config0_talker": cfg0,
         "gemv_sweep": sweep,
     }
     print(json.dumps(line), flush=True)
@@ -633,8 +791,54 @@ def profile_case_batch_frame(B):
                       "kernels_per_frame": eng.kernels_per_frame()}))
 
 
+def profile_case_attn_decode(streams=32, positions=4096, reps=8):
+    """ncu case: the decode attention of one talker layer (16 q / 8 kv heads,
+    head_dim 128) for `streams` streams over `positions` cached positions each
+    (one-layer cache, 1.07 GB at 32 x 4096; K / V filled with N(0,1)), the
+    kernel the config-3 step spends most of its time in.  Times `reps`
+    launches after 3 warm-up launches (CUDA events) and prints one JSON line."""
+    import ctypes as C
+    import torch
+    from qora_b200 import engine as E, _lib
+    torch.cuda.set_device(0)
+    ctx = E.Context(0)
+    H, KV, HD = 16, 8, 128
+    kv = E.KvCache(ctx, 1, KV, HD, positions, streams)
+    kp, vp, lp = C.c_void_p(), C.c_void_p(), C.c_void_p()
+    _lib.call("qora_kv_layer_ptrs", kv.h, 0, C.byref(kp), C.byref(vp), C.byref(lp))
+    n = streams * KV * positions * HD
+    for p in (kp, vp):
+        E._device_view(p.value, (n,), "<f4").copy_(torch.randn(n, device="cuda"))
+    E._device_view(lp.value, (streams,), "<i4").fill_(positions - 1)
+    qkv = torch.randn(streams, (H + 2 * KV) * HD, device="cuda")
+    gam = torch.from_numpy(np.full(HD, 0x3C00, np.uint16).view(np.int16)).cuda()
+    cos, sin = E.build_mrope_tables(HD, positions + 1, 1e6, [24, 20, 20])
+    cos, sin = torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda()
+    pos = torch.full((streams,), positions - 1, dtype=torch.int32, device="cuda")
+    out = torch.empty(streams, H * HD, device="cuda")
+    for _ in range(3):
+        kv.attend(0, qkv, H, gam, gam, cos, sin, pos, out=out)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        kv.attend(0, qkv, H, gam, gam, cos, sin, pos, out=out)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ctx.check_device_error()
+    us = 1000.0 * e0.elapsed_time(e1) / reps
+    byts = streams * KV * positions * HD * 4 * 2
+    print(json.dumps({"profile_case": "attn_decode", "streams": streams, "positions": positions,
+                      "us_per_launch": round(us, 2), "kv_bytes": byts,
+                      "GB/s": round(byts / (us * 1e-6) / 1e9, 1)}))
+
+
 def main():
     args = parse()
+    if args.profile_case == "attn_decode":
+        profile_case_attn_decode()
+        return
     if args.profile_case == "gemv":
         profile_case_gemv()
         return

@@ -74,6 +74,552 @@ __global__ void __launch_bounds__(kThreads) k_attention(const AttnArgs a) {
     attn::attn_item<HD, G, kThreads, 0>(a, blockIdx.x, blockIdx.y, blockIdx.z, threadIdx.x, sm);
 }
 
+// ------------------------------------------------------------------------
+// Causal prefill attention, tiled (the causal attention of
+// prefill_talker_raw_from, talker.rs:425-458): T new rows per stream at
+// positions L0 .. L0+T-1 (q normed and roped in place, K/V already appended
+// by k_qkv_post) attend to cache positions 0 .. their own.  One CTA takes a
+// block of kPfM query vectors (kPfM / G tokens x the G query heads of one kv
+// head) and walks the key positions in tiles of kPfBK, double-buffered with
+// cp.async, keeping a running max / sum per query (online softmax), so each
+// K/V byte is read once per query block instead of once per query row.
+// Exact f32 arithmetic; scores are (q.k) * 1/sqrt(hd) with the dot product
+// accumulated in head-dimension order.  Every row's result depends only on
+// its own query and keys (the key tiles start at position 0 whatever the
+// block), so a row comes out with the same bits in any prefill chunk.
+constexpr int kPfM = 64;        // query vectors per CTA
+constexpr int kPfBK = 32;       // key positions per tile
+constexpr int kPfThreads = 256;
+
+template <int HD>
+struct PfSmem {
+    float q[kPfM][HD + 4];          // +4: rows fall on different banks
+    float k[2][kPfBK][HD + 4];
+    float v[2][kPfBK][HD + 4];
+    float p[kPfM][kPfBK + 1];       // scores, then unnormalised probabilities
+    float mx[kPfM], l[kPfM], corr[kPfM];
+};
+
+__device__ __forceinline__ void pf_cp16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src)
+                 : "memory");
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kPfThreads, 2) k_prefill_attn(const AttnArgs a) {
+    constexpr int BQ = kPfM / G;    // tokens per CTA
+    constexpr int D4 = HD / 4;
+    constexpr int DJ = HD / 64;     // float4 columns per thread in P.V
+    extern __shared__ float4 pf_dyn[];
+    PfSmem<HD> &sm = *reinterpret_cast<PfSmem<HD> *>(pf_dyn);
+    griddep_launch_dependents();
+    griddep_wait();
+    const int qb = gridDim.x - 1 - blockIdx.x;  // the longest query blocks first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int L0 = __ldcg(a.len + b);
+    if (L0 + a.T > a.kv.max_pos) {
+        if (tid == 0 && qb == 0 && h == 0) raise_error(a.err, kDevRange);
+        return;
+    }
+    const int t0 = qb * BQ;
+    const int nq = min(BQ, a.T - t0);
+    if (nq <= 0) return;
+    const int kend = L0 + t0 + nq;  // keys [0, kend) are visible to some row of the block
+    const int ntiles = (kend + kPfBK - 1) / kPfBK;
+    const float *kbase = a.kv.k + ((int64_t)b * a.kv_heads + h) * a.kv.max_pos * HD;
+    const float *vbase = a.kv.v + ((int64_t)b * a.kv_heads + h) * a.kv.max_pos * HD;
+
+    auto load_tile = [&](int kt, int buf) {
+        const int k0 = kt * kPfBK;
+        for (int i = tid; i < kPfBK * D4; i += kPfThreads) {
+            const int n = i / D4, d4 = i % D4;
+            float *kd = &sm.k[buf][n][4 * d4];
+            float *vd = &sm.v[buf][n][4 * d4];
+            if (k0 + n < kend) {
+                pf_cp16(kd, kbase + (int64_t)(k0 + n) * HD + 4 * d4);
+                pf_cp16(vd, vbase + (int64_t)(k0 + n) * HD + 4 * d4);
+            } else {  // never visible: zeros (unwritten cache memory may hold anything)
+                *reinterpret_cast<float4 *>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4 *>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    load_tile(0, 0);
+    // query vectors: m = token * G + head within the kv head's group
+    for (int i = tid; i < kPfM * D4; i += kPfThreads) {
+        const int m = i / D4, d4 = i % D4;
+        const int tl = m / G, g = m % G;
+        float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tl < nq) {
+            const float *row = a.qkv + (int64_t)(b * a.T + t0 + tl) * a.ldqkv + (int64_t)(h * G + g) * HD;
+            q = __ldcg(reinterpret_cast<const float4 *>(row) + d4);
+        }
+        *reinterpret_cast<float4 *>(&sm.q[m][4 * d4]) = q;
+    }
+    if (tid < kPfM) {
+        sm.mx[tid] = -INFINITY;
+        sm.l[tid] = 0.0f;
+    }
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));  // talker.rs:305
+    // thread tiles: rows tm*4 .. +3; scores for keys tn + 16 j; P.V columns 4 td + 64 jj
+    const int tm = (warp >> 1) * 4 + (lane >> 3);
+    const int tn = (warp & 1) * 8 + (lane & 7);
+    float o[4][DJ][4];
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+#pragma unroll
+        for (int jj = 0; jj < DJ; jj++) o[i][jj][0] = o[i][jj][1] = o[i][jj][2] = o[i][jj][3] = 0.0f;
+
+    for (int kt = 0; kt < ntiles; kt++) {
+        const int buf = kt & 1;
+        if (kt + 1 < ntiles) load_tile(kt + 1, buf ^ 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+        __syncthreads();
+        // ---- scores S = Q K^T for this thread's 4 rows x 2 keys
+        float s[4][2];
+#pragma unroll
+        for (int i = 0; i < 4; i++) s[i][0] = s[i][1] = 0.0f;
+#pragma unroll 4
+        for (int d4 = 0; d4 < D4; d4++) {
+            float4 qv[4], kv[2];
+#pragma unroll
+            for (int i = 0; i < 4; i++) qv[i] = *reinterpret_cast<const float4 *>(&sm.q[tm * 4 + i][4 * d4]);
+#pragma unroll
+            for (int j = 0; j < 2; j++) kv[j] = *reinterpret_cast<const float4 *>(&sm.k[buf][tn + 16 * j][4 * d4]);
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    float t = s[i][j];
+                    t = __fmaf_rn(qv[i].x, kv[j].x, t);
+                    t = __fmaf_rn(qv[i].y, kv[j].y, t);
+                    t = __fmaf_rn(qv[i].z, kv[j].z, t);
+                    t = __fmaf_rn(qv[i].w, kv[j].w, t);
+                    s[i][j] = t;
+                }
+        }
+        const int k0 = kt * kPfBK;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const int m = tm * 4 + i, tl = m / G;
+            const int qpos = L0 + t0 + tl;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int n = tn + 16 * j;
+                const bool vis = tl < nq && k0 + n <= qpos;
+                sm.p[m][n] = vis ? __fmul_rn(s[i][j], scale) : -INFINITY;
+            }
+        }
+        __syncthreads();
+        // ---- online softmax: 4 threads per row, 8 keys each
+        {
+            const int row = tid >> 2, part = tid & 3;
+            float v[8];
+            float rmax = -INFINITY;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                v[e] = sm.p[row][part * 8 + e];
+                rmax = fmaxf(rmax, v[e]);
+            }
+            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 1));
+            rmax = fmaxf(rmax, __shfl_xor_sync(0xffffffffu, rmax, 2));
+            const float m_old = sm.mx[row];
+            const float m_new = fmaxf(m_old, rmax);
+            float psum = 0.0f;
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                const float pe = m_new == -INFINITY ? 0.0f : expf(v[e] - m_new);
+                sm.p[row][part * 8 + e] = pe;
+                psum += pe;
+            }
+            psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+            psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+            __syncwarp();
+            if (part == 0) {
+                const float c = m_new == -INFINITY ? 1.0f : expf(m_old - m_new);  // exp(-inf) = 0
+                sm.corr[row] = c;
+                sm.l[row] = __fmaf_rn(sm.l[row], c, psum);
+                sm.mx[row] = m_new;
+            }
+        }
+        __syncthreads();
+        // ---- O = O * corr + P V
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float c = sm.corr[tm * 4 + i];
+#pragma unroll
+            for (int jj = 0; jj < DJ; jj++) {
+                o[i][jj][0] = __fmul_rn(o[i][jj][0], c);
+                o[i][jj][1] = __fmul_rn(o[i][jj][1], c);
+                o[i][jj][2] = __fmul_rn(o[i][jj][2], c);
+                o[i][jj][3] = __fmul_rn(o[i][jj][3], c);
+            }
+        }
+#pragma unroll 4
+        for (int n = 0; n < kPfBK; n++) {
+            float pr[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) pr[i] = sm.p[tm * 4 + i][n];
+#pragma unroll
+            for (int jj = 0; jj < DJ; jj++) {
+                const float4 vv = *reinterpret_cast<const float4 *>(&sm.v[buf][n][4 * tn + 64 * jj]);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    o[i][jj][0] = __fmaf_rn(pr[i], vv.x, o[i][jj][0]);
+                    o[i][jj][1] = __fmaf_rn(pr[i], vv.y, o[i][jj][1]);
+                    o[i][jj][2] = __fmaf_rn(pr[i], vv.z, o[i][jj][2]);
+                    o[i][jj][3] = __fmaf_rn(pr[i], vv.w, o[i][jj][3]);
+                }
+            }
+        }
+        __syncthreads();  // the next iteration's prefetch overwrites this buffer
+    }
+    // ---- out = O / l
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int m = tm * 4 + i, tl = m / G, g = m % G;
+        if (tl >= nq) continue;
+        const float l = sm.l[m];
+        float *dst = a.out + (int64_t)(b * a.T + t0 + tl) * a.ldout + (int64_t)(h * G + g) * HD;
+#pragma unroll
+        for (int jj = 0; jj < DJ; jj++) {
+            float4 r;
+            r.x = __fdiv_rn(o[i][jj][0], l);
+            r.y = __fdiv_rn(o[i][jj][1], l);
+            r.z = __fdiv_rn(o[i][jj][2], l);
+            r.w = __fdiv_rn(o[i][jj][3], l);
+            *reinterpret_cast<float4 *>(dst + 4 * tn + 64 * jj) = r;
+        }
+    }
+}
+
+// ------------------------------------------------------------------------
+// Decode attention over a long cache, streamed (T = 1; the attention block of
+// forward_with_embedding, talker.rs:285-331): one CTA per (kv head, position
+// split, stream row) as k_attention.  A producer warp pulls the split's K and
+// V rows into a ring of kDsStages shared-memory stages with cp.async.bulk
+// (one contiguous copy per tile for K and one for V: a (stream, kv head)
+// slab holds its positions back to back), completion on a "full" mbarrier per
+// stage; eight compute warps each take every eighth position of a stage and
+// keep their own running max / sum / weighted V sum per query head (online
+// softmax), so no block-wide barrier falls inside the loop: a warp releases
+// a stage on its "empty" mbarrier and moves on.  The warps' states merge once
+// at the end, then the splits merge as in k_attention (last arriver, split
+// order).  qk-norm + RoPE of the query heads and of the new key, and the
+// append of the new K / V row at the cache length, are fused as in
+// k_attention; the split that holds the new row reads it from shared memory
+// (its bulk copy stops before that row).  Every mbarrier wait is bounded.
+constexpr int kDsWarps = 8;                    // compute warps
+constexpr int kDsThreads = (kDsWarps + 1) * 32; // + the producer warp
+constexpr int kDsStages = 4;
+constexpr int kDsTileBytes = 8192;             // K (and V) bytes per tile
+constexpr int kDsMinChunk = 128;               // positions per split at least
+
+template <int HD, int G>
+struct DsSmem {
+    static constexpr int TP = kDsTileBytes / (HD * 4);  // positions per tile
+    float k[kDsStages][TP][HD];
+    float v[kDsStages][TP][HD];
+    float q[G][HD];
+    float newk[HD], newv[HD];
+    float wo[kDsWarps][G][HD];     // each warp's weighted V sums at the end
+    float wm[kDsWarps][G], wl[kDsWarps][G];
+    uint64_t full[kDsStages], empty[kDsStages];
+    int last_flag;
+    int abort;
+};
+
+template <int HD, int G>
+__global__ void __launch_bounds__(kDsThreads, 2) k_attn_stream(const AttnArgs a) {
+    using Sm = DsSmem<HD, G>;
+    constexpr int TP = Sm::TP;
+    constexpr int J = HD / 32;     // head-dimension values per lane (contiguous)
+    extern __shared__ float4 ds_dyn[];
+    Sm &sm = *reinterpret_cast<Sm *>(ds_dyn);
+    const int kvh = blockIdx.x, split = blockIdx.y, r = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        for (int s = 0; s < kDsStages; s++) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], kDsWarps);
+        }
+        sm.abort = 0;
+        mbar_fence_init();
+    }
+    __syncthreads();
+    griddep_launch_dependents();
+    griddep_wait();
+    const int b = r;  // T = 1: one row per stream
+    const int L0 = a.len_static >= 0 ? a.len_static : __ldcg(a.len + b);
+    if (L0 + 1 > a.kv.max_pos) {
+        if (tid == 0 && split == 0 && kvh == 0) raise_error(a.err, kDevRange);
+        return;
+    }
+    const int Lq = L0 + 1;
+    const int nsplit0 = min(kAttnMaxSplit, max(1, Lq / kDsMinChunk));
+    const int chunk = ((Lq + nsplit0 - 1) / nsplit0 + TP - 1) / TP * TP;  // whole tiles
+    const int nsplit = (Lq + chunk - 1) / chunk;
+    if (split >= nsplit) return;
+    const int p0 = split * chunk, p1 = min(Lq, p0 + chunk);
+    const bool appender = (p1 == Lq);
+    const int ntiles = (p1 - p0 + TP - 1) / TP;
+    const float *cr = nullptr, *sr = nullptr;
+    if (!rope_rows<HD>(a, b, 0, L0, cr, sr)) {
+        if (tid == 0 && split == 0 && kvh == 0) raise_error(a.err, kDevRange);
+        return;
+    }
+    float *krow_base = a.kv.k + ((int64_t)b * a.kv_heads + kvh) * a.kv.max_pos * HD;
+    float *vrow_base = a.kv.v + ((int64_t)b * a.kv_heads + kvh) * a.kv.max_pos * HD;
+
+    if (warp == kDsWarps) {
+        // ------------------------------------------------------ producer
+        // tile i: positions [p0 + i TP, ..), its cached rows (< L0) by bulk copy
+        if (lane == 0) {
+            for (int i = 0; i < ntiles; i++) {
+                const int s = i % kDsStages;
+                if (i >= kDsStages &&
+                    !mbar_wait_bounded(&sm.empty[s], ((i / kDsStages) + 1) & 1, a.err)) {
+                    sm.abort = 1;
+                    break;
+                }
+                if (*(volatile int *)&sm.abort) break;
+                const int t0 = p0 + i * TP;
+                const int nrow = max(0, min(min(t0 + TP, p1), L0) - t0);
+                const uint32_t bytes = (uint32_t)nrow * HD * 4;
+                mbar_arrive_expect_tx(&sm.full[s], 2 * bytes);
+                if (bytes) {
+                    bulk_g2s(&sm.k[s][0][0], krow_base + (int64_t)t0 * HD, bytes, &sm.full[s]);
+                    bulk_g2s(&sm.v[s][0][0], vrow_base + (int64_t)t0 * HD, bytes, &sm.full[s]);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ------------------------------------------------------ compute warps
+        // query heads (qk-norm + RoPE) and, on the appending split, the new row
+        const float *row = a.qkv + (int64_t)r * a.ldqkv;
+        for (int it = warp; it < G + 2; it += kDsWarps) {
+            if (it >= G && !appender) continue;
+            float v[J];
+            const int64_t off = it < G ? (int64_t)(kvh * G + it) * HD
+                                       : (it == G ? (int64_t)(a.heads + kvh) * HD
+                                                  : (int64_t)(a.heads + a.kv_heads + kvh) * HD);
+#pragma unroll
+            for (int j = 0; j < J; j++) v[j] = __ldcg(row + off + lane + 32 * j);
+            if (it < G) {
+                norm_rope_head<HD>(v, a.q_gamma, cr, sr, true, lane);
+#pragma unroll
+                for (int j = 0; j < J; j++) sm.q[it][lane + 32 * j] = v[j];
+            } else if (it == G) {
+                norm_rope_head<HD>(v, a.k_gamma, cr, sr, true, lane);
+#pragma unroll
+                for (int j = 0; j < J; j++) {
+                    sm.newk[lane + 32 * j] = v[j];
+                    krow_base[(int64_t)L0 * HD + lane + 32 * j] = v[j];
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < J; j++) {
+                    sm.newv[lane + 32 * j] = v[j];
+                    vrow_base[(int64_t)L0 * HD + lane + 32 * j] = v[j];
+                }
+            }
+        }
+        asm volatile("bar.sync 1, %0;" ::"n"(kDsWarps * 32) : "memory");
+        // lane holds head-dimension values J*lane .. J*lane + J - 1
+        float qr[G][J], o[G][J], m[G], l[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+#pragma unroll
+            for (int j = 0; j < J; j++) {
+                qr[g][j] = sm.q[g][J * lane + j];
+                o[g][j] = 0.0f;
+            }
+            m[g] = -INFINITY;
+            l[g] = 0.0f;
+        }
+        const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));  // talker.rs:305
+        for (int i = 0; i < ntiles; i++) {
+            const int s = i % kDsStages;
+            const int t0 = p0 + i * TP;
+            const int cnt = min(TP, p1 - t0);
+            if (!mbar_wait_bounded(&sm.full[s], (i / kDsStages) & 1, a.err)) sm.abort = 1;
+            if (*(volatile int *)&sm.abort) break;
+            for (int pp = warp; pp < cnt; pp += kDsWarps) {
+                const bool fresh = appender && t0 + pp == L0;
+                const float *kr = fresh ? sm.newk : &sm.k[s][pp][0];
+                const float *vr = fresh ? sm.newv : &sm.v[s][pp][0];
+                float kk[J], vv[J];
+                if constexpr (J % 4 == 0) {   // head_dim 128: 16-byte pieces
+#pragma unroll
+                    for (int j = 0; j < J; j += 4) {
+                        const float4 k4 = *reinterpret_cast<const float4 *>(kr + J * lane + j);
+                        const float4 v4 = *reinterpret_cast<const float4 *>(vr + J * lane + j);
+                        kk[j] = k4.x; kk[j + 1] = k4.y; kk[j + 2] = k4.z; kk[j + 3] = k4.w;
+                        vv[j] = v4.x; vv[j + 1] = v4.y; vv[j + 2] = v4.z; vv[j + 3] = v4.w;
+                    }
+                } else {                      // head_dim 64: 8-byte pieces
+                    static_assert(J == 2, "head_dim 64 or 128");
+                    const float2 k2 = *reinterpret_cast<const float2 *>(kr + J * lane);
+                    const float2 v2 = *reinterpret_cast<const float2 *>(vr + J * lane);
+                    kk[0] = k2.x; kk[1] = k2.y;
+                    vv[0] = v2.x; vv[1] = v2.y;
+                }
+                float d[G];
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    float t = 0.0f;
+#pragma unroll
+                    for (int j = 0; j < J; j++) t = __fmaf_rn(qr[g][j], kk[j], t);
+                    d[g] = t;
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+                    for (int g = 0; g < G; g++) d[g] += __shfl_xor_sync(0xffffffffu, d[g], off);
+#pragma unroll
+                for (int g = 0; g < G; g++) {
+                    const float sc = __fmul_rn(d[g], scale);
+                    const float m_new = fmaxf(m[g], sc);
+                    const float corr = expf(m[g] - m_new);   // exp(-inf) = 0 at the first position
+                    const float pe = expf(sc - m_new);
+                    l[g] = __fmaf_rn(l[g], corr, pe);
+#pragma unroll
+                    for (int j = 0; j < J; j++) o[g][j] = __fmaf_rn(pe, vv[j], __fmul_rn(o[g][j], corr));
+                    m[g] = m_new;
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&sm.empty[s]);
+        }
+        // this warp's state -> shared memory
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+#pragma unroll
+            for (int j = 0; j < J; j++) sm.wo[warp][g][J * lane + j] = o[g][j];
+            if (lane == 0) {
+                sm.wm[warp][g] = m[g];
+                sm.wl[warp][g] = l[g];
+            }
+        }
+    }
+    __syncthreads();
+    if (sm.abort) {
+        // copies still in flight land before the CTA exits (bounded)
+        if (tid == 0)
+            for (int i = max(0, ntiles - kDsStages); i < ntiles; i++)
+                mbar_wait_bounded(&sm.full[i % kDsStages], (i / kDsStages) & 1, nullptr);
+        __syncthreads();
+        return;
+    }
+    // ---- merge the warps (fixed warp order): M = max m_w, L = sum l_w e^(m_w - M), O likewise
+    const int64_t out_base = (int64_t)r * a.ldout + (int64_t)kvh * G * HD;
+    const int64_t slot = ((int64_t)r * a.kv_heads + kvh) * kAttnMaxSplit;
+    for (int o = tid; o < G * HD; o += kDsThreads) {
+        const int g = o / HD, dd = o % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kDsWarps; w++) M = fmaxf(M, sm.wm[w][g]);
+        float L = 0.0f, O = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kDsWarps; w++) {
+            const float e = sm.wl[w][g] > 0.0f ? expf(sm.wm[w][g] - M) : 0.0f;
+            L = __fmaf_rn(sm.wl[w][g], e, L);
+            O = __fmaf_rn(sm.wo[w][g][dd], e, O);
+        }
+        if (nsplit == 1) {
+            a.out[out_base + o] = __fdiv_rn(O, L);
+        } else {
+            __stcg(a.part_o + (slot + split) * (G * HD) + o, O);
+            if (dd == 0) {
+                __stcg(a.part_ml + ((slot + split) * G + g) * 2 + 0, M);
+                __stcg(a.part_ml + ((slot + split) * G + g) * 2 + 1, L);
+            }
+        }
+    }
+    if (nsplit == 1) return;
+    // ---- split partials: the last split to arrive merges them in split order
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned tk = atomicAdd(&a.tickets[(int64_t)r * a.kv_heads + kvh], 1u);
+        sm.last_flag = (tk == (unsigned)(nsplit - 1));
+    }
+    __syncthreads();
+    if (!sm.last_flag) return;
+    __threadfence();
+    for (int o = tid; o < G * HD; o += kDsThreads) {
+        const int g = o / HD;
+        float M = -INFINITY;
+        for (int sp = 0; sp < nsplit; sp++) M = fmaxf(M, __ldcg(a.part_ml + ((slot + sp) * G + g) * 2));
+        float L = 0.0f, O = 0.0f;
+        for (int sp = 0; sp < nsplit; sp++) {
+            const float w = expf(__ldcg(a.part_ml + ((slot + sp) * G + g) * 2) - M);
+            L = __fmaf_rn(__ldcg(a.part_ml + ((slot + sp) * G + g) * 2 + 1), w, L);
+            O = __fmaf_rn(__ldcg(a.part_o + (slot + sp) * (G * HD) + o), w, O);
+        }
+        a.out[out_base + o] = __fdiv_rn(O, L);
+    }
+    if (tid == 0) a.tickets[(int64_t)r * a.kv_heads + kvh] = 0u;
+}
+
+template <int HD, int G>
+int launch_attn_stream_g(const AttnArgs &a, cudaStream_t st) {
+    // the kernel splits a row's positions into at most kAttnMaxSplit runs of
+    // whole tiles, at least kDsMinChunk positions each: this bounds the grid
+    const int ysplit = std::max(1, std::min(kAttnMaxSplit, a.kv.max_pos / kDsMinChunk));
+    dim3 grid(a.kv_heads, ysplit, a.streams);
+    constexpr size_t smem = sizeof(DsSmem<HD, G>);
+    static bool attr_done[64] = {};  // per device, per instantiation
+    int dev = 0;
+    QORA_CUDA(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        QORA_CUDA(cudaFuncSetAttribute(k_attn_stream<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)smem));
+        attr_done[dev] = true;
+    }
+    return launch_ex(k_attn_stream<HD, G>, grid, dim3(kDsThreads), smem, st, 1u, a);
+}
+
+template <int HD>
+int launch_attn_stream_hd(const AttnArgs &a, cudaStream_t st) {
+    switch (a.heads / a.kv_heads) {
+        case 1: return launch_attn_stream_g<HD, 1>(a, st);
+        case 2: return launch_attn_stream_g<HD, 2>(a, st);
+        case 4: return launch_attn_stream_g<HD, 4>(a, st);
+    }
+    return set_error(QORA_ERR_UNSUPPORTED, "heads/kv_heads = %d", a.heads / a.kv_heads);
+}
+
+template <int HD, int G>
+int launch_prefill_attn_g(const AttnArgs &a, cudaStream_t st) {
+    constexpr int BQ = kPfM / G;
+    static bool attr_done[64] = {};
+    int dev = 0;
+    QORA_CUDA(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        QORA_CUDA(cudaFuncSetAttribute(k_prefill_attn<HD, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(PfSmem<HD>)));
+        attr_done[dev] = true;
+    }
+    dim3 grid((a.T + BQ - 1) / BQ, a.kv_heads, a.streams);
+    return launch_ex(k_prefill_attn<HD, G>, grid, dim3(kPfThreads), sizeof(PfSmem<HD>), st, 1u, a);
+}
+
+template <int HD>
+int launch_prefill_attn_hd(const AttnArgs &a, cudaStream_t st) {
+    switch (a.heads / a.kv_heads) {
+        case 1: return launch_prefill_attn_g<HD, 1>(a, st);
+        case 2: return launch_prefill_attn_g<HD, 2>(a, st);
+        case 4: return launch_prefill_attn_g<HD, 4>(a, st);
+    }
+    return set_error(QORA_ERR_UNSUPPORTED, "heads/kv_heads = %d", a.heads / a.kv_heads);
+}
+
 template <int HD>
 int launch_attn_hd(const AttnArgs &a, cudaStream_t st) {
     const int G = a.heads / a.kv_heads;
@@ -103,10 +649,30 @@ int launch_qkv_post(const AttnArgs &a, cudaStream_t st) {
     return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d", a.kv.head_dim);
 }
 
+// Caches of at least this many positions decode on the streamed kernel.
+constexpr int kStreamMinCapacity = 256;
+
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
     if (!a.preappended && a.T != 1)
         return set_error(QORA_ERR_INVALID, "fused append needs T == 1");
     if (a.streams * a.T <= 0) return QORA_OK;
+    // every pre-appended (prefill) run takes the tiled causal kernel, whatever
+    // its length: a row's bits then do not depend on how a prompt was split
+    // into prefill calls (prefix cache, generate_new.rs:320-322)
+    if (a.preappended && a.len && a.pos_static < 0 && a.len_static < 0) {
+        switch (a.kv.head_dim) {  // tiled causal prefill
+            case 64: return launch_prefill_attn_hd<64>(a, st);
+            case 128: return launch_prefill_attn_hd<128>(a, st);
+        }
+    }
+    // decode over a long cache: the streamed kernel (a short cache such as
+    // the predictor's, refilled every frame, keeps the per-tile kernel)
+    if (!a.preappended && a.kv.max_pos >= kStreamMinCapacity && a.pos_static < 0 && a.stable_len < 0) {
+        switch (a.kv.head_dim) {
+            case 64: return launch_attn_stream_hd<64>(a, st);
+            case 128: return launch_attn_stream_hd<128>(a, st);
+        }
+    }
     switch (a.kv.head_dim) {
         case 64: return launch_attn_hd<64>(a, st);
         case 128: return launch_attn_hd<128>(a, st);

@@ -212,7 +212,7 @@ int qora_ctx_check_device_error(qora_ctx *ctx, void *stream) {
         case kDevNaN: return set_error(QORA_ERR_INVALID, "device: NaN reached argmax/sampler");
         case kDevTimeout: return set_error(QORA_ERR_TIMEOUT, "device: bounded wait expired");
         case kDevF16Range:
-            return set_error(QORA_ERR_RANGE, "device: GEMV input value outside the f16 operand range");
+            return set_error(QORA_ERR_RANGE, "device: infinite GEMV input value on the tensor-core path");
     }
     return set_error(QORA_ERR_CUDA, "device error code %d", v);
 }

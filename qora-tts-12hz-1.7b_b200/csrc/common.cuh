@@ -72,7 +72,7 @@ enum DeviceError : int {
     kDevRange = 1,   // position past the RoPE table or KV capacity
     kDevNaN = 2,     // NaN logits reached an argmax / sampler
     kDevTimeout = 3, // bounded wait expired
-    kDevF16Range = 4,// an input row value outside the f16 range of the tensor-core GEMV operands
+    kDevF16Range = 4,// an infinite input row value reached the tensor-core GEMV operands
 };
 
 // ------------------------------------------------------------ device memory
@@ -167,6 +167,9 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t by
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
                  "r"(bytes)
                  : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // dst (this CTA's shared memory) <- src (global), `bytes` a multiple of 16,
 // both addresses 16-byte aligned; completion is signalled on `bar`.
@@ -371,6 +374,7 @@ struct EmbDev {
     const uint8_t *packed = nullptr;
     const __half *scl = nullptr;
     int64_t rows = 0, n = 0;
+    float absmax = 0.0f;  // bound on |row value|: 8 * the table's largest scale
 };
 
 }  // namespace qora

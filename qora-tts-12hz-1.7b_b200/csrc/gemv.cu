@@ -460,6 +460,13 @@ int launch_rmsnorm_rows(const float *x, const __half *gamma, int64_t n, int rows
 // max|scale| * 2^E <= 2^12, so every (q - 8) * scale * 2^E (|q - 8| <= 8) stays
 // within 2^15 in f16 while small scales move away from the f16 subnormals.
 // -1 when a scale is not finite or too large for the f16 operands.
+// Value of a finite, non-negative f16 bit pattern (exact).
+static float f16_magnitude(uint16_t mx) {
+    const int ex = mx >> 10;
+    return ex ? (1.0f + (float)(mx & 0x3FF) / 1024.0f) * std::ldexp(1.0f, ex - 15)
+              : (float)(mx & 0x3FF) * std::ldexp(1.0f, -24);
+}
+
 static int mma_scale_exponent(const qora_q4_host *parts, int nparts) {
     uint16_t mx = 0;  // |scale| bits: ordered like the values for finite f16
     for (int i = 0; i < nparts; i++) {
@@ -467,9 +474,7 @@ static int mma_scale_exponent(const qora_q4_host *parts, int nparts) {
         for (int64_t j = 0; j < cnt; j++) mx = std::max<uint16_t>(mx, parts[i].scales[j] & 0x7FFFu);
     }
     if (mx >= 0x7C00u) return -1;  // inf / NaN
-    const int ex = mx >> 10;
-    const float m = ex ? (1.0f + (float)(mx & 0x3FF) / 1024.0f) * std::ldexp(1.0f, ex - 15)
-                       : (float)(mx & 0x3FF) * std::ldexp(1.0f, -24);
+    const float m = f16_magnitude(mx);
     if (m == 0.0f) return 15;
     if (m > 4096.0f) return -1;
     int e = 15;
@@ -525,6 +530,10 @@ int upload_emb(const qora_q4_host &h, DevBuf &packed, DevBuf &scl, EmbDev &out) 
     out.scl = scl.as<__half>();
     out.rows = h.k;
     out.n = h.n;
+    uint16_t mx = 0;  // the largest |scale|: rows are scale * (q - 8), |q - 8| <= 8
+    const int64_t cnt = h.k * (h.n / kGroup);
+    for (int64_t j = 0; j < cnt; j++) mx = std::max<uint16_t>(mx, h.scales[j] & 0x7FFFu);
+    out.absmax = mx >= 0x7C00u ? INFINITY : 8.0f * f16_magnitude(mx);
     return QORA_OK;
 }
 

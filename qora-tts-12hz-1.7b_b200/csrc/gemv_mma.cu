@@ -14,7 +14,10 @@
 //     the top 8 significant bits and sb the 3-bit remainder; (q - 8) * sa and
 //     (q - 8) * sb are then exact f16 values (<= 11 and <= 6 significant bits),
 //     so A1 + A2 = 2^E (q - 8) scale exactly;
-//   * x is split as xh = f16(x), xl = f16(x - xh) (22 significant bits);
+//   * each input row is scaled by a power of two 2^e_r (its largest value
+//     over the CTA's K slice lands in [2^14, 2^15), so any magnitude fits
+//     the f16 operands) and split as xh = f16(x), xl = f16(x - xh) (22
+//     significant bits); the epilogue multiplies by 2^-e_r;
 //   * D = A1 [xh; xl] (one N = 64 MMA: the xh and xl products side by side)
 //     + A2 xh (A2 xl, ~2^-19 relative, is dropped); the epilogue adds the two
 //     halves and multiplies by 2^-E.
@@ -94,9 +97,6 @@ constexpr size_t kMmaSmem =
 static_assert(kOpBytes % 128 == 0 && kRawBytes % 16 == 0, "stage alignment");
 static_assert(kMmaRows == 32 && kConvWarps == kConvGroups * kMmaGroups, "one converter warp per column group");
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
 // 16-byte asynchronous copy global -> shared (L2 only), both addresses 16-byte aligned.
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
@@ -154,6 +154,15 @@ __device__ __forceinline__ void cluster_wait() {
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
 }
 
+// Exponent e for which m * 2^e lies in [2^14, 2^15) (m > 0 finite; the
+// result is clamped to [-100, 100], so 2^e and 2^-e are normal floats);
+// 0 for m == 0 or a non-finite m.
+__device__ __forceinline__ int operand_exponent(float m) {
+    if (!(m > 0.0f) || !(m <= 3.4e38f)) return 0;
+    const int ex = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;  // floor(log2 m); subnormal: -127
+    return max(-100, min(100, 14 - ex));
+}
+
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
@@ -169,6 +178,8 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
     __shared__ __align__(8) uint64_t op_full[kOpStages], op_empty[kOpStages], d_full, recv_full;
     __shared__ uint32_t tmem_slot;
     __shared__ float inv_s[kMmaRows];
+    __shared__ int rexp_s[kMmaRows];      // B operand of row r is x * 2^rexp_s[r]
+    __shared__ float red_s[kConvWarps];
     __shared__ int abort_s;
     __shared__ int last_flag;
 
@@ -329,6 +340,13 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
         if (S > 1) cluster_wait();
     } else {
         // ---------------------------------------------------------- converters
+        float gmax = 0.0f;
+        if constexpr (XM == X_RMSNORM) {
+            // gamma is immutable: its largest magnitude over this CTA's K slice
+            // is known before the previous kernel is done
+            for (int i = threadIdx.x; i < nst * kStageK; i += kConvWarps * 32)
+                gmax = fmaxf(gmax, fabsf(__half2float(a.gamma[(int64_t)t_begin * kStageK + i])));
+        }
         griddep_launch_dependents();
         griddep_wait();
         const int64_t k = a.w.k;
@@ -343,6 +361,55 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
                 t = warp_sum(t);
                 if (lane == 0) inv_s[rr] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
             }
+        }
+        // ---- per-row power-of-two scale of the B operand: the row's values
+        // over this CTA's K slice are multiplied by 2^e (exact) so that the
+        // largest lies in [2^14, 2^15): no value can leave the f16 range and
+        // small ones keep the precision of the hi / lo split.  The epilogue
+        // multiplies by 2^-e (exact), so in-range inputs give the same bits
+        // as without the scale.  Bound of the row's largest value:
+        //   X_PLAIN   max |x| over the slice, read here (8 threads per row);
+        //   X_RMSNORM sqrt(k) * max |gamma|: a normalised row has
+        //             sum (x * inv)^2 <= k, so |x * inv| <= sqrt(k);
+        //   X_EMBED   8 * the table's largest scale (set at upload).
+        {
+            const int rr = threadIdx.x >> 3, part = threadIdx.x & 7;
+            float m = 0.0f;
+            if constexpr (XM == X_PLAIN) {
+                if (r_begin + rr < r_end) {
+                    // eight 16-byte loads in flight per thread (the row's 8
+                    // threads read 128 contiguous bytes per step), so a slice
+                    // of up to 256 values costs one round trip, overlapped
+                    // with the producer's first stage
+                    const float4 *xr = reinterpret_cast<const float4 *>(
+                        a.x + (int64_t)(r_begin + rr) * a.ldx + (int64_t)t_begin * kStageK);
+                    const int n4 = nst * (kStageK / 4);
+                    for (int i0 = part; i0 < n4; i0 += 64) {
+                        float4 v[8];
+#pragma unroll
+                        for (int u = 0; u < 8; u++)
+                            v[u] = i0 + 8 * u < n4 ? __ldcg(xr + i0 + 8 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+                        for (int u = 0; u < 8; u++)
+                            m = fmaxf(m, fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)),
+                                               fmaxf(fabsf(v[u].z), fabsf(v[u].w))));
+                    }
+                }
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+                m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+            } else if constexpr (XM == X_RMSNORM) {
+                gmax = warp_max(gmax);
+                if (lane == 0) red_s[warp] = gmax;
+                asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
+#pragma unroll
+                for (int w = 0; w < kConvWarps; w++) m = fmaxf(m, red_s[w]);
+                // (1 + 2^-10) covers the rounding of inv and of the products
+                m = __fmul_rn(__fmul_rn(__fsqrt_rn((float)k), m), 1.0009765625f);
+            } else {
+                m = a.emb.absmax;
+            }
+            if (part == 0) rexp_s[rr] = (r_begin + rr < r_end) ? operand_exponent(m) : 0;
             asm volatile("bar.sync 1, %0;" ::"n"(kConvWarps * 32) : "memory");
         }
         // Converter group cgp = warp / 4 takes stages t = cgp, cgp + 2, ...
@@ -371,6 +438,7 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
         }
         float inv_r = 1.0f;
         if constexpr (XM == X_RMSNORM) inv_r = inv_s[r];
+        const float rscale = __int_as_float((127 + rexp_s[r]) << 23);
 
         for (int t = cgp; t < nst; t += kConvGroups) {
             const int b = t % kRawStages, o = t % kOpStages;
@@ -444,7 +512,10 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
             uint32_t bh[4], bl[4];
             bool big = false;
 #pragma unroll
+            for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(xv[i], rscale);  // exact: a power of two
+#pragma unroll
             for (int i = 0; i < 4; i++) {
+                // after the scale only an infinite input can exceed the range
                 big |= fabsf(xv[2 * i]) > 65504.0f || fabsf(xv[2 * i + 1]) > 65504.0f;
                 const __half2 hh = __floats2half2_rn(xv[2 * i], xv[2 * i + 1]);
                 const float2 hf = __half22float2(hh);
@@ -481,7 +552,9 @@ __global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
             }
             const float unscale = __int_as_float((127 - E) << 23);
 #pragma unroll
-            for (int n = 0; n < kMmaRows; n++) vh[n] = __fmul_rn(__fadd_rn(vh[n], vl[n]), unscale);
+            for (int n = 0; n < kMmaRows; n++)
+                vh[n] = __fmul_rn(__fmul_rn(__fadd_rn(vh[n], vl[n]), unscale),
+                                  __int_as_float((127 - rexp_s[n]) << 23));
             const int cc2 = (EM == E_SWIGLU) ? (g >> 1) : g;
             const int hp = (EM == E_SWIGLU) ? (g & 1) : 0;
             if (S > 1) cluster_wait();  // every rank's mbarriers are initialised

@@ -199,7 +199,7 @@ static int run_layer(Launcher &ln, const LayerDev &ld, int H, int heads, int kvh
     at.part_ml = w.apml.as<float>();
     at.tickets = w.atk.as<unsigned>();
     at.err = ln.ctx->err.as<int>();
-    if (T > 1) {
+    if (T > 1 || ln.fixed) {  // prefill (any length): append first, then the causal kernel
         QORA_TRY(launch_qkv_post(at, ln.st));
         ln.count++;
         at.preappended = true;

@@ -130,3 +130,92 @@ def test_full_size_frames_match_oracle(E, ctx, orc, hd):
     om.t, om.p = om.m.talker_struct(), om.m.predictor_struct()
     _run(E, orc, ctx, cfg, tw, pw, om, T=16, F=3, persistent=True, seed=800,
          check_logits=_full_check)
+
+
+def _follow(E, orc, ctx, cfg, tw, pw, om, B, T, F, seed, graph):
+    """The engine's frame loop for B streams against the oracle teacher-forced
+    with the engine's own codes (generate_new.rs:606-665 step by step):
+      - code 0 must equal the oracle's sample_token (generate_new.rs:771-862)
+        drawn from the engine's own logits, previous codes and RNG state (the
+        sampler exactly), and the RNG states must agree after the draw;
+      - codes 1..15 must agree with the oracle's greedy argmax of its own
+        predictor logits (code_predictor.rs:218-273) fed the engine's codes,
+        >= 99.5 % of them (near-ties may flip);
+      - the talker logits after the step (forward_with_embedding on
+        E_talker[c0] + acoustic sum + text) within max-abs 2e-3 / rel 1e-3 of
+        the oracle's.
+    Following the engine keeps a legitimate near-tie from derailing the rest."""
+    import torch
+    talker = E.Talker(ctx, tw, max_batch=B)
+    pred = E.CodePredictor(ctx, pw, max_batch=B)
+    eng = E.Engine(talker, pred, B, max_pos=T + F + 4)
+    if graph:
+        eng.use_graph(True)
+    H = cfg.t_hidden
+    xs = np.stack([orc.synth_normal(seed + b, 1.0, T * H).reshape(T, H) for b in range(B)])
+    seeds = [seed + 100 + b for b in range(B)]
+    eng.prefill(xs, seeds)
+    texts = orc.synth_normal(seed + 200, 1.0, B * H).reshape(B, H)
+    params = orc.SampleParams(0.9, 50, 1.0, 1.05)
+    okv = [om.talker_kv(T + F + 4) for _ in range(B)]
+    pkv = om.predictor_kv()
+    hid = [om.talker_prefill(xs[b], okv[b], 0) for b in range(B)]
+    codes = torch.zeros(B, 16, dtype=torch.int32, device="cuda")
+    text_d = _cuda(texts)
+    worst_abs, worst_rel, agree, total = 0.0, 0.0, 0, 0
+    for f in range(F):
+        before = eng.state()
+        eng.frame(text_d, codes)
+        after = eng.state()
+        got = codes.cpu().numpy().astype(np.uint32)
+        glog = after["logits"].cpu().numpy()
+        for b in range(B):
+            lg0 = before["logits"].cpu().numpy()[b]
+            prev = before["prev"].cpu().numpy()[b].astype(np.uint32)
+            rng0 = int(before["rng"].cpu().numpy()[b]) & 0xFFFFFFFFFFFFFFFF
+            tok, rng1 = orc.sample_token(lg0, params, prev, rng0)
+            assert tok == got[b, 0], (f, b, tok, got[b, 0])
+            assert rng1 == int(after["rng"].cpu().numpy()[b]) & 0xFFFFFFFFFFFFFFFF
+            sem = om.embed_codec(int(got[b, 0]))
+            rc, _ = om.predictor_frame(hid[b], sem, pkv, forced=got[b, 1:])
+            agree += int(np.sum(rc == got[b, 1:]))
+            total += cfg.p_groups
+            emb = sem + om.acoustic_sum(got[b, 1:]) + texts[b]
+            hid[b], rl = om.talker_step(emb, okv[b], T + f)
+            err = float(np.max(np.abs(glog[b].astype(np.float64) - rl)))
+            worst_abs = max(worst_abs, err)
+            worst_rel = max(worst_rel, err / float(np.max(np.abs(rl))))
+            assert after["prev"].cpu().numpy()[b].astype(np.uint32).tolist() == got[b].tolist()
+        assert after["positions"].cpu().numpy().tolist() == [T + f + 1] * B
+    ctx.check_device_error()
+    print(f"B={B} frames={F}: worst abs {worst_abs:.3e} rel {worst_rel:.3e} "
+          f"predictor argmax {agree}/{total}")
+    assert worst_abs <= ABS_TOL and worst_rel <= REL_TOL
+    assert agree / total >= 0.995
+    return eng
+
+
+def _full_model(orc, hd=128):
+    import qora_b200
+    from test_gpu_full import _oracle_from
+    cfg = qora_b200.ModelConfig(t_max_pos=256, p_head_dim=hd)
+    tw, pw = qora_b200.synth_talker(cfg), qora_b200.synth_predictor(cfg)
+    om = orc.OracleModel.__new__(orc.OracleModel)
+    om.m = _oracle_from(orc, cfg, tw, pw)
+    om.t, om.p = om.m.talker_struct(), om.m.predictor_struct()
+    return cfg, tw, pw, om
+
+
+def test_full_size_64_frames_follow_oracle(E, ctx, orc):
+    """Batch 1 at 1.7B dims for 64 frames: one persistent-kernel launch per frame."""
+    cfg, tw, pw, om = _full_model(orc)
+    eng = _follow(E, orc, ctx, cfg, tw, pw, om, B=1, T=16, F=64, seed=810, graph=False)
+    assert eng.kernels_per_frame() == 1
+
+
+def test_full_size_batch32_frames_follow_oracle(E, ctx, orc):
+    """Batch 32 at 1.7B dims for 8 frames: the per-op kernels (tensor-core
+    GEMVs for every 32-row projection) captured in one CUDA graph per frame."""
+    cfg, tw, pw, om = _full_model(orc)
+    eng = _follow(E, orc, ctx, cfg, tw, pw, om, B=32, T=16, F=8, seed=820, graph=True)
+    assert eng.kernels_per_frame() > 100

@@ -7,8 +7,10 @@ forward_with_embedding, talker.rs:263-360).  Logits are compared at every
 step: max-abs <= 2e-3, relative (max-abs / max |logit|) <= 1e-3, and >= 99.5 %
 greedy-argmax agreement.
 
-Config 2: code predictor frames at head_dim 64 (BASELINE) and
-128 (the reference's config.json), teacher-forced, same logit tolerances.
+Config 2: all 512 code-predictor frames at head_dim 64
+(BASELINE) and 128 (the reference's config.json), batch 1, teacher-forced on
+the oracle's codes, same logit tolerances; code 0 per frame from xorshift64
+(seed 7) mod 2048, talker hidden N(0,1) from seed 7 + frame.
 """
 import numpy as np
 import pytest
@@ -17,6 +19,7 @@ pytestmark = pytest.mark.gpu
 
 ABS_TOL = 2e-3
 REL_TOL = 1e-3
+FRAMES2 = 512   # config 2: 512 predictor frames
 
 
 @pytest.fixture(scope="module")
@@ -123,7 +126,7 @@ def test_config2_predictor_teacher_forced(E, ctx, orc, hd):
     semtab = qora_b200.synth_q4(cfg.seed * 1000 + 900, cfg.sigma, cfg.t_vocab, cfg.t_hidden)
     st = 7
     worst_abs, worst_rel, agree, total = 0.0, 0.0, 0, 0
-    for frame in range(6):
+    for frame in range(FRAMES2):
         hid = orc.synth_normal(7 + frame, 1.0, cfg.t_hidden)
         st ^= (st << 13) & 0xFFFFFFFFFFFFFFFF
         st ^= st >> 7

@@ -190,15 +190,42 @@ def test_batched_tensor_core_is_deterministic(E, ctx, orc):
     assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
 
 
-def test_batched_input_outside_f16_range_is_an_error(E, ctx, orc):
-    # the tensor-core operands hold inputs in f16 (hi/lo halves): a value past
-    # the f16 range is reported instead of silently overflowing
+@pytest.mark.parametrize("k,n", [(2048, 1024), (6144, 2048)])
+def test_batched_any_input_range(E, ctx, orc, k, n):
+    """The tensor-core operands are f16 halves of each row scaled by a power of
+    two chosen per row, so activation outliers (|x| up to 1e5, past the f16
+    range) and rows of tiny values (|x| < 2^-14, f16 subnormals unscaled) keep
+    the 1e-4-of-scale bound, each row against its own output scale."""
+    import ctypes
+    import torch
+    rows = 16
+    w = orc.synth_q4(630 + k, 0.02, k, n)
+    x = orc.synth_normal(631 + k, 1.0, rows * k).reshape(rows, k)
+    x[3, 100] = 1.0e5                     # one outlier in a normal row
+    x[3, 7] = -7.5e4
+    x[5] *= 1.0e5                         # a whole row of large values
+    x[9] *= 2.0e-6                        # a row of values below 2^-14
+    x[11, ::3] = 0.0                      # zeros (skipped rows of the weight)
+    x[12] = 0.0                           # an all-zero row
+    got = _dev(E, ctx, w.packed, w.scales, k, n).gemv(torch.from_numpy(x).cuda()).cpu().numpy()
+    ctx.check_device_error()              # no range error
+    ref = np.zeros((rows, n), np.float32)
+    ws = w.cstruct()
+    orc.lib().oq_gemm(orc.ptr(x), rows, ctypes.addressof(ws), orc.ptr(ref))
+    for r in range(rows):
+        scale = float(np.max(np.abs(ref[r])))
+        err = float(np.max(np.abs(got[r].astype(np.float64) - ref[r])))
+        assert err <= 1e-4 * scale or (scale == 0.0 and err == 0.0), (r, err, scale)
+
+
+def test_batched_infinite_input_is_an_error(E, ctx, orc):
+    # an infinite input has no finite scale: reported instead of propagating silently
     import torch
     from qora_b200 import _lib
     k, n, rows = 1024, 1024, 8
     w = orc.synth_q4(620, 0.02, k, n)
     x = orc.synth_normal(621, 1.0, rows * k).reshape(rows, k)
-    x[3, 100] = 1.0e6
+    x[3, 100] = np.inf
     _dev(E, ctx, w.packed, w.scales, k, n).gemv(torch.from_numpy(x).cuda())
     with pytest.raises(_lib.QoraError) as ei:
         ctx.check_device_error()
