@@ -570,9 +570,27 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
                 }
                 const uint4 *nb = reinterpret_cast<const uint4 *>(S.nib[slot]);
                 const __half *sb = reinterpret_cast<const __half *>(S.scl[slot]);
-                for (int lr = tid; ok && lr < rows; lr += kNT) {
-                    const float x75 = __fmul_rn(xs[c0 + lr], 37778931862957161709568.0f);
-                    row_fma(acc, ssum, __fmul_rn(__half2float(sb[lr]), x75), nb[lr]);
+                int lr = tid;
+                if (ok) {
+                    // four rows' operands loaded before their FMAs (the
+                    // thread's rows in the same order: the same bits)
+                    for (; lr + 3 * kNT < rows; lr += 4 * kNT) {
+                        float xv[4], sv[4];
+                        uint4 wv[4];
+#pragma unroll
+                        for (int u = 0; u < 4; u++) {
+                            xv[u] = xs[c0 + lr + u * kNT];
+                            sv[u] = __half2float(sb[lr + u * kNT]);
+                            wv[u] = nb[lr + u * kNT];
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; u++)
+                            row_fma(acc, ssum, __fmul_rn(sv[u], __fmul_rn(xv[u], 37778931862957161709568.0f)), wv[u]);
+                    }
+                    for (; lr < rows; lr += kNT) {
+                        const float x75 = __fmul_rn(xs[c0 + lr], 37778931862957161709568.0f);
+                        row_fma(acc, ssum, __fmul_rn(__half2float(sb[lr]), x75), nb[lr]);
+                    }
                 }
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&S.empty[slot]);

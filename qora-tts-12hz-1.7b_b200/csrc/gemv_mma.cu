@@ -167,7 +167,7 @@ __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<ui
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
 template <int XM, int EM>
-__global__ void __launch_bounds__(kMmaThreads, 2) k_gemv_mma(const GemvArgs a) {
+__global__ void __maxnreg__(80) k_gemv_mma(const GemvArgs a) {
     constexpr int CO = (EM == E_SWIGLU) ? kMmaGroups / 2 : kMmaGroups;  // output groups per CTA
     constexpr int P = (EM == E_SWIGLU) ? 2 : 1;      // partials per output (gate, up)
     constexpr int RC = kMmaRows * CO / kUnits;       // rows per reduction unit (8, or 4 for SwiGLU)
