@@ -169,6 +169,23 @@ int qora_rope_tables_host(int32_t head_dim, int32_t max_pos, double theta,
  * [stream][kv_head][max_pos][head_dim] f32, plus a length per stream. */
 int qora_kv_create(qora_ctx *ctx, int32_t num_layers, int32_t kv_heads, int32_t head_dim,
                    int32_t max_pos, int32_t streams, qora_kv **out);
+/* RawKvCache / empty_kv_cache (gemv.rs:75-86) with paged storage: where the
+ * reference grows one Vec per layer as positions append, a paged cache draws
+ * fixed pages from a pool preallocated here: pool_pages pages of
+ * page_positions positions (a power of two >= 32) each, a page holding those
+ * positions for every layer and kv head.  A stream's pages are mapped from
+ * the pool as the entry points append to it (QORA_ERR_OOM, before any
+ * launch, when the pool is exhausted) and go back by qora_kv_reset;
+ * qora_kv_copy_stream between paged caches with the same page size shares
+ * the source's full pages instead of copying them (prefix snapshot,
+ * generate_new.rs:317-355).  max_pos bounds each stream's length.  Every
+ * entry point that takes a qora_kv accepts a paged one except
+ * qora_kv_layer_ptrs (no slab to point at). */
+int qora_kv_create_paged(qora_ctx *ctx, int32_t num_layers, int32_t kv_heads, int32_t head_dim,
+                         int32_t max_pos, int32_t streams, int32_t page_positions,
+                         int32_t pool_pages, qora_kv **out);
+/* Pages of a paged cache referenced by at least one stream, and free pages. */
+int qora_kv_pages_host(const qora_kv *kv, int32_t *mapped, int32_t *free_pages);
 void qora_kv_destroy(qora_kv *kv);
 /* Clear streams (code_predictor.rs:227-231).  ids_host NULL => all streams. */
 int qora_kv_reset(qora_kv *kv, const int32_t *ids_host, int32_t count, void *stream);

@@ -107,6 +107,10 @@ extern "C" {
 
     pub fn qora_kv_create(ctx: *mut qora_ctx, num_layers: i32, kv_heads: i32, head_dim: i32,
                           max_pos: i32, streams: i32, out: *mut *mut qora_kv) -> c_int;
+    pub fn qora_kv_create_paged(ctx: *mut qora_ctx, num_layers: i32, kv_heads: i32, head_dim: i32,
+                                max_pos: i32, streams: i32, page_positions: i32, pool_pages: i32,
+                                out: *mut *mut qora_kv) -> c_int;
+    pub fn qora_kv_pages_host(kv: *const qora_kv, mapped: *mut i32, free_pages: *mut i32) -> c_int;
     pub fn qora_kv_destroy(kv: *mut qora_kv);
     pub fn qora_kv_reset(kv: *mut qora_kv, ids: *const i32, count: i32,
                          stream: *mut c_void) -> c_int;

@@ -54,12 +54,12 @@ __global__ void __launch_bounds__(kThreads) k_qkv_post(const AttnArgs a) {
         } else if (it < a.heads + a.kv_heads) {
             const int h = it - a.heads;
             norm_rope_head<HD>(v, a.k_gamma, cr, sr, true, lane);
-            float *dst = a.kv.k + (((int64_t)b * a.kv_heads + h) * a.kv.max_pos + L0 + t) * HD;
+            float *dst = a.kv.k + a.kv.row(b, h, L0 + t);
 #pragma unroll
             for (int j = 0; j < J; j++) dst[lane + 32 * j] = v[j];
         } else {
             const int h = it - a.heads - a.kv_heads;
-            float *dst = a.kv.v + (((int64_t)b * a.kv_heads + h) * a.kv.max_pos + L0 + t) * HD;
+            float *dst = a.kv.v + a.kv.row(b, h, L0 + t);
 #pragma unroll
             for (int j = 0; j < J; j++) dst[lane + 32 * j] = v[j];
         }
@@ -128,18 +128,19 @@ __global__ void __launch_bounds__(kPfThreads, 2) k_prefill_attn(const AttnArgs a
     if (nq <= 0) return;
     const int kend = L0 + t0 + nq;  // keys [0, kend) are visible to some row of the block
     const int ntiles = (kend + kPfBK - 1) / kPfBK;
-    const float *kbase = a.kv.k + ((int64_t)b * a.kv_heads + h) * a.kv.max_pos * HD;
-    const float *vbase = a.kv.v + ((int64_t)b * a.kv_heads + h) * a.kv.max_pos * HD;
-
     auto load_tile = [&](int kt, int buf) {
         const int k0 = kt * kPfBK;
+        // a tile starts at a multiple of kPfBK, which divides the page size:
+        // its rows are one contiguous block of the cache
+        const float *kbase = a.kv.k + a.kv.row(b, h, k0);
+        const float *vbase = a.kv.v + a.kv.row(b, h, k0);
         for (int i = tid; i < kPfBK * D4; i += kPfThreads) {
             const int n = i / D4, d4 = i % D4;
             float *kd = &sm.k[buf][n][4 * d4];
             float *vd = &sm.v[buf][n][4 * d4];
             if (k0 + n < kend) {
-                pf_cp16(kd, kbase + (int64_t)(k0 + n) * HD + 4 * d4);
-                pf_cp16(vd, vbase + (int64_t)(k0 + n) * HD + 4 * d4);
+                pf_cp16(kd, kbase + (int64_t)n * HD + 4 * d4);
+                pf_cp16(vd, vbase + (int64_t)n * HD + 4 * d4);
             } else {  // never visible: zeros (unwritten cache memory may hold anything)
                 *reinterpret_cast<float4 *>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
                 *reinterpret_cast<float4 *>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -372,9 +373,6 @@ __global__ void __launch_bounds__(kDsThreads, 2) k_attn_stream(const AttnArgs a)
         if (tid == 0 && split == 0 && kvh == 0) raise_error(a.err, kDevRange);
         return;
     }
-    float *krow_base = a.kv.k + ((int64_t)b * a.kv_heads + kvh) * a.kv.max_pos * HD;
-    float *vrow_base = a.kv.v + ((int64_t)b * a.kv_heads + kvh) * a.kv.max_pos * HD;
-
     if (warp == kDsWarps) {
         // ------------------------------------------------------ producer
         // tile i: positions [p0 + i TP, ..), its cached rows (< L0) by bulk copy
@@ -391,9 +389,9 @@ __global__ void __launch_bounds__(kDsThreads, 2) k_attn_stream(const AttnArgs a)
                 const int nrow = max(0, min(min(t0 + TP, p1), L0) - t0);
                 const uint32_t bytes = (uint32_t)nrow * HD * 4;
                 mbar_arrive_expect_tx(&sm.full[s], 2 * bytes);
-                if (bytes) {
-                    bulk_g2s(&sm.k[s][0][0], krow_base + (int64_t)t0 * HD, bytes, &sm.full[s]);
-                    bulk_g2s(&sm.v[s][0][0], vrow_base + (int64_t)t0 * HD, bytes, &sm.full[s]);
+                if (bytes) {  // t0 is a multiple of TP, which divides the page size
+                    bulk_g2s(&sm.k[s][0][0], a.kv.k + a.kv.row(b, kvh, t0), bytes, &sm.full[s]);
+                    bulk_g2s(&sm.v[s][0][0], a.kv.v + a.kv.row(b, kvh, t0), bytes, &sm.full[s]);
                 }
             }
         }
@@ -416,16 +414,18 @@ __global__ void __launch_bounds__(kDsThreads, 2) k_attn_stream(const AttnArgs a)
                 for (int j = 0; j < J; j++) sm.q[it][lane + 32 * j] = v[j];
             } else if (it == G) {
                 norm_rope_head<HD>(v, a.k_gamma, cr, sr, true, lane);
+                float *dst = a.kv.k + a.kv.row(b, kvh, L0);
 #pragma unroll
                 for (int j = 0; j < J; j++) {
                     sm.newk[lane + 32 * j] = v[j];
-                    krow_base[(int64_t)L0 * HD + lane + 32 * j] = v[j];
+                    dst[lane + 32 * j] = v[j];
                 }
             } else {
+                float *dst = a.kv.v + a.kv.row(b, kvh, L0);
 #pragma unroll
                 for (int j = 0; j < J; j++) {
                     sm.newv[lane + 32 * j] = v[j];
-                    vrow_base[(int64_t)L0 * HD + lane + 32 * j] = v[j];
+                    dst[lane + 32 * j] = v[j];
                 }
             }
         }

@@ -5,11 +5,29 @@
 
 namespace qora {
 
-// Layer view of the KV cache: [stream][kv_head][max_pos][head_dim] f32.
+// Layer view of the KV cache (f32 rows of head_dim values).
+//   slab (table == nullptr): [stream][kv_head][max_pos][head_dim] from k / v;
+//   paged: a physical page holds 2^page_shift consecutive positions of every
+//   layer and kv head ([layer][kv_head][page_pos][head_dim], page_elems
+//   floats; k / v point at this layer's part of page 0), and logical page j
+//   of stream b lives in physical page table[b * table_stride + j].
+// Within one page (or a slab) a kv head's rows are contiguous, so any run of
+// positions that does not cross a multiple of the page size is one block.
 struct KVLayer {
     float *k = nullptr;
     float *v = nullptr;
     int kv_heads = 0, head_dim = 0, max_pos = 0;
+    const int *table = nullptr;
+    int table_stride = 0, page_shift = 0;
+    int64_t page_elems = 0;
+
+    // Element offset (from k / v) of position p of (stream b, kv head h).
+    __host__ __device__ __forceinline__ int64_t row(int b, int h, int p) const {
+        if (!table) return (((int64_t)b * kv_heads + h) * max_pos + p) * head_dim;
+        const int pg = table[(int64_t)b * table_stride + (p >> page_shift)];
+        return (int64_t)pg * page_elems +
+               ((int64_t)(h << page_shift) + (p & ((1 << page_shift) - 1))) * head_dim;
+    }
 };
 
 struct alignas(16) AttnArgs {

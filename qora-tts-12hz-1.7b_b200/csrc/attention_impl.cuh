@@ -140,8 +140,9 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
     const int p0 = split * chunk;
     const int p1 = min(Lq, p0 + chunk);
 
-    const float *krow_base = a.kv.k + ((int64_t)b * a.kv_heads + kvh) * a.kv.max_pos * HD;
-    const float *vrow_base = a.kv.v + ((int64_t)b * a.kv_heads + kvh) * a.kv.max_pos * HD;
+    // row p of this (stream, kv head) in the cache (slab or paged)
+    auto krow = [&](int p) { return a.kv.k + a.kv.row(b, kvh, p); };
+    auto vrow = [&](int p) { return a.kv.v + a.kv.row(b, kvh, p); };
     const float *row = a.qkv + (int64_t)r * a.ldqkv;
 
     // ---- prologue: query heads (normed + roped unless pre-appended), append
@@ -169,11 +170,11 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
         staged0 = (pre0 == old0);
         for (int i = tid; i < pre0 * (HD / 4); i += NT) {
             const int pp = i / (HD / 4), d4 = i % (HD / 4);
-            attn_cp_async16(&v_s[pp][4 * d4], vrow_base + (int64_t)(p0 + pp) * HD + 4 * d4);
+            attn_cp_async16(&v_s[pp][4 * d4], vrow(p0 + pp) + 4 * d4);
         }
         for (int i = tid; i < pre0 * HD; i += NT) {
             const int pp = i / HD, d = i % HD;
-            attn_cp_async4(&kt_s[d][pp], krow_base + (int64_t)(p0 + pp) * HD + d);
+            attn_cp_async4(&kt_s[d][pp], krow(p0 + pp) + d);
         }
         for (int it = warp; it < G + 2; it += NT / 32) {
             if (it >= G && !appender) continue;
@@ -213,7 +214,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
                 for (int j = 0; j < J; j++) q_s[it][lane + 32 * j] = v[j];
             } else if (it == G) {
                 norm_rope_head_pre<HD>(v, gv, cv, sv);
-                float *dst = const_cast<float *>(krow_base) + (int64_t)(L0 + t) * HD;
+                float *dst = krow(L0 + t);
 #pragma unroll
                 for (int j = 0; j < J; j++) dst[lane + 32 * j] = v[j];
                 if (in_tile0) {
@@ -221,7 +222,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
                     for (int j = 0; j < J; j++) kt_s[lane + 32 * j][nt] = v[j];
                 }
             } else {
-                float *dst = const_cast<float *>(vrow_base) + (int64_t)(L0 + t) * HD;
+                float *dst = vrow(L0 + t);
 #pragma unroll
                 for (int j = 0; j < J; j++) dst[lane + 32 * j] = v[j];
                 if (in_tile0) {
@@ -252,8 +253,8 @@ __device__ __forceinline__ void attn_item(const AttnArgs &a, int kvh, int split,
             const int pp = i / (HD / 4), d4 = i % (HD / 4);
             float4 k4 = make_float4(0.f, 0.f, 0.f, 0.f), v4 = make_float4(0.f, 0.f, 0.f, 0.f);
             if (pp < cnt) {
-                k4 = __ldcg(reinterpret_cast<const float4 *>(krow_base + (int64_t)(base + pp) * HD) + d4);
-                v4 = __ldcg(reinterpret_cast<const float4 *>(vrow_base + (int64_t)(base + pp) * HD) + d4);
+                k4 = __ldcg(reinterpret_cast<const float4 *>(krow(base + pp)) + d4);
+                v4 = __ldcg(reinterpret_cast<const float4 *>(vrow(base + pp)) + d4);
             }
             kt_s[4 * d4 + 0][pp] = k4.x;
             kt_s[4 * d4 + 1][pp] = k4.y;

@@ -80,7 +80,11 @@ extern "C" int qora_kv_attend(qora_kv *kv, int32_t layer, const float *qkv, int3
     at.part_ml = kv->attn_pml.as<float>();
     at.tickets = kv->attn_tk.as<unsigned>();
     cudaStream_t st = as_stream(stream);
+    QORA_TRY(kv_prepare(kv, 0, B, 1, st));  // the append at each stream's length
     QORA_TRY(launch_attention(at, st));
-    if (advance) QORA_TRY(kv_advance(kv, B, st));
+    if (advance) {
+        QORA_TRY(kv_advance(kv, B, st));
+        kv_note_growth(kv, 0, B, 1);
+    }
     return QORA_OK;
 }

@@ -93,8 +93,12 @@ extern "C" int qora_kv_attend_noalloc(qora_kv *kv, int32_t layer, const float *q
     at.part_ml = base + kNaPartO;
     at.tickets = reinterpret_cast<unsigned *>(base + kNaPartO + kNaPartML);
     cudaStream_t st = as_stream(stream);
+    QORA_TRY(kv_prepare(kv, 0, B, 1, st));  // paged caches: the append at each stream's length
     QORA_CUDA(cudaMemsetAsync(at.tickets, 0, tk * sizeof(unsigned), st));
     QORA_TRY(launch_attention(at, st));
-    if (advance) QORA_TRY(kv_advance(kv, B, st));
+    if (advance) {
+        QORA_TRY(kv_advance(kv, B, st));
+        kv_note_growth(kv, 0, B, 1);
+    }
     return QORA_OK;
 }

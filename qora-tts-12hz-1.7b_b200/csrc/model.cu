@@ -49,29 +49,46 @@ __global__ void k_fill_i32(int *p, int count, int v) {
     if (i < count) p[i] = v;
 }
 
-// Prefix snapshot / restore (generate_new.rs:317-355): rows [0, len) of one
-// source stream, every (layer, kv head), into `ndst` destination streams
+// Prefix snapshot / restore (generate_new.rs:317-355): rows [row0, len) of
+// one source stream, every (layer, kv head), into `ndst` destination streams
 // dst0.., and their lengths.  Only the source's live rows move; the source
-// length is read on the device, so the copy needs no host round trip.
-// grid (layers * kvh, ndst, row chunks); K and V rows are head_dim floats.
-__global__ void k_kv_copy_rows(const float *sk, const float *sv, size_t s_layer, size_t s_base,
-                               int s_max_pos, float *dk, float *dv, size_t d_layer, int d_max_pos,
-                               int dst0, int kvh, int hd, const int *src_len, int *dst_len) {
+// length is read on the device, so the copy needs no host round trip.  Both
+// caches are addressed through their layer views (slab or paged; layer l's
+// rows sit `step` elements after layer 0's).  grid (layers * kvh, ndst, row
+// chunks); K and V rows are head_dim floats.
+__global__ void k_kv_copy_rows(KVLayer src, int64_t src_step, KVLayer dst, int64_t dst_step, int dst0,
+                               int kvh, int hd, int row0, const int *src_len, int *dst_len) {
     griddep_launch_dependents();
     griddep_wait();
     const int l = blockIdx.x / kvh, h = blockIdx.x % kvh;
     const int ds = dst0 + blockIdx.y;
-    const int len = min(__ldcg(src_len), min(s_max_pos, d_max_pos));
-    const size_t so = l * s_layer + s_base + (size_t)h * s_max_pos * hd;
-    const size_t dof = l * d_layer + ((size_t)ds * kvh + h) * d_max_pos * hd;
-    const int n4 = len * hd / 4;  // head_dim is a multiple of 4
-    const float4 *k4 = reinterpret_cast<const float4 *>(sk + so), *v4 = reinterpret_cast<const float4 *>(sv + so);
-    float4 *dk4 = reinterpret_cast<float4 *>(dk + dof), *dv4 = reinterpret_cast<float4 *>(dv + dof);
+    const int len = min(__ldcg(src_len), min(src.max_pos, dst.max_pos));
+    const int d4n = hd / 4;  // head_dim is a multiple of 4
+    const int n4 = (len - row0) * d4n;
     for (int i = blockIdx.z * blockDim.x + threadIdx.x; i < n4; i += gridDim.z * blockDim.x) {
-        dk4[i] = __ldcg(k4 + i);
-        dv4[i] = __ldcg(v4 + i);
+        const int p = row0 + i / d4n, d4 = i % d4n;
+        const int64_t so = l * src_step + src.row(0, h, p) + 4 * d4;
+        const int64_t dof = l * dst_step + dst.row(ds, h, p) + 4 * d4;
+        *reinterpret_cast<float4 *>(dst.k + dof) = __ldcg(reinterpret_cast<const float4 *>(src.k + so));
+        *reinterpret_cast<float4 *>(dst.v + dof) = __ldcg(reinterpret_cast<const float4 *>(src.v + so));
     }
     if (blockIdx.x == 0 && blockIdx.z == 0 && threadIdx.x == 0) dst_len[ds] = __ldcg(src_len);
+}
+
+// One layer of a cache gathered into [stream][kv_head][max_pos][head_dim]
+// (the slab layout), rows [0, max_pos) of every stream.
+__global__ void k_kv_gather_layer(KVLayer L, int kvh, int hd, int max_pos, float *k_out, float *v_out) {
+    const int b = blockIdx.y, h = blockIdx.x % kvh;
+    const int64_t n4 = (int64_t)max_pos * hd / 4;
+    float4 *ko = reinterpret_cast<float4 *>(k_out + ((int64_t)b * kvh + h) * max_pos * hd);
+    float4 *vo = reinterpret_cast<float4 *>(v_out + ((int64_t)b * kvh + h) * max_pos * hd);
+    for (int64_t i = (int64_t)(blockIdx.x / kvh) * blockDim.x + threadIdx.x; i < n4;
+         i += (int64_t)(gridDim.x / kvh) * blockDim.x) {
+        const int p = (int)(i / (hd / 4)), d4 = (int)(i % (hd / 4));
+        const int64_t off = L.row(b, h, p) + 4 * d4;
+        ko[i] = __ldcg(reinterpret_cast<const float4 *>(L.k + off));
+        vo[i] = __ldcg(reinterpret_cast<const float4 *>(L.v + off));
+    }
 }
 
 int upload_f16(const uint16_t *h, int64_t n, DevBuf &buf) {
@@ -382,10 +399,173 @@ static int predictor_frame_impl(qora_predictor *p, qora_kv *kv, Launcher &ln, in
 
 // --------------------------------------------------------------------- engine
 
+namespace qora {
+
+// Page-table helpers of paged caches (host side; no-ops for a slab).
+void kv_release_stream(qora_kv *kv, int sid) {
+    if (!kv->paged()) return;
+    for (int j = 0; j < kv->pages_per_stream; j++) {
+        int &e = kv->host_table[(size_t)sid * kv->pages_per_stream + j];
+        if (e != kv->guard_page() && --kv->refs[(size_t)e] == 0) kv->free_pages.push_back(e);
+        e = kv->guard_page();
+    }
+}
+
+int kv_prepare(qora_kv *kv, int s0, int n, int add, cudaStream_t st) {
+    if (!kv->paged() || add <= 0) return QORA_OK;
+    // all or nothing: count the pages first, so a failed call maps none
+    size_t want = 0;
+    for (int sid = s0; sid < s0 + n; sid++) {
+        const int need = std::min(kv->max_pos, kv->host_len[(size_t)sid] + add);
+        const int pages = (need + kv->page_pos - 1) / kv->page_pos;
+        for (int j = 0; j < pages; j++)
+            want += kv->host_table[(size_t)sid * kv->pages_per_stream + j] == kv->guard_page();
+    }
+    if (want > kv->free_pages.size())
+        return set_error(QORA_ERR_OOM, "paged KV cache: %zu more pages needed, %zu of %d free", want,
+                         kv->free_pages.size(), kv->pool_pages);
+    bool changed = false;
+    for (int sid = s0; sid < s0 + n; sid++) {
+        const int need = std::min(kv->max_pos, kv->host_len[(size_t)sid] + add);
+        const int pages = (need + kv->page_pos - 1) / kv->page_pos;
+        for (int j = 0; j < pages; j++) {
+            int &e = kv->host_table[(size_t)sid * kv->pages_per_stream + j];
+            if (e != kv->guard_page()) continue;
+            e = kv->free_pages.back();
+            kv->free_pages.pop_back();
+            kv->refs[(size_t)e] = 1;
+            changed = true;
+        }
+    }
+    if (changed)
+        QORA_CUDA(cudaMemcpyAsync(kv->table.as<int>() + (size_t)s0 * kv->pages_per_stream,
+                                  kv->host_table.data() + (size_t)s0 * kv->pages_per_stream,
+                                  (size_t)n * kv->pages_per_stream * 4, cudaMemcpyHostToDevice, st));
+    return QORA_OK;
+}
+
+void kv_note_growth(qora_kv *kv, int s0, int n, int add) {
+    for (int sid = s0; sid < s0 + n; sid++)
+        kv->host_len[(size_t)sid] = std::min(kv->max_pos, kv->host_len[(size_t)sid] + add);
+}
+
+// Copies stream `ss` of `src` into streams [ds, ds + n) of `dst` (live rows only).
+int kv_copy_streams(qora_kv *dst, int32_t ds, int32_t n, const qora_kv *src, int32_t ss,
+                    cudaStream_t st) {
+    if (!dst || !src || dst->layers != src->layers || dst->kvh != src->kvh || dst->hd != src->hd ||
+        dst->max_pos < src->max_pos || ds < 0 || n <= 0 || ds + n > dst->streams || ss < 0 ||
+        ss >= src->streams)
+        return set_error(QORA_ERR_INVALID, "qora_kv_copy_stream: incompatible caches");
+    int len = src->host_len[(size_t)ss];
+    if (src->paged() || dst->paged()) {
+        // page mapping needs the exact length: read it (a prefix copy is rare)
+        QORA_CUDA(cudaMemcpyAsync(&len, src->lens() + ss, 4, cudaMemcpyDeviceToHost, st));
+        QORA_CUDA(cudaStreamSynchronize(st));
+    }
+    int row0 = 0;
+    if (dst->paged()) {
+        const bool share = src->paged() && src != dst && src->page_pos == dst->page_pos;
+        const bool share_self = src == dst;
+        const int full = (share || share_self) ? len / src->page_pos : 0;
+        for (int d = ds; d < ds + n; d++) {
+            if (share_self && d == ss) continue;
+            kv_release_stream(dst, d);
+            dst->host_len[(size_t)d] = 0;
+            if (share || share_self) {  // full pages are shared, not copied
+                for (int j = 0; j < full; j++) {
+                    const int pg = src->host_table[(size_t)ss * src->pages_per_stream + j];
+                    dst->host_table[(size_t)d * dst->pages_per_stream + j] = pg;
+                    dst->refs[(size_t)pg]++;
+                }
+                dst->host_len[(size_t)d] = full * src->page_pos;
+            }
+        }
+        row0 = full * src->page_pos;
+        for (int d = ds; d < ds + n; d++) {
+            if (share_self && d == ss) continue;
+            QORA_TRY(kv_prepare(dst, d, 1, len - dst->host_len[(size_t)d], st));
+            dst->host_len[(size_t)d] = len;
+        }
+        QORA_CUDA(cudaMemcpyAsync(dst->table.as<int>() + (size_t)ds * dst->pages_per_stream,
+                                  dst->host_table.data() + (size_t)ds * dst->pages_per_stream,
+                                  (size_t)n * dst->pages_per_stream * 4, cudaMemcpyHostToDevice, st));
+    } else {
+        for (int d = ds; d < ds + n; d++) dst->host_len[(size_t)d] = len;
+    }
+    const KVLayer sl = src->layer(0, ss), dl = dst->layer(0, 0);
+    const int64_t s_step = src->paged() ? (int64_t)src->kvh * src->page_pos * src->hd : (int64_t)src->layer_elems();
+    const int64_t d_step = dst->paged() ? (int64_t)dst->kvh * dst->page_pos * dst->hd : (int64_t)dst->layer_elems();
+    // row chunks: enough CTAs to keep HBM busy for a long prefix
+    const int chunks = std::max(1, std::min(64, src->max_pos * src->hd / 4 / 256 / 4));
+    return launch_ex(k_kv_copy_rows, dim3(src->layers * src->kvh, n, chunks), dim3(256), 0, st, 1u, sl,
+                     s_step, dl, d_step, ds, src->kvh, src->hd, row0, src->lens() + ss, dst->lens());
+}
+}  // namespace qora
+
 // =========================================================================
 // extern "C" entry points
 // =========================================================================
 extern "C" {
+
+int qora_kv_create_paged(qora_ctx *ctx, int32_t num_layers, int32_t kv_heads, int32_t head_dim,
+                         int32_t max_pos, int32_t streams, int32_t page_positions, int32_t pool_pages,
+                         qora_kv **out) {
+    if (!ctx || !out || num_layers <= 0 || kv_heads <= 0 || max_pos <= 0 || streams <= 0 ||
+        pool_pages <= 0)
+        return set_error(QORA_ERR_INVALID, "qora_kv_create_paged: bad arguments");
+    if (head_dim != 64 && head_dim != 128)
+        return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128)", head_dim);
+    // every tile the kernels read (16 or 32 positions, aligned) must lie in one page
+    if (page_positions < kPageMinPositions || (page_positions & (page_positions - 1)))
+        return set_error(QORA_ERR_INVALID, "page_positions %d: a power of two >= %d", page_positions,
+                         kPageMinPositions);
+    QORA_CUDA(cudaSetDevice(ctx->device));
+    qora_kv *kv = new qora_kv();
+    kv->ctx = ctx;
+    kv->layers = num_layers;
+    kv->kvh = kv_heads;
+    kv->hd = head_dim;
+    kv->max_pos = max_pos;
+    kv->streams = streams;
+    kv->page_pos = page_positions;
+    while ((1 << kv->page_shift) < page_positions) kv->page_shift++;
+    kv->pages_per_stream = (max_pos + page_positions - 1) / page_positions;
+    kv->pool_pages = pool_pages;
+    const size_t bytes = (size_t)(pool_pages + 1) * kv->page_elems() * 4;  // + the guard page
+    int rc = kv->k.alloc(bytes);
+    if (rc == QORA_OK) rc = kv->v.alloc(bytes);
+    if (rc == QORA_OK) rc = kv->len.alloc((size_t)streams * 4);
+    if (rc == QORA_OK) rc = kv->len.zero();
+    if (rc == QORA_OK) rc = kv->table.alloc((size_t)streams * kv->pages_per_stream * 4);
+    if (rc == QORA_OK) {
+        kv->host_table.assign((size_t)streams * kv->pages_per_stream, kv->guard_page());
+        kv->refs.assign((size_t)pool_pages, 0);
+        kv->free_pages.reserve((size_t)pool_pages);
+        for (int pg = pool_pages - 1; pg >= 0; pg--) kv->free_pages.push_back(pg);
+        kv->host_len.assign((size_t)streams, 0);
+        if (cudaMemcpy(kv->table.p, kv->host_table.data(), kv->table.bytes, cudaMemcpyHostToDevice) !=
+            cudaSuccess)
+            rc = set_error(QORA_ERR_CUDA, "qora_kv_create_paged: table upload failed");
+    }
+    if (rc == QORA_OK && cudaDeviceSynchronize() != cudaSuccess)
+        rc = set_error(QORA_ERR_CUDA, "qora_kv_create_paged: sync failed");
+    if (rc != QORA_OK) {
+        delete kv;
+        return rc;
+    }
+    *out = kv;
+    return QORA_OK;
+}
+
+int qora_kv_pages_host(const qora_kv *kv, int32_t *mapped, int32_t *free_pages) {
+    if (!kv) return set_error(QORA_ERR_INVALID, "null kv");
+    if (!kv->paged()) return set_error(QORA_ERR_UNSUPPORTED, "qora_kv_pages_host: not a paged cache");
+    int used = 0;
+    for (int r : kv->refs) used += r > 0;
+    if (mapped) *mapped = used;
+    if (free_pages) *free_pages = (int32_t)kv->free_pages.size();
+    return QORA_OK;
+}
 
 int qora_kv_create(qora_ctx *ctx, int32_t num_layers, int32_t kv_heads, int32_t head_dim,
                    int32_t max_pos, int32_t streams, qora_kv **out) {
@@ -406,6 +586,7 @@ int qora_kv_create(qora_ctx *ctx, int32_t num_layers, int32_t kv_heads, int32_t 
     if (rc == QORA_OK) rc = kv->v.alloc(bytes);
     if (rc == QORA_OK) rc = kv->len.alloc((size_t)streams * 4);
     if (rc == QORA_OK) rc = kv->len.zero();
+    kv->host_len.assign((size_t)streams, 0);
     if (rc == QORA_OK && cudaDeviceSynchronize() != cudaSuccess)
         rc = set_error(QORA_ERR_CUDA, "qora_kv_create: sync failed");
     if (rc != QORA_OK) {
@@ -421,15 +602,24 @@ void qora_kv_destroy(qora_kv *kv) { delete kv; }
 int qora_kv_reset(qora_kv *kv, const int32_t *ids_host, int32_t count, void *stream) {
     if (!kv) return set_error(QORA_ERR_INVALID, "null kv");
     cudaStream_t st = as_stream(stream);
+    if (ids_host)
+        for (int i = 0; i < count; i++)
+            if (ids_host[i] < 0 || ids_host[i] >= kv->streams)
+                return set_error(QORA_ERR_INVALID, "stream id %d out of range", ids_host[i]);
+    const int n = ids_host ? count : kv->streams;
+    for (int i = 0; i < n; i++) {
+        const int sid = ids_host ? ids_host[i] : i;
+        kv_release_stream(kv, sid);
+        kv->host_len[(size_t)sid] = 0;
+    }
     if (!ids_host) {
         QORA_CUDA(cudaMemsetAsync(kv->len.p, 0, kv->len.bytes, st));
-        return QORA_OK;
+    } else {
+        for (int i = 0; i < count; i++) QORA_CUDA(cudaMemsetAsync(kv->lens() + ids_host[i], 0, 4, st));
     }
-    for (int i = 0; i < count; i++) {
-        if (ids_host[i] < 0 || ids_host[i] >= kv->streams)
-            return set_error(QORA_ERR_INVALID, "stream id %d out of range", ids_host[i]);
-        QORA_CUDA(cudaMemsetAsync(kv->lens() + ids_host[i], 0, 4, st));
-    }
+    if (kv->paged())  // released entries point at the guard page again
+        QORA_CUDA(cudaMemcpyAsync(kv->table.p, kv->host_table.data(), kv->table.bytes,
+                                  cudaMemcpyHostToDevice, st));
     return QORA_OK;
 }
 
@@ -441,30 +631,13 @@ int qora_kv_lengths_host(qora_kv *kv, int32_t *len_host, void *stream) {
     return QORA_OK;
 }
 
-namespace qora {
-// Copies stream `ss` of `src` into streams [ds, ds + n) of `dst` (live rows only).
-int kv_copy_streams(qora_kv *dst, int32_t ds, int32_t n, const qora_kv *src, int32_t ss,
-                    cudaStream_t st) {
-    if (!dst || !src || dst->layers != src->layers || dst->kvh != src->kvh || dst->hd != src->hd ||
-        dst->max_pos < src->max_pos || ds < 0 || n <= 0 || ds + n > dst->streams || ss < 0 ||
-        ss >= src->streams)
-        return set_error(QORA_ERR_INVALID, "qora_kv_copy_stream: incompatible caches");
-    const size_t s_base = (size_t)ss * src->kvh * src->max_pos * src->hd;
-    // row chunks: enough CTAs to keep HBM busy for a long prefix
-    const int chunks = std::max(1, std::min(64, src->max_pos * src->hd / 4 / 256 / 4));
-    return launch_ex(k_kv_copy_rows, dim3(src->layers * src->kvh, n, chunks), dim3(256), 0, st, 1u,
-                     src->k.as<float>(), src->v.as<float>(), src->layer_elems(), s_base,
-                     src->max_pos, dst->k.as<float>(), dst->v.as<float>(), dst->layer_elems(),
-                     dst->max_pos, ds, src->kvh, src->hd, src->lens() + ss, dst->lens());
-}
-}  // namespace qora
-
 int qora_kv_copy_stream(qora_kv *dst, int32_t ds, const qora_kv *src, int32_t ss, void *stream) {
     return kv_copy_streams(dst, ds, 1, src, ss, as_stream(stream));
 }
 
 int qora_kv_layer_ptrs(qora_kv *kv, int32_t layer, float **k, float **v, int32_t **len) {
     if (!kv || layer < 0 || layer >= kv->layers) return set_error(QORA_ERR_INVALID, "bad layer");
+    if (kv->paged()) return set_error(QORA_ERR_UNSUPPORTED, "qora_kv_layer_ptrs: a paged cache has no slab");
     KVLayer L = kv->layer(layer);
     if (k) *k = L.k;
     if (v) *v = L.v;
@@ -476,6 +649,9 @@ int qora_kv_export_layer(qora_kv *kv, int32_t layer, float *k_out, float *v_out,
     if (!kv || layer < 0 || layer >= kv->layers || !k_out || !v_out)
         return set_error(QORA_ERR_INVALID, "qora_kv_export_layer: bad arguments");
     KVLayer L = kv->layer(layer);
+    if (kv->paged())  // gathered into the slab layout
+        return launch_ex(k_kv_gather_layer, dim3(kv->kvh * 8, kv->streams), dim3(256), 0, as_stream(stream), 1u,
+                         L, kv->kvh, kv->hd, kv->max_pos, k_out, v_out);
     const size_t bytes = kv->layer_elems() * 4;
     QORA_CUDA(cudaMemcpyAsync(k_out, L.k, bytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
     QORA_CUDA(cudaMemcpyAsync(v_out, L.v, bytes, cudaMemcpyDeviceToDevice, as_stream(stream)));
@@ -549,9 +725,12 @@ int qora_talker_step(qora_talker *t, qora_kv *kv, const float *emb, const int32_
     if (kv->layers != t->L || kv->kvh != t->kvh || kv->hd != t->hd)
         return set_error(QORA_ERR_SHAPE, "KV cache does not match the talker");
     Launcher ln{t->ctx, &t->w, as_stream(stream)};
+    QORA_TRY(kv_prepare(kv, 0, B, 1, ln.st));
     QORA_TRY(launch_copy_rowstats(emb, t->H, t->w.x.as<float>(), t->H, B, t->H,
                                   t->w.ss.as<float>(), t->H / kGroup, ln.st));
-    return talker_forward_step(t, kv, ln, B, positions, hidden, t->H, logits, t->vocab, nullptr);
+    QORA_TRY(talker_forward_step(t, kv, ln, B, positions, hidden, t->H, logits, t->vocab, nullptr));
+    kv_note_growth(kv, 0, B, 1);
+    return QORA_OK;
 }
 
 int qora_talker_decode(qora_talker *t, qora_kv *kv, qora_text_proj *tp, const uint32_t *tokens_host,
@@ -587,6 +766,7 @@ int talker_prefill_rows(qora_talker *t, qora_kv *kv, int s0, int ns, int T, cons
     Launcher ln{t->ctx, &t->w, st};
     ln.fixed = true;
     const int rows = ns * T;
+    QORA_TRY(kv_prepare(kv, s0, ns, T, st));
     QORA_TRY(launch_copy_rowstats(x, t->H, t->w.x.as<float>(), t->H, rows, t->H,
                                   t->w.ss.as<float>(), t->H / kGroup, st));
     for (int l = 0; l < t->L; l++)
@@ -594,8 +774,10 @@ int talker_prefill_rows(qora_talker *t, qora_kv *kv, int s0, int ns, int T, cons
                            kv->layer(l, s0), kv->lens() + s0, nullptr, t->rope_cos.as<float>(),
                            t->rope_sin.as<float>(), t->rope_max,
                            l + 1 < t->L ? t->layers[l + 1].qkv : t->head));
-    return launch_ex(k_advance, dim3((ns + 255) / 256), dim3(256), 0, st, 1u, kv->lens() + s0,
-                     (int *)nullptr, ns, T);
+    QORA_TRY(launch_ex(k_advance, dim3((ns + 255) / 256), dim3(256), 0, st, 1u, kv->lens() + s0,
+                       (int *)nullptr, ns, T));
+    kv_note_growth(kv, s0, ns, T);
+    return QORA_OK;
 }
 }  // namespace
 
@@ -611,6 +793,7 @@ int qora_talker_prefill(qora_talker *t, qora_kv *kv, int32_t kv_stream, const fl
         return set_error(QORA_ERR_INVALID, "prefix cache length %d != start_pos %d", cur, start_pos);
     if (start_pos + T > kv->max_pos || start_pos + T > t->rope_max)
         return set_error(QORA_ERR_RANGE, "prefill past capacity");
+    kv->host_len[(size_t)kv_stream] = cur;
     for (int t0 = 0; t0 < T; t0 += kMaxRows) {
         const int tc = std::min(kMaxRows, T - t0);
         QORA_TRY(talker_prefill_rows(t, kv, kv_stream, 1, tc, x + (int64_t)t0 * t->H, st));
@@ -744,8 +927,13 @@ int qora_predictor_frame(qora_predictor *p, qora_kv *kv, const float *hidden, co
     QORA_CUDA(cudaMemcpy2DAsync(p->x2.as<char>() + row, 2 * row, semantic, row, row, B,
                                 cudaMemcpyDeviceToDevice, st));
     Launcher ln{p->ctx, &p->w, st};
-    return predictor_frame_impl(p, kv, ln, B, p->x2.as<float>(), codes, p->groups, logits,
-                                (int64_t)p->groups * p->vocab, forced, p->groups);
+    // the frame resets the streams' caches and fills groups + 1 positions
+    for (int b = 0; b < B; b++) kv->host_len[(size_t)b] = 0;
+    QORA_TRY(kv_prepare(kv, 0, B, p->groups + 1, st));
+    QORA_TRY(predictor_frame_impl(p, kv, ln, B, p->x2.as<float>(), codes, p->groups, logits,
+                                  (int64_t)p->groups * p->vocab, forced, p->groups));
+    kv_note_growth(kv, 0, B, p->groups + 1);
+    return QORA_OK;
 }
 
 int qora_predictor_embed_sum(qora_predictor *p, const uint32_t *codes, int32_t B, float *out,

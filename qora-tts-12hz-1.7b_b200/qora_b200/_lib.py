@@ -85,6 +85,8 @@ SIGNATURES = {
     "qora_rms_norm_f16": (C.c_int, [_vp, _vp, _vp, _i64, _i32, _vp, _vp]),
     "qora_rope_tables_host": (C.c_int, [_i32, _i32, C.c_double, _vp, _i32, _vp, _vp]),
     "qora_kv_create": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _i32, _PP]),
+    "qora_kv_create_paged": (C.c_int, [_vp, _i32, _i32, _i32, _i32, _i32, _i32, _i32, _PP]),
+    "qora_kv_pages_host": (C.c_int, [_vp, _vp, _vp]),
     "qora_kv_destroy": (None, [_vp]),
     "qora_kv_reset": (C.c_int, [_vp, _vp, _i32, _vp]),
     "qora_kv_lengths_host": (C.c_int, [_vp, _vp, _vp]),

@@ -116,13 +116,26 @@ class KvCache:
     """RawKvCache for `streams` streams (gemv.rs:75-86), preallocated on device."""
 
     def __init__(self, ctx: Context, layers: int, kv_heads: int, head_dim: int, max_pos: int,
-                 streams: int = 1):
+                 streams: int = 1, page_positions: int = 0, pool_pages: int = 0):
+        """page_positions > 0: paged storage (qora_kv_create_paged), a pool of
+        pool_pages pages of page_positions positions mapped as streams grow."""
         self.ctx, self.layers, self.kv_heads, self.head_dim = ctx, layers, kv_heads, head_dim
         self.max_pos, self.streams = max_pos, streams
+        self.paged = page_positions > 0
         self._L = _lib.load()
         h = C.c_void_p()
-        _lib.call("qora_kv_create", ctx.h, layers, kv_heads, head_dim, max_pos, streams, C.byref(h))
+        if self.paged:
+            _lib.call("qora_kv_create_paged", ctx.h, layers, kv_heads, head_dim, max_pos, streams,
+                      page_positions, pool_pages, C.byref(h))
+        else:
+            _lib.call("qora_kv_create", ctx.h, layers, kv_heads, head_dim, max_pos, streams, C.byref(h))
         self.h = h
+
+    def pages(self):
+        """(mapped, free) pages of a paged cache."""
+        m, f = C.c_int32(), C.c_int32()
+        _lib.call("qora_kv_pages_host", self.h, C.byref(m), C.byref(f))
+        return m.value, f.value
 
     def __del__(self):
         if getattr(self, "h", None):
@@ -189,10 +202,11 @@ class Talker:
             self._L.qora_talker_destroy(self.h)
             self.h = None
 
-    def new_kv(self, max_pos: int | None = None, streams: int = 1) -> KvCache:
+    def new_kv(self, max_pos: int | None = None, streams: int = 1, page_positions: int = 0,
+               pool_pages: int = 0) -> KvCache:
         c = self.cfg
         return KvCache(self.ctx, c.t_layers, c.t_kv_heads, c.t_head_dim, max_pos or c.t_max_pos,
-                       streams)
+                       streams, page_positions, pool_pages)
 
     def forward_with_embedding(self, emb: torch.Tensor, kv: KvCache, positions, stream=None):
         """forward_with_embedding (talker.rs:263-360) for B = emb.shape[0] streams.

@@ -4,8 +4,8 @@ The 28-layer talker (1.7B dims, random-init Q4 weights) takes an ICL-style
 prefill of 2048 N(0,1) positions per stream (seed 42 + stream), then 2048
 greedy decode steps to 4096 positions, for 2 streams with caches of their
 own (the survey's config runs 32 streams; two suffice for parity, the bench
-times 32).  Each step's input is embed_codec_token of the engine's own
-argmax (last index on ties, code_predictor.rs:335-341) fed back through
+times 32), held in a paged cache (64-position pages mapped as they grow).
+Each step's input is embed_codec_token of the engine's own argmax (last index on ties, code_predictor.rs:335-341) fed back through
 forward_with_embedding (talker.rs:263-360): the greedy loop itself runs on
 the device.  The oracle is then teacher-forced with exactly those inputs:
 one pass over all 4096 rows (prefill_talker_raw_from arithmetic,
@@ -54,7 +54,9 @@ def test_config3_long_context(E, orc):
     tw = qora_b200.synth_talker(cfg)
     ctx = E.Context(0)
     talker = E.Talker(ctx, tw, max_batch=STREAMS)
-    kv = talker.new_kv(max_pos=PREFILL + STEPS, streams=STREAMS)
+    # the paged cache: 64-position pages mapped as the streams grow
+    kv = talker.new_kv(max_pos=PREFILL + STEPS, streams=STREAMS, page_positions=64,
+                       pool_pages=STREAMS * (PREFILL + STEPS) // 64)
     xs = [orc.synth_normal(42 + s, 1.0, PREFILL * H).reshape(PREFILL, H) for s in range(STREAMS)]
     hid = torch.stack([talker.prefill_talker_raw_from(torch.from_numpy(x).cuda(), kv, 0, kv_stream=s)
                        for s, x in enumerate(xs)])
@@ -70,6 +72,7 @@ def test_config3_long_context(E, orc):
         got[:, step + 1] = logits.cpu().numpy()
     ctx.check_device_error()
     assert list(kv.lengths()) == [PREFILL + STEPS] * STREAMS
+    assert kv.pages() == (STREAMS * (PREFILL + STEPS) // 64, 0)
     del kv, talker
     torch.cuda.empty_cache()
 
