@@ -362,9 +362,22 @@ __device__ __forceinline__ void norm_strided(float *xs, const __half *gamma, int
         xs[k] = __fmul_rn(__fmul_rn(xs[k], inv), __half2float(__ldg(gamma + k)));
 }
 
+// Whether an op's input may be built without block-wide waits: a tagged
+// vector that nothing else reads back (no saved copy, no ordering input).
+// Every thread then uses only the input values it polled itself (the rows
+// tid + 256 m it processes in every chunk), so it starts on them as soon as
+// they arrive; the RMSNorm's 1 / rms is applied to the column totals instead
+// (y = inv * sum_k W x gamma), from the sum of squares the item's reduction
+// gathers anyway.
+__device__ __forceinline__ bool streamed_input(const GemvDesc &d) {
+    return d.in_mode == IN_VEC && d.in && !d.in_plain && !d.save && !d.save_plain && !d.dep;
+}
+
 // Builds the GEMV input x[0..kpad) in shared memory (rows >= K are zero).
+// Streamed inputs (streamed_input): x * gamma per thread, no barrier, and
+// this thread's share of the sum of squares in ssp (0 without gamma).
 __device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &S, int tid,
-                            bool leader, int j0, int n_items, int avail) {
+                            bool leader, int j0, int n_items, int avail, float &ssp_out) {
     float *xs = S.u.xs;
     const int K = d.K;
     // gamma is immutable: its first loads go out before any wait
@@ -380,6 +393,23 @@ __device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d
         csync();
     }
     for (int k = K + tid; k < d.kpad; k += kNT) xs[k] = 0.0f;
+    ssp_out = 0.0f;
+    if (streamed_input(d)) {
+        const bool has_ss = d.gamma && tid < (K >> 5);
+        const uint64_t ssw = has_ss ? ld_relaxed_u64(d.ss_in + tid) : 0ull;
+        poll_vector(P, S, d.in, K, P.tag_base + d.in_tag, xs, tid);
+        if (d.gamma) {
+#pragma unroll
+            for (int m = 0; m < kGammaPre; m++) {
+                const int k = tid + m * kNT;
+                if (k < K) xs[k] = __fmul_rn(xs[k], gm[m]);
+            }
+            for (int k = tid + kGammaPre * kNT; k < K; k += kNT)
+                xs[k] = __fmul_rn(xs[k], __half2float(__ldg(d.gamma + k)));
+        }
+        if (has_ss) ssp_out = settle_word(P, S, d.ss_in + tid, ssw, P.tag_base + d.ss_tag);
+        return;
+    }
     float ss = 0.0f;
     switch (d.in_mode) {
         case IN_VEC: {
@@ -535,11 +565,18 @@ __device__ __forceinline__ void row_fma(uint64_t (&acc)[16], float &ssum, float 
 // The items of one GEMV op on this SM: each unit's G groups (1, or the
 // gate / up pair) in turn, all K rows each.
 __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef &op, FrameSmem &S,
-                           int tid, int cta, int grid, uint32_t &q, int &rbuf, bool tr, int op_i) {
+                           int tid, int cta, int grid, uint32_t &q, int &rbuf, bool tr, int op_i,
+                           float ssp) {
     uint64_t waited = 0, slots = 0, comp = 0, redc = 0;
     const int lane = tid & 31, warp = tid >> 5;
     const float *xs = S.u.xs;
     const uint32_t otag = P.tag_base + d.out_tag;
+    // streamed RMSNorm input: 1 / rms multiplies the column totals; the sum of
+    // squares rides on the first reduction's barrier (fixed warp order)
+    const bool defer_norm = streamed_input(d) && d.gamma;
+    float inv = 1.0f;
+    bool have_inv = !defer_norm;
+    const float ssw = defer_norm ? warp_sum(ssp) : 0.0f;
     for (int u = first_item(cta, op, grid); u < op.n_items; u += op.avail) {
         // the epilogue's residual / bias value, fetched while the item computes
         float pre = 0.0f;
@@ -616,11 +653,21 @@ __device__ void gemv_items(const FrameParams &P, const GemvDesc &d, const OpRef 
             const float stot = warp_sum(ssum);
             const float up = __int_as_float((127 + 74 - 4 * (lane & 3)) << 23);
             S.red[rbuf][warp][lane] = __fsub_rn(__fmul_rn(v[0], up), __fmul_rn(stot, 2.117582368135751e-22f));
+            if (!have_inv && lane == 0) S.bred[warp] = ssw;
             csync();
+            if (!have_inv) {
+                // rms_norm_f16 (gemv.rs:445-454): 1 / sqrt(ss / K + 1e-6)
+                float ss = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kNT / 32; w++) ss += S.bred[w];
+                inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)d.K), 1e-6f)));
+                have_inv = true;
+            }
             if (warp == 0) {
                 float t = 0.0f;
 #pragma unroll
                 for (int w = 0; w < kNT / 32; w++) t += S.red[rbuf][w][lane];
+                if (defer_norm) t = __fmul_rn(t, inv);
                 if (g == 0) y[0] = t;
                 else y[1] = t;
             }
@@ -746,11 +793,12 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
         stamp_all(P, i, 3, ta);
         if (op.type == OP_GEMV) {
             const GemvDesc &d = S.desc[b].g;
-            build_input(P, d, S, tid, j0 == 0, j0, op.n_items, op.avail);
+            float ssp = 0.0f;
+            build_input(P, d, S, tid, j0 == 0, j0, op.n_items, op.avail, ssp);
             last_gemv = i;
             stamp_all(P, i, 0, ta);
             stamp_all(P, i, 1, ta);
-            gemv_items(P, d, op, S, tid, cta, grid, q, rbuf, tr, i);
+            gemv_items(P, d, op, S, tid, cta, grid, q, rbuf, tr, i, ssp);
             if (d.adv_len && j0 == 0 && tid == 0) {
                 // end of the talker step: the cache and RoPE position advance
                 d.adv_len[0] += 1;
