@@ -373,11 +373,43 @@ __device__ __forceinline__ bool streamed_input(const GemvDesc &d) {
     return d.in_mode == IN_VEC && d.in && !d.in_plain && !d.save && !d.save_plain && !d.dep;
 }
 
-// Builds the GEMV input x[0..kpad) in shared memory (rows >= K are zero).
-// Streamed inputs (streamed_input): x * gamma per thread, no barrier, and
-// this thread's share of the sum of squares in ssp (0 without gamma).
+// Streamed inputs (streamed_input): x * gamma per thread, no barrier; returns
+// this thread's share of the sum of squares (0 without gamma).  Inlined into
+// the op loop: it is the input path of almost every op, and an out-of-line
+// call saves and restores the caller's live registers through local memory,
+// which the L1 left beside the weight ring cannot hold.
+__device__ __forceinline__ float build_streamed(const FrameParams &P, const GemvDesc &d, FrameSmem &S,
+                                                int tid) {
+    float *xs = S.u.xs;
+    const int K = d.K;
+    const bool has_ss = d.gamma && tid < (K >> 5);
+    const uint64_t ssw = has_ss ? ld_relaxed_u64(d.ss_in + tid) : 0ull;
+    // gamma is immutable: its loads go out before the wait
+    float gm[kGammaPre];
+#pragma unroll
+    for (int m = 0; m < kGammaPre; m++) {
+        const int k = tid + m * kNT;
+        gm[m] = (d.gamma && k < K) ? __half2float(__ldg(d.gamma + k)) : 0.0f;
+    }
+    for (int k = K + tid; k < d.kpad; k += kNT) xs[k] = 0.0f;
+    poll_vector(P, S, d.in, K, P.tag_base + d.in_tag, xs, tid);
+    if (d.gamma) {
+#pragma unroll
+        for (int m = 0; m < kGammaPre; m++) {
+            const int k = tid + m * kNT;
+            if (k < K) xs[k] = __fmul_rn(xs[k], gm[m]);
+        }
+        for (int k = tid + kGammaPre * kNT; k < K; k += kNT)
+            xs[k] = __fmul_rn(xs[k], __half2float(__ldg(d.gamma + k)));
+    }
+    return has_ss ? settle_word(P, S, d.ss_in + tid, ssw, P.tag_base + d.ss_tag) : 0.0f;
+}
+
+// Builds the GEMV input x[0..kpad) in shared memory (rows >= K are zero) for
+// the ops whose input is not streamed: plain vectors, embeddings, the frame
+// input, saved or ordered inputs.
 __device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d, FrameSmem &S, int tid,
-                            bool leader, int j0, int n_items, int avail, float &ssp_out) {
+                            bool leader, int j0, int n_items, int avail) {
     float *xs = S.u.xs;
     const int K = d.K;
     // gamma is immutable: its first loads go out before any wait
@@ -393,23 +425,6 @@ __device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d
         csync();
     }
     for (int k = K + tid; k < d.kpad; k += kNT) xs[k] = 0.0f;
-    ssp_out = 0.0f;
-    if (streamed_input(d)) {
-        const bool has_ss = d.gamma && tid < (K >> 5);
-        const uint64_t ssw = has_ss ? ld_relaxed_u64(d.ss_in + tid) : 0ull;
-        poll_vector(P, S, d.in, K, P.tag_base + d.in_tag, xs, tid);
-        if (d.gamma) {
-#pragma unroll
-            for (int m = 0; m < kGammaPre; m++) {
-                const int k = tid + m * kNT;
-                if (k < K) xs[k] = __fmul_rn(xs[k], gm[m]);
-            }
-            for (int k = tid + kGammaPre * kNT; k < K; k += kNT)
-                xs[k] = __fmul_rn(xs[k], __half2float(__ldg(d.gamma + k)));
-        }
-        if (has_ss) ssp_out = settle_word(P, S, d.ss_in + tid, ssw, P.tag_base + d.ss_tag);
-        return;
-    }
     float ss = 0.0f;
     switch (d.in_mode) {
         case IN_VEC: {
@@ -794,7 +809,8 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
         if (op.type == OP_GEMV) {
             const GemvDesc &d = S.desc[b].g;
             float ssp = 0.0f;
-            build_input(P, d, S, tid, j0 == 0, j0, op.n_items, op.avail, ssp);
+            if (streamed_input(d)) ssp = build_streamed(P, d, S, tid);
+            else build_input(P, d, S, tid, j0 == 0, j0, op.n_items, op.avail);
             last_gemv = i;
             stamp_all(P, i, 0, ta);
             stamp_all(P, i, 1, ta);

@@ -12,7 +12,12 @@ namespace fk {
 
 constexpr int kNT = 256;               // consumer threads (8 warps)
 constexpr int kThreads = kNT + 32;     // + one producer warp
-constexpr int kSlots = 9;              // weight ring slots per SM
+// Weight ring slots per SM.  Four keep every slot filled before its op's
+// input arrives, and leave ~120 KB of the SM's 256 KB of L1 + shared memory
+// to the data cache, which holds the kernel's stack (register saves around
+// the out-of-line op bodies); with nine slots the L1 kept ~28 KB and a frame
+// took 6 % longer.
+constexpr int kSlots = 4;
 constexpr int kSlotNib = 16384;        // nibble bytes per slot (1024 rows of one group)
 constexpr int kSlotScl = 2048;         // scale bytes per slot
 constexpr int kXMax = 6144;            // widest GEMV input (talker down projection)
