@@ -53,7 +53,7 @@ def parse():
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--no-config3", action="store_true")
     ap.add_argument("--profile-case", default=None,
-                    choices=["gemv", "frame_trace", "batch_frame", "attn_decode"],
+                    choices=["gemv", "frame_trace", "batch_frame", "attn_decode", "prefill"],
                     help="small fixed workload for an ncu capture instead of the bench")
     return ap.parse_args()
 
@@ -791,6 +791,36 @@ def profile_case_batch_frame(B):
                       "kernels_per_frame": eng.kernels_per_frame()}))
 
 
+def profile_case_prefill(tokens=2048):
+    """ncu case: one stream's config-3 prefill (1.7B dims, random-init Q4
+    weights, `tokens` N(0,1) rows in 512-row chunks), after one untimed
+    prefill of another stream, bracketed by cudaProfilerStart/Stop; prints
+    its CUDA-event time as one JSON line."""
+    import torch
+    import qora_b200 as qb
+    from qora_b200 import engine as E
+    torch.cuda.set_device(0)
+    cfg = qb.ModelConfig()
+    ctx = E.Context(0)
+    talker = E.Talker(ctx, qb.synth_talker(cfg), max_batch=1)
+    kv = talker.new_kv(max_pos=tokens, streams=2)
+    xs = [torch.from_numpy(qb.synth_normal(42 + s, 1.0, tokens * cfg.t_hidden)
+                           .reshape(tokens, cfg.t_hidden)).cuda() for s in range(2)]
+    talker.prefill_talker_raw_from(xs[0], kv, 0, kv_stream=0)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()
+    e0.record(st)
+    talker.prefill_talker_raw_from(xs[1], kv, 0, kv_stream=1)
+    e1.record(st)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ctx.check_device_error()
+    print(json.dumps({"profile_case": "prefill", "tokens": tokens,
+                      "ms": round(e0.elapsed_time(e1), 3)}))
+
+
 def profile_case_attn_decode(streams=32, positions=4096, reps=8):
     """ncu case: the decode attention of one talker layer (16 q / 8 kv heads,
     head_dim 128) for `streams` streams over `positions` cached positions each
@@ -836,6 +866,9 @@ def profile_case_attn_decode(streams=32, positions=4096, reps=8):
 
 def main():
     args = parse()
+    if args.profile_case == "prefill":
+        profile_case_prefill()
+        return
     if args.profile_case == "attn_decode":
         profile_case_attn_decode()
         return

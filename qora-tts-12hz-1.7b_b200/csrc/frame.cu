@@ -450,11 +450,16 @@ __device__ __noinline__ void build_input(const FrameParams &P, const GemvDesc &d
                     st_relaxed_u64(d.code_dst, tag_pack(__uint_as_float(code), P.tag_base + d.out_tag));
                 }
             } else {
-                float c[1];
+                float c[1] = {0.0f};
                 const bool pr[1] = {true};
                 if (!poll_tagged<1>(d.code_src, 0, P.tag_base + d.code_tag, c, pr, P.err, P.abort_flag))
                     S.abort = 1;
                 code = __float_as_uint(c[0]);
+            }
+            // an aborted wait leaves no code: row 0 keeps the reads in the table
+            if (code >= (uint32_t)d.emb.rows) {
+                raise_error(P.err, kDevRange);
+                code = 0;
             }
             for (int w = tid; w < (K >> 3); w += kNT) {
                 const EmbWord e = emb_word(d.emb, code, w);

@@ -43,6 +43,8 @@ struct GemvArgs {
     // before griddepcontrol.wait; spread over the grid's CTAs)
     const void *pf0 = nullptr, *pf1 = nullptr;
     uint64_t pf0_bytes = 0, pf1_bytes = 0;
+    const int *rexp = nullptr;      // prefill GEMM: per-row operand exponent
+    const uint8_t *bop = nullptr;   // prefill GEMM: B tiles (k_b_convert)
     // ---- filled by plan_gemv
     int B = 1, WR = 1, S = 1, Z = 1, NSUB = 1;
     int rows_per_cta_k = 128, rows_per_z = 0;
@@ -84,6 +86,20 @@ bool gemv_mma_eligible(const GemvArgs &a, int xmode, int emode);
 bool gemv_mma_supported(const GemvArgs &a, int xmode, int emode);
 GemvPlan plan_gemv_mma(int64_t k, int64_t C, int rows, int emode, int num_sms);
 int launch_gemv_mma(const GemvArgs &a, int xmode, int emode, const GemvPlan &p, cudaStream_t st);
+// Scratch of the prefill GEMM: per-row exponent and RMSNorm factor (`rows`
+// entries) and the B tiles (rows rounded up to 128, times k, times 4 bytes).
+struct GemmScratch {
+    int *rexp = nullptr;
+    float *rinv = nullptr;
+    uint8_t *bop = nullptr;
+    int rows = 0;
+    size_t bop_bytes = 0;
+};
+// Prefill GEMM (tensor cores, 128-column x 128-row tiles over all of K, any
+// row count up to kMaxRows): the bits of k_gemv_mma without a K split.
+// Three kernels (row prologue, B tiles, GEMM); *launches is increased by 3.
+bool gemm_mma_supported(const GemvArgs &a, int xmode, int emode);
+int launch_gemm_mma(GemvArgs a, int xmode, int emode, const GemmScratch &sc, cudaStream_t st, int *launches);
 
 // The plan for one launch: the tensor-core kernel where it qualifies, else
 // the CUDA-core kernel.

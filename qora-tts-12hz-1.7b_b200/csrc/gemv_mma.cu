@@ -652,6 +652,441 @@ __global__ void __maxnreg__(80) k_gemv_mma(const GemvArgs a) {
     gemv_global_stage(a, last_flag, gridDim.x * CO);
 }
 
+// ======================================================================
+// Prefill GEMM: the same contraction for many rows (a prompt chunk of up to
+// kMaxRows rows), one CTA per 128-column x 128-row tile over all of K.
+// k_gemv_mma converts each weight tile once per 32 rows and the input rows
+// once per column tile; here
+//   * k_row_prep finds each row's RMSNorm factor and power-of-two operand
+//     exponent (one CTA per row),
+//   * k_b_convert writes the B operand of every (128-row tile, 32-K stage)
+//     once, as 16 KB in the MMA's shared-memory layout (xh rows, then xl
+//     rows) in global memory,
+//   * k_gemm_mma streams those B tiles with one bulk copy per stage, converts
+//     only its weights (A1 / A2 into tensor memory), and issues one N = 256
+//     MMA (128 rows, xh and xl side by side) plus one N = 128 MMA (A2 xh) per
+//     16 K rows.
+// The operands, the K order of the accumulation and the epilogue arithmetic
+// are those of k_gemv_mma without a K split (the split its prefill plan uses
+// at the 1.7B dims), so every output has the same bits as there, whatever
+// the rows of the launch.
+//
+// k_gemm_mma warp roles (320 threads):
+//   warps 0..  kGGroups converter groups of four (group c takes stages
+//              t = c mod kGGroups; warp g of a group: column group g, TMEM
+//              lanes 32 g ..), then the epilogue (warp w: column group w % 4,
+//              rows kGEpiRows (w / 4) .. + kGEpiRows - 1);
+//   next warp  streams each stage's weights (bulk copies into a raw ring) and
+//              B tile (one bulk copy into the operand ring);
+//   last warp  allocates tensor memory and issues the MMAs (one thread).
+constexpr int kGRows = 128;
+constexpr int kGGroups = 4;                    // converter groups (four warps each)
+constexpr int kGConvWarps = 4 * kGGroups;
+constexpr int kGProdWarp = kGConvWarps;
+constexpr int kGMmaWarp = kGConvWarps + 1;
+constexpr int kGThreads = 32 * (kGConvWarps + 2);
+constexpr int kGEpiRows = kGRows / kGGroups;    // epilogue rows per converter warp
+constexpr int kGRawSlots = 3;                  // weight slots per converter group (own stages)
+constexpr int kGOpStages = 8;
+constexpr int kGRawNib = 0;
+constexpr int kGRawScl = kGRawNib + kMmaGroups * kNibGroupStride;
+constexpr int kGRawBytes = kGRawScl + kMmaGroups * kSclGroupStride;
+constexpr int kGBTile = kGRows * kStageK * 2;  // one of xh / xl: 128 rows x 32 K (f16)
+constexpr int kGOpBytes = 2 * kGBTile;         // one B tile (global and shared layout alike)
+constexpr uint32_t kGTmemCols = 512;           // D: 256 (xh rows, then xl rows), A: 8 stages x 32
+constexpr uint32_t kGTmemA = 256;
+constexpr uint32_t kGTmemAStage = 32;
+constexpr size_t kGSmem = 128 + (size_t)kGOpStages * kGOpBytes + (size_t)kGGroups * kGRawSlots * kGRawBytes;
+static_assert(kGRawScl % 16 == 0 && kGRawBytes % 16 == 0 && kGOpBytes % 128 == 0, "bulk-copy alignment");
+static_assert(kGOpStages * kGOpBytes >= 4 * kGRows * 32 * 4, "SwiGLU exchange fits the operand stages");
+
+// Byte offset of element (row r, k) of a B tile (K-major core matrices of
+// 8 rows x 8 K, 128 contiguous bytes; 4 per row block along K), hi half.
+__device__ __forceinline__ int btile_off(int r, int kc) { return ((r >> 3) * 4 + kc) * 128 + (r & 7) * 16; }
+
+// Per-row prologue constants of a prefill GEMM input (one CTA per row):
+//   rexp[r]  operand exponent: of max |x[r][0..k)| (X_PLAIN, the value
+//            k_gemv_mma finds over an unsplit K), or of the bound
+//            sqrt(k) max |gamma| (1 + 2^-10) (X_RMSNORM);
+//   rinv[r]  X_RMSNORM: 1 / sqrt(ss / k + 1e-6) (rms_norm_f16, gemv.rs:445-454)
+//            from the per-32-column sums of squares, summed as k_gemv_mma sums them.
+template <int XM>
+__global__ void __launch_bounds__(256) k_row_prep(const GemvArgs a, int *rexp, float *rinv) {
+    __shared__ float red[8];
+    const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int64_t k = a.w.k;
+    float m = 0.0f;
+    if constexpr (XM == X_RMSNORM) {
+        for (int64_t i = threadIdx.x; i < k; i += 256) m = fmaxf(m, fabsf(__half2float(a.gamma[i])));
+    }
+    griddep_launch_dependents();
+    griddep_wait();
+    if constexpr (XM == X_PLAIN) {
+        const float4 *xr = reinterpret_cast<const float4 *>(a.x + (int64_t)r * a.ldx);
+        for (int64_t i = threadIdx.x; i < k / 4; i += 256) {
+            const float4 v = __ldcg(xr + i);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    } else {
+        if (warp == 0) {
+            float t = 0.0f;
+            for (int i = lane; i < a.ss_tiles; i += 32) t += __ldcg(a.ss + (int64_t)r * a.ldss + i);
+            t = warp_sum(t);
+            if (lane == 0) rinv[r] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(t, (float)k), 1e-6f)));
+        }
+    }
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float t = 0.0f;
+#pragma unroll
+        for (int w = 0; w < 8; w++) t = fmaxf(t, red[w]);
+        if constexpr (XM == X_RMSNORM) t = __fmul_rn(__fmul_rn(__fsqrt_rn((float)k), t), 1.0009765625f);
+        rexp[r] = operand_exponent(t);
+    }
+}
+
+// B tiles of a prefill GEMM: block (row tile, group of 4 stages), thread
+// (row r = tid % 128, stages 2 (tid / 128) + {0, 1}).  Row r's 32 K values
+// of a stage: x (normalised: (x * inv) * gamma), times 2^rexp, split as
+// xh = f16(x), xl = f16(x - xh), exactly as k_gemv_mma forms its B operand;
+// rows past `rows` are zero.
+template <int XM>
+__global__ void __launch_bounds__(256) k_b_convert(const GemvArgs a, const int *rexp, const float *rinv,
+                                                   uint8_t *bop) {
+    const int rt = blockIdx.x, r = threadIdx.x & 127;
+    const int row = rt * kGRows + r;
+    const bool rvalid = row < a.rows;
+    const int nst = (int)(a.w.k / kStageK);
+    griddep_launch_dependents();
+    griddep_wait();
+    const float rscale = __int_as_float((127 + (rvalid ? __ldcg(rexp + row) : 0)) << 23);
+    float inv_r = 1.0f;
+    if constexpr (XM == X_RMSNORM) inv_r = rvalid ? __ldcg(rinv + row) : 1.0f;
+    bool big = false;
+    for (int s = 0; s < 2; s++) {
+        const int t = blockIdx.y * 4 + 2 * (threadIdx.x >> 7) + s;
+        if (t >= nst) break;
+        const int64_t k0 = (int64_t)t * kStageK;
+        uint8_t *tile = bop + ((int64_t)rt * nst + t) * kGOpBytes;
+#pragma unroll
+        for (int kc = 0; kc < 4; kc++) {
+            float xv[8];
+            if (rvalid) {
+                const float4 *xp = reinterpret_cast<const float4 *>(a.x + (int64_t)row * a.ldx + k0 + 8 * kc);
+                const float4 u0 = __ldcg(xp), u1 = __ldcg(xp + 1);
+                xv[0] = u0.x; xv[1] = u0.y; xv[2] = u0.z; xv[3] = u0.w;
+                xv[4] = u1.x; xv[5] = u1.y; xv[6] = u1.z; xv[7] = u1.w;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) xv[i] = 0.0f;
+            }
+            if constexpr (XM == X_RMSNORM) {
+                const uint4 gq = __ldg(reinterpret_cast<const uint4 *>(a.gamma + k0 + 8 * kc));
+                const uint32_t gw[4] = {gq.x, gq.y, gq.z, gq.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float2 gf = __half22float2(u2h(gw[i]));
+                    xv[2 * i] = __fmul_rn(__fmul_rn(xv[2 * i], inv_r), gf.x);
+                    xv[2 * i + 1] = __fmul_rn(__fmul_rn(xv[2 * i + 1], inv_r), gf.y);
+                }
+            }
+            uint32_t bh[4], bl[4];
+#pragma unroll
+            for (int i = 0; i < 8; i++) xv[i] = __fmul_rn(xv[i], rscale);  // exact: a power of two
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                big |= fabsf(xv[2 * i]) > 65504.0f || fabsf(xv[2 * i + 1]) > 65504.0f;
+                const __half2 hh = __floats2half2_rn(xv[2 * i], xv[2 * i + 1]);
+                const float2 hf = __half22float2(hh);
+                bh[i] = h2u(hh);
+                bl[i] = h2u(__floats2half2_rn(__fsub_rn(xv[2 * i], hf.x), __fsub_rn(xv[2 * i + 1], hf.y)));
+            }
+            const int off = btile_off(r, kc);
+            __stcg(reinterpret_cast<uint4 *>(tile + off), make_uint4(bh[0], bh[1], bh[2], bh[3]));
+            __stcg(reinterpret_cast<uint4 *>(tile + kGBTile + off), make_uint4(bl[0], bl[1], bl[2], bl[3]));
+        }
+    }
+    if (big) raise_error(a.err, kDevF16Range);
+}
+
+template <int XM, int EM>
+__global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
+    constexpr int CO = (EM == E_SWIGLU) ? kMmaGroups / 2 : kMmaGroups;  // output groups per CTA
+    extern __shared__ uint8_t gm_dyn[];
+    __shared__ __align__(8) uint64_t b_full[kGOpStages], a_full[kGOpStages], op_empty[kGOpStages], d_full;
+    __shared__ uint32_t tmem_slot;
+    __shared__ int rexp_s[kGRows];
+    __shared__ int abort_s;
+    __shared__ int grp_go[kGGroups];  // a converter group's decision for its current stage
+
+    uint8_t *smem = reinterpret_cast<uint8_t *>(((uintptr_t)gm_dyn + 127) & ~(uintptr_t)127);
+    uint8_t *op_base = smem;
+    uint8_t *raw_base = smem + kGOpStages * kGOpBytes;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t c0 = (int64_t)blockIdx.x * kMmaGroups;
+    const int nst = (int)(a.w.k / kStageK);
+    const int r_begin = blockIdx.y * kGRows;
+    const int nvalid = min(kGRows, a.rows - r_begin);
+    volatile int *abort_v = &abort_s;
+
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < kGOpStages; i++) {
+            mbar_init(&b_full[i], 1);     // expect_tx arrival (+ the B tile's bytes)
+            mbar_init(&a_full[i], 4);     // the converter group: A in tensor memory
+            mbar_init(&op_empty[i], 1);   // the MMAs of the stage (commit)
+        }
+        mbar_init(&d_full, 1);
+        abort_s = 0;
+        mbar_fence_init();
+    }
+    if (warp == kGMmaWarp) {
+        tc::tmem_alloc(&tmem_slot, kGTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+
+    if (warp == kGProdWarp) {
+        // ---------------------------------------------------------- producer
+        // one bulk copy per stage: the stage's B tile, once the MMAs of the
+        // stage that last used its operand slot are done
+        auto issue_b = [&](int t) {
+            if (lane == 0) {
+                const int o = t % kGOpStages;
+                mbar_arrive_expect_tx(&b_full[o], kGOpBytes);
+                bulk_g2s(op_base + o * kGOpBytes, a.bop + ((int64_t)blockIdx.y * nst + t) * kGOpBytes, kGOpBytes,
+                         &b_full[o]);
+            }
+        };
+        if (lane == 0 && (a.pf0_bytes | a.pf1_bytes)) {
+            const uint64_t nctas = (uint64_t)gridDim.x * gridDim.y;
+            const uint64_t id = (uint64_t)blockIdx.y * gridDim.x + blockIdx.x;
+            l2_prefetch_share(a.pf0, a.pf0_bytes, id, nctas);
+            l2_prefetch_share(a.pf1, a.pf1_bytes, id, nctas);
+        }
+        griddep_launch_dependents();
+        griddep_wait();
+        const int preb = min(nst, kGOpStages);
+        for (int t = 0; t < preb; t++) issue_b(t);
+        int issued_b = preb;
+        for (int t = 0; t + kGOpStages < nst; t++) {
+            bool ok = true;
+            if (lane == 0) ok = wait_or_abort(&op_empty[t % kGOpStages], (t / kGOpStages) & 1, abort_v, a.err);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            issue_b(t + kGOpStages);
+            issued_b = t + kGOpStages + 1;
+        }
+        // the copies of the last stages land before the CTA may exit (bounded)
+        if (lane == 0) {
+            for (int t = max(0, issued_b - kGOpStages); t < issued_b; t++) {
+                const long long t0 = clock64();
+                while (!mbar_try_wait(&b_full[t % kGOpStages], (t / kGOpStages) & 1))
+                    if (clock64() - t0 > (1ll << 31)) break;
+            }
+        }
+        __syncwarp();
+    } else if (warp == kGMmaWarp) {
+        // ---------------------------------------------------------- MMA issue
+        if (lane == 0) {
+            constexpr uint32_t id256 = tc::idesc_f16_f32(128, 2 * kGRows);
+            constexpr uint32_t id128 = tc::idesc_f16_f32(128, kGRows);
+            for (int t = 0; t < nst; t++) {
+                const int o = t % kGOpStages;
+                if (!wait_or_abort(&a_full[o], (t / kGOpStages) & 1, abort_v, a.err)) break;
+                if (!wait_or_abort(&b_full[o], (t / kGOpStages) & 1, abort_v, a.err)) break;
+                tc::fence_after_sync();
+                const uint32_t bbase = smem_u32(op_base + o * kGOpBytes);
+                const uint32_t abase = tmem + kGTmemA + (uint32_t)o * kGTmemAStage;
+#pragma unroll
+                for (int j = 0; j < kStageK / 16; j++) {
+                    // K = 16: two 8-k core columns of B (rows: 128 xh, then 128 xl)
+                    const uint64_t bhl = tc::smem_desc(bbase + (uint32_t)j * 256, kLBO, kSBO);
+                    tc::mma_f16_ts(tmem, abase + 8 * j, bhl, id256, (t | j) != 0 ? 1u : 0u);
+                    tc::mma_f16_ts(tmem, abase + 16 + 8 * j, bhl, id128, 1u);  // A2 * xh
+                }
+                tc::commit(&op_empty[o]);
+            }
+            tc::commit(&d_full);
+        }
+        __syncwarp();
+    } else {
+        // ---------------------------------------------------------- converters
+        // Converter group cgp = warp / 4 takes stages t = cgp + kGGroups j and
+        // streams their weights itself: 16-byte cp.async pieces (thread
+        // (g, lane): row `lane` of column group g; lanes 0-3 also a quarter of
+        // the group's scales) into its own ring of kGRawSlots slots, one
+        // cp.async group per stage, issued kGRawSlots - 1 stages ahead.
+        const int g = warp & 3, cgp = warp >> 2;
+        const int nj = nst > cgp ? (nst - cgp + kGGroups - 1) / kGGroups : 0;
+        uint8_t *raw_grp = raw_base + cgp * kGRawSlots * kGRawBytes;
+        auto prefetch = [&](int j) {  // weights of the group's j-th stage (immutable)
+            if (j < nj) {
+                uint8_t *raw = raw_grp + (j % kGRawSlots) * kGRawBytes;
+                const int64_t k0 = (int64_t)(cgp + kGGroups * j) * kStageK;
+                cp_async16(raw + kGRawNib + g * kNibGroupStride + lane * 16, a.w.nib + (c0 + g) * a.w.kpad + k0 + lane);
+                if (lane < 4)
+                    cp_async16(raw + kGRawScl + g * kSclGroupStride + lane * 16,
+                               reinterpret_cast<const uint8_t *>(a.w.scl + (c0 + g) * a.w.kpad + k0) + lane * 16);
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+        };
+        auto group_sync = [&]() { asm volatile("bar.sync %0, 128;" ::"r"(2 + cgp) : "memory"); };
+        for (int j = 0; j < kGRawSlots; j++) prefetch(j);
+        griddep_launch_dependents();
+        griddep_wait();
+        if (threadIdx.x < kGRows)
+            rexp_s[threadIdx.x] = (int)threadIdx.x < nvalid ? __ldcg(a.rexp + r_begin + threadIdx.x) : 0;
+        // A role: column 32 g + lane of the tile, as in k_gemv_mma
+        const int cq = lane & 7;
+        const uint32_t sel = (uint32_t)(cq >> 1) | ((uint32_t)(4 + (cq >> 1)) << 8);
+        const uint32_t nmask = (cq & 1) ? 0x00F000F0u : 0x000F000Fu;
+        const __half2 m1 = __float2half2_rn((cq & 1) ? 0.0625f : 1.0f);
+        const __half2 c1 = __float2half2_rn((cq & 1) ? -72.0f : -1032.0f);
+        const int E = a.w.mma_exp;
+        const __half2 pw = __float2half2_rn(__int_as_float((127 + E) << 23));
+        const uint32_t a_lane = tmem + ((uint32_t)(32 * g) << 16) + kGTmemA;
+
+        for (int j = 0; j < nj; j++) {
+            const int t = cgp + kGGroups * j, o = t % kGOpStages;
+            // one thread waits until tensor-memory stage o is free (the MMAs of
+            // stage t - kGOpStages are done) and decides for the group, which
+            // leaves the loop as a whole (its barriers stay matched)
+            if (g == 0 && lane == 0) {
+                bool ok = t < kGOpStages || wait_or_abort(&op_empty[o], ((t / kGOpStages) & 1) ^ 1, abort_v, a.err);
+                grp_go[cgp] = ok && !*abort_v;
+            }
+            // this thread's pieces of stage j have landed; the group's barrier
+            // makes every piece (and the decision) visible to the group
+            asm volatile("cp.async.wait_group %0;" ::"n"(kGRawSlots - 1) : "memory");
+            group_sync();
+            if (!*reinterpret_cast<volatile int *>(&grp_go[cgp])) break;
+            tc::fence_after_sync();
+            const uint8_t *raw = raw_grp + (j % kGRawSlots) * kGRawBytes;
+            const uint8_t *nibg = raw + kGRawNib + g * kNibGroupStride + (lane >> 3) * 4;
+            uint4 sc4[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                sc4[i] = *reinterpret_cast<const uint4 *>(raw + kGRawScl + g * kSclGroupStride + 16 * i);
+            uint32_t A1[16], A2[16];
+#pragma unroll
+            for (int p = 0; p < 16; p++) {
+                const uint32_t w0 = *reinterpret_cast<const uint32_t *>(nibg + (2 * p) * 16);
+                const uint32_t w1 = *reinterpret_cast<const uint32_t *>(nibg + (2 * p + 1) * 16);
+                const uint32_t sw = (p & 3) == 0 ? sc4[p >> 2].x
+                                  : (p & 3) == 1 ? sc4[p >> 2].y
+                                  : (p & 3) == 2 ? sc4[p >> 2].z : sc4[p >> 2].w;
+                const __half2 s2 = __hmul2(u2h(sw), pw);            // exact (power of two)
+                const __half2 sa = u2h(h2u(s2) & 0xFFF8FFF8u);      // top 8 significant bits
+                const __half2 sb = __hsub2(s2, sa);                 // exact remainder
+                const uint32_t pr = __byte_perm(w0, w1, sel);
+                const __half2 q8 = __hfma2(u2h((pr & nmask) | 0x64006400u), m1, c1);
+                A1[p] = h2u(__hmul2(q8, sa));
+                A2[p] = h2u(__hmul2(q8, sb));
+            }
+            tc::st_32x32b_x16(a_lane + (uint32_t)o * kGTmemAStage, A1);
+            tc::st_32x32b_x16(a_lane + (uint32_t)o * kGTmemAStage + 16, A2);
+            tc::fence_before_sync();  // tensor-memory stores -> the MMA thread
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&a_full[o]);
+            group_sync();        // every thread of the group is done with this slot
+            prefetch(j + kGRawSlots);
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        asm volatile("bar.sync 1, %0;" ::"n"(kGConvWarps * 32) : "memory");  // rexp_s
+
+        // ---------------------------------------------------------- epilogue
+        // warp w: column group w % 4 (its TMEM lanes), rows kGEpiRows (w / 4) ..
+        bool ok = wait_or_abort(&d_full, 0, abort_v, a.err);
+        ok = __all_sync(0xffffffffu, ok);
+        tc::fence_after_sync();
+        const float unscale = __int_as_float((127 - E) << 23);
+        const int64_t n_out = (EM == E_SWIGLU) ? (a.w.C / 2) * 32 : a.w.n;
+        float *xch = reinterpret_cast<float *>(op_base);  // SwiGLU: [group][row][column]
+#pragma unroll 1
+        for (int ch = 0; ch < kGEpiRows / 32; ch++) {
+            const int n0 = kGEpiRows * cgp + 32 * ch;
+            float vh[32], vl[32];
+            if (ok) {
+                tc::ld_32x32b_x32(tmem + ((uint32_t)(32 * g) << 16) + (uint32_t)n0, vh);
+                tc::ld_32x32b_x32(tmem + ((uint32_t)(32 * g) << 16) + (uint32_t)(kGRows + n0), vl);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; i++) vh[i] = vl[i] = 0.0f;
+            }
+#pragma unroll
+            for (int n = 0; n < 32; n++)
+                vh[n] = __fmul_rn(__fmul_rn(__fadd_rn(vh[n], vl[n]), unscale),
+                                  __int_as_float((127 - rexp_s[n0 + n]) << 23));
+            if constexpr (EM == E_SWIGLU) {
+#pragma unroll
+                for (int n = 0; n < 32; n++) xch[(g * kGRows + n0 + n) * 32 + lane] = vh[n];
+            } else {
+                const int64_t grp = c0 + g;
+#pragma unroll 4
+                for (int n = 0; n < 32; n++) {
+                    const int row = n0 + n;
+                    if (row < nvalid) {
+                        if constexpr (EM == E_RESID) {
+                            // x[j] += attn_out / mlp (talker.rs:334-336, 347-349)
+                            const float yr = __ldcg(a.y + (int64_t)(r_begin + row) * a.ldy + grp * 32 + lane);
+                            finalize_resid(a, r_begin + row, grp, lane, __fadd_rn(yr, vh[n]));
+                        } else {
+                            finalize_group<EM>(a, r_begin + row, grp, lane, vh[n], 0.0f, n_out, CO);
+                        }
+                    }
+                }
+            }
+        }
+        if constexpr (EM == E_SWIGLU) {
+            // silu(gate) * up (talker.rs:341-345): group 2u is gate, 2u + 1 up
+            asm volatile("bar.sync 1, %0;" ::"n"(kGConvWarps * 32) : "memory");
+            constexpr int RW = 2 * kGRows / kGConvWarps;  // rows per warp (two units)
+            const int u = warp & 1, rb = (warp >> 1) * RW;
+            for (int n = 0; n < RW; n++) {
+                const int row = rb + n;
+                if (row < nvalid)
+                    finalize_group<EM>(a, r_begin + row, c0 / 2 + u, lane, xch[((2 * u) * kGRows + row) * 32 + lane],
+                                       xch[((2 * u + 1) * kGRows + row) * 32 + lane], n_out, CO);
+            }
+        }
+        // tail columns beyond the last full group stay zero (gemv.rs:846-861)
+        if (EM == E_STORE && a.w.n > a.w.C * 32 && blockIdx.x == 0) {
+            for (int rr = 0; rr < nvalid; rr++)
+                for (int64_t col = a.w.C * 32 + threadIdx.x; col < a.w.n; col += kGConvWarps * 32)
+                    a.y[(int64_t)(r_begin + rr) * a.ldy + col] = 0.0f;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();  // tensor memory read back
+    if (warp == kGMmaWarp) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kGTmemCols);
+    }
+}
+
+template <int XM, int EM>
+int gemm_attrs() {
+    QORA_CUDA(cudaFuncSetAttribute(k_gemm_mma<XM, EM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGSmem));
+    return QORA_OK;
+}
+
+template <int XM>
+int launch_gemm_e(const GemvArgs &a, int emode, dim3 grid, cudaStream_t st) {
+    const dim3 block(kGThreads);
+    switch (emode) {
+        case E_STORE: return launch_ex(k_gemm_mma<XM, E_STORE>, grid, block, kGSmem, st, 1u, a);
+        case E_BIAS: return launch_ex(k_gemm_mma<XM, E_BIAS>, grid, block, kGSmem, st, 1u, a);
+        case E_RESID: return launch_ex(k_gemm_mma<XM, E_RESID>, grid, block, kGSmem, st, 1u, a);
+        case E_SWIGLU: return launch_ex(k_gemm_mma<XM, E_SWIGLU>, grid, block, kGSmem, st, 1u, a);
+    }
+    return set_error(QORA_ERR_INVALID, "bad epilogue mode %d", emode);
+}
+
 template <int XM, int EM>
 int mma_attrs() {
     QORA_CUDA(cudaFuncSetAttribute(k_gemv_mma<XM, EM>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
@@ -731,6 +1166,14 @@ int query_max_clusters(int dev) {
 }  // namespace
 
 int gemv_mma_init() {
+    QORA_TRY((gemm_attrs<X_PLAIN, E_STORE>()));
+    QORA_TRY((gemm_attrs<X_PLAIN, E_BIAS>()));
+    QORA_TRY((gemm_attrs<X_PLAIN, E_RESID>()));
+    QORA_TRY((gemm_attrs<X_PLAIN, E_SWIGLU>()));
+    QORA_TRY((gemm_attrs<X_RMSNORM, E_STORE>()));
+    QORA_TRY((gemm_attrs<X_RMSNORM, E_BIAS>()));
+    QORA_TRY((gemm_attrs<X_RMSNORM, E_RESID>()));
+    QORA_TRY((gemm_attrs<X_RMSNORM, E_SWIGLU>()));
     QORA_TRY(mma_attrs_e<X_PLAIN>());
     QORA_TRY(mma_attrs_e<X_RMSNORM>());
     QORA_TRY(mma_attrs_e<X_EMBED>());
@@ -788,6 +1231,53 @@ GemvPlan plan_gemv_mma(int64_t k, int64_t C, int rows, int emode, int num_sms) {
     p.block = dim3(kMmaThreads);
     (void)emode;
     return p;
+}
+
+// QORA_PREFILL_GEMM=0 in the environment sends prefill GEMMs back to
+// k_gemv_mma (the same bits, for comparison).
+bool prefill_gemm_disabled_by_env() {
+    static const bool off = [] {
+        const char *v = getenv("QORA_PREFILL_GEMM");
+        return v && v[0] == '0';
+    }();
+    return off;
+}
+
+bool gemm_mma_supported(const GemvArgs &a, int xmode, int emode) {
+    if (prefill_gemm_disabled_by_env()) return false;
+    if (xmode != X_PLAIN && xmode != X_RMSNORM) return false;
+    if (!gemv_mma_supported(a, xmode, emode)) return false;
+    // no normalised side copy and no global stage (argmax, cache advance)
+    if (a.side || a.tbest_v || a.amax || a.adv_len) return false;
+    return a.rows >= 1 && a.rows <= kMaxRows;
+}
+
+int launch_gemm_mma(GemvArgs a, int xmode, int emode, const GemmScratch &sc, cudaStream_t st, int *launches) {
+    if (!gemm_mma_supported(a, xmode, emode))
+        return set_error(QORA_ERR_INVALID, "prefill GEMM: unsupported launch");
+    const int rt = (a.rows + kGRows - 1) / kGRows, nst = (int)(a.w.k / kStageK);
+    if (!sc.rexp || !sc.rinv || !sc.bop || a.rows > sc.rows || (size_t)rt * nst * kGOpBytes > sc.bop_bytes)
+        return set_error(QORA_ERR_INVALID, "prefill GEMM: scratch too small (%d rows, k %lld)", a.rows,
+                         (long long)a.w.k);
+    a.S = 1;
+    a.gticket = nullptr;
+    a.rexp = sc.rexp;
+    a.bop = sc.bop;
+    const dim3 grid((unsigned)(a.w.C / kMmaGroups), (unsigned)rt);
+    const dim3 cgrid((unsigned)rt, (unsigned)((nst + 3) / 4));
+    if (xmode == X_PLAIN) {
+        QORA_TRY(launch_ex(k_row_prep<X_PLAIN>, dim3((unsigned)a.rows), dim3(256), 0, st, 1u, a, sc.rexp, sc.rinv));
+        QORA_TRY(launch_ex(k_b_convert<X_PLAIN>, cgrid, dim3(256), 0, st, 1u, a, (const int *)sc.rexp,
+                           (const float *)sc.rinv, sc.bop));
+        QORA_TRY(launch_gemm_e<X_PLAIN>(a, emode, grid, st));
+    } else {
+        QORA_TRY(launch_ex(k_row_prep<X_RMSNORM>, dim3((unsigned)a.rows), dim3(256), 0, st, 1u, a, sc.rexp, sc.rinv));
+        QORA_TRY(launch_ex(k_b_convert<X_RMSNORM>, cgrid, dim3(256), 0, st, 1u, a, (const int *)sc.rexp,
+                           (const float *)sc.rinv, sc.bop));
+        QORA_TRY(launch_gemm_e<X_RMSNORM>(a, emode, grid, st));
+    }
+    if (launches) *launches += 3;
+    return QORA_OK;
 }
 
 int launch_gemv_mma(const GemvArgs &a, int xmode, int emode, const GemvPlan &p, cudaStream_t st) {

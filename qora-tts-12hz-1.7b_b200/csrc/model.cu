@@ -155,6 +155,11 @@ struct Launcher {
 
     int gemv(GemvArgs a, int xm, int em) {
         GemvPlan p;
+        if (!a.err) a.err = ctx->err.as<int>();
+        if (fixed && gemm_mma_supported(a, xm, em)) {
+            // prefill: the tensor-core GEMM (k_gemv_mma's bits without a K split)
+            return launch_gemm_mma(a, xm, em, w->gemm_scratch(), st, &count);
+        }
         if (fixed && gemv_mma_supported(a, xm, em)) {
             // the tensor-core kernel with the K split planned for a full
             // kMaxRows chunk, whatever this launch's row count: the same split

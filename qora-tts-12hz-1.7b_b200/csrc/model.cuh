@@ -24,8 +24,18 @@ struct LayerDev {
 
 // Activation and scratch buffers sized for `rows` rows.
 struct Work {
-    DevBuf x, ss, qkv, attn, h, logits, gticket, tbest_v, tbest_i, apo, apml, atk;
+    DevBuf x, ss, qkv, attn, h, logits, gticket, tbest_v, tbest_i, apo, apml, atk, rexp, rinv, bop;
     int rows = 0;
+
+    GemmScratch gemm_scratch() {
+        GemmScratch s;
+        s.rexp = rexp.as<int>();
+        s.rinv = rinv.as<float>();
+        s.bop = bop.as<uint8_t>();
+        s.rows = rows;
+        s.bop_bytes = bop.bytes;
+        return s;
+    }
 
     int alloc(int rows_, int64_t hidden, int64_t qkvn, int64_t qd, int64_t ffn, int64_t vocab,
               int kvh, int heads, int hd) {
@@ -44,6 +54,11 @@ struct Work {
         QORA_TRY(apml.alloc(attn_part_ml_floats(rows, kvh, heads) * 4));
         QORA_TRY(atk.alloc((size_t)rows * kvh * 4));
         QORA_TRY(atk.zero());
+        QORA_TRY(rexp.alloc((size_t)rows * 4));
+        QORA_TRY(rinv.alloc((size_t)rows * 4));
+        // prefill GEMM B tiles: rows rounded up to 128, the widest K (hidden, qd or ffn)
+        const int64_t kmax = std::max<int64_t>(hidden, std::max<int64_t>(qd, ffn));
+        QORA_TRY(bop.alloc((size_t)((rows + 127) / 128) * 128 * kmax * 4));
         QORA_CUDA(cudaDeviceSynchronize());
         return QORA_OK;
     }
