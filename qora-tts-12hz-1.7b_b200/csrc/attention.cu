@@ -11,6 +11,7 @@
 // heads sharing that kv head, so every K/V byte is read once per row.  Splits
 // are merged flash-decoding style by the last-arriving CTA in split order.
 #include "attention_impl.cuh"
+#include "tc.cuh"
 
 namespace qora {
 
@@ -295,6 +296,332 @@ __global__ void __launch_bounds__(kPfThreads, 2) k_prefill_attn(const AttnArgs a
             r.w = __fdiv_rn(o[i][jj][3], l);
             *reinterpret_cast<float4 *>(dst + 4 * tn + 64 * jj) = r;
         }
+    }
+}
+
+// ------------------------------------------------------------------------
+// Causal prefill attention on the tensor cores (head_dim 128): the same
+// computation as k_prefill_attn, with Q K^T and P V as tcgen05 MMAs.
+// One CTA takes 128 query vectors (128 / G tokens x the G query heads of one
+// kv head: vector m = head (m / BQ), token (m % BQ)) = the MMA's M rows, and
+// walks the key positions in tiles of 64 that start at multiples of 64
+// (absolute positions, so every row's result has the same bits in any
+// prefill chunk).  Per tile:
+//   * the K / V rows are read from the cache (row addressing: slab or
+//     paged), K as B[key][d] and V transposed as B[d][key], both split into
+//     f16 hi + lo (x = xh + xl to ~22 bits) in the canonical K-major layout;
+//   * S = Qh Kh + Qh Kl + Ql Kh (the dropped Ql Kl is ~2^-22 relative),
+//     accumulated in f32 in tensor memory; Q and K are scaled by powers of
+//     two fixed per launch (from the qk-norm bounds sqrt(128) max |gamma|),
+//     undone exactly in the softmax;
+//   * the online softmax of k_prefill_attn on S (row m in TMEM lane m: two
+//     threads per row, each the whole row's max and sum, half the row's P);
+//   * O_tile = Ph Vh + Ph Vl + Pl Vh (P in [0, 1] as f16 hi + lo), added by
+//     the CUDA cores into the row's running output: O = O * corr + O_tile.
+// One thread issues the MMAs; completion comes through mbarriers.  V values
+// beyond the f16 range raise kDevF16Range.
+constexpr int kTcM = 128;        // query vectors per CTA (MMA M)
+constexpr int kTcN = 64;         // keys per tile
+constexpr int kTcThreads = 256;
+constexpr uint32_t kTcTmemCols = 256;  // S: 64 columns, O_tile: 128
+// shared memory (bytes): Q hi / lo [128 x 128], K hi / lo [64 x 128],
+// V^T hi / lo [128 x 64], P hi / lo [128 x 64], all f16 K-major core matrices
+constexpr int kTcQ = 0, kTcQl = 32768, kTcK = 65536, kTcKl = 81920, kTcV = 98304, kTcVl = 114688,
+              kTcP = 131072, kTcPl = 147456, kTcBytes = 163840;
+
+// Byte offset of (row r, 8-element K block kb) in a K-major operand whose
+// rows have `nkb` K blocks: core matrices of 8 rows x 16 bytes, K blocks
+// adjacent (LBO 128), 8-row blocks nkb * 128 apart (SBO).
+__device__ __forceinline__ int tc_off(int r, int kb, int nkb) { return ((r >> 3) * nkb + kb) * 128 + (r & 7) * 16; }
+
+__device__ __forceinline__ uint32_t tc_h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+
+// hi / lo f16 pairs of 8 values (already scaled), as two 16-byte rows
+__device__ __forceinline__ bool tc_split8(const float (&x)[8], uint4 &hi, uint4 &lo) {
+    uint32_t h[4], l[4];
+    bool big = false;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        big |= fabsf(x[2 * i]) > 65504.0f || fabsf(x[2 * i + 1]) > 65504.0f;
+        const __half2 hh = __floats2half2_rn(x[2 * i], x[2 * i + 1]);
+        const float2 hf = __half22float2(hh);
+        h[i] = tc_h2u(hh);
+        l[i] = tc_h2u(__floats2half2_rn(__fsub_rn(x[2 * i], hf.x), __fsub_rn(x[2 * i + 1], hf.y)));
+    }
+    hi = make_uint4(h[0], h[1], h[2], h[3]);
+    lo = make_uint4(l[0], l[1], l[2], l[3]);
+    return big;
+}
+
+// Exponent e with (bound * 2^e) in [2^14, 2^15) (0 for a zero or non-finite
+// bound; clamped to [-60, 60], so that 2^-(eq + ek) is a normal float).
+__device__ __forceinline__ int tc_exponent(float m) {
+    if (!(m > 0.0f) || !(m <= 3.4e38f)) return 0;
+    const int ex = (int)((__float_as_uint(m) >> 23) & 0xFF) - 127;
+    return max(-60, min(60, 14 - ex));
+}
+
+template <int G>
+__global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArgs a) {
+    constexpr int HD = 128;
+    constexpr int BQ = kTcM / G;    // tokens per CTA
+    extern __shared__ __align__(1024) uint8_t tc_dyn[];
+    uint8_t *sm = tc_dyn;
+    __shared__ __align__(8) uint64_t bar_s, bar_o;
+    __shared__ uint32_t tmem_slot;
+    __shared__ float red_s[8];
+    const int qb = gridDim.x - 1 - blockIdx.x;  // the longest query blocks first
+    const int h = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) {
+        mbar_init(&bar_s, 1);
+        mbar_init(&bar_o, 1);
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        tc::tmem_alloc(&tmem_slot, kTcTmemCols);
+        tc::tmem_relinquish();
+    }
+    // power-of-two operand scales from the qk-norm bounds (immutable gammas):
+    // |q|, |k| <= sqrt(128) max |gamma| after the norm and the rotation
+    {
+        float m = 0.0f;
+        if (tid < HD) m = fabsf(__half2float(a.q_gamma[tid]));
+        else m = fabsf(__half2float(a.k_gamma[tid - HD]));
+        m = warp_max(m);
+        if (lane == 0) red_s[warp] = m;
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    float gq = 0.0f, gk = 0.0f;
+#pragma unroll
+    for (int w = 0; w < 4; w++) {
+        gq = fmaxf(gq, red_s[w]);
+        gk = fmaxf(gk, red_s[4 + w]);
+    }
+    const float sq = __fmul_rn(__fsqrt_rn((float)HD), 1.0009765625f);
+    const int eq = tc_exponent(__fmul_rn(sq, gq)), ek = tc_exponent(__fmul_rn(sq, gk));
+    const float qs = __int_as_float((127 + eq) << 23), ks = __int_as_float((127 + ek) << 23);
+    const float unscale = __int_as_float((127 - eq - ek) << 23);
+
+    griddep_launch_dependents();
+    griddep_wait();
+    const int L0 = __ldcg(a.len + b);
+    bool bad = L0 + a.T > a.kv.max_pos;
+    if (bad && tid == 0 && qb == 0 && h == 0) raise_error(a.err, kDevRange);
+    const int t0 = qb * BQ;
+    const int nq = min(BQ, a.T - t0);
+    const int kend = L0 + t0 + max(nq, 0);  // keys [0, kend) are visible to some row
+    const int ntiles = (bad || nq <= 0) ? 0 : (kend + kTcN - 1) / kTcN;
+    bool big = false;
+
+    // ---- Q (A operand of S): vector m = head g = m / BQ, token m % BQ
+    for (int i = tid; i < kTcM * (HD / 8); i += kTcThreads) {
+        const int m = i >> 4, kb = i & 15;
+        const int g = m / BQ, tl = m % BQ;
+        float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (tl < nq) {
+            const float4 *src = reinterpret_cast<const float4 *>(
+                a.qkv + (int64_t)(b * a.T + t0 + tl) * a.ldqkv + (int64_t)(h * G + g) * HD + 8 * kb);
+            const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
+            x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
+            x[4] = u1.x; x[5] = u1.y; x[6] = u1.z; x[7] = u1.w;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) x[e] = __fmul_rn(x[e], qs);
+        uint4 hi, lo;
+        big |= tc_split8(x, hi, lo);
+        *reinterpret_cast<uint4 *>(sm + kTcQ + tc_off(m, kb, 16)) = hi;
+        *reinterpret_cast<uint4 *>(sm + kTcQl + tc_off(m, kb, 16)) = lo;
+    }
+
+    // softmax role: row m = 32 (warp % 4) + lane (its TMEM lane), half hs =
+    // warp / 4 of the row's keys for P and of the output columns
+    const int mrow = 32 * (warp & 3) + lane, hs = warp >> 2;
+    const int tl_r = mrow % BQ;
+    const int qpos = L0 + t0 + tl_r;
+    const bool rvalid = tl_r < nq;
+    const float scale = __fdiv_rn(1.0f, __fsqrt_rn((float)HD));  // talker.rs:305
+    float m_run = -INFINITY, l_run = 0.0f;
+    float o[64];
+#pragma unroll
+    for (int i = 0; i < 64; i++) o[i] = 0.0f;
+    const uint32_t t_lane = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+    constexpr uint32_t id_s = tc::idesc_f16_f32(128, kTcN);
+    constexpr uint32_t id_o = tc::idesc_f16_f32(128, HD);
+    const uint32_t sbase = smem_u32(sm);
+
+    for (int kt = 0; kt < ntiles; kt++) {
+        const int k0 = kt * kTcN;
+        // ---- K tile: B[key n][d]; thread -> (key, 8-d block) pairs
+        for (int i = tid; i < kTcN * (HD / 8); i += kTcThreads) {
+            const int n = i >> 4, kb = i & 15;
+            float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+            if (k0 + n < kend) {  // never visible otherwise: zeros
+                const float4 *src = reinterpret_cast<const float4 *>(a.kv.k + a.kv.row(b, h, k0 + n) + 8 * kb);
+                const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
+                x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
+                x[4] = u1.x; x[5] = u1.y; x[6] = u1.z; x[7] = u1.w;
+            }
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = __fmul_rn(x[e], ks);
+            uint4 hi, lo;
+            big |= tc_split8(x, hi, lo);
+            *reinterpret_cast<uint4 *>(sm + kTcK + tc_off(n, kb, 16)) = hi;
+            *reinterpret_cast<uint4 *>(sm + kTcKl + tc_off(n, kb, 16)) = lo;
+        }
+        // ---- V tile transposed: B[d][key]; thread -> (4 d, 8 keys)
+        {
+            const int d4 = tid & 31, nb = tid >> 5;  // d = 4 d4 .. +3, keys 8 nb .. +7
+            float x[4][8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int n = 8 * nb + j;
+                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (k0 + n < kend) v = __ldcg(reinterpret_cast<const float4 *>(a.kv.v + a.kv.row(b, h, k0 + n)) + d4);
+                x[0][j] = v.x;
+                x[1][j] = v.y;
+                x[2][j] = v.z;
+                x[3][j] = v.w;
+            }
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                uint4 hi, lo;
+                big |= tc_split8(x[c], hi, lo);
+                *reinterpret_cast<uint4 *>(sm + kTcV + tc_off(4 * d4 + c, nb, 8)) = hi;
+                *reinterpret_cast<uint4 *>(sm + kTcVl + tc_off(4 * d4 + c, nb, 8)) = lo;
+            }
+        }
+        tc::fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncthreads();
+        // ---- S = Qh Kh + Qh Kl + Ql Kh
+        if (tid == 0) {
+            tc::fence_after_sync();
+#pragma unroll
+            for (int j = 0; j < HD / 16; j++) {
+                const uint64_t qh = tc::smem_desc(sbase + kTcQ + 256 * j, 128, 2048);
+                const uint64_t ql = tc::smem_desc(sbase + kTcQl + 256 * j, 128, 2048);
+                const uint64_t kh = tc::smem_desc(sbase + kTcK + 256 * j, 128, 2048);
+                const uint64_t kl = tc::smem_desc(sbase + kTcKl + 256 * j, 128, 2048);
+                tc::mma_f16(tmem, qh, kh, id_s, j != 0 ? 1u : 0u);
+                tc::mma_f16(tmem, qh, kl, id_s, 1u);
+                tc::mma_f16(tmem, ql, kh, id_s, 1u);
+            }
+            tc::commit(&bar_s);
+        }
+        // bounded wait (phase kt of bar_s)
+        {
+            const long long tw = clock64();
+            while (!mbar_try_wait(&bar_s, kt & 1))
+                if (clock64() - tw > (1ll << 31)) {
+                    raise_error(a.err, kDevTimeout);
+                    break;
+                }
+        }
+        tc::fence_after_sync();
+        // ---- online softmax (the arithmetic of k_prefill_attn)
+        float sv[64];
+        {
+            float s0[32], s1[32];
+            tc::ld_32x32b_x32(t_lane, s0);
+            tc::ld_32x32b_x32(t_lane + 32, s1);
+#pragma unroll
+            for (int c = 0; c < 32; c++) {
+                sv[c] = s0[c];
+                sv[32 + c] = s1[c];
+            }
+        }
+        float rmax = -INFINITY;
+#pragma unroll
+        for (int c = 0; c < 64; c++) {
+            const bool vis = rvalid && k0 + c <= qpos;
+            sv[c] = vis ? __fmul_rn(__fmul_rn(sv[c], unscale), scale) : -INFINITY;
+            rmax = fmaxf(rmax, sv[c]);
+        }
+        const float m_new = fmaxf(m_run, rmax);
+        float psum = 0.0f;
+#pragma unroll
+        for (int c = 0; c < 64; c++) {
+            sv[c] = m_new == -INFINITY ? 0.0f : expf(sv[c] - m_new);
+            psum += sv[c];
+        }
+        const float corr = m_new == -INFINITY ? 1.0f : expf(m_run - m_new);  // exp(-inf) = 0
+        l_run = __fmaf_rn(l_run, corr, psum);
+        m_run = m_new;
+        // P (A operand of O): row mrow, keys 32 hs .. +31
+#pragma unroll
+        for (int kb = 0; kb < 4; kb++) {
+            float x[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) x[e] = sv[32 * hs + 8 * kb + e];
+            uint4 hi, lo;
+            tc_split8(x, hi, lo);
+            *reinterpret_cast<uint4 *>(sm + kTcP + tc_off(mrow, 4 * hs + kb, 8)) = hi;
+            *reinterpret_cast<uint4 *>(sm + kTcPl + tc_off(mrow, 4 * hs + kb, 8)) = lo;
+        }
+        tc::fence_proxy_async_smem();
+        tc::fence_before_sync();
+        __syncthreads();
+        // ---- O_tile = Ph Vh + Ph Vl + Pl Vh
+        if (tid == 0) {
+            tc::fence_after_sync();
+#pragma unroll
+            for (int j = 0; j < kTcN / 16; j++) {
+                const uint64_t ph = tc::smem_desc(sbase + kTcP + 256 * j, 128, 1024);
+                const uint64_t pl = tc::smem_desc(sbase + kTcPl + 256 * j, 128, 1024);
+                const uint64_t vh = tc::smem_desc(sbase + kTcV + 256 * j, 128, 1024);
+                const uint64_t vl = tc::smem_desc(sbase + kTcVl + 256 * j, 128, 1024);
+                tc::mma_f16(tmem + kTcN, ph, vh, id_o, j != 0 ? 1u : 0u);
+                tc::mma_f16(tmem + kTcN, ph, vl, id_o, 1u);
+                tc::mma_f16(tmem + kTcN, pl, vh, id_o, 1u);
+            }
+            tc::commit(&bar_o);
+        }
+        {
+            const long long tw = clock64();
+            while (!mbar_try_wait(&bar_o, kt & 1))
+                if (clock64() - tw > (1ll << 31)) {
+                    raise_error(a.err, kDevTimeout);
+                    break;
+                }
+        }
+        tc::fence_after_sync();
+        {
+            float u0[32], u1[32];
+            tc::ld_32x32b_x32(t_lane + kTcN + 64 * hs, u0);
+            tc::ld_32x32b_x32(t_lane + kTcN + 64 * hs + 32, u1);
+#pragma unroll
+            for (int c = 0; c < 32; c++) {
+                o[c] = __fadd_rn(__fmul_rn(o[c], corr), u0[c]);
+                o[32 + c] = __fadd_rn(__fmul_rn(o[32 + c], corr), u1[c]);
+            }
+        }
+        tc::fence_before_sync();
+        __syncthreads();  // shared operands and tensor memory are rewritten next
+    }
+    if (big) raise_error(a.err, kDevF16Range);
+    // ---- out = O / l: row mrow, columns 64 hs .. +63
+    if (rvalid && ntiles > 0) {
+        const int g = mrow / BQ;
+        float *dst = a.out + (int64_t)(b * a.T + t0 + tl_r) * a.ldout + (int64_t)(h * G + g) * HD + 64 * hs;
+#pragma unroll
+        for (int c = 0; c < 64; c += 4) {
+            float4 r;
+            r.x = __fdiv_rn(o[c], l_run);
+            r.y = __fdiv_rn(o[c + 1], l_run);
+            r.z = __fdiv_rn(o[c + 2], l_run);
+            r.w = __fdiv_rn(o[c + 3], l_run);
+            *reinterpret_cast<float4 *>(dst + c) = r;
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 0) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTcTmemCols);
     }
 }
 
@@ -610,8 +937,39 @@ int launch_prefill_attn_g(const AttnArgs &a, cudaStream_t st) {
     return launch_ex(k_prefill_attn<HD, G>, grid, dim3(kPfThreads), sizeof(PfSmem<HD>), st, 1u, a);
 }
 
+// QORA_PREFILL_ATTN_TC=0 in the environment keeps head_dim-128 prefills on
+// the CUDA-core kernel (for comparison).
+bool prefill_attn_tc_disabled() {
+    static const bool off = [] {
+        const char *v = getenv("QORA_PREFILL_ATTN_TC");
+        return v && v[0] == '0';
+    }();
+    return off;
+}
+
+template <int G>
+int launch_prefill_attn_tc_g(const AttnArgs &a, cudaStream_t st) {
+    constexpr int BQ = kTcM / G;
+    static bool attr_done[64] = {};
+    int dev = 0;
+    QORA_CUDA(cudaGetDevice(&dev));
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+        QORA_CUDA(cudaFuncSetAttribute(k_prefill_attn_tc<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcBytes));
+        attr_done[dev] = true;
+    }
+    dim3 grid((a.T + BQ - 1) / BQ, a.kv_heads, a.streams);
+    return launch_ex(k_prefill_attn_tc<G>, grid, dim3(kTcThreads), (size_t)kTcBytes, st, 1u, a);
+}
+
 template <int HD>
 int launch_prefill_attn_hd(const AttnArgs &a, cudaStream_t st) {
+    if (HD == 128 && !prefill_attn_tc_disabled()) {
+        switch (a.heads / a.kv_heads) {
+            case 1: return launch_prefill_attn_tc_g<1>(a, st);
+            case 2: return launch_prefill_attn_tc_g<2>(a, st);
+            case 4: return launch_prefill_attn_tc_g<4>(a, st);
+        }
+    }
     switch (a.heads / a.kv_heads) {
         case 1: return launch_prefill_attn_g<HD, 1>(a, st);
         case 2: return launch_prefill_attn_g<HD, 2>(a, st);

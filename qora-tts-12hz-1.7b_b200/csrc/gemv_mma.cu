@@ -654,17 +654,18 @@ __global__ void __maxnreg__(80) k_gemv_mma(const GemvArgs a) {
 
 // ======================================================================
 // Prefill GEMM: the same contraction for many rows (a prompt chunk of up to
-// kMaxRows rows), one CTA per 128-column x 128-row tile over all of K.
+// kMaxRows rows), one CTA per 128-column x RT-row tile over all of K
+// (RT = 128, or 64 when 128-row tiles would leave SMs idle).
 // k_gemv_mma converts each weight tile once per 32 rows and the input rows
 // once per column tile; here
 //   * k_row_prep finds each row's RMSNorm factor and power-of-two operand
 //     exponent (one CTA per row),
 //   * k_b_convert writes the B operand of every (128-row tile, 32-K stage)
-//     once, as 16 KB in the MMA's shared-memory layout (xh rows, then xl
-//     rows) in global memory,
+//     once, in the MMA's shared-memory layout (xh rows, then xl rows; 16 KB
+//     for a 128-row tile) in global memory,
 //   * k_gemm_mma streams those B tiles with one bulk copy per stage, converts
-//     only its weights (A1 / A2 into tensor memory), and issues one N = 256
-//     MMA (128 rows, xh and xl side by side) plus one N = 128 MMA (A2 xh) per
+//     only its weights (A1 / A2 into tensor memory), and issues one N = 2 RT
+//     MMA (RT rows, xh and xl side by side) plus one N = RT MMA (A2 xh) per
 //     16 K rows.
 // The operands, the K order of the accumulation and the epilogue arithmetic
 // are those of k_gemv_mma without a K split (the split its prefill plan uses
@@ -675,30 +676,33 @@ __global__ void __maxnreg__(80) k_gemv_mma(const GemvArgs a) {
 //   warps 0..  kGGroups converter groups of four (group c takes stages
 //              t = c mod kGGroups; warp g of a group: column group g, TMEM
 //              lanes 32 g ..), then the epilogue (warp w: column group w % 4,
-//              rows kGEpiRows (w / 4) .. + kGEpiRows - 1);
+//              rows 32 (w / 4) .. + 31 of the row tile);
 //   next warp  streams each stage's weights (bulk copies into a raw ring) and
 //              B tile (one bulk copy into the operand ring);
 //   last warp  allocates tensor memory and issues the MMAs (one thread).
-constexpr int kGRows = 128;
 constexpr int kGGroups = 4;                    // converter groups (four warps each)
 constexpr int kGConvWarps = 4 * kGGroups;
 constexpr int kGProdWarp = kGConvWarps;
 constexpr int kGMmaWarp = kGConvWarps + 1;
 constexpr int kGThreads = 32 * (kGConvWarps + 2);
-constexpr int kGEpiRows = kGRows / kGGroups;    // epilogue rows per converter warp
 constexpr int kGRawSlots = 3;                  // weight slots per converter group (own stages)
 constexpr int kGOpStages = 8;
 constexpr int kGRawNib = 0;
 constexpr int kGRawScl = kGRawNib + kMmaGroups * kNibGroupStride;
 constexpr int kGRawBytes = kGRawScl + kMmaGroups * kSclGroupStride;
-constexpr int kGBTile = kGRows * kStageK * 2;  // one of xh / xl: 128 rows x 32 K (f16)
-constexpr int kGOpBytes = 2 * kGBTile;         // one B tile (global and shared layout alike)
+// Row tiles of RT = 128 or 64 rows (64 when 128-row tiles would leave many
+// SMs idle).  One B tile: xh rows then xl rows, RT x 32 K each (f16), in the
+// same layout in global and shared memory.
+constexpr int gbtile(int RT) { return RT * kStageK * 2; }
+constexpr int gopbytes(int RT) { return 2 * gbtile(RT); }
 constexpr uint32_t kGTmemCols = 512;           // D: 256 (xh rows, then xl rows), A: 8 stages x 32
 constexpr uint32_t kGTmemA = 256;
 constexpr uint32_t kGTmemAStage = 32;
-constexpr size_t kGSmem = 128 + (size_t)kGOpStages * kGOpBytes + (size_t)kGGroups * kGRawSlots * kGRawBytes;
-static_assert(kGRawScl % 16 == 0 && kGRawBytes % 16 == 0 && kGOpBytes % 128 == 0, "bulk-copy alignment");
-static_assert(kGOpStages * kGOpBytes >= 4 * kGRows * 32 * 4, "SwiGLU exchange fits the operand stages");
+constexpr size_t gsmem(int RT) {
+    return 128 + (size_t)kGOpStages * gopbytes(RT) + (size_t)kGGroups * kGRawSlots * kGRawBytes;
+}
+static_assert(kGRawScl % 16 == 0 && kGRawBytes % 16 == 0 && gopbytes(64) % 128 == 0, "bulk-copy alignment");
+static_assert(kGOpStages * gopbytes(64) >= 4 * 64 * 32 * 4, "SwiGLU exchange fits the operand stages");
 
 // Byte offset of element (row r, k) of a B tile (K-major core matrices of
 // 8 rows x 8 K, 128 contiguous bytes; 4 per row block along K), hi half.
@@ -747,16 +751,17 @@ __global__ void __launch_bounds__(256) k_row_prep(const GemvArgs a, int *rexp, f
     }
 }
 
-// B tiles of a prefill GEMM: block (row tile, group of 4 stages), thread
-// (row r = tid % 128, stages 2 (tid / 128) + {0, 1}).  Row r's 32 K values
+// B tiles of a prefill GEMM: block (row tile of RT rows, group of 4
+// stages), thread (row r = tid % RT, stages tid / RT + 256 / RT j).  Row r's 32 K values
 // of a stage: x (normalised: (x * inv) * gamma), times 2^rexp, split as
 // xh = f16(x), xl = f16(x - xh), exactly as k_gemv_mma forms its B operand;
 // rows past `rows` are zero.
-template <int XM>
+template <int XM, int RT>
 __global__ void __launch_bounds__(256) k_b_convert(const GemvArgs a, const int *rexp, const float *rinv,
                                                    uint8_t *bop) {
-    const int rt = blockIdx.x, r = threadIdx.x & 127;
-    const int row = rt * kGRows + r;
+    constexpr int SL = 256 / RT;  // threads per row: stage slots of the block's 4 stages
+    const int rt = blockIdx.x, r = threadIdx.x % RT;
+    const int row = rt * RT + r;
     const bool rvalid = row < a.rows;
     const int nst = (int)(a.w.k / kStageK);
     griddep_launch_dependents();
@@ -765,11 +770,11 @@ __global__ void __launch_bounds__(256) k_b_convert(const GemvArgs a, const int *
     float inv_r = 1.0f;
     if constexpr (XM == X_RMSNORM) inv_r = rvalid ? __ldcg(rinv + row) : 1.0f;
     bool big = false;
-    for (int s = 0; s < 2; s++) {
-        const int t = blockIdx.y * 4 + 2 * (threadIdx.x >> 7) + s;
+    for (int s = threadIdx.x / RT; s < 4; s += SL) {
+        const int t = blockIdx.y * 4 + s;
         if (t >= nst) break;
         const int64_t k0 = (int64_t)t * kStageK;
-        uint8_t *tile = bop + ((int64_t)rt * nst + t) * kGOpBytes;
+        uint8_t *tile = bop + ((int64_t)rt * nst + t) * gopbytes(RT);
 #pragma unroll
         for (int kc = 0; kc < 4; kc++) {
             float xv[8];
@@ -805,19 +810,20 @@ __global__ void __launch_bounds__(256) k_b_convert(const GemvArgs a, const int *
             }
             const int off = btile_off(r, kc);
             __stcg(reinterpret_cast<uint4 *>(tile + off), make_uint4(bh[0], bh[1], bh[2], bh[3]));
-            __stcg(reinterpret_cast<uint4 *>(tile + kGBTile + off), make_uint4(bl[0], bl[1], bl[2], bl[3]));
+            __stcg(reinterpret_cast<uint4 *>(tile + gbtile(RT) + off), make_uint4(bl[0], bl[1], bl[2], bl[3]));
         }
     }
     if (big) raise_error(a.err, kDevF16Range);
 }
 
-template <int XM, int EM>
+template <int XM, int EM, int RT>
 __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
     constexpr int CO = (EM == E_SWIGLU) ? kMmaGroups / 2 : kMmaGroups;  // output groups per CTA
+    constexpr int kGOpBytes = gopbytes(RT);
     extern __shared__ uint8_t gm_dyn[];
     __shared__ __align__(8) uint64_t b_full[kGOpStages], a_full[kGOpStages], op_empty[kGOpStages], d_full;
     __shared__ uint32_t tmem_slot;
-    __shared__ int rexp_s[kGRows];
+    __shared__ int rexp_s[RT];
     __shared__ int abort_s;
     __shared__ int grp_go[kGGroups];  // a converter group's decision for its current stage
 
@@ -827,8 +833,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t c0 = (int64_t)blockIdx.x * kMmaGroups;
     const int nst = (int)(a.w.k / kStageK);
-    const int r_begin = blockIdx.y * kGRows;
-    const int nvalid = min(kGRows, a.rows - r_begin);
+    const int r_begin = blockIdx.y * RT;
+    const int nvalid = min(RT, a.rows - r_begin);
     volatile int *abort_v = &abort_s;
 
     if (threadIdx.x == 0) {
@@ -893,8 +899,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
     } else if (warp == kGMmaWarp) {
         // ---------------------------------------------------------- MMA issue
         if (lane == 0) {
-            constexpr uint32_t id256 = tc::idesc_f16_f32(128, 2 * kGRows);
-            constexpr uint32_t id128 = tc::idesc_f16_f32(128, kGRows);
+            constexpr uint32_t id256 = tc::idesc_f16_f32(128, 2 * RT);  // xh and xl rows
+            constexpr uint32_t id128 = tc::idesc_f16_f32(128, RT);      // xh rows
             for (int t = 0; t < nst; t++) {
                 const int o = t % kGOpStages;
                 if (!wait_or_abort(&a_full[o], (t / kGOpStages) & 1, abort_v, a.err)) break;
@@ -939,7 +945,7 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
         for (int j = 0; j < kGRawSlots; j++) prefetch(j);
         griddep_launch_dependents();
         griddep_wait();
-        if (threadIdx.x < kGRows)
+        if (threadIdx.x < RT)
             rexp_s[threadIdx.x] = (int)threadIdx.x < nvalid ? __ldcg(a.rexp + r_begin + threadIdx.x) : 0;
         // A role: column 32 g + lane of the tile, as in k_gemv_mma
         const int cq = lane & 7;
@@ -1000,7 +1006,8 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
         asm volatile("bar.sync 1, %0;" ::"n"(kGConvWarps * 32) : "memory");  // rexp_s
 
         // ---------------------------------------------------------- epilogue
-        // warp w: column group w % 4 (its TMEM lanes), rows kGEpiRows (w / 4) ..
+        // warp w: column group w % 4 (its TMEM lanes), rows 32 (w / 4) .. + 31
+        // (converter groups past RT / 32 have no rows)
         bool ok = wait_or_abort(&d_full, 0, abort_v, a.err);
         ok = __all_sync(0xffffffffu, ok);
         tc::fence_after_sync();
@@ -1008,12 +1015,12 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
         const int64_t n_out = (EM == E_SWIGLU) ? (a.w.C / 2) * 32 : a.w.n;
         float *xch = reinterpret_cast<float *>(op_base);  // SwiGLU: [group][row][column]
 #pragma unroll 1
-        for (int ch = 0; ch < kGEpiRows / 32; ch++) {
-            const int n0 = kGEpiRows * cgp + 32 * ch;
+        for (int ch = cgp; ch < RT / 32; ch += kGGroups) {
+            const int n0 = 32 * ch;
             float vh[32], vl[32];
             if (ok) {
                 tc::ld_32x32b_x32(tmem + ((uint32_t)(32 * g) << 16) + (uint32_t)n0, vh);
-                tc::ld_32x32b_x32(tmem + ((uint32_t)(32 * g) << 16) + (uint32_t)(kGRows + n0), vl);
+                tc::ld_32x32b_x32(tmem + ((uint32_t)(32 * g) << 16) + (uint32_t)(RT + n0), vl);
             } else {
 #pragma unroll
                 for (int i = 0; i < 32; i++) vh[i] = vl[i] = 0.0f;
@@ -1024,7 +1031,7 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
                                   __int_as_float((127 - rexp_s[n0 + n]) << 23));
             if constexpr (EM == E_SWIGLU) {
 #pragma unroll
-                for (int n = 0; n < 32; n++) xch[(g * kGRows + n0 + n) * 32 + lane] = vh[n];
+                for (int n = 0; n < 32; n++) xch[(g * RT + n0 + n) * 32 + lane] = vh[n];
             } else {
                 const int64_t grp = c0 + g;
 #pragma unroll 4
@@ -1045,13 +1052,13 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
         if constexpr (EM == E_SWIGLU) {
             // silu(gate) * up (talker.rs:341-345): group 2u is gate, 2u + 1 up
             asm volatile("bar.sync 1, %0;" ::"n"(kGConvWarps * 32) : "memory");
-            constexpr int RW = 2 * kGRows / kGConvWarps;  // rows per warp (two units)
+            constexpr int RW = 2 * RT / kGConvWarps;  // rows per warp (two units)
             const int u = warp & 1, rb = (warp >> 1) * RW;
             for (int n = 0; n < RW; n++) {
                 const int row = rb + n;
                 if (row < nvalid)
-                    finalize_group<EM>(a, r_begin + row, c0 / 2 + u, lane, xch[((2 * u) * kGRows + row) * 32 + lane],
-                                       xch[((2 * u + 1) * kGRows + row) * 32 + lane], n_out, CO);
+                    finalize_group<EM>(a, r_begin + row, c0 / 2 + u, lane, xch[((2 * u) * RT + row) * 32 + lane],
+                                       xch[((2 * u + 1) * RT + row) * 32 + lane], n_out, CO);
             }
         }
         // tail columns beyond the last full group stay zero (gemv.rs:846-861)
@@ -1071,20 +1078,35 @@ __global__ void __launch_bounds__(kGThreads, 1) k_gemm_mma(const GemvArgs a) {
 
 template <int XM, int EM>
 int gemm_attrs() {
-    QORA_CUDA(cudaFuncSetAttribute(k_gemm_mma<XM, EM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGSmem));
+    QORA_CUDA(cudaFuncSetAttribute(k_gemm_mma<XM, EM, 128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)gsmem(128)));
+    QORA_CUDA(cudaFuncSetAttribute(k_gemm_mma<XM, EM, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)gsmem(64)));
     return QORA_OK;
 }
 
-template <int XM>
+template <int XM, int RT>
 int launch_gemm_e(const GemvArgs &a, int emode, dim3 grid, cudaStream_t st) {
     const dim3 block(kGThreads);
     switch (emode) {
-        case E_STORE: return launch_ex(k_gemm_mma<XM, E_STORE>, grid, block, kGSmem, st, 1u, a);
-        case E_BIAS: return launch_ex(k_gemm_mma<XM, E_BIAS>, grid, block, kGSmem, st, 1u, a);
-        case E_RESID: return launch_ex(k_gemm_mma<XM, E_RESID>, grid, block, kGSmem, st, 1u, a);
-        case E_SWIGLU: return launch_ex(k_gemm_mma<XM, E_SWIGLU>, grid, block, kGSmem, st, 1u, a);
+        case E_STORE: return launch_ex(k_gemm_mma<XM, E_STORE, RT>, grid, block, gsmem(RT), st, 1u, a);
+        case E_BIAS: return launch_ex(k_gemm_mma<XM, E_BIAS, RT>, grid, block, gsmem(RT), st, 1u, a);
+        case E_RESID: return launch_ex(k_gemm_mma<XM, E_RESID, RT>, grid, block, gsmem(RT), st, 1u, a);
+        case E_SWIGLU: return launch_ex(k_gemm_mma<XM, E_SWIGLU, RT>, grid, block, gsmem(RT), st, 1u, a);
     }
     return set_error(QORA_ERR_INVALID, "bad epilogue mode %d", emode);
+}
+
+// Row prologue, B tiles and GEMM of one prefill GEMM with RT-row tiles.
+template <int XM, int RT>
+int launch_gemm_rt(const GemvArgs &a, int emode, const GemmScratch &sc, cudaStream_t st) {
+    const int rt = (a.rows + RT - 1) / RT, nst = (int)(a.w.k / kStageK);
+    const dim3 grid((unsigned)(a.w.C / kMmaGroups), (unsigned)rt);
+    const dim3 cgrid((unsigned)rt, (unsigned)((nst + 3) / 4));
+    QORA_TRY(launch_ex(k_row_prep<XM>, dim3((unsigned)a.rows), dim3(256), 0, st, 1u, a, sc.rexp, sc.rinv));
+    QORA_TRY(launch_ex(k_b_convert<XM, RT>, cgrid, dim3(256), 0, st, 1u, a, (const int *)sc.rexp,
+                       (const float *)sc.rinv, sc.bop));
+    return launch_gemm_e<XM, RT>(a, emode, grid, st);
 }
 
 template <int XM, int EM>
@@ -1255,26 +1277,26 @@ bool gemm_mma_supported(const GemvArgs &a, int xmode, int emode) {
 int launch_gemm_mma(GemvArgs a, int xmode, int emode, const GemmScratch &sc, cudaStream_t st, int *launches) {
     if (!gemm_mma_supported(a, xmode, emode))
         return set_error(QORA_ERR_INVALID, "prefill GEMM: unsupported launch");
-    const int rt = (a.rows + kGRows - 1) / kGRows, nst = (int)(a.w.k / kStageK);
-    if (!sc.rexp || !sc.rinv || !sc.bop || a.rows > sc.rows || (size_t)rt * nst * kGOpBytes > sc.bop_bytes)
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // 64-row tiles when 128-row tiles would fill under three quarters of the SMs
+    const int64_t tiles128 = (a.w.C / kMmaGroups) * ((a.rows + 127) / 128);
+    const int RT = (a.rows <= 64 || tiles128 * 4 < 3LL * sms) ? 64 : 128;
+    const int nst = (int)(a.w.k / kStageK);
+    const size_t need = (size_t)((a.rows + RT - 1) / RT) * nst * gopbytes(RT);
+    if (!sc.rexp || !sc.rinv || !sc.bop || a.rows > sc.rows || need > sc.bop_bytes)
         return set_error(QORA_ERR_INVALID, "prefill GEMM: scratch too small (%d rows, k %lld)", a.rows,
                          (long long)a.w.k);
     a.S = 1;
     a.gticket = nullptr;
     a.rexp = sc.rexp;
     a.bop = sc.bop;
-    const dim3 grid((unsigned)(a.w.C / kMmaGroups), (unsigned)rt);
-    const dim3 cgrid((unsigned)rt, (unsigned)((nst + 3) / 4));
     if (xmode == X_PLAIN) {
-        QORA_TRY(launch_ex(k_row_prep<X_PLAIN>, dim3((unsigned)a.rows), dim3(256), 0, st, 1u, a, sc.rexp, sc.rinv));
-        QORA_TRY(launch_ex(k_b_convert<X_PLAIN>, cgrid, dim3(256), 0, st, 1u, a, (const int *)sc.rexp,
-                           (const float *)sc.rinv, sc.bop));
-        QORA_TRY(launch_gemm_e<X_PLAIN>(a, emode, grid, st));
+        QORA_TRY(RT == 64 ? (launch_gemm_rt<X_PLAIN, 64>(a, emode, sc, st)) : (launch_gemm_rt<X_PLAIN, 128>(a, emode, sc, st)));
     } else {
-        QORA_TRY(launch_ex(k_row_prep<X_RMSNORM>, dim3((unsigned)a.rows), dim3(256), 0, st, 1u, a, sc.rexp, sc.rinv));
-        QORA_TRY(launch_ex(k_b_convert<X_RMSNORM>, cgrid, dim3(256), 0, st, 1u, a, (const int *)sc.rexp,
-                           (const float *)sc.rinv, sc.bop));
-        QORA_TRY(launch_gemm_e<X_RMSNORM>(a, emode, grid, st));
+        QORA_TRY(RT == 64 ? (launch_gemm_rt<X_RMSNORM, 64>(a, emode, sc, st))
+                          : (launch_gemm_rt<X_RMSNORM, 128>(a, emode, sc, st)));
     }
     if (launches) *launches += 3;
     return QORA_OK;

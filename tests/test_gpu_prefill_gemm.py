@@ -51,10 +51,10 @@ _CHILD = textwrap.dedent("""
 """)
 
 
-def _run(tmp_path, flag):
-    path = str(tmp_path / f"prefill_{flag}.npz")
+def _run(tmp_path, flag, var="QORA_PREFILL_GEMM"):
+    path = str(tmp_path / f"prefill_{var}_{flag}.npz")
     code = _CHILD.format(pkg=os.path.join(ROOT, "qora-tts-12hz-1.7b_b200"), path=path)
-    env = dict(os.environ, QORA_PREFILL_GEMM=flag)
+    env = dict(os.environ, **{var: flag})
     r = subprocess.run([sys.executable, "-c", code], env=env, capture_output=True, text=True, timeout=900)
     assert r.returncode == 0, r.stderr[-3000:]
     return np.load(path)
@@ -71,3 +71,20 @@ def test_prefill_gemm_matches_split_free_gemv_bitwise(tmp_path):
         else:
             err = float(np.max(np.abs(a.astype(np.float64) - b)))
             assert err <= 1e-5 * max(1.0, float(np.max(np.abs(b)))), (key, err)
+
+
+def test_prefill_attention_tc_matches_cuda_core(tmp_path):
+    """k_prefill_attn_tc (tcgen05; Q, K, V, P as f16 hi + lo pairs) against the
+    f32 CUDA-core k_prefill_attn (QORA_PREFILL_ATTN_TC=0) at head_dim 128:
+    the same prefills agree to f32 summation-order differences (relative
+    1e-5 of each tensor's largest magnitude, through two layers)."""
+    new, old = _run(tmp_path, "1", "QORA_PREFILL_ATTN_TC"), _run(tmp_path, "0", "QORA_PREFILL_ATTN_TC")
+    worst = 0.0
+    for key in new.files:
+        if not key.startswith("full"):
+            continue                  # head_dim 64: the CUDA-core kernel either way
+        a, b = new[key].astype(np.float64), old[key].astype(np.float64)
+        err = float(np.max(np.abs(a - b))) / max(1e-30, float(np.max(np.abs(b))))
+        worst = max(worst, err)
+        assert err <= 1e-5, (key, err)
+    print(f"prefill attention tc vs cuda-core: worst relative {worst:.2e}")
