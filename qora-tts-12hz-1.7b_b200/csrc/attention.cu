@@ -307,15 +307,18 @@ __global__ void __launch_bounds__(kPfThreads, 2) k_prefill_attn(const AttnArgs a
 // walks the key positions in tiles of 64 that start at multiples of 64
 // (absolute positions, so every row's result has the same bits in any
 // prefill chunk).  Per tile:
-//   * the K / V rows are read from the cache (row addressing: slab or
-//     paged), K as B[key][d] and V transposed as B[d][key], both split into
-//     f16 hi + lo (x = xh + xl to ~22 bits) in the canonical K-major layout;
+//   * the K / V rows of the tile come from the cache (row addressing: slab
+//     or paged) into an f32 staging buffer with cp.async, issued while the
+//     previous tile computes; K goes to B[key][d] and V transposed to
+//     B[d][key], both split into f16 hi + lo (x = xh + xl to ~22 bits) in
+//     the canonical K-major layout;
 //   * S = Qh Kh + Qh Kl + Ql Kh (the dropped Ql Kl is ~2^-22 relative),
 //     accumulated in f32 in tensor memory; Q and K are scaled by powers of
 //     two fixed per launch (from the qk-norm bounds sqrt(128) max |gamma|),
 //     undone exactly in the softmax;
-//   * the online softmax of k_prefill_attn on S (row m in TMEM lane m: two
-//     threads per row, each the whole row's max and sum, half the row's P);
+//   * an online softmax on S (row m in TMEM lane m; two threads per row,
+//     each half the keys, the halves' max and sum combined in shared memory;
+//     exp as the hardware exponential);
 //   * O_tile = Ph Vh + Ph Vl + Pl Vh (P in [0, 1] as f16 hi + lo), added by
 //     the CUDA cores into the row's running output: O = O * corr + O_tile.
 // One thread issues the MMAs; completion comes through mbarriers.  V values
@@ -326,8 +329,9 @@ constexpr int kTcThreads = 256;
 constexpr uint32_t kTcTmemCols = 256;  // S: 64 columns, O_tile: 128
 // shared memory (bytes): Q hi / lo [128 x 128], K hi / lo [64 x 128],
 // V^T hi / lo [128 x 64], P hi / lo [128 x 64], all f16 K-major core matrices
+// and the f32 K / V rows of the next tile (cp.async staging, 2 x 32 KB)
 constexpr int kTcQ = 0, kTcQl = 32768, kTcK = 65536, kTcKl = 81920, kTcV = 98304, kTcVl = 114688,
-              kTcP = 131072, kTcPl = 147456, kTcBytes = 163840;
+              kTcP = 131072, kTcPl = 147456, kTcSK = 163840, kTcSV = 196608, kTcBytes = 229376;
 
 // Byte offset of (row r, 8-element K block kb) in a K-major operand whose
 // rows have `nkb` K blocks: core matrices of 8 rows x 16 bytes, K blocks
@@ -370,6 +374,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
     __shared__ __align__(8) uint64_t bar_s, bar_o;
     __shared__ uint32_t tmem_slot;
     __shared__ float red_s[8];
+    __shared__ float red_m[2][kTcM], red_l[2][kTcM];  // per-half row max / sum of a tile
     const int qb = gridDim.x - 1 - blockIdx.x;  // the longest query blocks first
     const int h = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -416,6 +421,26 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
     const int kend = L0 + t0 + max(nq, 0);  // keys [0, kend) are visible to some row
     const int ntiles = (bad || nq <= 0) ? 0 : (kend + kTcN - 1) / kTcN;
     bool big = false;
+    // f32 K / V rows of tile kt -> staging (16-byte cp.async pieces; rows past
+    // kend are zeros: never visible, and unwritten cache memory may hold anything)
+    auto stage_tile = [&](int kt) {
+        const int k0 = kt * kTcN;
+        for (int i = tid; i < kTcN * (HD / 4); i += kTcThreads) {
+            const int n = i >> 5, d4 = i & 31;
+            float *kd = reinterpret_cast<float *>(sm + kTcSK) + n * HD + 4 * d4;
+            float *vd = reinterpret_cast<float *>(sm + kTcSV) + n * HD + 4 * d4;
+            if (k0 + n < kend) {
+                const int64_t row = a.kv.row(b, h, k0 + n);
+                pf_cp16(kd, a.kv.k + row + 4 * d4);
+                pf_cp16(vd, a.kv.v + row + 4 * d4);
+            } else {
+                *reinterpret_cast<float4 *>(kd) = make_float4(0.f, 0.f, 0.f, 0.f);
+                *reinterpret_cast<float4 *>(vd) = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (ntiles > 0) stage_tile(0);
 
     // ---- Q (A operand of S): vector m = head g = m / BQ, token m % BQ
     for (int i = tid; i < kTcM * (HD / 8); i += kTcThreads) {
@@ -455,16 +480,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
 
     for (int kt = 0; kt < ntiles; kt++) {
         const int k0 = kt * kTcN;
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();  // tile kt staged (every thread's pieces)
+        const float *skf = reinterpret_cast<const float *>(sm + kTcSK);
+        const float *svf = reinterpret_cast<const float *>(sm + kTcSV);
         // ---- K tile: B[key n][d]; thread -> (key, 8-d block) pairs
         for (int i = tid; i < kTcN * (HD / 8); i += kTcThreads) {
             const int n = i >> 4, kb = i & 15;
-            float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-            if (k0 + n < kend) {  // never visible otherwise: zeros
-                const float4 *src = reinterpret_cast<const float4 *>(a.kv.k + a.kv.row(b, h, k0 + n) + 8 * kb);
-                const float4 u0 = __ldcg(src), u1 = __ldcg(src + 1);
-                x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
-                x[4] = u1.x; x[5] = u1.y; x[6] = u1.z; x[7] = u1.w;
-            }
+            const float4 u0 = *reinterpret_cast<const float4 *>(skf + n * HD + 8 * kb);
+            const float4 u1 = *reinterpret_cast<const float4 *>(skf + n * HD + 8 * kb + 4);
+            float x[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
             for (int e = 0; e < 8; e++) x[e] = __fmul_rn(x[e], ks);
             uint4 hi, lo;
@@ -478,9 +503,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
             float x[4][8];
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                const int n = 8 * nb + j;
-                float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-                if (k0 + n < kend) v = __ldcg(reinterpret_cast<const float4 *>(a.kv.v + a.kv.row(b, h, k0 + n)) + d4);
+                const float4 v = *reinterpret_cast<const float4 *>(svf + (8 * nb + j) * HD + 4 * d4);
                 x[0][j] = v.x;
                 x[1][j] = v.y;
                 x[2][j] = v.z;
@@ -496,7 +519,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
         }
         tc::fence_proxy_async_smem();
         tc::fence_before_sync();
-        __syncthreads();
+        __syncthreads();  // operands written, staging read
+        if (kt + 1 < ntiles) stage_tile(kt + 1);  // lands while this tile computes
         // ---- S = Qh Kh + Qh Kl + Ql Kh
         if (tid == 0) {
             tc::fence_after_sync();
@@ -522,41 +546,33 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
                 }
         }
         tc::fence_after_sync();
-        // ---- online softmax (the arithmetic of k_prefill_attn)
-        float sv[64];
-        {
-            float s0[32], s1[32];
-            tc::ld_32x32b_x32(t_lane, s0);
-            tc::ld_32x32b_x32(t_lane + 32, s1);
-#pragma unroll
-            for (int c = 0; c < 32; c++) {
-                sv[c] = s0[c];
-                sv[32 + c] = s1[c];
-            }
-        }
+        // ---- online softmax: each of the row's two threads takes half the
+        // keys; the halves' max and sum meet in shared memory (half 0 first)
+        float sv[32];
+        tc::ld_32x32b_x32(t_lane + 32 * hs, sv);
         float rmax = -INFINITY;
 #pragma unroll
-        for (int c = 0; c < 64; c++) {
-            const bool vis = rvalid && k0 + c <= qpos;
+        for (int c = 0; c < 32; c++) {
+            const bool vis = rvalid && k0 + 32 * hs + c <= qpos;
             sv[c] = vis ? __fmul_rn(__fmul_rn(sv[c], unscale), scale) : -INFINITY;
             rmax = fmaxf(rmax, sv[c]);
         }
-        const float m_new = fmaxf(m_run, rmax);
+        red_m[hs][mrow] = rmax;
+        __syncthreads();
+        const float m_new = fmaxf(m_run, fmaxf(red_m[0][mrow], red_m[1][mrow]));
         float psum = 0.0f;
 #pragma unroll
-        for (int c = 0; c < 64; c++) {
-            sv[c] = m_new == -INFINITY ? 0.0f : expf(sv[c] - m_new);
+        for (int c = 0; c < 32; c++) {
+            sv[c] = m_new == -INFINITY ? 0.0f : __expf(sv[c] - m_new);
             psum += sv[c];
         }
-        const float corr = m_new == -INFINITY ? 1.0f : expf(m_run - m_new);  // exp(-inf) = 0
-        l_run = __fmaf_rn(l_run, corr, psum);
-        m_run = m_new;
+        red_l[hs][mrow] = psum;
         // P (A operand of O): row mrow, keys 32 hs .. +31
 #pragma unroll
         for (int kb = 0; kb < 4; kb++) {
             float x[8];
 #pragma unroll
-            for (int e = 0; e < 8; e++) x[e] = sv[32 * hs + 8 * kb + e];
+            for (int e = 0; e < 8; e++) x[e] = sv[8 * kb + e];
             uint4 hi, lo;
             tc_split8(x, hi, lo);
             *reinterpret_cast<uint4 *>(sm + kTcP + tc_off(mrow, 4 * hs + kb, 8)) = hi;
@@ -580,6 +596,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
             }
             tc::commit(&bar_o);
         }
+        const float corr = m_new == -INFINITY ? 1.0f : __expf(m_run - m_new);  // exp(-inf) = 0
+        l_run = __fmaf_rn(l_run, corr, __fadd_rn(red_l[0][mrow], red_l[1][mrow]));
+        m_run = m_new;
         {
             const long long tw = clock64();
             while (!mbar_try_wait(&bar_o, kt & 1))
