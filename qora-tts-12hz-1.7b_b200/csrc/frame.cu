@@ -100,6 +100,18 @@ static_assert(sizeof(GemvDesc) <= 16 * kDescWords && sizeof(AttnArgs) <= 16 * kD
 static_assert(sizeof(OpRef) == 16, "op table staging");
 
 __device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(kNT) : "memory"); }
+// csync that also ORs a flag over the compute threads: every thread gets the
+// same answer (an abort the producer warp raises mid-op may reach the threads
+// at different times; this makes them leave together).
+__device__ __forceinline__ bool csync_or(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, %2, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)v), "n"(kNT)
+        : "memory");
+    return r != 0;
+}
 
 __device__ __forceinline__ int ld_volatile(const int *p) {
     int v;
@@ -800,14 +812,19 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
     uint32_t q = 0;
     int rbuf = 0, b = 0, last_gemv = -1;
     int i = next_op(S, -1, P.n_ops, cta, grid);
-    if (i < P.n_ops) stage_issue(P, S, i, b, tid);
+    if (i < P.n_ops) {
+        stage_issue(P, S, i, b, tid);
+        stage_wait(P, S, i, b, tid);
+    }
+    csync();
+    // One barrier per op: it ends op i (every thread is done with the shared
+    // buffers it used), publishes op i+1's staged descriptor and carries the
+    // abort decision.
     while (i < P.n_ops) {
         const OpRef op = S.ops[i];
         const int j0 = first_item(cta, op, grid);
         const bool tr = P.trace && j0 == 0 && tid == 0;
         const bool ta = P.trace && tid == 0;  // every SM: across-SM stamps
-        stage_wait(P, S, i, b, tid);
-        csync();
         const int nx = next_op(S, i, P.n_ops, cta, grid);
         if (nx < P.n_ops) stage_issue(P, S, nx, b ^ 1, tid);  // lands while op i runs
         stamp_all(P, i, 3, ta);
@@ -838,9 +855,10 @@ __device__ void consumer(const FrameParams &P, FrameSmem &S, int tid, int cta, i
                 st_relaxed_u64(P.code0_t, tag_pack(__uint_as_float((uint32_t)S.u.samp.out_code), P.tag_base + i + 1));
             }
         }
-        csync();
+        if (nx < P.n_ops) stage_wait(P, S, nx, b ^ 1, tid);
+        const bool stop = csync_or(*(volatile int *)&S.abort != 0);
         stamp_all(P, i, 2, ta);
-        if (*(volatile int *)&S.abort) return;
+        if (stop) return;
         b ^= 1;
         i = nx;
     }
