@@ -448,7 +448,7 @@ def engine_rate(E, talker, pred, torch, qb, B, K, W, seed0, with_e2e=False, pref
 # DRAM bytes per launch from the committed ncu captures (text copied here,
 # never read at run time): k_frame on the bench's batch-1 frame workload, and
 # k_gemv's DRAM bytes per algorithmic byte on the talker gate/up shape.
-KFRAME_DRAM_BYTES = 937957888        # profiles/k_frame_b1_frame.md
+KFRAME_DRAM_BYTES = 946941952        # profiles/k_frame_b1_frame.md
 KGEMV_DRAM_PER_ALG_BYTE = 1.0058     # profiles/k_gemv_b1_2048x6144.md
 
 

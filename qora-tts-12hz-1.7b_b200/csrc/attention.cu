@@ -327,11 +327,15 @@ constexpr int kTcM = 128;        // query vectors per CTA (MMA M)
 constexpr int kTcN = 64;         // keys per tile
 constexpr int kTcThreads = 256;
 constexpr uint32_t kTcTmemCols = 256;  // S: 64 columns, O_tile: 128
-// shared memory (bytes): Q hi / lo [128 x 128], K hi / lo [64 x 128],
-// V^T hi / lo [128 x 64], P hi / lo [128 x 64], all f16 K-major core matrices
-// and the f32 K / V rows of the next tile (cp.async staging, 2 x 32 KB)
+// shared memory (bytes): Q hi / lo [128 x 128], K hi / lo [64 x 128] (P hi /
+// lo [128 x 64] in the same slots once S is computed), V^T hi / lo [128 x 64],
+// all f16 K-major core matrices; then the f32 K / V rows of the next tile
+// (cp.async staging, rows padded by 16 bytes so that 8 consecutive rows fall
+// on different banks)
+constexpr int kTcSRow = 128 + 4;  // staging row stride (floats)
 constexpr int kTcQ = 0, kTcQl = 32768, kTcK = 65536, kTcKl = 81920, kTcV = 98304, kTcVl = 114688,
-              kTcP = 131072, kTcPl = 147456, kTcSK = 163840, kTcSV = 196608, kTcBytes = 229376;
+              kTcP = kTcK, kTcPl = kTcKl, kTcSK = 131072, kTcSV = kTcSK + 64 * kTcSRow * 4,
+              kTcBytes = kTcSV + 64 * kTcSRow * 4;
 
 // Byte offset of (row r, 8-element K block kb) in a K-major operand whose
 // rows have `nkb` K blocks: core matrices of 8 rows x 16 bytes, K blocks
@@ -427,8 +431,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
         const int k0 = kt * kTcN;
         for (int i = tid; i < kTcN * (HD / 4); i += kTcThreads) {
             const int n = i >> 5, d4 = i & 31;
-            float *kd = reinterpret_cast<float *>(sm + kTcSK) + n * HD + 4 * d4;
-            float *vd = reinterpret_cast<float *>(sm + kTcSV) + n * HD + 4 * d4;
+            float *kd = reinterpret_cast<float *>(sm + kTcSK) + n * kTcSRow + 4 * d4;
+            float *vd = reinterpret_cast<float *>(sm + kTcSV) + n * kTcSRow + 4 * d4;
             if (k0 + n < kend) {
                 const int64_t row = a.kv.row(b, h, k0 + n);
                 pf_cp16(kd, a.kv.k + row + 4 * d4);
@@ -443,8 +447,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
     if (ntiles > 0) stage_tile(0);
 
     // ---- Q (A operand of S): vector m = head g = m / BQ, token m % BQ
+    // thread -> (row, 8-d block) with 8 consecutive rows per 8 lanes: each
+    // quarter-warp's 16-byte stores fill distinct bank slots
     for (int i = tid; i < kTcM * (HD / 8); i += kTcThreads) {
-        const int m = i >> 4, kb = i & 15;
+        const int m = (i & 7) | ((i >> 7) << 3), kb = (i >> 3) & 15;
         const int g = m / BQ, tl = m % BQ;
         float x[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         if (tl < nq) {
@@ -486,9 +492,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
         const float *svf = reinterpret_cast<const float *>(sm + kTcSV);
         // ---- K tile: B[key n][d]; thread -> (key, 8-d block) pairs
         for (int i = tid; i < kTcN * (HD / 8); i += kTcThreads) {
-            const int n = i >> 4, kb = i & 15;
-            const float4 u0 = *reinterpret_cast<const float4 *>(skf + n * HD + 8 * kb);
-            const float4 u1 = *reinterpret_cast<const float4 *>(skf + n * HD + 8 * kb + 4);
+            const int n = (i & 7) | ((i >> 7) << 3), kb = (i >> 3) & 15;
+            const float4 u0 = *reinterpret_cast<const float4 *>(skf + n * kTcSRow + 8 * kb);
+            const float4 u1 = *reinterpret_cast<const float4 *>(skf + n * kTcSRow + 8 * kb + 4);
             float x[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
             for (int e = 0; e < 8; e++) x[e] = __fmul_rn(x[e], ks);
@@ -497,24 +503,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
             *reinterpret_cast<uint4 *>(sm + kTcK + tc_off(n, kb, 16)) = hi;
             *reinterpret_cast<uint4 *>(sm + kTcKl + tc_off(n, kb, 16)) = lo;
         }
-        // ---- V tile transposed: B[d][key]; thread -> (4 d, 8 keys)
+        // ---- V tile transposed: B[d][key]; thread -> (d, four 8-key blocks):
+        // consecutive lanes read consecutive words and store distinct slots
         {
-            const int d4 = tid & 31, nb = tid >> 5;  // d = 4 d4 .. +3, keys 8 nb .. +7
-            float x[4][8];
+            const int d = tid & 127, nb0 = (tid >> 7) * 4;
 #pragma unroll
-            for (int j = 0; j < 8; j++) {
-                const float4 v = *reinterpret_cast<const float4 *>(svf + (8 * nb + j) * HD + 4 * d4);
-                x[0][j] = v.x;
-                x[1][j] = v.y;
-                x[2][j] = v.z;
-                x[3][j] = v.w;
-            }
+            for (int q = 0; q < 4; q++) {
+                const int nb = nb0 + q;
+                float x[8];
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
+                for (int j = 0; j < 8; j++) x[j] = svf[(8 * nb + j) * kTcSRow + d];
                 uint4 hi, lo;
-                big |= tc_split8(x[c], hi, lo);
-                *reinterpret_cast<uint4 *>(sm + kTcV + tc_off(4 * d4 + c, nb, 8)) = hi;
-                *reinterpret_cast<uint4 *>(sm + kTcVl + tc_off(4 * d4 + c, nb, 8)) = lo;
+                big |= tc_split8(x, hi, lo);
+                *reinterpret_cast<uint4 *>(sm + kTcV + tc_off(d, nb, 8)) = hi;
+                *reinterpret_cast<uint4 *>(sm + kTcVl + tc_off(d, nb, 8)) = lo;
             }
         }
         tc::fence_proxy_async_smem();
