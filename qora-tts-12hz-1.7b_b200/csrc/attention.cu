@@ -302,11 +302,13 @@ __global__ void __launch_bounds__(kPfThreads, 2) k_prefill_attn(const AttnArgs a
 // ------------------------------------------------------------------------
 // Causal prefill attention on the tensor cores (head_dim 128): the same
 // computation as k_prefill_attn, with Q K^T and P V as tcgen05 MMAs.
-// One CTA takes 128 query vectors (128 / G tokens x the G query heads of one
-// kv head: vector m = head (m / BQ), token (m % BQ)) = the MMA's M rows, and
-// walks the key positions in tiles of 64 that start at multiples of 64
-// (absolute positions, so every row's result has the same bits in any
-// prefill chunk).  Per tile:
+// A pair of CTAs takes 128 query vectors (128 / G tokens x the G query heads
+// of one kv head: vector m = head (m / BQ), token (m % BQ)) = the MMA's M
+// rows; the key positions go in tiles of 64 that start at multiples of 64
+// (absolute positions), the even tiles to one CTA and the odd ones to the
+// other, whose two online-softmax states are merged at the end in a fixed
+// order (so every row's result has the same bits in any prefill chunk).
+// Per tile:
 //   * the K / V rows of the tile come from the cache (row addressing: slab
 //     or paged) into an f32 staging buffer with cp.async, issued while the
 //     previous tile computes; K goes to B[key][d] and V transposed to
@@ -379,8 +381,10 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
     __shared__ uint32_t tmem_slot;
     __shared__ float red_s[8];
     __shared__ float red_m[2][kTcM], red_l[2][kTcM];  // per-half row max / sum of a tile
+    __shared__ int last_flag;
     const int qb = gridDim.x - 1 - blockIdx.x;  // the longest query blocks first
-    const int h = blockIdx.y, b = blockIdx.z;
+    const int h = blockIdx.y, b = blockIdx.z >> 1;
+    const int sp = blockIdx.z & 1;               // this CTA's key tiles: kt = sp mod 2
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (tid == 0) {
         mbar_init(&bar_s, 1);
@@ -423,7 +427,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
     const int t0 = qb * BQ;
     const int nq = min(BQ, a.T - t0);
     const int kend = L0 + t0 + max(nq, 0);  // keys [0, kend) are visible to some row
-    const int ntiles = (bad || nq <= 0) ? 0 : (kend + kTcN - 1) / kTcN;
+    const bool run = !bad && nq > 0;
+    const int ntiles = run ? (kend + kTcN - 1) / kTcN : 0;
     bool big = false;
     // f32 K / V rows of tile kt -> staging (16-byte cp.async pieces; rows past
     // kend are zeros: never visible, and unwritten cache memory may hold anything)
@@ -444,7 +449,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    if (ntiles > 0) stage_tile(0);
+    if (sp < ntiles) stage_tile(sp);
 
     // ---- Q (A operand of S): vector m = head g = m / BQ, token m % BQ
     // thread -> (row, 8-d block) with 8 consecutive rows per 8 lanes: each
@@ -484,7 +489,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
     constexpr uint32_t id_o = tc::idesc_f16_f32(128, HD);
     const uint32_t sbase = smem_u32(sm);
 
-    for (int kt = 0; kt < ntiles; kt++) {
+    for (int kt = sp, it = 0; kt < ntiles; kt += 2, it++) {
         const int k0 = kt * kTcN;
         asm volatile("cp.async.wait_all;" ::: "memory");
         __syncthreads();  // tile kt staged (every thread's pieces)
@@ -522,7 +527,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
         tc::fence_proxy_async_smem();
         tc::fence_before_sync();
         __syncthreads();  // operands written, staging read
-        if (kt + 1 < ntiles) stage_tile(kt + 1);  // lands while this tile computes
+        if (kt + 2 < ntiles) stage_tile(kt + 2);  // lands while this tile computes
         // ---- S = Qh Kh + Qh Kl + Ql Kh
         if (tid == 0) {
             tc::fence_after_sync();
@@ -541,7 +546,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
         // bounded wait (phase kt of bar_s)
         {
             const long long tw = clock64();
-            while (!mbar_try_wait(&bar_s, kt & 1))
+            while (!mbar_try_wait(&bar_s, it & 1))
                 if (clock64() - tw > (1ll << 31)) {
                     raise_error(a.err, kDevTimeout);
                     break;
@@ -603,7 +608,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
         m_run = m_new;
         {
             const long long tw = clock64();
-            while (!mbar_try_wait(&bar_o, kt & 1))
+            while (!mbar_try_wait(&bar_o, it & 1))
                 if (clock64() - tw > (1ll << 31)) {
                     raise_error(a.err, kDevTimeout);
                     break;
@@ -624,18 +629,50 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
         __syncthreads();  // shared operands and tensor memory are rewritten next
     }
     if (big) raise_error(a.err, kDevF16Range);
-    // ---- out = O / l: row mrow, columns 64 hs .. +63
-    if (rvalid && ntiles > 0) {
-        const int g = mrow / BQ;
-        float *dst = a.out + (int64_t)(b * a.T + t0 + tl_r) * a.ldout + (int64_t)(h * G + g) * HD + 64 * hs;
+    // ---- the two CTAs' partial states (even and odd key tiles) meet in
+    // global scratch; the second to finish merges them, split 0 first, and
+    // writes out = O / l: row mrow, columns 64 hs .. +63
+    if (run) {
+        const int64_t pair = ((int64_t)b * a.kv_heads + h) * gridDim.x + qb;
+        float *po = a.part_o + (pair * 2 + sp) * (kTcM * HD) + mrow * HD + 64 * hs;
+        float *pml = a.part_ml + (pair * 2 + sp) * (kTcM * 2) + mrow * 2;
 #pragma unroll
-        for (int c = 0; c < 64; c += 4) {
-            float4 r;
-            r.x = __fdiv_rn(o[c], l_run);
-            r.y = __fdiv_rn(o[c + 1], l_run);
-            r.z = __fdiv_rn(o[c + 2], l_run);
-            r.w = __fdiv_rn(o[c + 3], l_run);
-            *reinterpret_cast<float4 *>(dst + c) = r;
+        for (int c = 0; c < 64; c += 4) __stcg(reinterpret_cast<float4 *>(po + c), make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]));
+        if (hs == 0) {
+            __stcg(pml, m_run);
+            __stcg(pml + 1, l_run);
+        }
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) last_flag = atomicAdd(&a.tickets[pair], 1u) == 1u;
+        __syncthreads();
+        if (last_flag) {
+            __threadfence();
+            const float *p0 = a.part_o + (pair * 2) * (kTcM * HD) + mrow * HD + 64 * hs;
+            const float *p1 = p0 + kTcM * HD;
+            const float *q0 = a.part_ml + (pair * 2) * (kTcM * 2) + mrow * 2;
+            const float *q1 = q0 + kTcM * 2;
+            const float m0 = __ldcg(q0), l0 = __ldcg(q0 + 1), m1 = __ldcg(q1), l1 = __ldcg(q1 + 1);
+            const float M = fmaxf(m0, m1);
+            const float w0 = m0 == -INFINITY ? 0.0f : __expf(m0 - M);
+            const float w1 = m1 == -INFINITY ? 0.0f : __expf(m1 - M);
+            const float L = __fadd_rn(__fmul_rn(l0, w0), __fmul_rn(l1, w1));
+            if (rvalid) {
+                const int g = mrow / BQ;
+                float *dst = a.out + (int64_t)(b * a.T + t0 + tl_r) * a.ldout + (int64_t)(h * G + g) * HD + 64 * hs;
+#pragma unroll
+                for (int c = 0; c < 64; c += 4) {
+                    const float4 u = __ldcg(reinterpret_cast<const float4 *>(p0 + c));
+                    const float4 v = __ldcg(reinterpret_cast<const float4 *>(p1 + c));
+                    float4 r;
+                    r.x = __fdiv_rn(__fadd_rn(__fmul_rn(u.x, w0), __fmul_rn(v.x, w1)), L);
+                    r.y = __fdiv_rn(__fadd_rn(__fmul_rn(u.y, w0), __fmul_rn(v.y, w1)), L);
+                    r.z = __fdiv_rn(__fadd_rn(__fmul_rn(u.z, w0), __fmul_rn(v.z, w1)), L);
+                    r.w = __fdiv_rn(__fadd_rn(__fmul_rn(u.w, w0), __fmul_rn(v.w, w1)), L);
+                    *reinterpret_cast<float4 *>(dst + c) = r;
+                }
+            }
+            if (tid == 0) a.tickets[pair] = 0u;
         }
     }
     tc::fence_before_sync();
@@ -978,7 +1015,8 @@ int launch_prefill_attn_tc_g(const AttnArgs &a, cudaStream_t st) {
         QORA_CUDA(cudaFuncSetAttribute(k_prefill_attn_tc<G>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcBytes));
         attr_done[dev] = true;
     }
-    dim3 grid((a.T + BQ - 1) / BQ, a.kv_heads, a.streams);
+    // two CTAs per query block (even and odd key tiles)
+    dim3 grid((a.T + BQ - 1) / BQ, a.kv_heads, 2 * a.streams);
     return launch_ex(k_prefill_attn_tc<G>, grid, dim3(kTcThreads), (size_t)kTcBytes, st, 1u, a);
 }
 
