@@ -631,33 +631,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
     if (big) raise_error(a.err, kDevF16Range);
     // ---- the two CTAs' partial states (even and odd key tiles) meet in
     // global scratch; the second to finish merges them, split 0 first, and
-    // writes out = O / l: row mrow, columns 64 hs .. +63
+    // writes out = O / l: row mrow, columns 64 hs .. +63.  The scratch is
+    // indexed by the query vector itself ((stream, token) row x query head),
+    // so it needs rows x heads x 2 x (128 + 2) floats whatever the block
+    // shape: within attn_part_o_floats / attn_part_ml_floats of those rows.
     if (run) {
         const int64_t pair = ((int64_t)b * a.kv_heads + h) * gridDim.x + qb;
-        float *po = a.part_o + (pair * 2 + sp) * (kTcM * HD) + mrow * HD + 64 * hs;
-        float *pml = a.part_ml + (pair * 2 + sp) * (kTcM * 2) + mrow * 2;
+        const int64_t vec = (int64_t)(b * a.T + t0 + tl_r) * a.heads + h * G + mrow / BQ;
+        if (rvalid) {
+            float *po = a.part_o + (vec * 2 + sp) * HD + 64 * hs;
 #pragma unroll
-        for (int c = 0; c < 64; c += 4) __stcg(reinterpret_cast<float4 *>(po + c), make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]));
-        if (hs == 0) {
-            __stcg(pml, m_run);
-            __stcg(pml + 1, l_run);
+            for (int c = 0; c < 64; c += 4)
+                __stcg(reinterpret_cast<float4 *>(po + c), make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]));
+            if (hs == 0) {
+                __stcg(a.part_ml + (vec * 2 + sp) * 2, m_run);
+                __stcg(a.part_ml + (vec * 2 + sp) * 2 + 1, l_run);
+            }
         }
         __threadfence();
         __syncthreads();
         if (tid == 0) last_flag = atomicAdd(&a.tickets[pair], 1u) == 1u;
         __syncthreads();
-        if (last_flag) {
+        if (last_flag && rvalid) {
             __threadfence();
-            const float *p0 = a.part_o + (pair * 2) * (kTcM * HD) + mrow * HD + 64 * hs;
-            const float *p1 = p0 + kTcM * HD;
-            const float *q0 = a.part_ml + (pair * 2) * (kTcM * 2) + mrow * 2;
-            const float *q1 = q0 + kTcM * 2;
+            const float *p0 = a.part_o + (vec * 2) * HD + 64 * hs;
+            const float *p1 = p0 + HD;
+            const float *q0 = a.part_ml + (vec * 2) * 2;
+            const float *q1 = q0 + 2;
             const float m0 = __ldcg(q0), l0 = __ldcg(q0 + 1), m1 = __ldcg(q1), l1 = __ldcg(q1 + 1);
             const float M = fmaxf(m0, m1);
             const float w0 = m0 == -INFINITY ? 0.0f : __expf(m0 - M);
             const float w1 = m1 == -INFINITY ? 0.0f : __expf(m1 - M);
             const float L = __fadd_rn(__fmul_rn(l0, w0), __fmul_rn(l1, w1));
-            if (rvalid) {
+            {
                 const int g = mrow / BQ;
                 float *dst = a.out + (int64_t)(b * a.T + t0 + tl_r) * a.ldout + (int64_t)(h * G + g) * HD + 64 * hs;
 #pragma unroll
@@ -672,8 +678,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_prefill_attn_tc(const AttnArg
                     *reinterpret_cast<float4 *>(dst + c) = r;
                 }
             }
-            if (tid == 0) a.tickets[pair] = 0u;
         }
+        if (last_flag && tid == 0) a.tickets[pair] = 0u;
     }
     tc::fence_before_sync();
     __syncthreads();
