@@ -1001,6 +1001,10 @@ int launch_prefill_attn_g(const AttnArgs &a, cudaStream_t st) {
     return launch_ex(k_prefill_attn<HD, G>, grid, dim3(kPfThreads), sizeof(PfSmem<HD>), st, 1u, a);
 }
 
+// Caches of at least this many positions decode on the streamed kernel and
+// prefill on the tensor-core kernel.
+constexpr int kStreamMinCapacity = 256;
+
 // QORA_PREFILL_ATTN_TC=0 in the environment keeps head_dim-128 prefills on
 // the CUDA-core kernel (for comparison).
 bool prefill_attn_tc_disabled() {
@@ -1026,9 +1030,14 @@ int launch_prefill_attn_tc_g(const AttnArgs &a, cudaStream_t st) {
     return launch_ex(k_prefill_attn_tc<G>, grid, dim3(kTcThreads), (size_t)kTcBytes, st, 1u, a);
 }
 
+// The tensor-core kernel serves caches of kStreamMinCapacity positions or
+// more (the talker's); short caches (the predictor's, whose per-op batched
+// path prefills 2 tokens per stream) keep the f32 kernel, whose small CTAs
+// suit them.  The choice depends on the cache only, so every prefill call
+// into one cache uses the same kernel (same bits however a prompt is split).
 template <int HD>
 int launch_prefill_attn_hd(const AttnArgs &a, cudaStream_t st) {
-    if (HD == 128 && !prefill_attn_tc_disabled()) {
+    if (HD == 128 && a.kv.max_pos >= kStreamMinCapacity && !prefill_attn_tc_disabled()) {
         switch (a.heads / a.kv_heads) {
             case 1: return launch_prefill_attn_tc_g<1>(a, st);
             case 2: return launch_prefill_attn_tc_g<2>(a, st);
@@ -1072,8 +1081,6 @@ int launch_qkv_post(const AttnArgs &a, cudaStream_t st) {
     return set_error(QORA_ERR_UNSUPPORTED, "head_dim %d", a.kv.head_dim);
 }
 
-// Caches of at least this many positions decode on the streamed kernel.
-constexpr int kStreamMinCapacity = 256;
 
 int launch_attention(const AttnArgs &a, cudaStream_t st) {
     if (!a.preappended && a.T != 1)

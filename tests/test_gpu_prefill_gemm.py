@@ -88,3 +88,30 @@ def test_prefill_attention_tc_matches_cuda_core(tmp_path):
         worst = max(worst, err)
         assert err <= 1e-5, (key, err)
     print(f"prefill attention tc vs cuda-core: worst relative {worst:.2e}")
+
+
+def test_tc_prefill_bits_do_not_depend_on_the_split():
+    """The talker's cache (>= 256 positions) prefills on k_prefill_attn_tc and
+    the prefill GEMM: a 300-token prompt prefilled in one call and as 120 +
+    180 tokens (the prefix-cache path, generate_new.rs:320-322) gives the
+    same last hidden and the same cached K / V, bit for bit."""
+    import torch
+    import qora_b200 as qb
+    from qora_b200 import engine as E
+    ctx = E.Context(0)
+    cfg = qb.ModelConfig(t_layers=2, t_max_pos=512)
+    talker = E.Talker(ctx, qb.synth_talker(cfg), max_batch=1)
+    H, T, P = cfg.t_hidden, 300, 120
+    x = torch.from_numpy(qb.synth_normal(77, 1.0, T * H).reshape(T, H)).cuda()
+    whole = talker.new_kv(max_pos=512, streams=1)
+    split = talker.new_kv(max_pos=512, streams=1)
+    h1 = talker.prefill_talker_raw_from(x, whole, 0)
+    talker.prefill_talker_raw_from(x[:P].contiguous(), split, 0)
+    h2 = talker.prefill_talker_raw_from(x[P:].contiguous(), split, P)
+    ctx.check_device_error()
+    assert np.array_equal(h1.cpu().numpy().view(np.uint32), h2.cpu().numpy().view(np.uint32))
+    for layer in range(cfg.t_layers):
+        k1, v1 = whole.layer_tensors(layer)
+        k2, v2 = split.layer_tensors(layer)
+        assert np.array_equal(k1[:, :, :T].cpu().numpy(), k2[:, :, :T].cpu().numpy()), layer
+        assert np.array_equal(v1[:, :, :T].cpu().numpy(), v2[:, :, :T].cpu().numpy()), layer
