@@ -1,9 +1,9 @@
-"""Config 3 (BASELINE.json configs[3]): the long-context KV stress at full size.
+"""Config 3: the long-context KV stress at full size.
 
 The 28-layer talker (1.7B dims, random-init Q4 weights) takes an ICL-style
 prefill of 2048 N(0,1) positions per stream (seed 42 + stream), then 2048
 greedy decode steps to 4096 positions, for 2 streams with caches of their
-own (the survey's config runs 32 streams; two suffice for parity, the bench
+own (the configuration runs 32 streams; two suffice for parity, the bench
 times 32), held in a paged cache (64-position pages mapped as they grow).
 Each step's input is embed_codec_token of the engine's own argmax (last index on ties, code_predictor.rs:335-341) fed back through
 forward_with_embedding (talker.rs:263-360): the greedy loop itself runs on
