@@ -391,6 +391,72 @@ int qora_engine_kernels_per_frame(qora_engine *e, int32_t *count);
 int qora_engine_state(qora_engine *e, float **logits, float **hidden, uint32_t **prev,
                       uint64_t **rng, int32_t **positions);
 
+/* ------------------------------------------------------------ decoder.rs */
+/* The speech decoder (SpeechDecoderWeights + decode_to_audio, decoder.rs:24-66,
+ * 395-582): 16 codes per 12.5 Hz frame -> 24 kHz f32 samples, all in f32. */
+typedef struct qora_decoder qora_decoder;
+
+/* Its configuration (decoder.rs:1-14, loader.rs:503-716; the 12 Hz
+ * tokenizer's values in the comments).  Fixed by the reference and not
+ * configurable: pre-conv taps 3, upsample ConvTranspose kernel 2 / stride 2,
+ * ConvNeXt depthwise taps 7, Vocos conv taps 7, residual dilations 1, 3, 9,
+ * output conv taps 7, norm eps 1e-5. */
+typedef struct qora_decoder_dims {
+    int32_t codebook_dim;      /* 256 */
+    int32_t codebook_size;     /* 2048 */
+    int32_t num_quantizers;    /* 16: rvq_first + 15 rvq_rest */
+    int32_t vq_dim;            /* 512: width of the codebook output projections */
+    int32_t latent;            /* 1024: pre-conv and upsample channels */
+    int32_t hidden;            /* 512 */
+    int32_t num_heads;         /* 16 */
+    int32_t head_dim;          /* 64 (the only value supported) */
+    int32_t intermediate;      /* 1024 (a multiple of 64) */
+    int32_t num_layers;        /* 8 */
+    int32_t sliding_window;    /* 72 (at most 128) */
+    int32_t upsample_stages;   /* 2 */
+    int32_t upsample_inner;    /* 4096: ConvNeXt pwconv1 width */
+    int32_t vocos_blocks;      /* 4 (at most 7) */
+    int32_t vocos_channels[8]; /* 1536, 768, 384, 192, 96: blocks + 1 entries used */
+    int32_t vocos_kernels[8];  /* 16, 10, 8, 6: each the stride or twice it */
+    int32_t vocos_strides[8];  /* 8, 5, 4, 3 */
+    int32_t rope_max_pos;      /* 8000 (loader.rs:671): later positions are not rotated */
+    double rope_theta;         /* 10000 */
+} qora_decoder_dims;
+
+/* load_speech_decoder (loader.rs:503-716) in three steps: create, one
+ * qora_decoder_set_tensor per checkpoint tensor (its safetensors name and its
+ * values in the checkpoint's own layout, read as f32: Linear [out][in], Conv1d
+ * [out][in][k], ConvTranspose1d [in][out][k], codebooks as embedding_sum and
+ * cluster_usage, normalised here as ema_codebook does, loader.rs:488-501),
+ * then finalize (uploads; QORA_ERR_INVALID naming the first tensor not set).
+ * An unknown name or a wrong value count is an error. */
+int qora_decoder_create(qora_ctx *ctx, const qora_decoder_dims *dims, qora_decoder **out);
+int qora_decoder_set_tensor(qora_decoder *dec, const char *name, const float *data_host,
+                            int64_t count);
+int qora_decoder_finalize(qora_decoder *dec);
+void qora_decoder_destroy(qora_decoder *dec);
+/* Samples decoded from `frames` frames: frames * 1920 at the 12 Hz dims. */
+int qora_decoder_samples(const qora_decoder *dec, int64_t frames, int64_t *samples);
+/* decode_to_audio (decoder.rs:395-582) from host codes [num_quantizers][frames]
+ * (quantizer-major, as the reference's codes[q][t]); warmup_host
+ * [num_quantizers][warmup_frames] is prepended and its share of the samples
+ * trimmed (warmup_trim_len, decoder.rs:649-656) when it is non-NULL and
+ * warmup_frames > 0.  Writes *n_samples = frames * hop samples, clamped to
+ * [-1, 1], into samples_host (capacity values; QORA_ERR_SHAPE when too
+ * small).  frames == 0 gives no samples (decoder.rs:401-404).  A code outside
+ * the codebook reads row 0 and gives QORA_ERR_RANGE at the next
+ * qora_ctx_check_device_error (the reference panics on the slice). */
+int qora_decode_to_audio(qora_decoder *dec, const uint32_t *codes_host, int64_t frames,
+                         const uint32_t *warmup_host, int64_t warmup_frames, float *samples_host,
+                         int64_t capacity, int64_t *n_samples, void *stream);
+/* The same on the device: codes [num_quantizers][warmup_frames + frames]
+ * (each row its warm-up codes, then its codes), samples receives
+ * frames * hop values; *launches (optional) the kernels launched.
+ * Asynchronous on `stream`. */
+int qora_decode_to_audio_device(qora_decoder *dec, const uint32_t *codes, int64_t frames,
+                                int64_t warmup_frames, float *samples, int32_t *launches,
+                                void *stream);
+
 #ifdef __cplusplus
 }
 #endif

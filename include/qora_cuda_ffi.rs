@@ -12,6 +12,19 @@ pub const QORA_OK: c_int = 0;
 #[repr(C)] pub struct qora_engine { _p: [u8; 0] }
 #[repr(C)] pub struct qora_text_proj { _p: [u8; 0] }
 #[repr(C)] pub struct qora_model_file { _p: [u8; 0] }
+#[repr(C)] pub struct qora_decoder { _p: [u8; 0] }
+
+/// qora_decoder_dims: SpeechDecoderWeights' configuration (decoder.rs:56-66).
+#[repr(C)]
+#[derive(Clone, Copy)]
+pub struct qora_decoder_dims {
+    pub codebook_dim: i32, pub codebook_size: i32, pub num_quantizers: i32, pub vq_dim: i32,
+    pub latent: i32, pub hidden: i32, pub num_heads: i32, pub head_dim: i32,
+    pub intermediate: i32, pub num_layers: i32, pub sliding_window: i32,
+    pub upsample_stages: i32, pub upsample_inner: i32, pub vocos_blocks: i32,
+    pub vocos_channels: [i32; 8], pub vocos_kernels: [i32; 8], pub vocos_strides: [i32; 8],
+    pub rope_max_pos: i32, pub rope_theta: f64,
+}
 
 #[repr(C)]
 #[derive(Clone, Copy)]
@@ -205,6 +218,23 @@ extern "C" {
     pub fn qora_engine_state(e: *mut qora_engine, logits: *mut *mut f32, hidden: *mut *mut f32,
                              prev: *mut *mut u32, rng: *mut *mut u64,
                              positions: *mut *mut i32) -> c_int;
+
+    // load_speech_decoder (loader.rs:503-716): one set_tensor per safetensors tensor
+    pub fn qora_decoder_create(ctx: *mut qora_ctx, dims: *const qora_decoder_dims,
+                               out: *mut *mut qora_decoder) -> c_int;
+    pub fn qora_decoder_set_tensor(dec: *mut qora_decoder, name: *const c_char,
+                                   data_host: *const f32, count: i64) -> c_int;
+    pub fn qora_decoder_finalize(dec: *mut qora_decoder) -> c_int;
+    pub fn qora_decoder_destroy(dec: *mut qora_decoder);
+    pub fn qora_decoder_samples(dec: *const qora_decoder, frames: i64, samples: *mut i64) -> c_int;
+    // decode_to_audio (decoder.rs:395-582)
+    pub fn qora_decode_to_audio(dec: *mut qora_decoder, codes_host: *const u32, frames: i64,
+                                warmup_host: *const u32, warmup_frames: i64,
+                                samples_host: *mut f32, capacity: i64, n_samples: *mut i64,
+                                stream: *mut c_void) -> c_int;
+    pub fn qora_decode_to_audio_device(dec: *mut qora_decoder, codes: *const u32, frames: i64,
+                                       warmup_frames: i64, samples: *mut f32, launches: *mut i32,
+                                       stream: *mut c_void) -> c_int;
 }
 
 /// Turns a status into a Result with the library's message (the reference

@@ -65,6 +65,16 @@ class SampleParams(C.Structure):
                 ("repetition_penalty", C.c_float)]
 
 
+class DecoderDims(C.Structure):
+    """qora_decoder_dims (include/qora_cuda.h)."""
+    _fields_ = [(n, C.c_int32) for n in ("codebook_dim", "codebook_size", "num_quantizers", "vq_dim",
+                                          "latent", "hidden", "num_heads", "head_dim", "intermediate",
+                                          "num_layers", "sliding_window", "upsample_stages",
+                                          "upsample_inner", "vocos_blocks")] + \
+               [("vocos_channels", C.c_int32 * 8), ("vocos_kernels", C.c_int32 * 8),
+                ("vocos_strides", C.c_int32 * 8), ("rope_max_pos", C.c_int32), ("rope_theta", C.c_double)]
+
+
 # name -> (restype, argtypes); every entry point declared in include/qora_cuda.h
 _vp, _i32, _i64, _f32, _u64 = C.c_void_p, C.c_int32, C.c_int64, C.c_float, C.c_uint64
 _PP = C.POINTER(C.c_void_p)
@@ -129,6 +139,13 @@ SIGNATURES = {
     "qora_engine_set_temperature": (C.c_int, [_vp, _f32]),
     "qora_engine_trace": (C.c_int, [_vp, _i32, _i32, _vp, _vp, _vp]),
     "qora_engine_kernels_per_frame": (C.c_int, [_vp, C.POINTER(C.c_int32)]),
+    "qora_decoder_create": (C.c_int, [_vp, _vp, _PP]),
+    "qora_decoder_set_tensor": (C.c_int, [_vp, C.c_char_p, _vp, _i64]),
+    "qora_decoder_finalize": (C.c_int, [_vp]),
+    "qora_decoder_destroy": (None, [_vp]),
+    "qora_decoder_samples": (C.c_int, [_vp, _i64, C.POINTER(C.c_int64)]),
+    "qora_decode_to_audio": (C.c_int, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, C.POINTER(C.c_int64), _vp]),
+    "qora_decode_to_audio_device": (C.c_int, [_vp, _vp, _i64, _i64, _vp, C.POINTER(C.c_int32), _vp]),
     "qora_engine_state": (C.c_int, [_vp, _PP, _PP, _PP, _PP, _PP]),
 }
 
