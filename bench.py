@@ -52,8 +52,10 @@ def parse():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-roofline", action="store_true")
     ap.add_argument("--no-config3", action="store_true")
+    ap.add_argument("--no-decoder", action="store_true")
+    ap.add_argument("--frames", type=int, default=None, help="frames of the decoder profile case")
     ap.add_argument("--profile-case", default=None,
-                    choices=["gemv", "frame_trace", "batch_frame", "attn_decode", "prefill"],
+                    choices=["gemv", "frame_trace", "batch_frame", "attn_decode", "prefill", "decoder"],
                     help="small fixed workload for an ncu capture instead of the bench")
     return ap.parse_args()
 
@@ -505,6 +507,99 @@ def talker_step_rate(E, ctx, tw, torch, qb, steps=256, prefill=32):
             "steps_per_s": round(1000.0 / ms, 1)}
 
 
+DECODER_FRAMES = 241          # the reference's decode measurement (alynaze.txt:17-22: 241 frames)
+FP32_PEAK_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12   # nominal: SMs x FP32 lanes x 2 x clocks.max.sm
+
+
+def decoder_flops(d, frames: int) -> int:
+    """Algorithmic FLOPs (2 per multiply-add) of decode_to_audio over `frames`
+    frames: every projection and convolution term, the attention's scores and
+    weighted sums over each position's window; element-wise ops not counted."""
+    F = frames
+    HD = d.num_heads * d.head_dim
+    f = 2 * 2 * d.codebook_dim * d.vq_dim * F                 # codebook output projections
+    f += 2 * d.vq_dim * d.latent * 3 * F                      # pre-conv
+    f += 2 * d.latent * d.hidden * F                          # input projection
+    keys = sum(min(t + 1, d.sliding_window) for t in range(F))
+    f += d.num_layers * (2 * F * (d.hidden * 3 * HD + HD * d.hidden + 2 * d.hidden * d.intermediate
+                                  + d.intermediate * d.hidden) + 2 * 2 * HD * keys)
+    f += 2 * d.hidden * d.latent * F                          # output projection
+    L = F
+    for _ in range(d.upsample_stages):
+        L *= 2
+        f += 2 * d.latent * d.latent * L + 2 * d.latent * 7 * L + 2 * 2 * d.latent * d.upsample_inner * L
+    ch = d.vocos_channels
+    f += 2 * d.latent * ch[0] * 7 * L
+    for b, (k, s) in enumerate(zip(d.vocos_kernels, d.vocos_strides)):
+        L *= s
+        f += 2 * ch[b] * ch[b + 1] * (k // s) * L + 3 * (2 * ch[b + 1] * ch[b + 1] * 8 * L)
+    f += 2 * ch[-1] * 7 * L
+    return f
+
+
+def decoder_rate(ctx, torch, frames=DECODER_FRAMES, reps=5, cpu_frames_n=None):
+    """The speech decoder (decode_to_audio, decoder.rs:395-582) at the 12 Hz
+    tokenizer dims on `frames` frames of uniform random codes (seed 5),
+    random-init f32 weights: device time per decode (codes resident, CUDA
+    events over `reps` decodes after 2 untimed ones), end to end through
+    qora_decode_to_audio (host codes in, host samples out), the implicit-GEMM
+    roofline, and the oracle's time per frame on a few frames (CPU)."""
+    from qora_b200.decoder import DecoderDims, SpeechDecoder, synth_decoder
+    d = DecoderDims()
+    W = synth_decoder(d)
+    dec = SpeechDecoder(ctx, d, W)
+    codes = np.random.default_rng(5).integers(0, d.codebook_size, (d.num_quantizers, frames)).astype(np.uint32)
+    cd = torch.from_numpy(codes.astype(np.int32)).cuda()
+    out = torch.empty(frames * d.hop, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+    launches = 0
+    for _ in range(2):
+        launches = dec.decode_device(cd, frames, out, stream=st)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        dec.decode_device(cd, frames, out, stream=st)
+    e1.record(st)
+    torch.cuda.synchronize()
+    ctx.check_device_error()
+    ms = e0.elapsed_time(e1) / reps
+    dec.decode_to_audio(codes)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        host = dec.decode_to_audio(codes)
+    e2e_ms = 1000.0 * (time.perf_counter() - t0) / reps
+    flops = decoder_flops(d, frames)
+    tf = flops / (ms * 1e-3) / 1e12
+    audio_s = frames * d.hop / 24000.0
+    res = {"workload": f"decode_to_audio of {frames} frames ({audio_s:.2f} s of 24 kHz audio), 12 Hz tokenizer "
+                       "dims, random-init f32 weights, uniform random codes; largest activation "
+                       f"{d.vocos_channels[-1] * frames * d.hop * 4 / 1e6:.0f} MB > L2",
+           "frames": frames, "ms_per_decode": round(ms, 3), "frames_per_s": round(frames / (ms * 1e-3), 1),
+           "audio_s_per_s": round(audio_s / (ms * 1e-3), 1), "gpu_launches_per_decode": launches,
+           "e2e": {"ms_per_decode": round(e2e_ms, 3), "frames_per_s": round(frames / (e2e_ms * 1e-3), 1),
+                   "h2d_bytes_per_decode": int(codes.nbytes), "d2h_bytes_per_decode": int(host.nbytes)},
+           "roofline": {"bound": "fp32 CUDA-core FMA", "kernel": "whole decode (k_dec_conv dominant)",
+                        "achieved": round(tf, 2), "peak": round(FP32_PEAK_TFLOPS, 1), "unit": "TFLOP/s",
+                        "frac": round(tf / FP32_PEAK_TFLOPS, 4),
+                        "peak_source": "nominal: 148 SMs x 128 FP32 lanes x 2 x 1965 MHz (not in "
+                                       "MEASURED_PEAKS.json)",
+                        "flops_per_decode": flops},
+           "vs_published_cpu": "the reference decodes 241 frames in ~15 s on its 22-thread laptop CPU "
+                               "(alynaze.txt:22)"}
+    if cpu_frames_n:
+        import pydecoder as pd
+        cc = codes[:, :cpu_frames_n]
+        t0 = time.perf_counter()
+        pd.decode_to_audio(W, cc, dims=d)
+        dt = time.perf_counter() - t0
+        res["cpu_baseline"] = {"value": round(cpu_frames_n / dt, 3), "unit": "frames/s", "cores": 1,
+                               "kind": "port", "sample": f"{cpu_frames_n} frames through the oracle's "
+                                                         "decode_to_audio (single-threaded C restatement)"}
+    del dec
+    return res
+
+
 def run_ours(args):
     import torch
     import qora_b200 as qb
@@ -645,6 +740,9 @@ def run_ours(args):
     if world == 1 and not args.no_sweep:
         cfg2 = [predictor_rate(E, ctx, qb, torch, hd, 64) for hd in (64, 128)]
         cfg0 = talker_step_rate(E, ctx, tw, torch, qb)
+    dec = None
+    if world == 1 and not args.no_decoder:
+        dec = decoder_rate(ctx, torch, cpu_frames_n=None if args.no_cpu else 2)
     clk.__exit__(None, None, None)
 
     cpu = None
@@ -681,6 +779,7 @@ def run_ours(args):
         "config3": cfg3,
         "config2_predictor": cfg2,
         "config0_talker": cfg0,
+        "decoder": dec,
         "gemv_sweep": sweep,
     }
     print(json.dumps(line), flush=True)
@@ -821,6 +920,35 @@ def profile_case_prefill(tokens=2048):
                       "ms": round(e0.elapsed_time(e1), 3)}))
 
 
+def profile_case_decoder(frames=DECODER_FRAMES):
+    """ncu case: one decode_to_audio of `frames` frames at the 12 Hz tokenizer
+    dims (as the bench's decoder leg), after one untimed decode, bracketed by
+    cudaProfilerStart/Stop; prints its CUDA-event time as one JSON line."""
+    import torch
+    from qora_b200 import engine as E
+    from qora_b200.decoder import DecoderDims, SpeechDecoder, synth_decoder
+    torch.cuda.set_device(0)
+    ctx = E.Context(0)
+    d = DecoderDims()
+    dec = SpeechDecoder(ctx, d, synth_decoder(d))
+    codes = np.random.default_rng(5).integers(0, d.codebook_size, (d.num_quantizers, frames)).astype(np.int32)
+    cd = torch.from_numpy(codes).cuda()
+    out = torch.empty(frames * d.hop, dtype=torch.float32, device="cuda")
+    st = torch.cuda.current_stream()
+    dec.decode_device(cd, frames, out, stream=st)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.profiler.start()
+    e0.record(st)
+    n = dec.decode_device(cd, frames, out, stream=st)
+    e1.record(st)
+    torch.cuda.synchronize()
+    torch.cuda.profiler.stop()
+    ctx.check_device_error()
+    print(json.dumps({"profile_case": "decoder", "frames": frames, "launches": n,
+                      "ms": round(e0.elapsed_time(e1), 3)}))
+
+
 def profile_case_attn_decode(streams=32, positions=4096, reps=8):
     """ncu case: the decode attention of one talker layer (16 q / 8 kv heads,
     head_dim 128) for `streams` streams over `positions` cached positions each
@@ -866,6 +994,9 @@ def profile_case_attn_decode(streams=32, positions=4096, reps=8):
 
 def main():
     args = parse()
+    if args.profile_case == "decoder":
+        profile_case_decoder(args.frames or DECODER_FRAMES)
+        return
     if args.profile_case == "prefill":
         profile_case_prefill()
         return

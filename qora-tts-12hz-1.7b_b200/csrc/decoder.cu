@@ -36,10 +36,20 @@ namespace {
 
 constexpr int kCvBM = 128;      // output channels per CTA tile
 constexpr int kCvBN = 128;      // positions per CTA tile
-constexpr int kCvBK = 8;        // input channels per pipeline stage
 constexpr int kCvThreads = 256;
 constexpr int kCvMaxHalo = 64;  // (taps - 1) * dilation
-constexpr int kCvXPer = (kCvBK * (kCvBN + kCvMaxHalo) + kCvThreads - 1) / kCvThreads;
+// input channels per pipeline stage: 16 for pointwise convolutions (8 K rows
+// per stage would leave the stage's loads and barrier uncovered), 8 otherwise
+template <int KS> constexpr int cv_bk() { return KS == 1 ? 16 : 8; }
+template <int KS> constexpr int cv_halo() { return KS == 1 ? 0 : kCvMaxHalo; }
+template <int KS> constexpr int cv_xper() {
+    return (cv_bk<KS>() * (kCvBN + cv_halo<KS>()) + kCvThreads - 1) / kCvThreads;
+}
+template <int KS> constexpr int cv_smem_floats(int halo) {
+    return 2 * cv_bk<KS>() * KS * kCvBM + 2 * cv_bk<KS>() * (kCvBN + halo);
+}
+constexpr int kCvRecvFloats = kCvBM * kCvBN;   // a K-split cluster's partial tiles (split-wide)
+constexpr int kCvMaxSplit = 8;
 
 enum DecPro { P_NONE = 0, P_SNAKE = 1, P_RMS = 2, P_LN = 3 };
 enum DecEpi { E_BIAS = 0, E_RESID = 1, E_SCALE_RESID = 2, E_GELU = 3, E_SWIGLU = 4 };
@@ -51,6 +61,7 @@ struct ConvArgs {
     const float *bias = nullptr;   // [oc] or null (no bias)
     float *out = nullptr;          // [oc_out][len * phases]; element (oc, j, phase p) at j * phases + p
     int ic = 0, oc = 0, oc_pad = 0, dil = 1, phases = 1;
+    int ksplit = 1;                // CTAs of a cluster (blockIdx.z) splitting the input channels
     const float *pa = nullptr, *pb = nullptr;  // per input channel: SnakeBeta exp(alpha), exp(-beta);
                                                // RMSNorm gamma; LayerNorm gamma, beta
     const float *ra = nullptr, *rb = nullptr;  // per position: RMSNorm 1/rms; LayerNorm mean, 1/std
@@ -94,17 +105,22 @@ __device__ __forceinline__ float prologue(float v, int ic, int64_t pos, const Co
 }
 
 // Implicit-GEMM convolution: one CTA per (128 positions, 128 output channels,
-// phase).  Thread (tx, ty) of the 16 x 16 grid owns output channels
+// phase); the phases of a position tile are adjacent CTAs (blockIdx.x =
+// tile * phases + phase), so their interleaved outputs are written to the
+// same L2 sectors at about the same time and their common input tile is
+// read from DRAM once.  Thread (tx, ty) of the 16 x 16 grid owns output channels
 // ty*4 .. +3 and 64 + ty*4 .. +3 of the tile and positions tx + 16 i
 // (i = 0..7), so a warp's input reads are 16 consecutive words (broadcast to
 // the two ty rows) and its weight reads two float4 broadcasts.  Weights reach
 // shared memory by cp.async (one row of 128 output channels per (ic, tap)),
 // input rows through registers (the prologue is applied on the way), both
-// double-buffered over stages of 8 input channels.
+// double-buffered over stages of cv_bk input channels.
 template <int KS, int PRO, int EPI>
-__global__ void __launch_bounds__(kCvThreads) k_dec_conv(const ConvArgs a) {
+__global__ void __launch_bounds__(kCvThreads, 2) k_dec_conv(const ConvArgs a) {
     extern __shared__ float4 dsm4[];
     float *dsm = reinterpret_cast<float *>(dsm4);
+    constexpr int kCvBK = cv_bk<KS>();
+    constexpr int kCvXPer = cv_xper<KS>();
     constexpr int WK = kCvBK * KS;
     const int halo = (KS - 1) * a.dil;
     const int XW = kCvBN + halo;
@@ -112,17 +128,20 @@ __global__ void __launch_bounds__(kCvThreads) k_dec_conv(const ConvArgs a) {
     float *Xs = dsm + 2 * WK * kCvBM;       // [2][kCvBK][XW]
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
     const int oc0 = blockIdx.y * kCvBM;
-    const int64_t j0 = (int64_t)blockIdx.x * kCvBN;
-    const int p = blockIdx.z;
+    const int p = (int)(blockIdx.x % (unsigned)a.phases);
+    const int64_t j0 = (int64_t)(blockIdx.x / (unsigned)a.phases) * kCvBN;
     const float *wp = a.w + (int64_t)p * a.ic * KS * a.oc_pad;
-    const int nst = (a.ic + kCvBK - 1) / kCvBK;
+    // K split: cluster rank q (= blockIdx.z) takes stages [st0, st1)
+    const int S = a.ksplit, q = blockIdx.z;
+    const int nall = (a.ic + kCvBK - 1) / kCvBK;
+    const int st0 = q * nall / S, st1 = (q + 1) * nall / S;
 
     auto orow = [&](int r) { return r < 4 ? ty * 4 + r : 64 + ty * 4 + (r - 4); };
     float acc[8][8];
 #pragma unroll
     for (int r = 0; r < 8; r++) {
         const int oc = oc0 + orow(r);
-        const float b = (EPI != E_SWIGLU && a.bias && oc < a.oc) ? __ldg(a.bias + oc) : 0.0f;
+        const float b = (EPI != E_SWIGLU && a.bias && oc < a.oc && q == 0) ? __ldg(a.bias + oc) : 0.0f;
 #pragma unroll
         for (int i = 0; i < 8; i++) acc[r][i] = b;
     }
@@ -173,14 +192,14 @@ __global__ void __launch_bounds__(kCvThreads) k_dec_conv(const ConvArgs a) {
         }
     };
 
-    load_w(0, 0);
-    fetch_x(0);
-    store_x(0, 0);
+    load_w(st0, 0);
+    fetch_x(st0);
+    store_x(st0, 0);
     cp_async_wait_all();
     __syncthreads();
-    for (int st = 0; st < nst; st++) {
-        const int buf = st & 1;
-        const bool more = st + 1 < nst;
+    for (int st = st0; st < st1; st++) {
+        const int buf = (st - st0) & 1;
+        const bool more = st + 1 < st1;
         if (more) {
             load_w(st + 1, buf ^ 1);
             fetch_x(st + 1);
@@ -212,6 +231,41 @@ __global__ void __launch_bounds__(kCvThreads) k_dec_conv(const ConvArgs a) {
     }
 
     const int64_t out_len = a.len * a.phases;
+    // K split: rank q finishes positions tx + 16 i for i in [q * 8 / S, (q + 1) * 8 / S)
+    // of the tile; every rank sends it those partial sums (distributed shared
+    // memory, receive buffer [S][128 rows][128 / S positions]), which it adds
+    // in rank order, rank 0's (bias-first) partial first.
+    int i_lo = 0, i_hi = 8;
+    if (S > 1) {
+        const int per = 8 / S, cw = kCvBN / S;
+        float *recv = dsm;                 // the stages' buffers are free after the loop
+        asm volatile("barrier.cluster.arrive.aligned;\n\tbarrier.cluster.wait.aligned;" ::: "memory");
+#pragma unroll
+        for (int r = 0; r < 8; r++)
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const int owner = i / per, cl = tx + 16 * (i - owner * per);
+                float *dst = recv + ((int64_t)q * kCvBM + orow(r)) * cw + cl;
+                uint32_t ra;
+                asm volatile("mapa.shared::cluster.u32 %0, %1, %2;"
+                             : "=r"(ra)
+                             : "r"((uint32_t)__cvta_generic_to_shared(dst)), "r"(owner));
+                asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(acc[r][i]) : "memory");
+            }
+        asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+        i_lo = q * per;
+        i_hi = i_lo + per;
+#pragma unroll
+        for (int r = 0; r < 8; r++)
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                if (i < i_lo || i >= i_hi) continue;
+                const int cl = tx + 16 * (i - i_lo);
+                float v = 0.0f;
+                for (int s2 = 0; s2 < S; s2++) v += recv[((int64_t)s2 * kCvBM + orow(r)) * cw + cl];
+                acc[r][i] = v;
+            }
+    }
     if constexpr (EPI == E_SWIGLU) {
         // rows ty*4 + r are gate channels and 64 + ty*4 + r the matching up
         // channels of output channels blockIdx.y * 64 + ty*4 + r
@@ -223,7 +277,7 @@ __global__ void __launch_bounds__(kCvThreads) k_dec_conv(const ConvArgs a) {
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 const int64_t j = j0 + tx + 16 * i;
-                if (j >= a.len) continue;
+                if (j >= a.len || i < i_lo || i >= i_hi) continue;
                 const float g = acc[r][i], u = acc[r + 4][i];
                 a.out[(int64_t)ch * out_len + j] = (g / (1.0f + expf(-g))) * u;
             }
@@ -237,7 +291,7 @@ __global__ void __launch_bounds__(kCvThreads) k_dec_conv(const ConvArgs a) {
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 const int64_t j = j0 + tx + 16 * i;
-                if (j >= a.len) continue;
+                if (j >= a.len || i < i_lo || i >= i_hi) continue;
                 const int64_t o = (int64_t)oc * out_len + j * a.phases + p;
                 float v = acc[r][i];
                 if constexpr (EPI == E_RESID) v = v + a.resid[o];           // signal[j] += residual[j]
@@ -528,29 +582,64 @@ struct qora_decoder {
 namespace qora {
 namespace {
 
+int g_sms[64];   // SM count per device (set when a decoder is created)
+
 template <int KS, int PRO, int EPI>
 int launch_conv_t(const ConvArgs &a, int device, cudaStream_t st) {
     static std::atomic<uint64_t> attr_done{0};
     const int halo = (KS - 1) * a.dil;
-    if (halo > kCvMaxHalo) return set_error(QORA_ERR_UNSUPPORTED, "convolution halo %d > %d", halo, kCvMaxHalo);
-    const size_t smem = (size_t)(2 * kCvBK * KS * kCvBM + 2 * kCvBK * (kCvBN + halo)) * sizeof(float);
+    if (halo > cv_halo<KS>()) return set_error(QORA_ERR_UNSUPPORTED, "convolution halo %d > %d", halo, cv_halo<KS>());
+    size_t smem = (size_t)cv_smem_floats<KS>(halo) * sizeof(float);
+    if (a.ksplit > 1) smem = std::max<size_t>(smem, (size_t)kCvRecvFloats * sizeof(float));
     const uint64_t bit = 1ull << (device & 63);
     if (!(attr_done.load() & bit)) {
-        const int max_smem = (2 * kCvBK * KS * kCvBM + 2 * kCvBK * (kCvBN + kCvMaxHalo)) * (int)sizeof(float);
+        const int max_smem = std::max(cv_smem_floats<KS>(cv_halo<KS>()), kCvRecvFloats) * (int)sizeof(float);
         QORA_CUDA(cudaFuncSetAttribute(k_dec_conv<KS, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        max_smem));
         attr_done.fetch_or(bit);
     }
-    const int64_t gx = (a.len + kCvBN - 1) / kCvBN;
+    const int64_t gx = (a.len + kCvBN - 1) / kCvBN * a.phases;
     const int gy = (a.oc + kCvBM - 1) / kCvBM;
-    if (gx > INT32_MAX || a.phases > 65535) return set_error(QORA_ERR_SHAPE, "convolution too long");
-    k_dec_conv<KS, PRO, EPI><<<dim3((unsigned)gx, gy, a.phases), kCvThreads, smem, st>>>(a);
+    if (gx > INT32_MAX || gy > 65535) return set_error(QORA_ERR_SHAPE, "convolution too long");
+    if (a.ksplit == 1) {
+        k_dec_conv<KS, PRO, EPI><<<dim3((unsigned)gx, gy, 1), kCvThreads, smem, st>>>(a);
+    } else {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)gx, gy, a.ksplit);
+        cfg.blockDim = dim3(kCvThreads, 1, 1);
+        cfg.dynamicSmemBytes = smem;
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = 1;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = a.ksplit;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        QORA_CUDA(cudaLaunchKernelEx(&cfg, k_dec_conv<KS, PRO, EPI>, a));
+    }
     QORA_LAUNCH_CHECK();
     return QORA_OK;
 }
 
 // The (taps, prologue, epilogue) combinations the decoder uses.
-int launch_conv(int taps, int pro, int epi, const ConvArgs &a, int device, cudaStream_t st) {
+// K split of a convolution whose tiles fill less than one wave of two CTAs
+// per SM (the transformer's projections over a few hundred frames): the
+// largest power of two up to 8 that keeps the grid within that wave and
+// leaves each split at least two stages.
+int choose_split(int taps, const ConvArgs &a, int sms) {
+    if (a.phases != 1) return 1;
+    const int bk = taps == 1 ? 16 : 8;
+    const int64_t tiles = (a.len + kCvBN - 1) / kCvBN * ((a.oc + kCvBM - 1) / kCvBM);
+    const int nall = (a.ic + bk - 1) / bk;
+    int S = 1;
+    while (S < kCvMaxSplit && tiles * 2 * S <= 2 * (int64_t)sms && nall >= 2 * 2 * S) S *= 2;
+    return S;
+}
+
+int launch_conv(int taps, int pro, int epi, const ConvArgs &a0, int device, cudaStream_t st) {
+    ConvArgs a = a0;
+    a.ksplit = choose_split(taps, a, g_sms[device & 63]);
 #define QORA_CONV_CASE(K, P, E) \
     if (taps == K && pro == P && epi == E) return launch_conv_t<K, P, E>(a, device, st)
     QORA_CONV_CASE(1, P_NONE, E_BIAS);          // codebook projection, input projection
@@ -1092,6 +1181,7 @@ int qora_decoder_create(qora_ctx *ctx, const qora_decoder_dims *dims, qora_decod
     QORA_TRY(check_dims(*dims));
     auto *dec = new qora_decoder();
     dec->ctx = ctx;
+    g_sms[ctx->device & 63] = ctx->num_sms;
     dec->d = *dims;
     int64_t hop = (int64_t)1 << dims->upsample_stages;
     for (int b = 0; b < dims->vocos_blocks; b++) hop *= dims->vocos_strides[b];
