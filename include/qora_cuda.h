@@ -435,6 +435,12 @@ int qora_decoder_set_tensor(qora_decoder *dec, const char *name, const float *da
                             int64_t count);
 int qora_decoder_finalize(qora_decoder *dec);
 void qora_decoder_destroy(qora_decoder *dec);
+/* Which convolutions run on the tensor cores (3 x TF32 products, f32
+ * accumulation): mode 0 none (all on the CUDA cores), 1 (the default) those
+ * whose tiles fill the GPU, 2 every one that has a tensor-core form (the
+ * Vocos convolutions and transposed convolutions, the upsample transposed
+ * convolutions and ConvNeXt pointwise convolutions). */
+int qora_decoder_use_tensor_cores(qora_decoder *dec, int32_t mode);
 /* Samples decoded from `frames` frames: frames * 1920 at the 12 Hz dims. */
 int qora_decoder_samples(const qora_decoder *dec, int64_t frames, int64_t *samples);
 /* decode_to_audio (decoder.rs:395-582) from host codes [num_quantizers][frames]

@@ -30,6 +30,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "tc.cuh"
 
 namespace qora {
 namespace {
@@ -67,6 +68,8 @@ struct ConvArgs {
     const float *ra = nullptr, *rb = nullptr;  // per position: RMSNorm 1/rms; LayerNorm mean, 1/std
     const float *resid = nullptr;  // [oc][len * phases] (E_RESID, E_SCALE_RESID; may alias out)
     const float *escale = nullptr; // [oc] (E_SCALE_RESID)
+    const uint8_t *wtc = nullptr;  // tensor-core weight image (tc_image) or null
+    int *err = nullptr;            // device error flag
 };
 
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
@@ -529,6 +532,312 @@ __global__ void __launch_bounds__(kFinT) k_dec_final(const float *in, int C, int
     if (t < L && t >= skip) out[t - skip] = acc < -1.0f ? -1.0f : (acc > 1.0f ? 1.0f : acc);
 }
 
+// ----------------------------------------------------------------------
+// The same implicit-GEMM convolution on the tcgen05 tensor cores, f32-exact
+// to within f32 rounding: both operands are split into TF32 hi + lo parts
+// (hi = x rounded to TF32, lo = x - hi rounded to TF32, so hi + lo carries
+// 22 significant bits) and each term is the three products hi*hi + hi*lo +
+// lo*hi.  The tensor core's accumulation into tensor memory does not round
+// to nearest, and its error grows with the number of MMAs accumulated into
+// one accumulator; so the MMAs of each chunk of stages (about 60 MMAs)
+// accumulate into one of two tensor-memory buffers, and the epilogue warps
+// add each chunk into f32 registers (round to nearest) while the next chunk
+// runs in the other buffer.  One CTA computes 128 output channels x 256
+// positions (one phase of a transposed convolution).
+//
+// Operands in shared memory, canonical K-major layout without swizzle
+// (8-row x 16-byte core matrices; rows 16 bytes apart, K groups of 4 TF32
+// values `LBO` apart):
+//   A (weights) per stage and tap: [hi, lo][2 K groups][128 rows][4], LBO
+//     2048, arriving as one bulk copy per stage from an image prepared on
+//     upload (tc_image below);
+//   B (inputs) per stage: [hi, lo][2 K groups][256 + halo rows][4], LBO
+//     16 * (256 + 64), row n = position j0 - halo + n, written by the
+//     converter warps (prologue applied, hi / lo split).  Tap t reads rows
+//     t * dil .. t * dil + 255: its descriptor starts t * dil * 16 bytes in.
+// Warp roles (288 threads): warps 0-7 stage B, add the chunks into
+// registers and run the epilogue; warp 8 allocates tensor memory and its
+// lane 0 issues the A bulk copies and the MMAs (8 input channels per stage:
+// K = 8 per MMA).  Every wait is bounded (kDevTimeout, then a CTA-wide
+// abort).
+constexpr int kTcOc = 128;
+constexpr int kTcPos = 256;
+constexpr int kTcBK = 8;
+constexpr int kTcConvWarps = 8;
+constexpr int kTcThreads = (kTcConvWarps + 1) * 32;
+constexpr int kTcRowsB = kTcPos + kCvMaxHalo;
+constexpr uint32_t kTcATap = 2 * 2 * kTcOc * 16;      // 8192 bytes per tap and stage
+constexpr uint32_t kTcALbo = kTcOc * 16;              // 2048
+constexpr uint32_t kTcBLbo = kTcRowsB * 16;           // 5120
+constexpr uint32_t kTcBHalf = 2 * kTcBLbo;            // hi part, then lo part
+constexpr uint32_t kTcBBytes = 2 * kTcBHalf;          // 20480
+constexpr uint32_t kTcTmemCols = 2 * kTcPos;          // two accumulators
+constexpr size_t kTcMinSmem = 120 * 1024;             // one CTA per SM (all of tensor memory)
+template <int KS> constexpr int tc_stages() { return KS >= 3 ? 2 : 4; }
+template <int KS> constexpr int tc_chunk() { return (64 / (3 * KS)) > 1 ? 64 / (3 * KS) : 1; }
+template <int KS> constexpr uint32_t tc_stage_bytes() { return KS * kTcATap + kTcBBytes; }
+template <int KS> constexpr size_t tc_smem() {
+    return (size_t)tc_stages<KS>() * tc_stage_bytes<KS>() + 1024 > kTcMinSmem
+               ? (size_t)tc_stages<KS>() * tc_stage_bytes<KS>() + 1024
+               : kTcMinSmem;
+}
+
+__host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
+    return (1u << 4)                     // D: f32
+           | (2u << 7) | (2u << 10)      // A, B: TF32, both K-major
+           | ((uint32_t)(N >> 3) << 17)  // N / 8
+           | ((uint32_t)(M >> 4) << 24); // M / 16
+}
+
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// x rounded to TF32 (nearest, ties away from zero), as a 32-bit pattern.
+__device__ __forceinline__ uint32_t to_tf32(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+
+template <int KS, int PRO, int EPI>
+__global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a, const uint8_t *aimg) {
+    constexpr int NS = tc_stages<KS>();
+    constexpr int CH = tc_chunk<KS>();
+    constexpr uint32_t SB = tc_stage_bytes<KS>();
+    constexpr uint32_t ABYTES = KS * kTcATap;
+    extern __shared__ uint8_t tc_raw[];
+    __shared__ __align__(8) uint64_t a_full[NS], b_full[NS], s_empty[NS], d_full[2], d_empty[2];
+    __shared__ uint32_t tmem_slot;
+    __shared__ int abort_s;
+    uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int p = (int)(blockIdx.x % (unsigned)a.phases);
+    const int64_t j0 = (int64_t)(blockIdx.x / (unsigned)a.phases) * kTcPos;
+    const int oc0 = blockIdx.y * kTcOc;
+    const int halo = (KS - 1) * a.dil;
+    const int nst = (a.ic + kTcBK - 1) / kTcBK;
+    const uint8_t *aimg_t = aimg + ((int64_t)p * gridDim.y + blockIdx.y) * nst * (int64_t)ABYTES;
+    volatile int *abort_v = &abort_s;
+
+    if (tid == 0) {
+        for (int i = 0; i < NS; i++) {
+            mbar_init(&a_full[i], 1);
+            mbar_init(&b_full[i], kTcConvWarps);
+            mbar_init(&s_empty[i], 1);
+        }
+        for (int i = 0; i < 2; i++) {
+            mbar_init(&d_full[i], 1);
+            mbar_init(&d_empty[i], kTcConvWarps);
+        }
+        abort_s = 0;
+        mbar_fence_init();
+    }
+    if (warp == kTcConvWarps) {
+        tc::tmem_alloc(&tmem_slot, kTcTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = tmem_slot;
+    auto wait = [&](uint64_t *bar, uint32_t parity) -> bool {
+        if (mbar_try_wait(bar, parity)) return true;
+        const long long t0 = clock64();
+        for (uint32_t i = 1;; i++) {
+            if (mbar_try_wait(bar, parity)) return true;
+            if ((i & 31) == 0) {
+                if (*abort_v) return false;
+                if (clock64() - t0 > (1ll << 31)) {
+                    raise_error(a.err, kDevTimeout);
+                    *abort_v = 1;
+                    return false;
+                }
+            }
+        }
+    };
+
+    if (warp == kTcConvWarps) {
+        if (lane == 0) {
+            // ------------------------------------------------ A copies + MMAs
+            auto issue_a = [&](int s) {
+                const int buf = s % NS;
+                mbar_arrive_expect_tx(&a_full[buf], ABYTES);
+                bulk_g2s(sm + buf * SB, aimg_t + (int64_t)s * ABYTES, ABYTES, &a_full[buf]);
+            };
+            int issued = 0, used = 0;
+            for (; issued < min(NS, nst); issued++) issue_a(issued);
+            constexpr uint32_t idesc = idesc_tf32_f32(kTcOc, kTcPos);
+            for (int s = 0; s < nst; s++) {
+                const int buf = s % NS, c = s / CH;
+                const bool first = s % CH == 0;
+                if (!wait(&a_full[buf], (s / NS) & 1)) break;
+                used = s + 1;
+                if (!wait(&b_full[buf], (s / NS) & 1)) break;
+                // chunk c reuses the accumulator of chunk c - 2 once it is added up
+                if (first && c >= 2 && !wait(&d_empty[c & 1], ((c >> 1) - 1) & 1)) break;
+                tc::fence_after_sync();
+                const uint32_t d = tmem + (uint32_t)(c & 1) * kTcPos;
+                const uint32_t sA = smem_u32(sm + buf * SB), sB = sA + ABYTES;
+#pragma unroll
+                for (int t = 0; t < KS; t++) {
+                    const uint64_t ah = tc::smem_desc(sA + t * kTcATap, kTcALbo, 128);
+                    const uint64_t al = tc::smem_desc(sA + t * kTcATap + kTcATap / 2, kTcALbo, 128);
+                    const uint32_t boff = (uint32_t)(t * a.dil) * 16u;
+                    const uint64_t bh = tc::smem_desc(sB + boff, kTcBLbo, 128);
+                    const uint64_t bl = tc::smem_desc(sB + kTcBHalf + boff, kTcBLbo, 128);
+                    mma_tf32(d, ah, bh, idesc, (first && t == 0) ? 0u : 1u);
+                    mma_tf32(d, ah, bl, idesc, 1u);
+                    mma_tf32(d, al, bh, idesc, 1u);
+                }
+                tc::commit(&s_empty[buf]);
+                if (s % CH == CH - 1 || s == nst - 1) tc::commit(&d_full[c & 1]);
+                // refill the previous stage's buffer once its MMAs are done
+                // (the ones just issued queue behind them)
+                if (s >= 1 && issued < nst) {
+                    if (!wait(&s_empty[(s - 1) % NS], ((s - 1) / NS) & 1)) break;
+                    issue_a(issued++);
+                }
+            }
+            // every A copy issued lands before the CTA can exit
+            for (int s = used; s < issued; s++) {
+                const int buf = s % NS;
+                const uint64_t t0 = global_ns();
+                while (!mbar_try_wait(&a_full[buf], (s / NS) & 1) && global_ns() - t0 < 1000000000ull) {
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // warp w owns tensor-memory lanes 32 (w % 4) .. + 31 (output channels)
+        // and columns 128 (w / 4) .. + 127 (positions) of each accumulator
+        const int lg = warp & 3, half = warp >> 2;
+        float accr[128];
+#pragma unroll
+        for (int i = 0; i < 128; i++) accr[i] = 0.0f;
+        auto drain = [&](int c) {
+            const bool ok = wait(&d_full[c & 1], (c >> 1) & 1);
+            tc::fence_after_sync();
+            if (ok) {
+                const uint32_t base = tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(c & 1) * kTcPos + half * 128;
+#pragma unroll
+                for (int q = 0; q < 4; q++) {
+                    float v[32];
+                    tc::ld_32x32b_x32(base + q * 32, v);
+#pragma unroll
+                    for (int i = 0; i < 32; i++) accr[q * 32 + i] += v[i];
+                }
+            }
+            tc::fence_before_sync();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&d_empty[c & 1]);
+        };
+        // ---------------------------------------------------- B staging
+        // item (K group kg, row n): 4 input channels at one position; a
+        // stage's raw values are loaded into registers one stage ahead, so
+        // their latency passes while the converters wait for a free buffer
+        constexpr int kItems = (2 * kTcRowsB + kTcConvWarps * 32 - 1) / (kTcConvWarps * 32);
+        const int rows = kTcPos + halo;
+        float raw[kItems][4];
+        auto fetch = [&](int s) {
+            const int ic0 = s * kTcBK;
+#pragma unroll
+            for (int q = 0; q < kItems; q++) {
+                const int it = tid + q * kTcConvWarps * 32;
+                const int kg = it / rows, n = it - kg * rows;
+                const int64_t pos = j0 - halo + n;
+                const bool pin = it < 2 * rows && pos >= 0 && pos < a.len;
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int ic = ic0 + 4 * kg + u;
+                    raw[q][u] = (pin && ic < a.ic) ? __ldg(a.in + (int64_t)ic * a.len + pos) : 0.0f;
+                }
+            }
+        };
+        fetch(0);
+        for (int s = 0; s < nst; s++) {
+            const int buf = s % NS;
+            if (s >= NS && !wait(&s_empty[buf], ((s / NS) - 1) & 1)) break;
+            uint8_t *B = sm + buf * SB + ABYTES;
+            const int ic0 = s * kTcBK;
+#pragma unroll
+            for (int q = 0; q < kItems; q++) {
+                const int it = tid + q * kTcConvWarps * 32;
+                if (it >= 2 * rows) continue;
+                const int kg = it / rows, n = it - kg * rows;
+                const int64_t pos = j0 - halo + n;
+                const bool pin = pos >= 0 && pos < a.len;
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) {
+                    const int ic = ic0 + 4 * kg + u;
+                    float v = raw[q][u];
+                    // positions outside the input are the convolution's zero padding
+                    if (PRO != P_NONE && pin && ic < a.ic) v = prologue<PRO>(v, ic, pos, a);
+                    hi[u] = to_tf32(v);
+                    lo[u] = to_tf32(v - __uint_as_float(hi[u]));
+                }
+                *reinterpret_cast<uint4 *>(B + kg * kTcBLbo + n * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4 *>(B + kTcBHalf + kg * kTcBLbo + n * 16) =
+                    make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            tc::fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&b_full[buf]);
+            if (s + 1 < nst) fetch(s + 1);
+            // the previous chunk is added up while this one runs
+            if (s > 0 && s % CH == 0) drain(s / CH - 1);
+        }
+        drain((nst - 1) / CH);
+        // ---------------------------------------------------- epilogue
+        // 32 columns at a time, transposed through shared memory (the stage
+        // buffers are idle now) so that a warp's stores run along positions
+        float *scr = reinterpret_cast<float *>(sm) + warp * (32 * 33);
+        const int64_t out_len = a.len * a.phases;
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+            const int col0 = half * 128 + q * 32;
+#pragma unroll
+            for (int i = 0; i < 32; i++) scr[lane * 33 + i] = accr[q * 32 + i];
+            __syncwarp();
+            const int64_t j = j0 + col0 + lane;
+            // the residuals of the 32 rows are loaded together, then combined
+            float rv[32];
+#pragma unroll
+            for (int rr = 0; rr < 32; rr++) {
+                const int oc = oc0 + lg * 32 + rr;
+                rv[rr] = 0.0f;
+                if ((EPI == E_RESID || EPI == E_SCALE_RESID) && oc < a.oc && j < a.len)
+                    rv[rr] = a.resid[(int64_t)oc * out_len + j * a.phases + p];
+            }
+#pragma unroll
+            for (int rr = 0; rr < 32; rr++) {
+                const int oc = oc0 + lg * 32 + rr;
+                if (oc >= a.oc || j >= a.len) continue;
+                const int64_t o = (int64_t)oc * out_len + j * a.phases + p;
+                float x = scr[rr * 33 + lane];
+                if (a.bias) x = __ldg(a.bias + oc) + x;
+                if constexpr (EPI == E_RESID) x = x + rv[rr];
+                if constexpr (EPI == E_SCALE_RESID) x = rv[rr] + x * __ldg(a.escale + oc);
+                if constexpr (EPI == E_GELU) x = gelu_ref(x);
+                a.out[o] = x;
+            }
+            __syncwarp();
+        }
+    }
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == kTcConvWarps) {
+        tc::fence_after_sync();
+        tc::tmem_dealloc(tmem, kTcTmemCols);
+    }
+}
+
 }  // namespace
 }  // namespace qora
 
@@ -539,14 +848,15 @@ namespace {
 struct DecLayer {
     DevBuf qkv_w, o_w, gu_w, down_w, in_norm, post_norm, attn_scale, mlp_scale;
 };
+// *_tc: the same weights as tensor-core images (tc_image)
 struct DecUpsample {
-    DevBuf ct_w, ct_b, dw_w, dw_b, ln_w, ln_b, pw1_w, pw1_b, pw2_w, pw2_b, gamma;
+    DevBuf ct_w, ct_b, dw_w, dw_b, ln_w, ln_b, pw1_w, pw1_b, pw2_w, pw2_b, gamma, ct_tc, pw1_tc, pw2_tc;
 };
 struct DecResidual {
-    DevBuf a1, ib1, c1_w, c1_b, a2, ib2, c2_w, c2_b;
+    DevBuf a1, ib1, c1_w, c1_b, a2, ib2, c2_w, c2_b, c1_tc, c2_tc;
 };
 struct DecBlock {
-    DevBuf pre_a, pre_ib, ct_w, ct_b;
+    DevBuf pre_a, pre_ib, ct_w, ct_b, ct_tc;
     DecResidual res[3];
 };
 
@@ -570,7 +880,8 @@ struct qora_decoder {
     qora::DevBuf cb, vq_w0, vq_wr, pre_w, pre_b, in_w, in_b, norm_w, out_w, out_b, rope_cos, rope_sin;
     std::vector<qora::DecLayer> layers;
     std::vector<qora::DecUpsample> ups;
-    qora::DevBuf init_w, init_b, fin_a, fin_ib, fin_w, fin_b;
+    qora::DevBuf init_w, init_b, init_tc, fin_a, fin_ib, fin_w, fin_b;
+    int tc_mode = 1;   // tensor-core convolutions: 0 never, 1 when the grid fills the GPU, 2 always
     std::vector<qora::DecBlock> blocks;
     // workspace for `ws_frames` frames
     int64_t ws_frames = 0;
@@ -623,6 +934,24 @@ int launch_conv_t(const ConvArgs &a, int device, cudaStream_t st) {
 }
 
 // The (taps, prologue, epilogue) combinations the decoder uses.
+template <int KS, int PRO, int EPI>
+int launch_conv_tc_t(const ConvArgs &a, int device, cudaStream_t st) {
+    static std::atomic<uint64_t> attr_done{0};
+    if ((KS - 1) * a.dil > kCvMaxHalo) return set_error(QORA_ERR_UNSUPPORTED, "convolution halo too large");
+    const uint64_t bit = 1ull << (device & 63);
+    if (!(attr_done.load() & bit)) {
+        QORA_CUDA(cudaFuncSetAttribute(k_dec_conv_tc<KS, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)tc_smem<KS>()));
+        attr_done.fetch_or(bit);
+    }
+    const int64_t gx = (a.len + kTcPos - 1) / kTcPos * a.phases;
+    const int gy = (a.oc + kTcOc - 1) / kTcOc;
+    if (gx > INT32_MAX || gy > 65535) return set_error(QORA_ERR_SHAPE, "convolution too long");
+    k_dec_conv_tc<KS, PRO, EPI><<<dim3((unsigned)gx, gy, 1), kTcThreads, tc_smem<KS>(), st>>>(a, a.wtc);
+    QORA_LAUNCH_CHECK();
+    return QORA_OK;
+}
+
 // K split of a convolution whose tiles fill less than one wave of two CTAs
 // per SM (the transformer's projections over a few hundred frames): the
 // largest power of two up to 8 that keeps the grid within that wave and
@@ -637,8 +966,26 @@ int choose_split(int taps, const ConvArgs &a, int sms) {
     return S;
 }
 
-int launch_conv(int taps, int pro, int epi, const ConvArgs &a0, int device, cudaStream_t st) {
+int launch_conv(int taps, int pro, int epi, const ConvArgs &a0, int device, cudaStream_t st, int tc_mode, int *err) {
     ConvArgs a = a0;
+    a.err = err;
+    if (a.wtc && tc_mode != 0 && epi != E_SWIGLU) {
+        const int64_t tiles = (a.len + kTcPos - 1) / kTcPos * ((a.oc + kTcOc - 1) / kTcOc) * a.phases;
+        if (tc_mode == 2 || tiles >= g_sms[device & 63]) {
+#define QORA_TC_CASE(K, P, E) \
+    if (taps == K && pro == P && epi == E) return launch_conv_tc_t<K, P, E>(a, device, st)
+            QORA_TC_CASE(7, P_NONE, E_BIAS);      // Vocos input conv
+            QORA_TC_CASE(1, P_NONE, E_BIAS);      // upsample transposed conv
+            QORA_TC_CASE(1, P_LN, E_GELU);        // ConvNeXt pwconv1
+            QORA_TC_CASE(1, P_NONE, E_SCALE_RESID);  // ConvNeXt pwconv2
+            QORA_TC_CASE(1, P_SNAKE, E_BIAS);     // Vocos transposed conv (kernel = stride)
+            QORA_TC_CASE(2, P_SNAKE, E_BIAS);     // Vocos transposed conv (kernel = 2 x stride)
+            QORA_TC_CASE(7, P_SNAKE, E_BIAS);     // residual conv1
+            QORA_TC_CASE(1, P_SNAKE, E_RESID);    // residual conv2
+#undef QORA_TC_CASE
+        }
+    }
+    a.wtc = nullptr;
     a.ksplit = choose_split(taps, a, g_sms[device & 63]);
 #define QORA_CONV_CASE(K, P, E) \
     if (taps == K && pro == P && epi == E) return launch_conv_t<K, P, E>(a, device, st)
@@ -684,6 +1031,43 @@ std::vector<float> convt_layout(const float *w, int64_t ic, int64_t oc, int64_t 
                 for (int64_t a = 0; a < oc; a++)
                     o[(size_t)(((p * ic + b) * m + q) * ocp + a)] = w[(b * oc + a) * k + p + s * (m - 1 - q)];
     return o;
+}
+
+// f32 -> TF32 (nearest, ties away from zero) as the f32 it represents;
+// infinities and NaNs unchanged.
+float tf32_rna(float x) {
+    uint32_t u;
+    std::memcpy(&u, &x, 4);
+    if ((u & 0x7F800000u) != 0x7F800000u) u = (u + 0x1000u) & 0xFFFFE000u;
+    float r;
+    std::memcpy(&r, &u, 4);
+    return r;
+}
+
+// Tensor-core image of a convolution's weights wl [phases][ic][taps][oc_pad]
+// (conv_layout / convt_layout): per (phase, 128-channel tile, stage of 8
+// input channels, tap) the A operand of k_dec_conv_tc as it lies in shared
+// memory, [hi, lo][2 K groups][128 rows][4 values], zero outside the
+// weights; a stage's taps are contiguous, so one bulk copy loads a stage.
+std::vector<float> tc_image(const std::vector<float> &wl, int64_t phases, int64_t ic, int64_t oc, int64_t ks) {
+    const int64_t ocp = round4(oc), tiles = (oc + kTcOc - 1) / kTcOc, nst = (ic + kTcBK - 1) / kTcBK;
+    std::vector<float> img((size_t)(phases * tiles * nst * ks * 2 * 2 * kTcOc * 4), 0.0f);
+    size_t idx = 0;
+    for (int64_t p = 0; p < phases; p++)
+        for (int64_t ot = 0; ot < tiles; ot++)
+            for (int64_t st = 0; st < nst; st++)
+                for (int64_t t = 0; t < ks; t++)
+                    for (int h = 0; h < 2; h++)
+                        for (int kg = 0; kg < 2; kg++)
+                            for (int64_t row = 0; row < kTcOc; row++)
+                                for (int u = 0; u < 4; u++, idx++) {
+                                    const int64_t c = st * kTcBK + 4 * kg + u, o = ot * kTcOc + row;
+                                    if (c >= ic || o >= oc) continue;
+                                    const float w = wl[(size_t)(((p * ic + c) * ks + t) * ocp + o)];
+                                    const float hi = tf32_rna(w);
+                                    img[idx] = h == 0 ? hi : tf32_rna(w - hi);
+                                }
+    return img;
 }
 
 int upload(DevBuf &buf, const std::vector<float> &v) {
@@ -856,20 +1240,36 @@ int finalize(qora_decoder *dec) {
         const std::string ct = "decoder.upsample." + std::to_string(i) + ".0.conv.";
         const std::string cn = "decoder.upsample." + std::to_string(i) + ".1.";
         DecUpsample &U = dec->ups[i];
-        QORA_TRY(upload(U.ct_w, convt_layout(tensor_of(dec, ct + "weight"), d.latent, d.latent, kUpKernel, kUpStride)));
+        {
+            const std::vector<float> l = convt_layout(tensor_of(dec, ct + "weight"), d.latent, d.latent, kUpKernel, kUpStride);
+            QORA_TRY(upload(U.ct_w, l));
+            QORA_TRY(upload(U.ct_tc, tc_image(l, kUpStride, d.latent, d.latent, kUpKernel / kUpStride)));
+        }
         QORA_TRY(upload_raw(dec, ct + "bias", U.ct_b));
         QORA_TRY(upload_raw(dec, cn + "dwconv.conv.weight", U.dw_w));
         QORA_TRY(upload_raw(dec, cn + "dwconv.conv.bias", U.dw_b));
         QORA_TRY(upload_raw(dec, cn + "norm.weight", U.ln_w));
         QORA_TRY(upload_raw(dec, cn + "norm.bias", U.ln_b));
-        QORA_TRY(upload(U.pw1_w, conv_layout(tensor_of(dec, cn + "pwconv1.weight"), d.upsample_inner, d.latent, 1)));
+        {
+            const std::vector<float> l = conv_layout(tensor_of(dec, cn + "pwconv1.weight"), d.upsample_inner, d.latent, 1);
+            QORA_TRY(upload(U.pw1_w, l));
+            QORA_TRY(upload(U.pw1_tc, tc_image(l, 1, d.latent, d.upsample_inner, 1)));
+        }
         QORA_TRY(upload_raw(dec, cn + "pwconv1.bias", U.pw1_b));
-        QORA_TRY(upload(U.pw2_w, conv_layout(tensor_of(dec, cn + "pwconv2.weight"), d.latent, d.upsample_inner, 1)));
+        {
+            const std::vector<float> l = conv_layout(tensor_of(dec, cn + "pwconv2.weight"), d.latent, d.upsample_inner, 1);
+            QORA_TRY(upload(U.pw2_w, l));
+            QORA_TRY(upload(U.pw2_tc, tc_image(l, 1, d.upsample_inner, d.latent, 1)));
+        }
         QORA_TRY(upload_raw(dec, cn + "pwconv2.bias", U.pw2_b));
         QORA_TRY(upload_raw(dec, cn + "gamma", U.gamma));
     }
-    QORA_TRY(upload(dec->init_w, conv_layout(tensor_of(dec, "decoder.decoder.0.conv.weight"), d.vocos_channels[0],
-                                             d.latent, kVocosTaps)));
+    {
+        const std::vector<float> l = conv_layout(tensor_of(dec, "decoder.decoder.0.conv.weight"), d.vocos_channels[0],
+                                                 d.latent, kVocosTaps);
+        QORA_TRY(upload(dec->init_w, l));
+        QORA_TRY(upload(dec->init_tc, tc_image(l, 1, d.latent, d.vocos_channels[0], kVocosTaps)));
+    }
     QORA_TRY(upload_raw(dec, "decoder.decoder.0.conv.bias", dec->init_b));
     dec->blocks.clear();
     dec->blocks.resize(d.vocos_blocks);
@@ -878,17 +1278,29 @@ int finalize(qora_decoder *dec) {
         const int64_t ci = d.vocos_channels[b], co = d.vocos_channels[b + 1];
         DecBlock &B = dec->blocks[b];
         QORA_TRY(upload_snake(dec, p + "0.", B.pre_a, B.pre_ib));
-        QORA_TRY(upload(B.ct_w, convt_layout(tensor_of(dec, p + "1.conv.weight"), ci, co, d.vocos_kernels[b],
-                                             d.vocos_strides[b])));
+        {
+            const int s = d.vocos_strides[b];
+            const std::vector<float> l = convt_layout(tensor_of(dec, p + "1.conv.weight"), ci, co, d.vocos_kernels[b], s);
+            QORA_TRY(upload(B.ct_w, l));
+            QORA_TRY(upload(B.ct_tc, tc_image(l, s, ci, co, d.vocos_kernels[b] / s)));
+        }
         QORA_TRY(upload_raw(dec, p + "1.conv.bias", B.ct_b));
         for (int r = 0; r < 3; r++) {
             const std::string u = p + std::to_string(r + 2) + ".";
             DecResidual &R = B.res[r];
             QORA_TRY(upload_snake(dec, u + "act1.", R.a1, R.ib1));
-            QORA_TRY(upload(R.c1_w, conv_layout(tensor_of(dec, u + "conv1.conv.weight"), co, co, kVocosTaps)));
+            {
+                const std::vector<float> l = conv_layout(tensor_of(dec, u + "conv1.conv.weight"), co, co, kVocosTaps);
+                QORA_TRY(upload(R.c1_w, l));
+                QORA_TRY(upload(R.c1_tc, tc_image(l, 1, co, co, kVocosTaps)));
+            }
             QORA_TRY(upload_raw(dec, u + "conv1.conv.bias", R.c1_b));
             QORA_TRY(upload_snake(dec, u + "act2.", R.a2, R.ib2));
-            QORA_TRY(upload(R.c2_w, conv_layout(tensor_of(dec, u + "conv2.conv.weight"), co, co, 1)));
+            {
+                const std::vector<float> l = conv_layout(tensor_of(dec, u + "conv2.conv.weight"), co, co, 1);
+                QORA_TRY(upload(R.c2_w, l));
+                QORA_TRY(upload(R.c2_tc, tc_image(l, 1, co, co, 1)));
+            }
             QORA_TRY(upload_raw(dec, u + "conv2.conv.bias", R.c2_b));
         }
     }
@@ -1006,19 +1418,19 @@ int run(qora_decoder *dec, const uint32_t *codes, int64_t F, int64_t skip, float
         codes, F, d.num_quantizers, dec->cb.as<float>(), d.codebook_size, d.codebook_dim, e0, er, err);
     QORA_LAUNCH_CHECK();
     n++;
-    QORA_TRY(launch_conv(1, P_NONE, E_BIAS, conv_args(e0, F, dec->vq_w0, nullptr, vq, d.codebook_dim, d.vq_dim), dev, st));
+    QORA_TRY(launch_conv(1, P_NONE, E_BIAS, conv_args(e0, F, dec->vq_w0, nullptr, vq, d.codebook_dim, d.vq_dim), dev, st, dec->tc_mode, err));
     {
         ConvArgs a = conv_args(er, F, dec->vq_wr, nullptr, vq, d.codebook_dim, d.vq_dim);
         a.resid = vq;
-        QORA_TRY(launch_conv(1, P_NONE, E_RESID, a, dev, st));
+        QORA_TRY(launch_conv(1, P_NONE, E_RESID, a, dev, st, dec->tc_mode, err));
     }
     // 2. pre-conv (decoder.rs:433)
     QORA_TRY(launch_conv(kPreTaps, P_NONE, E_BIAS,
-                         conv_args(vq, F, dec->pre_w, dec->pre_b.as<float>(), pre, d.vq_dim, d.latent), dev, st));
+                         conv_args(vq, F, dec->pre_w, dec->pre_b.as<float>(), pre, d.vq_dim, d.latent), dev, st, dec->tc_mode, err));
     n += 3;
     // 3. transformer (decoder.rs:196-333)
     QORA_TRY(launch_conv(1, P_NONE, E_BIAS, conv_args(pre, F, dec->in_w, dec->in_b.as<float>(), x, d.latent, d.hidden),
-                         dev, st));
+                         dev, st, dec->tc_mode, err));
     n++;
     const float scale = 1.0f / std::sqrt((float)d.head_dim);
     const int gs = (int)((F + 31) / 32);
@@ -1029,7 +1441,7 @@ int run(qora_decoder *dec, const uint32_t *codes, int64_t F, int64_t skip, float
         ConvArgs a = conv_args(x, F, L.qkv_w, nullptr, qkv, d.hidden, (int)(3 * HD));
         a.pa = L.in_norm.as<float>();
         a.ra = ra;
-        QORA_TRY(launch_conv(1, P_RMS, E_BIAS, a, dev, st));
+        QORA_TRY(launch_conv(1, P_RMS, E_BIAS, a, dev, st, dec->tc_mode, err));
         const int nk = kAttQ + d.sliding_window - 1;
         const size_t asmem = sizeof(float) * (size_t)(kAttQ * kAttRow + 2 * nk * kAttRow + kAttQ * d.sliding_window);
         QORA_TRY(attn_attr(dev));
@@ -1040,17 +1452,17 @@ int run(qora_decoder *dec, const uint32_t *codes, int64_t F, int64_t skip, float
         a = conv_args(att, F, L.o_w, nullptr, x, (int)HD, d.hidden);
         a.resid = x;
         a.escale = L.attn_scale.as<float>();
-        QORA_TRY(launch_conv(1, P_NONE, E_SCALE_RESID, a, dev, st));
+        QORA_TRY(launch_conv(1, P_NONE, E_SCALE_RESID, a, dev, st, dec->tc_mode, err));
         k_dec_colstats<false><<<gs, 256, 0, st>>>(x, d.hidden, F, kDecEps, ra, nullptr);
         QORA_LAUNCH_CHECK();
         a = conv_args(x, F, L.gu_w, nullptr, h, d.hidden, 2 * d.intermediate);
         a.pa = L.post_norm.as<float>();
         a.ra = ra;
-        QORA_TRY(launch_conv(1, P_RMS, E_SWIGLU, a, dev, st));
+        QORA_TRY(launch_conv(1, P_RMS, E_SWIGLU, a, dev, st, dec->tc_mode, err));
         a = conv_args(h, F, L.down_w, nullptr, x, d.intermediate, d.hidden);
         a.resid = x;
         a.escale = L.mlp_scale.as<float>();
-        QORA_TRY(launch_conv(1, P_NONE, E_SCALE_RESID, a, dev, st));
+        QORA_TRY(launch_conv(1, P_NONE, E_SCALE_RESID, a, dev, st, dec->tc_mode, err));
         n += 7;
     }
     k_dec_colstats<false><<<gs, 256, 0, st>>>(x, d.hidden, F, kDecEps, ra, nullptr);
@@ -1059,7 +1471,7 @@ int run(qora_decoder *dec, const uint32_t *codes, int64_t F, int64_t skip, float
         ConvArgs a = conv_args(x, F, dec->out_w, dec->out_b.as<float>(), tfo, d.hidden, d.latent);
         a.pa = dec->norm_w.as<float>();
         a.ra = ra;
-        QORA_TRY(launch_conv(1, P_RMS, E_BIAS, a, dev, st));
+        QORA_TRY(launch_conv(1, P_RMS, E_BIAS, a, dev, st, dec->tc_mode, err));
     }
     n += 2;
     // 4. upsample: ConvTranspose k=2 s=2 + ConvNeXt (decoder.rs:450-482, 337-382)
@@ -1070,24 +1482,27 @@ int run(qora_decoder *dec, const uint32_t *codes, int64_t F, int64_t skip, float
         const DecUpsample &U = dec->ups[i];
         const int ui = (ci + 1) % 3, di = (ui + 1) % 3, pi = (ui + 2) % 3;
         float *u = big[ui], *dw = big[di], *p1 = big[pi];
-        QORA_TRY(launch_conv(kUpKernel / kUpStride, P_NONE, E_BIAS,
-                             conv_args(cur, L, U.ct_w, U.ct_b.as<float>(), u, d.latent, d.latent, 1, kUpStride), dev, st));
+        ConvArgs a = conv_args(cur, L, U.ct_w, U.ct_b.as<float>(), u, d.latent, d.latent, 1, kUpStride);
+        a.wtc = U.ct_tc.as<uint8_t>();
+        QORA_TRY(launch_conv(kUpKernel / kUpStride, P_NONE, E_BIAS, a, dev, st, dec->tc_mode, err));
         L *= kUpStride;
         k_dec_dwconv<<<grid_for((int64_t)d.latent * L, sms), 256, 0, st>>>(u, U.dw_w.as<float>(), U.dw_b.as<float>(),
                                                                             d.latent, kDwTaps, L, dw);
         QORA_LAUNCH_CHECK();
         k_dec_colstats<true><<<(unsigned)((L + 31) / 32), 256, 0, st>>>(dw, d.latent, L, kDecEps, ra, rb);
         QORA_LAUNCH_CHECK();
-        ConvArgs a = conv_args(dw, L, U.pw1_w, U.pw1_b.as<float>(), p1, d.latent, d.upsample_inner);
+        a = conv_args(dw, L, U.pw1_w, U.pw1_b.as<float>(), p1, d.latent, d.upsample_inner);
+        a.wtc = U.pw1_tc.as<uint8_t>();
         a.pa = U.ln_w.as<float>();
         a.pb = U.ln_b.as<float>();
         a.ra = ra;
         a.rb = rb;
-        QORA_TRY(launch_conv(1, P_LN, E_GELU, a, dev, st));
+        QORA_TRY(launch_conv(1, P_LN, E_GELU, a, dev, st, dec->tc_mode, err));
         a = conv_args(p1, L, U.pw2_w, U.pw2_b.as<float>(), u, d.upsample_inner, d.latent);
+        a.wtc = U.pw2_tc.as<uint8_t>();
         a.resid = u;
         a.escale = U.gamma.as<float>();
-        QORA_TRY(launch_conv(1, P_NONE, E_SCALE_RESID, a, dev, st));
+        QORA_TRY(launch_conv(1, P_NONE, E_SCALE_RESID, a, dev, st, dec->tc_mode, err));
         cur = u;
         ci = ui;
         n += 5;
@@ -1095,10 +1510,9 @@ int run(qora_decoder *dec, const uint32_t *codes, int64_t F, int64_t skip, float
     // 5. Vocos input conv (decoder.rs:485)
     {
         const int ni = (ci + 1) % 3;
-        QORA_TRY(launch_conv(kVocosTaps, P_NONE, E_BIAS,
-                             conv_args(cur, L, dec->init_w, dec->init_b.as<float>(), big[ni], d.latent,
-                                       d.vocos_channels[0]),
-                             dev, st));
+        ConvArgs a = conv_args(cur, L, dec->init_w, dec->init_b.as<float>(), big[ni], d.latent, d.vocos_channels[0]);
+        a.wtc = dec->init_tc.as<uint8_t>();
+        QORA_TRY(launch_conv(kVocosTaps, P_NONE, E_BIAS, a, dev, st, dec->tc_mode, err));
         cur = big[ni];
         ci = ni;
         n++;
@@ -1110,22 +1524,25 @@ int run(qora_decoder *dec, const uint32_t *codes, int64_t F, int64_t skip, float
         const int ni = (ci + 1) % 3, ti = (ci + 2) % 3;
         float *sig = big[ni], *tmp = big[ti];
         ConvArgs a = conv_args(cur, L, B.ct_w, B.ct_b.as<float>(), sig, cin, co, 1, s);
+        a.wtc = B.ct_tc.as<uint8_t>();
         a.pa = B.pre_a.as<float>();
         a.pb = B.pre_ib.as<float>();
-        QORA_TRY(launch_conv(d.vocos_kernels[b] / s, P_SNAKE, E_BIAS, a, dev, st));
+        QORA_TRY(launch_conv(d.vocos_kernels[b] / s, P_SNAKE, E_BIAS, a, dev, st, dec->tc_mode, err));
         L *= s;
         n++;
         for (int r = 0; r < 3; r++) {
             const DecResidual &R = B.res[r];
             a = conv_args(sig, L, R.c1_w, R.c1_b.as<float>(), tmp, co, co, kResDilations[r]);
+            a.wtc = R.c1_tc.as<uint8_t>();
             a.pa = R.a1.as<float>();
             a.pb = R.ib1.as<float>();
-            QORA_TRY(launch_conv(kVocosTaps, P_SNAKE, E_BIAS, a, dev, st));
+            QORA_TRY(launch_conv(kVocosTaps, P_SNAKE, E_BIAS, a, dev, st, dec->tc_mode, err));
             a = conv_args(tmp, L, R.c2_w, R.c2_b.as<float>(), sig, co, co);
+            a.wtc = R.c2_tc.as<uint8_t>();
             a.pa = R.a2.as<float>();
             a.pb = R.ib2.as<float>();
             a.resid = sig;
-            QORA_TRY(launch_conv(1, P_SNAKE, E_RESID, a, dev, st));
+            QORA_TRY(launch_conv(1, P_SNAKE, E_RESID, a, dev, st, dec->tc_mode, err));
             n += 2;
         }
         cur = sig;
@@ -1222,6 +1639,12 @@ int qora_decoder_finalize(qora_decoder *dec) {
     QORA_TRY(finalize(dec));
     dec->host.clear();
     dec->ready = true;
+    return QORA_OK;
+}
+
+int qora_decoder_use_tensor_cores(qora_decoder *dec, int32_t mode) {
+    if (!dec || mode < 0 || mode > 2) return set_error(QORA_ERR_INVALID, "qora_decoder_use_tensor_cores: bad argument");
+    dec->tc_mode = mode;
     return QORA_OK;
 }
 

@@ -216,6 +216,12 @@ class SpeechDecoder:
         except Exception:
             pass
 
+    def use_tensor_cores(self, mode: int) -> None:
+        """0: every convolution on the CUDA cores; 1 (default): the tensor
+        cores where the grid fills the GPU; 2: the tensor cores wherever the
+        convolution has a tensor-core form."""
+        _lib.call("qora_decoder_use_tensor_cores", self.h, mode)
+
     def samples(self, frames: int) -> int:
         n = C.c_int64()
         _lib.call("qora_decoder_samples", self.h, frames, C.byref(n))

@@ -13,7 +13,10 @@ Cases: the tiny dims (real strides, kernels and structure, small channel
 counts) with and without a warm-up prefix; the real 12 Hz tokenizer dims on
 a few frames; a long case past the real 72-position attention window and the
 64-query attention tiles (real transformer dims, small Vocos); the reference's
-edge behaviour (no frames, an out-of-codebook code)."""
+edge behaviour (no frames, an out-of-codebook code).  The parity cases run
+twice: every convolution on the CUDA cores (tensor-core mode 0), and every
+convolution that has a tensor-core form on the tcgen05 3 x TF32 kernel
+(mode 2; the default mode 1 picks per launch by grid size)."""
 import numpy as np
 import pytest
 
@@ -47,23 +50,26 @@ def _compare(got, ref, what):
     assert rel <= TOL_RMS, (what, rel)
 
 
-def _setup(ctx, dims, seed=4321):
+def _setup(ctx, dims, seed=4321, tc=1):
     from qora_b200.decoder import SpeechDecoder, synth_decoder
     W = synth_decoder(dims, seed)
-    return W, SpeechDecoder(ctx, dims, W)
+    dec = SpeechDecoder(ctx, dims, W)
+    dec.use_tensor_cores(tc)
+    return W, dec
 
 
-def test_tiny_matches_oracle(ctx):
+@pytest.mark.parametrize("tc", [0, 2])
+def test_tiny_matches_oracle(ctx, tc):
     import pydecoder as D
     from qora_b200.decoder import DecoderDims
     dims = DecoderDims.tiny()
-    W, dec = _setup(ctx, dims)
+    W, dec = _setup(ctx, dims, tc=tc)
     for T, seed in ((1, 1), (12, 2), (65, 3)):
         codes = _codes(dims, T, seed)
         got = dec.decode_to_audio(codes)
         ctx.check_device_error()
         assert got.size == T * dims.hop
-        _compare(got, D.decode_to_audio(W, codes, dims=dims), f"tiny T={T}")
+        _compare(got, D.decode_to_audio(W, codes, dims=dims), f"tiny T={T} tc={tc}")
 
 
 def test_tiny_warmup_prefix_is_trimmed(ctx):
@@ -83,30 +89,32 @@ def test_tiny_warmup_prefix_is_trimmed(ctx):
                                   dec.decode_to_audio(codes))
 
 
-def test_real_dims_match_oracle(ctx):
+@pytest.mark.parametrize("tc", [0, 2])
+def test_real_dims_match_oracle(ctx, tc):
     import pydecoder as D
     from qora_b200.decoder import DecoderDims
     dims = DecoderDims()
-    W, dec = _setup(ctx, dims)
+    W, dec = _setup(ctx, dims, tc=tc)
     codes = _codes(dims, 6, 7)
     got = dec.decode_to_audio(codes)
     ctx.check_device_error()
     assert got.size == 6 * 1920
-    _compare(got, D.decode_to_audio(W, codes, dims=dims), "real dims T=6")
+    _compare(got, D.decode_to_audio(W, codes, dims=dims), f"real dims T=6 tc={tc}")
 
 
-def test_long_sequence_past_the_window(ctx):
+@pytest.mark.parametrize("tc", [0, 2])
+def test_long_sequence_past_the_window(ctx, tc):
     """150 frames (3 attention query tiles, positions past the 72-position
     sliding window) with a 30-frame warm-up, real transformer and upsample
     dims, small Vocos channels (the oracle's run time)."""
     import pydecoder as D
     from qora_b200.decoder import DecoderDims
     dims = DecoderDims(vocos_channels=(96, 48, 24, 12, 8))
-    W, dec = _setup(ctx, dims, seed=99)
+    W, dec = _setup(ctx, dims, seed=99, tc=tc)
     codes, wu = _codes(dims, 150, 8), _codes(dims, 30, 9)
     got = dec.decode_to_audio(codes, warmup=wu)
     ctx.check_device_error()
-    _compare(got, D.decode_to_audio(W, codes, warmup=wu, dims=dims), "long 30 + 150")
+    _compare(got, D.decode_to_audio(W, codes, warmup=wu, dims=dims), f"long 30 + 150 tc={tc}")
 
 
 def test_device_entry_matches_host_entry(ctx):
