@@ -970,8 +970,16 @@ int launch_conv(int taps, int pro, int epi, const ConvArgs &a0, int device, cuda
     ConvArgs a = a0;
     a.err = err;
     if (a.wtc && tc_mode != 0 && epi != E_SWIGLU) {
+        // mode 1: the kernel with the smaller estimated time, from B200
+        // measurements of both (tensor cores: about 2.4 + 0.2 x taps us per
+        // 8-channel stage per CTA, in waves of one CTA per SM; CUDA cores:
+        // about 28 TFLOP/s plus 10 us)
+        const int sms = g_sms[device & 63];
         const int64_t tiles = (a.len + kTcPos - 1) / kTcPos * ((a.oc + kTcOc - 1) / kTcOc) * a.phases;
-        if (tc_mode == 2 || tiles >= g_sms[device & 63]) {
+        const int64_t nst = (a.ic + kTcBK - 1) / kTcBK;
+        const double t_tc = (double)((tiles + sms - 1) / sms) * (double)nst * (2.4 + 0.2 * taps);
+        const double t_simt = 2.0 * a.ic * taps * (double)a.oc * a.len * a.phases / 28e6 + 10.0;
+        if (tc_mode == 2 || t_tc < t_simt) {
 #define QORA_TC_CASE(K, P, E) \
     if (taps == K && pro == P && epi == E) return launch_conv_tc_t<K, P, E>(a, device, st)
             QORA_TC_CASE(7, P_NONE, E_BIAS);      // Vocos input conv

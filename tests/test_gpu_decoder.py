@@ -16,7 +16,8 @@ a few frames; a long case past the real 72-position attention window and the
 edge behaviour (no frames, an out-of-codebook code).  The parity cases run
 twice: every convolution on the CUDA cores (tensor-core mode 0), and every
 convolution that has a tensor-core form on the tcgen05 3 x TF32 kernel
-(mode 2; the default mode 1 picks per launch by grid size)."""
+(mode 2; the default mode 1 picks per launch by estimated time, checked
+against the other two on a longer real-dims decode)."""
 import numpy as np
 import pytest
 
@@ -115,6 +116,24 @@ def test_long_sequence_past_the_window(ctx, tc):
     got = dec.decode_to_audio(codes, warmup=wu)
     ctx.check_device_error()
     _compare(got, D.decode_to_audio(W, codes, warmup=wu, dims=dims), f"long 30 + 150 tc={tc}")
+
+
+def test_default_mode_matches_both_kernels(ctx):
+    """Mode 1 mixes the two kernels by estimated time; on a 60-frame real-dims
+    decode (where the big Vocos convolutions go to the tensor cores and the
+    small ones stay on the CUDA cores) it agrees with all-CUDA-core and
+    all-tensor-core decodes within the parity tolerance."""
+    from qora_b200.decoder import DecoderDims
+    dims = DecoderDims()
+    _, dec = _setup(ctx, dims, seed=5)
+    codes = _codes(dims, 60, 13)
+    out = {}
+    for tc in (0, 1, 2):
+        dec.use_tensor_cores(tc)
+        out[tc] = dec.decode_to_audio(codes)
+    ctx.check_device_error()
+    _compare(out[1], out[0].astype(np.float64), "60 frames mode 1 vs 0")
+    _compare(out[1], out[2].astype(np.float64), "60 frames mode 1 vs 2")
 
 
 def test_device_entry_matches_host_entry(ctx):
