@@ -80,11 +80,24 @@ __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// sin(x)^2.  sin^2 has period pi, so x is first reduced to r = x - k pi,
+// k the integer nearest x / pi, by Cody and Waite's two-constant reduction
+// (pi = PI_HI + PI_LO, each product taken with a fused multiply-add), which
+// leaves |r| <= pi / 2 with an error far below f32 rounding for |x| < 1e5;
+// there the hardware sine __sinf is within 2^-21.4 of sin(r).  Infinite or
+// NaN x gives NaN, as sin does.
+__device__ __forceinline__ float sin_sq(float x) {
+    const float k = rintf(x * 0.318309886183790672f);
+    float r = fmaf(-k, 3.14159274101257324f, x);
+    r = fmaf(-k, -8.74227766e-08f, r);
+    const float s = __sinf(r);
+    return s * s;
+}
+
 // snake_beta (conv.rs:620-641) with a = exp(alpha), ib = exp(-beta) precomputed
-// on the host: x + ib * sin(a x)^2, as x + ((ib * s) * s).
+// on the host: x + ib * sin(a x)^2.
 __device__ __forceinline__ float snake(float x, float a, float ib) {
-    const float s = sinf(a * x);
-    return x + ib * s * s;
+    return x + ib * sin_sq(a * x);
 }
 
 // gelu (conv.rs:692-694): x * 0.5 * (1 + tanh(x * 0.70710677)).
@@ -738,25 +751,35 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
             if (lane == 0) mbar_arrive(&d_empty[c & 1]);
         };
         // ---------------------------------------------------- B staging
-        // item (K group kg, row n): 4 input channels at one position; a
-        // stage's raw values are loaded into registers one stage ahead, so
-        // their latency passes while the converters wait for a free buffer
+        // item (K group kg, row n): 4 input channels at one position.  A
+        // thread's items are the same every stage, so their geometry is
+        // worked out once; a stage's raw values are loaded into registers
+        // one stage ahead, so their latency passes while the converters wait
+        // for a free buffer.
         constexpr int kItems = (2 * kTcRowsB + kTcConvWarps * 32 - 1) / (kTcConvWarps * 32);
         const int rows = kTcPos + halo;
+        int it_kg[kItems], it_soff[kItems];
+        int64_t it_pos[kItems];
+        bool it_on[kItems], it_in[kItems];
+#pragma unroll
+        for (int q = 0; q < kItems; q++) {
+            const int it = tid + q * kTcConvWarps * 32;
+            const int kg = it >= rows ? 1 : 0, n = it - kg * rows;
+            it_on[q] = it < 2 * rows;
+            it_kg[q] = kg;
+            it_soff[q] = kg * (int)kTcBLbo + n * 16;
+            it_pos[q] = j0 - halo + n;
+            it_in[q] = it_on[q] && it_pos[q] >= 0 && it_pos[q] < a.len;
+        }
         float raw[kItems][4];
         auto fetch = [&](int s) {
             const int ic0 = s * kTcBK;
 #pragma unroll
             for (int q = 0; q < kItems; q++) {
-                const int it = tid + q * kTcConvWarps * 32;
-                const int kg = it / rows, n = it - kg * rows;
-                const int64_t pos = j0 - halo + n;
-                const bool pin = it < 2 * rows && pos >= 0 && pos < a.len;
+                const float *src = a.in + (int64_t)(ic0 + 4 * it_kg[q]) * a.len + it_pos[q];
 #pragma unroll
-                for (int u = 0; u < 4; u++) {
-                    const int ic = ic0 + 4 * kg + u;
-                    raw[q][u] = (pin && ic < a.ic) ? __ldg(a.in + (int64_t)ic * a.len + pos) : 0.0f;
-                }
+                for (int u = 0; u < 4; u++)
+                    raw[q][u] = (it_in[q] && ic0 + 4 * it_kg[q] + u < a.ic) ? __ldg(src + (int64_t)u * a.len) : 0.0f;
             }
         };
         fetch(0);
@@ -765,26 +788,39 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
             if (s >= NS && !wait(&s_empty[buf], ((s / NS) - 1) & 1)) break;
             uint8_t *B = sm + buf * SB + ABYTES;
             const int ic0 = s * kTcBK;
+            // the stage's per-channel prologue constants
+            float ca[8], cb[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const int ic = min(ic0 + u, a.ic - 1);
+                ca[u] = (PRO == P_SNAKE || PRO == P_RMS || PRO == P_LN) ? __ldg(a.pa + ic) : 0.0f;
+                cb[u] = (PRO == P_SNAKE || PRO == P_LN) ? __ldg(a.pb + ic) : 0.0f;
+            }
 #pragma unroll
             for (int q = 0; q < kItems; q++) {
-                const int it = tid + q * kTcConvWarps * 32;
-                if (it >= 2 * rows) continue;
-                const int kg = it / rows, n = it - kg * rows;
-                const int64_t pos = j0 - halo + n;
-                const bool pin = pos >= 0 && pos < a.len;
+                if (!it_on[q]) continue;
+                float ra = 0.0f, rb = 0.0f;
+                if ((PRO == P_RMS || PRO == P_LN) && it_in[q]) {
+                    ra = __ldg(a.ra + it_pos[q]);
+                    if (PRO == P_LN) rb = __ldg(a.rb + it_pos[q]);
+                }
                 uint32_t hi[4], lo[4];
 #pragma unroll
                 for (int u = 0; u < 4; u++) {
-                    const int ic = ic0 + 4 * kg + u;
                     float v = raw[q][u];
+                    const int cu = 4 * it_kg[q] + u;
                     // positions outside the input are the convolution's zero padding
-                    if (PRO != P_NONE && pin && ic < a.ic) v = prologue<PRO>(v, ic, pos, a);
+                    if (it_in[q] && ic0 + cu < a.ic) {
+                        const float pa = it_kg[q] ? ca[4 + u] : ca[u], pb = it_kg[q] ? cb[4 + u] : cb[u];
+                        if constexpr (PRO == P_SNAKE) v = snake(v, pa, pb);
+                        if constexpr (PRO == P_RMS) v = v * ra * pa;
+                        if constexpr (PRO == P_LN) v = (v - ra) * rb * pa + pb;
+                    }
                     hi[u] = to_tf32(v);
                     lo[u] = to_tf32(v - __uint_as_float(hi[u]));
                 }
-                *reinterpret_cast<uint4 *>(B + kg * kTcBLbo + n * 16) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4 *>(B + kTcBHalf + kg * kTcBLbo + n * 16) =
-                    make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4 *>(B + it_soff[q]) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4 *>(B + kTcBHalf + it_soff[q]) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
             tc::fence_proxy_async_smem();
             __syncwarp();
@@ -971,14 +1007,16 @@ int launch_conv(int taps, int pro, int epi, const ConvArgs &a0, int device, cuda
     a.err = err;
     if (a.wtc && tc_mode != 0 && epi != E_SWIGLU) {
         // mode 1: the kernel with the smaller estimated time, from B200
-        // measurements of both (tensor cores: about 2.4 + 0.2 x taps us per
+        // measurements of both (tensor cores: about 2.0 + 0.12 x taps us per
         // 8-channel stage per CTA, in waves of one CTA per SM; CUDA cores:
-        // about 28 TFLOP/s plus 10 us)
+        // about 28 TFLOP/s (14 for pointwise convolutions, which stream
+        // their input and residual) plus 10 us)
         const int sms = g_sms[device & 63];
         const int64_t tiles = (a.len + kTcPos - 1) / kTcPos * ((a.oc + kTcOc - 1) / kTcOc) * a.phases;
         const int64_t nst = (a.ic + kTcBK - 1) / kTcBK;
-        const double t_tc = (double)((tiles + sms - 1) / sms) * (double)nst * (2.4 + 0.2 * taps);
-        const double t_simt = 2.0 * a.ic * taps * (double)a.oc * a.len * a.phases / 28e6 + 10.0;
+        const double t_tc = (double)((tiles + sms - 1) / sms) * (double)nst * (2.0 + 0.12 * taps);
+        const double t_simt =
+            2.0 * a.ic * taps * (double)a.oc * a.len * a.phases / (taps == 1 ? 14e6 : 28e6) + 10.0;
         if (tc_mode == 2 || t_tc < t_simt) {
 #define QORA_TC_CASE(K, P, E) \
     if (taps == K && pro == P && epi == E) return launch_conv_tc_t<K, P, E>(a, device, st)
