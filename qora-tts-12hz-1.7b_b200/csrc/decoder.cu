@@ -630,12 +630,17 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
     __shared__ int abort_s;
     uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int p = (int)(blockIdx.x % (unsigned)a.phases);
-    const int64_t j0 = (int64_t)(blockIdx.x / (unsigned)a.phases) * kTcPos;
-    const int oc0 = blockIdx.y * kTcOc;
+    // one-dimensional grid, output-channel tile fastest, then phase, then
+    // position tile: the CTAs that read the same input tile run together
+    const int n_oct = (a.oc + kTcOc - 1) / kTcOc;
+    const int oct = (int)(blockIdx.x % (unsigned)n_oct);
+    const unsigned rest = blockIdx.x / (unsigned)n_oct;
+    const int p = (int)(rest % (unsigned)a.phases);
+    const int64_t j0 = (int64_t)(rest / (unsigned)a.phases) * kTcPos;
+    const int oc0 = oct * kTcOc;
     const int halo = (KS - 1) * a.dil;
     const int nst = (a.ic + kTcBK - 1) / kTcBK;
-    const uint8_t *aimg_t = aimg + ((int64_t)p * gridDim.y + blockIdx.y) * nst * (int64_t)ABYTES;
+    const uint8_t *aimg_t = aimg + ((int64_t)p * n_oct + oct) * nst * (int64_t)ABYTES;
     volatile int *abort_v = &abort_s;
 
     if (tid == 0) {
@@ -969,7 +974,8 @@ int launch_conv_t(const ConvArgs &a, int device, cudaStream_t st) {
     return QORA_OK;
 }
 
-// The (taps, prologue, epilogue) combinations the decoder uses.
+// One k_dec_conv_tc launch: output-channel tiles x phases x position tiles,
+// one CTA per SM (all of tensor memory each).
 template <int KS, int PRO, int EPI>
 int launch_conv_tc_t(const ConvArgs &a, int device, cudaStream_t st) {
     static std::atomic<uint64_t> attr_done{0};
@@ -983,7 +989,8 @@ int launch_conv_tc_t(const ConvArgs &a, int device, cudaStream_t st) {
     const int64_t gx = (a.len + kTcPos - 1) / kTcPos * a.phases;
     const int gy = (a.oc + kTcOc - 1) / kTcOc;
     if (gx > INT32_MAX || gy > 65535) return set_error(QORA_ERR_SHAPE, "convolution too long");
-    k_dec_conv_tc<KS, PRO, EPI><<<dim3((unsigned)gx, gy, 1), kTcThreads, tc_smem<KS>(), st>>>(a, a.wtc);
+    if (gx * gy > INT32_MAX) return set_error(QORA_ERR_SHAPE, "convolution too long");
+    k_dec_conv_tc<KS, PRO, EPI><<<dim3((unsigned)(gx * gy), 1, 1), kTcThreads, tc_smem<KS>(), st>>>(a, a.wtc);
     QORA_LAUNCH_CHECK();
     return QORA_OK;
 }
