@@ -234,7 +234,8 @@ int qora_kv_attend_noalloc(qora_kv *kv, int32_t layer, const float *qkv, int32_t
 /* ------------------------------------------------------------ save.rs */
 /* load_model (save.rs:262-409; records gemv.rs:595-687): maps a .qora-tts
  * checkpoint (Q4 format) read-only and parses its talker and code-predictor
- * sections; the speech decoder after them is not read.  Every length is
+ * sections (the speech decoder after them is read by qora_model_file_decoder,
+ * with the decoder's entry points below).  Every length is
  * checked against the file; a malformed file, a version other than 1 or an
  * f16 (format 0) checkpoint is an error.  The RoPE base is recovered from the
  * stored tables and must reproduce them exactly. */
@@ -435,6 +436,16 @@ int qora_decoder_set_tensor(qora_decoder *dec, const char *name, const float *da
                             int64_t count);
 int qora_decoder_finalize(qora_decoder *dec);
 void qora_decoder_destroy(qora_decoder *dec);
+/* load_model's speech decoder (load_decoder_weights, save.rs:446-552): the
+ * decoder section of a .qora-tts file opened by qora_model_file_open, uploaded
+ * as a finalized decoder (its dims taken from the section; the file's
+ * processed tensors are handed over under their checkpoint names, so the
+ * decoder equals one loaded tensor by tensor from the speech tokenizer).
+ * QORA_ERR_INVALID when the file has no well-formed decoder section,
+ * QORA_ERR_UNSUPPORTED for a decoder structure this engine does not run. */
+int qora_model_file_decoder(const qora_model_file *f, qora_ctx *ctx, qora_decoder **out);
+/* The dims the decoder was created with. */
+int qora_decoder_get_dims(const qora_decoder *dec, qora_decoder_dims *dims);
 /* Which convolutions run on the tensor cores (3 x TF32 products, f32
  * accumulation): mode 0 none (all on the CUDA cores), 1 (the default) those
  * whose tiles fill the GPU, 2 every one that has a tensor-core form (the

@@ -226,6 +226,9 @@ extern "C" {
                                    data_host: *const f32, count: i64) -> c_int;
     pub fn qora_decoder_finalize(dec: *mut qora_decoder) -> c_int;
     pub fn qora_decoder_destroy(dec: *mut qora_decoder);
+    pub fn qora_model_file_decoder(f: *const qora_model_file, ctx: *mut qora_ctx,
+                                   out: *mut *mut qora_decoder) -> c_int;
+    pub fn qora_decoder_get_dims(dec: *const qora_decoder, dims: *mut qora_decoder_dims) -> c_int;
     pub fn qora_decoder_use_tensor_cores(dec: *mut qora_decoder, mode: i32) -> c_int;
     pub fn qora_decoder_samples(dec: *const qora_decoder, frames: i64, samples: *mut i64) -> c_int;
     // decode_to_audio (decoder.rs:395-582)

@@ -1695,6 +1695,12 @@ int qora_decoder_finalize(qora_decoder *dec) {
     return QORA_OK;
 }
 
+int qora_decoder_get_dims(const qora_decoder *dec, qora_decoder_dims *dims) {
+    if (!dec || !dims) return set_error(QORA_ERR_INVALID, "qora_decoder_get_dims: bad argument");
+    *dims = dec->d;
+    return QORA_OK;
+}
+
 int qora_decoder_use_tensor_cores(qora_decoder *dec, int32_t mode) {
     if (!dec || mode < 0 || mode > 2) return set_error(QORA_ERR_INVALID, "qora_decoder_use_tensor_cores: bad argument");
     dec->tc_mode = mode;

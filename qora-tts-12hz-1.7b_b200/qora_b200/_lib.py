@@ -143,6 +143,8 @@ SIGNATURES = {
     "qora_decoder_set_tensor": (C.c_int, [_vp, C.c_char_p, _vp, _i64]),
     "qora_decoder_finalize": (C.c_int, [_vp]),
     "qora_decoder_destroy": (None, [_vp]),
+    "qora_model_file_decoder": (C.c_int, [_vp, _vp, _PP]),
+    "qora_decoder_get_dims": (C.c_int, [_vp, _vp]),
     "qora_decoder_use_tensor_cores": (C.c_int, [_vp, _i32]),
     "qora_decoder_samples": (C.c_int, [_vp, _i64, C.POINTER(C.c_int64)]),
     "qora_decode_to_audio": (C.c_int, [_vp, _vp, _i64, _vp, _i64, _vp, _i64, C.POINTER(C.c_int64), _vp]),

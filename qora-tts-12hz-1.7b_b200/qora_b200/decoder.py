@@ -205,6 +205,27 @@ class SpeechDecoder:
             _lib.call("qora_decoder_set_tensor", self.h, name.encode(), a.ctypes.data, a.size)
         _lib.call("qora_decoder_finalize", self.h)
 
+    @classmethod
+    def from_model_file(cls, ctx, mf) -> "SpeechDecoder":
+        """The speech decoder of a .qora-tts checkpoint (load_decoder_weights,
+        save.rs:446-552); `mf` a qora_b200.ModelFile."""
+        self = cls.__new__(cls)
+        self.ctx, self._L = ctx, _lib.load()
+        h = C.c_void_p()
+        _lib.call("qora_model_file_decoder", mf.h, ctx.h, C.byref(h))
+        self.h = h
+        cd = _lib.DecoderDims()
+        _lib.call("qora_decoder_get_dims", self.h, C.byref(cd))
+        nb = cd.vocos_blocks
+        self.dims = DecoderDims(
+            codebook_dim=cd.codebook_dim, codebook_size=cd.codebook_size, num_quantizers=cd.num_quantizers,
+            vq_dim=cd.vq_dim, latent=cd.latent, hidden=cd.hidden, num_heads=cd.num_heads, head_dim=cd.head_dim,
+            intermediate=cd.intermediate, num_layers=cd.num_layers, sliding_window=cd.sliding_window,
+            upsample_stages=cd.upsample_stages, upsample_inner=cd.upsample_inner,
+            vocos_channels=tuple(cd.vocos_channels[:nb + 1]), vocos_kernels=tuple(cd.vocos_kernels[:nb]),
+            vocos_strides=tuple(cd.vocos_strides[:nb]), rope_max_pos=cd.rope_max_pos, rope_theta=cd.rope_theta)
+        return self
+
     def close(self):
         if getattr(self, "h", None):
             self._L.qora_decoder_destroy(self.h)

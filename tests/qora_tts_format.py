@@ -1,8 +1,10 @@
-"""Writer of the reference's .qora-tts checkpoint layout (save.rs:22-138 and the
-record helpers gemv.rs:595-631), for the model-file reader tests: header
+"""Writer of the reference's .qora-tts checkpoint layout (save.rs:22-262 and
+the record helpers gemv.rs:595-631), for the model-file reader tests: header
 "QTTS", u32 version, u8 format (1 = Q4), then the talker and code-predictor
-sections, then bytes standing in for the speech decoder (not read)."""
+sections, then the speech-decoder section (decoder_section) or bytes standing
+in for it."""
 import ctypes as C
+import io
 import struct
 
 import numpy as np
@@ -114,3 +116,99 @@ def write(path, tw, pw, cfg, fmt=1, version=1, theta=None, tail=b"decoder sectio
         for a in rope_tables(cfg.p_head_dim, cfg.p_max_pos, theta):
             _f32(f, a)
         f.write(tail)
+
+
+def decoder_section(W, dims) -> bytes:
+    """The speech-decoder section as save_decoder writes it (save.rs:171-262),
+    from checkpoint-named weights W after load_speech_decoder's processing
+    (loader.rs:503-716): codebooks divided by max(cluster_usage, 1e-8)
+    (ema_codebook), linear weights and the codebook projections transposed to
+    [in][out] (read_linear_f32 / transpose_2d), ConvNeXt pointwise weights
+    transposed likewise; convolutions with their headers (save.rs:139-169);
+    the standard RoPE tables (loader.rs:668-682)."""
+    f = io.BytesIO()
+    F32 = np.float32
+    lin = lambda key: np.ascontiguousarray(np.asarray(W[key], F32).reshape(W[key].shape[0], -1).T)
+    ema = lambda pre: (np.asarray(W[pre + "embedding_sum"], F32)
+                       / np.fmax(np.asarray(W[pre + "cluster_usage"], F32), F32(1e-8))[:, None]).astype(F32)
+
+    def conv(key, dil=1, stride=1):
+        w = np.asarray(W[key + "weight"], F32)
+        for v in (w.shape[1], w.shape[0], w.shape[2], stride, 0, dil):
+            _u32(f, v)
+        _f32(f, w)
+        _f32(f, W[key + "bias"])
+
+    def convt(key, stride):
+        w = np.asarray(W[key + "weight"], F32)
+        for v in (w.shape[0], w.shape[1], w.shape[2], stride, 0):
+            _u32(f, v)
+        _f32(f, w)
+        _f32(f, W[key + "bias"])
+
+    for v in (dims.hidden, dims.num_heads, dims.head_dim, dims.intermediate, dims.sliding_window,
+              dims.codebook_dim):
+        _u32(f, v)
+    q = "decoder.quantizer."
+    _f32(f, ema(q + "rvq_first.vq.layers.0._codebook."))
+    _f32(f, lin(q + "rvq_first.output_proj.weight"))
+    _u32(f, dims.num_quantizers - 1)
+    for g in range(dims.num_quantizers - 1):
+        _f32(f, ema(q + f"rvq_rest.vq.layers.{g}._codebook."))
+    _f32(f, lin(q + "rvq_rest.output_proj.weight"))
+    conv("decoder.pre_conv.conv.")
+    t = "decoder.pre_transformer."
+    _f32(f, lin(t + "input_proj.weight"))
+    _f32(f, W[t + "input_proj.bias"])
+    _u32(f, dims.num_layers)
+    for i in range(dims.num_layers):
+        L = f"{t}layers.{i}."
+        for n in ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj", "self_attn.o_proj",
+                  "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj"):
+            _f32(f, lin(L + n + ".weight"))
+        for n in ("input_layernorm.weight", "post_attention_layernorm.weight",
+                  "self_attn_layer_scale.scale", "mlp_layer_scale.scale"):
+            _f32(f, W[L + n])
+    _f32(f, W[t + "norm.weight"])
+    _f32(f, lin(t + "output_proj.weight"))
+    _f32(f, W[t + "output_proj.bias"])
+    _u32(f, dims.upsample_stages)
+    for i in range(dims.upsample_stages):
+        ct, cn = f"decoder.upsample.{i}.0.conv.", f"decoder.upsample.{i}.1."
+        _u32(f, dims.latent)
+        convt(ct, 2)
+        dw = np.asarray(W[cn + "dwconv.conv.weight"], F32)
+        for v in (dims.latent, dw.shape[2], 3):
+            _u32(f, v)
+        _f32(f, dw)
+        _f32(f, W[cn + "dwconv.conv.bias"])
+        _f32(f, W[cn + "norm.weight"])
+        _f32(f, W[cn + "norm.bias"])
+        _f32(f, lin(cn + "pwconv1.weight"))
+        _f32(f, W[cn + "pwconv1.bias"])
+        _f32(f, lin(cn + "pwconv2.weight"))
+        _f32(f, W[cn + "pwconv2.bias"])
+        _f32(f, W[cn + "gamma"])
+    conv("decoder.decoder.0.conv.")
+    _u32(f, len(dims.vocos_strides))
+    for b, s in enumerate(dims.vocos_strides):
+        p = f"decoder.decoder.{b + 1}.block."
+        _f32(f, W[p + "0.alpha"])
+        _f32(f, W[p + "0.beta"])
+        convt(p + "1.conv.", s)
+        _u32(f, 3)
+        for r, dil in enumerate((1, 3, 9)):
+            u = f"{p}{r + 2}."
+            _f32(f, W[u + "act1.alpha"])
+            _f32(f, W[u + "act1.beta"])
+            conv(u + "conv1.conv.", dil)
+            _f32(f, W[u + "act2.alpha"])
+            _f32(f, W[u + "act2.beta"])
+            conv(u + "conv2.conv.")
+    nb = len(dims.vocos_strides)
+    _f32(f, W[f"decoder.decoder.{nb + 1}.alpha"])
+    _f32(f, W[f"decoder.decoder.{nb + 1}.beta"])
+    conv(f"decoder.decoder.{nb + 2}.conv.")
+    for a in rope_tables(dims.head_dim, dims.rope_max_pos, dims.rope_theta):
+        _f32(f, a)
+    return f.getvalue()
