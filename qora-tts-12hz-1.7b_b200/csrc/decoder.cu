@@ -568,15 +568,16 @@ __global__ void __launch_bounds__(kFinT) k_dec_final(const float *in, int C, int
 //     16 * (256 + 64), row n = position j0 - halo + n, written by the
 //     converter warps (prologue applied, hi / lo split).  Tap t reads rows
 //     t * dil .. t * dil + 255: its descriptor starts t * dil * 16 bytes in.
-// Warp roles (288 threads): warps 0-7 stage B, add the chunks into
-// registers and run the epilogue; warp 8 allocates tensor memory and its
+// Warp roles (544 threads): warps 0-15 stage B, add the chunks into
+// registers (64 running sums per thread) and run the epilogue; warp 16
+// allocates tensor memory and its
 // lane 0 issues the A bulk copies and the MMAs (8 input channels per stage:
 // K = 8 per MMA).  Every wait is bounded (kDevTimeout, then a CTA-wide
 // abort).
 constexpr int kTcOc = 128;
 constexpr int kTcPos = 256;
 constexpr int kTcBK = 8;
-constexpr int kTcConvWarps = 8;
+constexpr int kTcConvWarps = 16;
 constexpr int kTcThreads = (kTcConvWarps + 1) * 32;
 constexpr int kTcRowsB = kTcPos + kCvMaxHalo;
 constexpr uint32_t kTcATap = 2 * 2 * kTcOc * 16;      // 8192 bytes per tap and stage
@@ -733,18 +734,20 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
         __syncwarp();
     } else {
         // warp w owns tensor-memory lanes 32 (w % 4) .. + 31 (output channels)
-        // and columns 128 (w / 4) .. + 127 (positions) of each accumulator
-        const int lg = warp & 3, half = warp >> 2;
-        float accr[128];
+        // and columns 64 (w / 4) .. + 63 (positions) of each accumulator
+        constexpr int kCols = kTcPos / (kTcConvWarps / 4);
+        const int lg = warp & 3, quarter = warp >> 2;
+        float accr[kCols];
 #pragma unroll
-        for (int i = 0; i < 128; i++) accr[i] = 0.0f;
+        for (int i = 0; i < kCols; i++) accr[i] = 0.0f;
         auto drain = [&](int c) {
             const bool ok = wait(&d_full[c & 1], (c >> 1) & 1);
             tc::fence_after_sync();
             if (ok) {
-                const uint32_t base = tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(c & 1) * kTcPos + half * 128;
+                const uint32_t base =
+                    tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(c & 1) * kTcPos + quarter * kCols;
 #pragma unroll
-                for (int q = 0; q < 4; q++) {
+                for (int q = 0; q < kCols / 32; q++) {
                     float v[32];
                     tc::ld_32x32b_x32(base + q * 32, v);
 #pragma unroll
@@ -841,8 +844,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
         float *scr = reinterpret_cast<float *>(sm) + warp * (32 * 33);
         const int64_t out_len = a.len * a.phases;
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-            const int col0 = half * 128 + q * 32;
+        for (int q = 0; q < kCols / 32; q++) {
+            const int col0 = quarter * kCols + q * 32;
 #pragma unroll
             for (int i = 0; i < 32; i++) scr[lane * 33 + i] = accr[q * 32 + i];
             __syncwarp();
