@@ -565,7 +565,7 @@ __global__ void __launch_bounds__(kFinT) k_dec_final(const float *in, int C, int
 //     2048, arriving as one bulk copy per stage from an image prepared on
 //     upload (tc_image below);
 //   B (inputs) per stage: [hi, lo][2 K groups][256 + halo rows][4], LBO
-//     16 * (256 + 64), row n = position j0 - halo + n, written by the
+//     16 * (256 + 56), row n = position j0 - halo + n, written by the
 //     converter warps (prologue applied, hi / lo split).  Tap t reads rows
 //     t * dil .. t * dil + 255: its descriptor starts t * dil * 16 bytes in.
 // Warp roles (544 threads): warps 0-15 stage B, add the chunks into
@@ -579,22 +579,37 @@ constexpr int kTcPos = 256;
 constexpr int kTcBK = 8;
 constexpr int kTcConvWarps = 16;
 constexpr int kTcThreads = (kTcConvWarps + 1) * 32;
-constexpr int kTcRowsB = kTcPos + kCvMaxHalo;
+// tensor-core halo limit: 56 rows (the real decoder's largest is 6 x 9 = 54)
+// keeps three 7-tap stages within the 227 KB of shared memory a CTA may use;
+// a convolution with a longer halo runs on the CUDA-core kernel
+constexpr int kTcMaxHalo = 56;
+constexpr int kTcRowsB = kTcPos + kTcMaxHalo;
 constexpr uint32_t kTcATap = 2 * 2 * kTcOc * 16;      // 8192 bytes per tap and stage
 constexpr uint32_t kTcALbo = kTcOc * 16;              // 2048
-constexpr uint32_t kTcBLbo = kTcRowsB * 16;           // 5120
+constexpr uint32_t kTcBLbo = kTcRowsB * 16;           // 4992
 constexpr uint32_t kTcBHalf = 2 * kTcBLbo;            // hi part, then lo part
-constexpr uint32_t kTcBBytes = 2 * kTcBHalf;          // 20480
+constexpr uint32_t kTcBBytes = 2 * kTcBHalf;          // 19968
 constexpr uint32_t kTcTmemCols = 2 * kTcPos;          // two accumulators
 constexpr size_t kTcMinSmem = 120 * 1024;             // one CTA per SM (all of tensor memory)
-template <int KS> constexpr int tc_stages() { return KS >= 3 ? 2 : 4; }
-template <int KS> constexpr int tc_chunk() { return (64 / (3 * KS)) > 1 ? 64 / (3 * KS) : 1; }
+constexpr size_t kTcMaxSmem = 227 * 1024;             // dynamic + static shared memory of a CTA
+constexpr size_t kTcAlign = 128;                      // stage buffers start 128-byte aligned
+constexpr size_t kTcStatic = 256;                     // the kernel's barriers and flags, rounded up
 template <int KS> constexpr uint32_t tc_stage_bytes() { return KS * kTcATap + kTcBBytes; }
+// pipeline depth: as many stages as fit, up to 4 (7 taps: 3)
+template <int KS> constexpr int tc_stages() {
+    return (kTcMaxSmem - kTcAlign - kTcStatic) / tc_stage_bytes<KS>() < 4
+               ? (int)((kTcMaxSmem - kTcAlign - kTcStatic) / tc_stage_bytes<KS>())
+               : 4;
+}
+template <int KS> constexpr int tc_chunk() { return (64 / (3 * KS)) > 1 ? 64 / (3 * KS) : 1; }
 template <int KS> constexpr size_t tc_smem() {
-    return (size_t)tc_stages<KS>() * tc_stage_bytes<KS>() + 1024 > kTcMinSmem
-               ? (size_t)tc_stages<KS>() * tc_stage_bytes<KS>() + 1024
+    return (size_t)tc_stages<KS>() * tc_stage_bytes<KS>() + kTcAlign > kTcMinSmem
+               ? (size_t)tc_stages<KS>() * tc_stage_bytes<KS>() + kTcAlign
                : kTcMinSmem;
 }
+static_assert(tc_stages<7>() >= 3, "three 7-tap stages fit");
+static_assert(tc_smem<7>() + kTcStatic <= kTcMaxSmem, "shared memory of a CTA");
+static_assert(kTcRowsB % 8 == 0 && tc_stage_bytes<7>() % 16 == 0, "16-byte rows, 8-row core matrices");
 
 __host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
     return (1u << 4)                     // D: f32
@@ -629,7 +644,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
     __shared__ __align__(8) uint64_t a_full[NS], b_full[NS], s_empty[NS], d_full[2], d_empty[2];
     __shared__ uint32_t tmem_slot;
     __shared__ int abort_s;
-    uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)tc_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *sm = reinterpret_cast<uint8_t *>(((uintptr_t)tc_raw + (kTcAlign - 1)) & ~(uintptr_t)(kTcAlign - 1));
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // one-dimensional grid, output-channel tile fastest, then phase, then
     // position tile: the CTAs that read the same input tile run together
@@ -982,7 +997,7 @@ int launch_conv_t(const ConvArgs &a, int device, cudaStream_t st) {
 template <int KS, int PRO, int EPI>
 int launch_conv_tc_t(const ConvArgs &a, int device, cudaStream_t st) {
     static std::atomic<uint64_t> attr_done{0};
-    if ((KS - 1) * a.dil > kCvMaxHalo) return set_error(QORA_ERR_UNSUPPORTED, "convolution halo too large");
+    if ((KS - 1) * a.dil > kTcMaxHalo) return set_error(QORA_ERR_UNSUPPORTED, "convolution halo too large");
     const uint64_t bit = 1ull << (device & 63);
     if (!(attr_done.load() & bit)) {
         QORA_CUDA(cudaFuncSetAttribute(k_dec_conv_tc<KS, PRO, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1015,7 +1030,7 @@ int choose_split(int taps, const ConvArgs &a, int sms) {
 int launch_conv(int taps, int pro, int epi, const ConvArgs &a0, int device, cudaStream_t st, int tc_mode, int *err) {
     ConvArgs a = a0;
     a.err = err;
-    if (a.wtc && tc_mode != 0 && epi != E_SWIGLU) {
+    if (a.wtc && tc_mode != 0 && epi != E_SWIGLU && (taps - 1) * a.dil <= kTcMaxHalo) {
         // mode 1: the kernel with the smaller estimated time, from B200
         // measurements of both (tensor cores: about 2.0 + 0.12 x taps us per
         // 8-channel stage per CTA, in waves of one CTA per SM; CUDA cores:
