@@ -561,22 +561,26 @@ __global__ void __launch_bounds__(kFinT) k_dec_final(const float *in, int C, int
 // Operands in shared memory, canonical K-major layout without swizzle
 // (8-row x 16-byte core matrices; rows 16 bytes apart, K groups of 4 TF32
 // values `LBO` apart):
-//   A (weights) per stage and tap: [hi, lo][2 K groups][128 rows][4], LBO
-//     2048, arriving as one bulk copy per stage from an image prepared on
-//     upload (tc_image below);
-//   B (inputs) per stage: [hi, lo][2 K groups][256 + halo rows][4], LBO
-//     16 * (256 + 56), row n = position j0 - halo + n, written by the
-//     converter warps (prologue applied, hi / lo split).  Tap t reads rows
-//     t * dil .. t * dil + 255: its descriptor starts t * dil * 16 bytes in.
+// A stage holds BK input channels (BK / 4 K groups): 16 for pointwise
+// convolutions (their stages are short, so fewer, longer stages keep the
+// converters' per-stage round trip off the tensor cores), 8 otherwise.
+//   A (weights) per stage and tap: [hi, lo][BK / 4 K groups][128 rows][4],
+//     LBO 2048, arriving as one bulk copy per stage from an image prepared
+//     on upload (tc_image below);
+//   B (inputs) per stage: [hi, lo][BK / 4 K groups][256 + halo rows][4], LBO
+//     16 * (256 + 56) (16 * 256 for pointwise convolutions), row n =
+//     position j0 - halo + n, written by the converter warps (prologue
+//     applied, hi / lo split).  Tap t reads rows t * dil .. t * dil + 255:
+//     its descriptor starts t * dil * 16 bytes in; K step j (8 channels)
+//     starts 2 j K groups in.
 // Warp roles (544 threads): warps 0-15 stage B, add the chunks into
 // registers (64 running sums per thread) and run the epilogue; warp 16
-// allocates tensor memory and its
-// lane 0 issues the A bulk copies and the MMAs (8 input channels per stage:
-// K = 8 per MMA).  Every wait is bounded (kDevTimeout, then a CTA-wide
+// allocates tensor memory and its lane 0 issues the A bulk copies and the
+// MMAs (K = 8 per MMA).  Every wait is bounded (kDevTimeout, then a CTA-wide
 // abort).
 constexpr int kTcOc = 128;
 constexpr int kTcPos = 256;
-constexpr int kTcBK = 8;
+constexpr int kTcBK = 8;                              // channels per MMA (K = 8 TF32)
 constexpr int kTcConvWarps = 16;
 constexpr int kTcThreads = (kTcConvWarps + 1) * 32;
 // tensor-core halo limit: 56 rows (the real decoder's largest is 6 x 9 = 54)
@@ -584,24 +588,31 @@ constexpr int kTcThreads = (kTcConvWarps + 1) * 32;
 // a convolution with a longer halo runs on the CUDA-core kernel
 constexpr int kTcMaxHalo = 56;
 constexpr int kTcRowsB = kTcPos + kTcMaxHalo;
-constexpr uint32_t kTcATap = 2 * 2 * kTcOc * 16;      // 8192 bytes per tap and stage
 constexpr uint32_t kTcALbo = kTcOc * 16;              // 2048
-constexpr uint32_t kTcBLbo = kTcRowsB * 16;           // 4992
-constexpr uint32_t kTcBHalf = 2 * kTcBLbo;            // hi part, then lo part
-constexpr uint32_t kTcBBytes = 2 * kTcBHalf;          // 19968
+// input channels per stage, and the layout sizes that follow from it
+__host__ __device__ constexpr int tc_bk_of(int ks) { return ks == 1 ? 16 : 8; }
+template <int KS> constexpr int tc_bk() { return tc_bk_of(KS); }
+template <int KS> constexpr int tc_rows() { return KS == 1 ? kTcPos : kTcRowsB; }
+template <int KS> constexpr uint32_t tc_atap() { return 2u * (tc_bk<KS>() / 4) * kTcALbo; }  // bytes per tap
+template <int KS> constexpr uint32_t tc_blbo() { return (uint32_t)tc_rows<KS>() * 16u; }
+template <int KS> constexpr uint32_t tc_bhalf() { return (uint32_t)(tc_bk<KS>() / 4) * tc_blbo<KS>(); }
+template <int KS> constexpr uint32_t tc_bbytes() { return 2u * tc_bhalf<KS>(); }  // hi part, then lo part
 constexpr uint32_t kTcTmemCols = 2 * kTcPos;          // two accumulators
 constexpr size_t kTcMinSmem = 120 * 1024;             // one CTA per SM (all of tensor memory)
 constexpr size_t kTcMaxSmem = 227 * 1024;             // dynamic + static shared memory of a CTA
 constexpr size_t kTcAlign = 128;                      // stage buffers start 128-byte aligned
 constexpr size_t kTcStatic = 256;                     // the kernel's barriers and flags, rounded up
-template <int KS> constexpr uint32_t tc_stage_bytes() { return KS * kTcATap + kTcBBytes; }
+template <int KS> constexpr uint32_t tc_stage_bytes() { return KS * tc_atap<KS>() + tc_bbytes<KS>(); }
 // pipeline depth: as many stages as fit, up to 4 (7 taps: 3)
 template <int KS> constexpr int tc_stages() {
     return (kTcMaxSmem - kTcAlign - kTcStatic) / tc_stage_bytes<KS>() < 4
                ? (int)((kTcMaxSmem - kTcAlign - kTcStatic) / tc_stage_bytes<KS>())
                : 4;
 }
-template <int KS> constexpr int tc_chunk() { return (64 / (3 * KS)) > 1 ? 64 / (3 * KS) : 1; }
+// stages per accumulation chunk: about 64 MMAs (3 per tap and 8 channels)
+template <int KS> constexpr int tc_chunk() {
+    return (64 / (3 * KS * (tc_bk<KS>() / kTcBK))) > 1 ? 64 / (3 * KS * (tc_bk<KS>() / kTcBK)) : 1;
+}
 template <int KS> constexpr size_t tc_smem() {
     return (size_t)tc_stages<KS>() * tc_stage_bytes<KS>() + kTcAlign > kTcMinSmem
                ? (size_t)tc_stages<KS>() * tc_stage_bytes<KS>() + kTcAlign
@@ -610,6 +621,9 @@ template <int KS> constexpr size_t tc_smem() {
 static_assert(tc_stages<7>() >= 3, "three 7-tap stages fit");
 static_assert(tc_smem<7>() + kTcStatic <= kTcMaxSmem, "shared memory of a CTA");
 static_assert(kTcRowsB % 8 == 0 && tc_stage_bytes<7>() % 16 == 0, "16-byte rows, 8-row core matrices");
+static_assert(tc_stages<1>() == 4 && tc_smem<1>() + kTcStatic <= kTcMaxSmem, "four pointwise stages fit");
+static_assert(tc_stage_bytes<1>() == 49152 && tc_stage_bytes<2>() == 36352 && tc_stage_bytes<7>() == 77312,
+              "stage sizes");
 
 __host__ __device__ constexpr uint32_t idesc_tf32_f32(int M, int N) {
     return (1u << 4)                     // D: f32
@@ -639,7 +653,9 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
     constexpr int NS = tc_stages<KS>();
     constexpr int CH = tc_chunk<KS>();
     constexpr uint32_t SB = tc_stage_bytes<KS>();
-    constexpr uint32_t ABYTES = KS * kTcATap;
+    constexpr int BK = tc_bk<KS>(), KG = BK / 4;
+    constexpr uint32_t ATAP = tc_atap<KS>(), BLBO = tc_blbo<KS>(), BHALF = tc_bhalf<KS>();
+    constexpr uint32_t ABYTES = KS * ATAP;
     extern __shared__ uint8_t tc_raw[];
     __shared__ __align__(8) uint64_t a_full[NS], b_full[NS], s_empty[NS], d_full[2], d_empty[2];
     __shared__ uint32_t tmem_slot;
@@ -655,7 +671,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
     const int64_t j0 = (int64_t)(rest / (unsigned)a.phases) * kTcPos;
     const int oc0 = oct * kTcOc;
     const int halo = (KS - 1) * a.dil;
-    const int nst = (a.ic + kTcBK - 1) / kTcBK;
+    const int nst = (a.ic + BK - 1) / BK;
     const uint8_t *aimg_t = aimg + ((int64_t)p * n_oct + oct) * nst * (int64_t)ABYTES;
     volatile int *abort_v = &abort_s;
 
@@ -720,14 +736,18 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
                 const uint32_t sA = smem_u32(sm + buf * SB), sB = sA + ABYTES;
 #pragma unroll
                 for (int t = 0; t < KS; t++) {
-                    const uint64_t ah = tc::smem_desc(sA + t * kTcATap, kTcALbo, 128);
-                    const uint64_t al = tc::smem_desc(sA + t * kTcATap + kTcATap / 2, kTcALbo, 128);
-                    const uint32_t boff = (uint32_t)(t * a.dil) * 16u;
-                    const uint64_t bh = tc::smem_desc(sB + boff, kTcBLbo, 128);
-                    const uint64_t bl = tc::smem_desc(sB + kTcBHalf + boff, kTcBLbo, 128);
-                    mma_tf32(d, ah, bh, idesc, (first && t == 0) ? 0u : 1u);
-                    mma_tf32(d, ah, bl, idesc, 1u);
-                    mma_tf32(d, al, bh, idesc, 1u);
+#pragma unroll
+                    for (int j = 0; j < BK / kTcBK; j++) {
+                        const uint32_t ak = sA + t * ATAP + j * 2 * kTcALbo;
+                        const uint64_t ah = tc::smem_desc(ak, kTcALbo, 128);
+                        const uint64_t al = tc::smem_desc(ak + ATAP / 2, kTcALbo, 128);
+                        const uint32_t boff = (uint32_t)(t * a.dil) * 16u + (uint32_t)j * 2u * BLBO;
+                        const uint64_t bh = tc::smem_desc(sB + boff, BLBO, 128);
+                        const uint64_t bl = tc::smem_desc(sB + BHALF + boff, BLBO, 128);
+                        mma_tf32(d, ah, bh, idesc, (first && t == 0 && j == 0) ? 0u : 1u);
+                        mma_tf32(d, ah, bl, idesc, 1u);
+                        mma_tf32(d, al, bh, idesc, 1u);
+                    }
                 }
                 tc::commit(&s_empty[buf]);
                 if (s % CH == CH - 1 || s == nst - 1) tc::commit(&d_full[c & 1]);
@@ -779,7 +799,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
         // worked out once; a stage's raw values are loaded into registers
         // one stage ahead, so their latency passes while the converters wait
         // for a free buffer.
-        constexpr int kItems = (2 * kTcRowsB + kTcConvWarps * 32 - 1) / (kTcConvWarps * 32);
+        constexpr int kItems = (KG * tc_rows<KS>() + kTcConvWarps * 32 - 1) / (kTcConvWarps * 32);
         const int rows = kTcPos + halo;
         int it_kg[kItems], it_soff[kItems];
         int64_t it_pos[kItems];
@@ -787,16 +807,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
 #pragma unroll
         for (int q = 0; q < kItems; q++) {
             const int it = tid + q * kTcConvWarps * 32;
-            const int kg = it >= rows ? 1 : 0, n = it - kg * rows;
-            it_on[q] = it < 2 * rows;
+            const int kg = KG == 2 ? (it >= rows ? 1 : 0) : min(it / rows, KG - 1), n = it - kg * rows;
+            it_on[q] = it < KG * rows;
             it_kg[q] = kg;
-            it_soff[q] = kg * (int)kTcBLbo + n * 16;
+            it_soff[q] = kg * (int)BLBO + n * 16;
             it_pos[q] = j0 - halo + n;
             it_in[q] = it_on[q] && it_pos[q] >= 0 && it_pos[q] < a.len;
         }
         float raw[kItems][4];
         auto fetch = [&](int s) {
-            const int ic0 = s * kTcBK;
+            const int ic0 = s * BK;
 #pragma unroll
             for (int q = 0; q < kItems; q++) {
                 const float *src = a.in + (int64_t)(ic0 + 4 * it_kg[q]) * a.len + it_pos[q];
@@ -810,14 +830,28 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
             const int buf = s % NS;
             if (s >= NS && !wait(&s_empty[buf], ((s / NS) - 1) & 1)) break;
             uint8_t *B = sm + buf * SB + ABYTES;
-            const int ic0 = s * kTcBK;
-            // the stage's per-channel prologue constants
-            float ca[8], cb[8];
+            const int ic0 = s * BK;
+            // the stage's per-channel prologue constants: all 8 channels of an
+            // 8-channel stage, or the 4 of each item's K group of a 16-channel one
+            constexpr bool kPerItem = KG > 2;
+            float ca[kPerItem ? 1 : 8], cb[kPerItem ? 1 : 8];
+            float ia[kPerItem ? kItems : 1][4], ib[kPerItem ? kItems : 1][4];
+            if constexpr (kPerItem) {
 #pragma unroll
-            for (int u = 0; u < 8; u++) {
-                const int ic = min(ic0 + u, a.ic - 1);
-                ca[u] = (PRO == P_SNAKE || PRO == P_RMS || PRO == P_LN) ? __ldg(a.pa + ic) : 0.0f;
-                cb[u] = (PRO == P_SNAKE || PRO == P_LN) ? __ldg(a.pb + ic) : 0.0f;
+                for (int q = 0; q < kItems; q++)
+#pragma unroll
+                    for (int u = 0; u < 4; u++) {
+                        const int ic = min(ic0 + 4 * it_kg[q] + u, a.ic - 1);
+                        ia[q][u] = (PRO == P_SNAKE || PRO == P_RMS || PRO == P_LN) ? __ldg(a.pa + ic) : 0.0f;
+                        ib[q][u] = (PRO == P_SNAKE || PRO == P_LN) ? __ldg(a.pb + ic) : 0.0f;
+                    }
+            } else {
+#pragma unroll
+                for (int u = 0; u < 8; u++) {
+                    const int ic = min(ic0 + u, a.ic - 1);
+                    ca[u] = (PRO == P_SNAKE || PRO == P_RMS || PRO == P_LN) ? __ldg(a.pa + ic) : 0.0f;
+                    cb[u] = (PRO == P_SNAKE || PRO == P_LN) ? __ldg(a.pb + ic) : 0.0f;
+                }
             }
 #pragma unroll
             for (int q = 0; q < kItems; q++) {
@@ -834,7 +868,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
                     const int cu = 4 * it_kg[q] + u;
                     // positions outside the input are the convolution's zero padding
                     if (it_in[q] && ic0 + cu < a.ic) {
-                        const float pa = it_kg[q] ? ca[4 + u] : ca[u], pb = it_kg[q] ? cb[4 + u] : cb[u];
+                        float pa, pb;
+                        if constexpr (kPerItem) {
+                            pa = ia[q][u];
+                            pb = ib[q][u];
+                        } else {
+                            pa = it_kg[q] ? ca[4 + u] : ca[u];
+                            pb = it_kg[q] ? cb[4 + u] : cb[u];
+                        }
                         if constexpr (PRO == P_SNAKE) v = snake(v, pa, pb);
                         if constexpr (PRO == P_RMS) v = v * ra * pa;
                         if constexpr (PRO == P_LN) v = (v - ra) * rb * pa + pb;
@@ -843,7 +884,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) k_dec_conv_tc(const ConvArgs a,
                     lo[u] = to_tf32(v - __uint_as_float(hi[u]));
                 }
                 *reinterpret_cast<uint4 *>(B + it_soff[q]) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4 *>(B + kTcBHalf + it_soff[q]) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<uint4 *>(B + BHALF + it_soff[q]) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
             tc::fence_proxy_async_smem();
             __syncwarp();
@@ -1033,7 +1074,7 @@ int launch_conv(int taps, int pro, int epi, const ConvArgs &a0, int device, cuda
     if (a.wtc && tc_mode != 0 && epi != E_SWIGLU && (taps - 1) * a.dil <= kTcMaxHalo) {
         // mode 1: the kernel with the smaller estimated time, from B200
         // measurements of both (tensor cores: about 2.0 + 0.12 x taps us per
-        // 8-channel stage per CTA, in waves of one CTA per SM; CUDA cores:
+        // 8 input channels per CTA, in waves of one CTA per SM; CUDA cores:
         // about 28 TFLOP/s (14 for pointwise convolutions, which stream
         // their input and residual) plus 10 us)
         const int sms = g_sms[device & 63];
@@ -1116,23 +1157,24 @@ float tf32_rna(float x) {
 }
 
 // Tensor-core image of a convolution's weights wl [phases][ic][taps][oc_pad]
-// (conv_layout / convt_layout): per (phase, 128-channel tile, stage of 8
+// (conv_layout / convt_layout): per (phase, 128-channel tile, stage of BK
 // input channels, tap) the A operand of k_dec_conv_tc as it lies in shared
-// memory, [hi, lo][2 K groups][128 rows][4 values], zero outside the
+// memory, [hi, lo][BK / 4 K groups][128 rows][4 values], zero outside the
 // weights; a stage's taps are contiguous, so one bulk copy loads a stage.
 std::vector<float> tc_image(const std::vector<float> &wl, int64_t phases, int64_t ic, int64_t oc, int64_t ks) {
-    const int64_t ocp = round4(oc), tiles = (oc + kTcOc - 1) / kTcOc, nst = (ic + kTcBK - 1) / kTcBK;
-    std::vector<float> img((size_t)(phases * tiles * nst * ks * 2 * 2 * kTcOc * 4), 0.0f);
+    const int bk = tc_bk_of((int)ks), kgs = bk / 4;
+    const int64_t ocp = round4(oc), tiles = (oc + kTcOc - 1) / kTcOc, nst = (ic + bk - 1) / bk;
+    std::vector<float> img((size_t)(phases * tiles * nst * ks * 2 * kgs * kTcOc * 4), 0.0f);
     size_t idx = 0;
     for (int64_t p = 0; p < phases; p++)
         for (int64_t ot = 0; ot < tiles; ot++)
             for (int64_t st = 0; st < nst; st++)
                 for (int64_t t = 0; t < ks; t++)
                     for (int h = 0; h < 2; h++)
-                        for (int kg = 0; kg < 2; kg++)
+                        for (int kg = 0; kg < kgs; kg++)
                             for (int64_t row = 0; row < kTcOc; row++)
                                 for (int u = 0; u < 4; u++, idx++) {
-                                    const int64_t c = st * kTcBK + 4 * kg + u, o = ot * kTcOc + row;
+                                    const int64_t c = st * bk + 4 * kg + u, o = ot * kTcOc + row;
                                     if (c >= ic || o >= oc) continue;
                                     const float w = wl[(size_t)(((p * ic + c) * ks + t) * ocp + o)];
                                     const float hi = tf32_rna(w);
