@@ -558,12 +558,12 @@ __global__ void __launch_bounds__(kFinT) k_dec_final(const float *in, int C, int
 // runs in the other buffer.  One CTA computes 128 output channels x 256
 // positions (one phase of a transposed convolution).
 //
-// Operands in shared memory, canonical K-major layout without swizzle
-// (8-row x 16-byte core matrices; rows 16 bytes apart, K groups of 4 TF32
-// values `LBO` apart):
-// A stage holds BK input channels (BK / 4 K groups): 16 for pointwise
-// convolutions (their stages are short, so fewer, longer stages keep the
-// converters' per-stage round trip off the tensor cores), 8 otherwise.
+// A pipeline stage holds BK input channels (BK / 4 K groups of 4): 16 for
+// pointwise convolutions (their stages are short, so fewer, longer stages
+// keep the converters' per-stage round trip off the tensor cores), 8
+// otherwise.  Operands in shared memory, canonical K-major layout without
+// swizzle (8-row x 16-byte core matrices; rows 16 bytes apart, K groups of
+// 4 TF32 values `LBO` apart):
 //   A (weights) per stage and tap: [hi, lo][BK / 4 K groups][128 rows][4],
 //     LBO 2048, arriving as one bulk copy per stage from an image prepared
 //     on upload (tc_image below);
