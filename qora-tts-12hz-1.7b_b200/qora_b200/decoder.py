@@ -278,3 +278,52 @@ class SpeechDecoder:
         _lib.call("qora_decode_to_audio_device", self.h, codes_dev.data_ptr(), frames, warmup_frames,
                   samples_dev.data_ptr(), C.byref(n), s)
         return int(n.value)
+
+
+# ------------------------------------------------- the decoder's code inputs
+def warmup_tail(codes, k: int) -> np.ndarray:
+    """warmup_tail (generate_new.rs:728-737): the last k frames of every
+    quantizer row of codes [num_quantizers][T], the warm-up codes the next
+    chunk of the same voice hands to decode_to_audio (generate_new.rs:704;
+    main.rs:642).  k == 0 or k >= T gives all of codes; no rows gives none."""
+    codes = np.asarray(codes, dtype=np.uint32)
+    if codes.size == 0 and (codes.ndim < 2 or codes.shape[0] == 0):
+        return np.zeros((0, 0), np.uint32)
+    if codes.ndim != 2:
+        raise ValueError(f"codes must be [num_quantizers][frames], got shape {codes.shape}")
+    T = codes.shape[1]
+    if k == 0 or k >= T:
+        return codes.copy()
+    return codes[:, T - k:].copy()
+
+
+_VCOD = b"VCOD"
+
+
+def write_codes_file(path, codes) -> None:
+    """write_codes_file (generate_new.rs:739-753): "VCOD", u32 quantizer
+    rows, u32 frames, then the codes row by row as u16, all little-endian
+    (a code keeps its low 16 bits, as the reference's `as u16`)."""
+    codes = np.asarray(codes, dtype=np.uint32)
+    if codes.ndim != 2 or codes.shape[0] == 0:
+        raise ValueError(f"codes must be [num_quantizers][frames] with at least one row, got {codes.shape}")
+    with open(path, "wb") as f:
+        f.write(_VCOD)
+        f.write(np.array(codes.shape, dtype="<u4").tobytes())
+        f.write((codes & 0xFFFF).astype("<u2").tobytes())
+
+
+def read_codes_file(path) -> np.ndarray:
+    """load_all_voice_codes (main.rs:697-737): a VCOD file -> codes
+    [num_quantizers][frames] uint32.  A wrong magic or a short file raises
+    ValueError (the reference prints and exits)."""
+    with open(path, "rb") as f:
+        raw = f.read()
+    if raw[:4] != _VCOD:
+        raise ValueError("invalid codes file (bad magic)")
+    if len(raw) < 12:
+        raise ValueError("codes file too short for its header")
+    nq, T = (int(v) for v in np.frombuffer(raw, dtype="<u4", count=2, offset=4))
+    if len(raw) < 12 + 2 * nq * T:
+        raise ValueError(f"codes file holds {len(raw) - 12} code bytes, {2 * nq * T} expected")
+    return np.frombuffer(raw, dtype="<u2", count=nq * T, offset=12).astype(np.uint32).reshape(nq, T)

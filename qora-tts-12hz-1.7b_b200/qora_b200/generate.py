@@ -13,6 +13,8 @@ from __future__ import annotations
 import ctypes as C
 from dataclasses import dataclass
 
+import numpy as np
+
 from . import _lib
 
 # Special token ids (generate_new.rs:24-35)
@@ -42,9 +44,27 @@ class TTSParams:
     codec_bos_id: int = CODEC_BOS
     onset_frames: int = 0
     onset_temperature: float = 0.3
+    decode_warmup: bool = False      # warm the decoder up on the reference clip's codes
+    warmup_frames: int = 0           # only their last N frames (0: all)
 
     def sample_params(self) -> _lib.SampleParams:
         return _lib.SampleParams(self.temperature, self.top_k, self.top_p, self.repetition_penalty)
+
+
+def decoder_warmup(params: TTSParams, chain_codes=None, ref_codes=None):
+    """The warm-up codes decode_to_audio gets (generate_new.rs:695-712):
+    the previous chunk's tail of the same voice when there is one; else, with
+    decode_warmup set, the reference clip's codes (their last warmup_frames
+    frames when that is above 0); else None.  Codes are [num_quantizers][T]."""
+    from .decoder import warmup_tail
+    if chain_codes is not None:
+        cc = np.asarray(chain_codes, dtype=np.uint32)
+        if cc.ndim == 2 and cc.shape[0] > 0 and cc.shape[1] > 0:
+            return cc
+    if params.decode_warmup and ref_codes is not None:
+        rc = np.asarray(ref_codes, dtype=np.uint32)
+        return warmup_tail(rc, params.warmup_frames) if params.warmup_frames > 0 else rc
+    return None
 
 
 def frame_temperature(params: TTSParams, frame_idx: int) -> float:
